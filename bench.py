@@ -1,0 +1,335 @@
+"""Benchmark of the NVFP4 grouped GEMM (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl ours|reference]
+
+A step is one grouped-GEMM call over the whole configuration (default: cfg2,
+G=8 experts, M_g=1024, N=4096, K=7168, per-group global scale U[0.5, 2]).
+
+Our arm (default):
+  * `value`: whole-job NVFP4 TFLOP/s with inputs resident in HBM, timed with CUDA
+    events on the launching stream over exactly K calls (barrier + synchronize on
+    both sides, max over ranks). Inputs (232 MB for cfg2) exceed the 126 MB L2.
+  * `e2e`: the same metric through the public API with host buffers: every step
+    copies the operands from pinned host memory, calls custom_kernel and copies
+    the fp16 outputs back.
+  * `roofline`: the grouped-GEMM kernel against the dense FP4 tensor peak derived
+    from MEASURED_PEAKS.json (4 x the measured cuBLAS bf16 figure).
+  * `cpu_baseline`: the CPU oracle (numpy restatement of the reference's
+    ref_kernel) on the full configuration, rank 0 at N=1 only.
+With N GPUs each rank runs its own set of experts of the same shape (weak scaling;
+expert parallelism needs no collective on the data path).
+
+Reference arm (--impl reference): the reference's CPU path (the oracle port of
+ref_kernel) timed on the host cores; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAK_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+FP4_PER_BF16 = 4.0  # dense FP4 : dense BF16 tensor throughput on B200 (9 : 2.25 PFLOP/s)
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="cfg2")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tile-n", type=int, default=None)
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAK_FALLBACK, "fallback"
+
+
+def load_traffic(kernel_tag: str, config: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        d = json.load(f)
+    e = d.get(f"{kernel_tag}:{config}")
+    return None if e is None else e.get("dram_bytes_per_launch")
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples taken while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int, enabled: bool = True):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+        if not enabled:
+            return
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_baseline(cfg: str):
+    """Time the CPU oracle (numpy restatement of ref_kernel) on the configuration."""
+    import numpy as np
+
+    from oracle import nvfp4_oracle as O
+    import submission
+
+    pkg = submission.load_package()
+    prob = pkg.workloads.make_config(cfg, seed=0, device="cpu")
+    groups = [g for g in range(prob.num_groups) if prob.m[g] > 0]
+    arrays = [(prob.a[g].numpy(), prob.b[g].numpy(), prob.sfa_plain[g].numpy(),
+               prob.sfb_plain[g].numpy(), prob.b2[g].numpy() if prob.gated else None,
+               prob.sfb2_plain[g].numpy() if prob.gated else None, prob.alpha[g],
+               prob.alpha2[g] if prob.gated else 1.0) for g in groups]
+    budget_s = 20.0
+    done_flops = 0.0
+    t0 = time.perf_counter()
+    calls = 0
+    for (a, b, sfa, sfb, b2, sfb2, al, al2), g in zip(arrays, groups):
+        if b2 is not None:
+            O.ref_gated(a, b, b2, sfa, sfb, sfb2, al, al2)
+        else:
+            O.ref_gemm(a, b, sfa, sfb, al)
+        done_flops += 2.0 * prob.m[g] * prob.n * prob.k * (2 if prob.gated else 1)
+        calls += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    threads = os.cpu_count()
+    return {"value": done_flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{cfg}: {calls} of {prob.num_groups} groups through the numpy oracle "
+                      f"(dequantise + fp32 BLAS matmul + fp16), {dt:.2f} s",
+            "us_per_call_extrapolated": dt / max(done_flops, 1.0) * prob.flops() * 1e6}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    res = []
+    for _ in range(args.warmup):
+        pass  # the CPU path has no warm-up state worth excluding beyond the first step below
+    steps = max(1, min(args.steps, 3))
+    for _ in range(steps):
+        res.append(cpu_baseline(args.config))
+    v = statistics.median(r["value"] for r in res)
+    line = {
+        "impl": "reference", "metric": f"NVFP4 grouped GEMM TFLOP/s ({args.config})",
+        "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.config},
+        "cpu_baseline": {**res[0], "value": v},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    import submission
+
+    pkg = submission.load_package()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+
+    # Each rank owns its own experts (seed = rank): weak scaling, no data-path collective.
+    prob = pkg.workloads.make_config(args.config, seed=rank, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sizes = prob.problem_sizes()
+
+    def step():
+        pkg.grouped_gemm(prob.a, prob.b, prob.sfa, prob.sfb, prob.c, sizes, alpha=prob.alpha,
+                         b2=prob.b2, sfb2=prob.sfb2, alpha2=prob.alpha2, tile_n=args.tile_n,
+                         stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------------------------------------------------------- device-resident timing
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks = ClockSampler(local_rank, enabled=not args.no_clocks)
+    time.sleep(0.3 if not args.no_clocks else 0.0)
+    barrier()
+    torch.cuda.synchronize(dev)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clk = clocks.stop()
+    ms_total = max_over_ranks(ev0.elapsed_time(ev1))
+    ms_per_step = ms_total / args.steps
+    errors = pkg.check_device_errors(dev, stream)
+    flops_rank = prob.flops()
+    value = flops_rank * world / (ms_per_step * 1e-3) / 1e12
+
+    # ---------------------------------------------------------------- end to end (host buffers)
+    e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
+    host_in = [t.cpu().pin_memory() for t in
+               prob.a + prob.b + prob.sfa + prob.sfb + (prob.b2 or []) + (prob.sfb2 or [])]
+    dev_in = prob.a + prob.b + prob.sfa + prob.sfb + (prob.b2 or []) + (prob.sfb2 or [])
+    host_out = [torch.empty(c.shape, dtype=c.dtype).pin_memory() for c in prob.c]
+    data = prob.reference_data()
+    scales = prob.global_scales()
+
+    def e2e_step():
+        for h, d in zip(host_in, dev_in):
+            d.copy_(h, non_blocking=True)
+        pkg.custom_kernel(data, global_scales=scales, tile_n=args.tile_n, stream=stream)
+        for h, c in zip(host_out, prob.c):
+            h.copy_(c, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    ev0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / e2e_steps
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+
+    # ---------------------------------------------------------------- CPU baseline (rank 0, N=1)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.config)
+
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks, peak_kind = load_peaks()
+    tensor_peak = FP4_PER_BF16 * float(peaks["bf16_tflops"])
+    achieved = flops_rank / (ms_per_step * 1e-3) / 1e12
+    kernel_tag = "gated" if prob.gated else f"n{args.tile_n or 256}"
+    traffic = load_traffic(kernel_tag, args.config)
+    line = {
+        "metric": f"NVFP4 grouped GEMM TFLOP/s ({args.config})",
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": max(args.warmup, 3),
+        "ms_per_step": ms_per_step,
+        "us_per_call": ms_per_step * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e2m1xe4m3->f32->f16",
+        "data": "synthetic (seeded; e2m1 codes uniform over 16, E4M3 scales 2^U{-4..3})",
+        "config": {"workload": args.config, "groups_per_gpu": prob.num_groups,
+                   "m_per_group": prob.m if len(prob.m) <= 16 else f"{sum(prob.m)} rows",
+                   "n": prob.n, "k": prob.k, "gated": prob.gated,
+                   "input_bytes_per_gpu": prob.input_bytes(),
+                   "l2": "inputs larger than L2 (126 MB); no flush",
+                   "parallelism": f"ep{world} (experts sharded, no data-path collective)"},
+        "gpu_launches": args.steps,  # one persistent GEMM kernel per call (descriptors reused)
+        "device_error_bits": errors,
+        "e2e": {"value": flops_rank * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "custom_kernel(data) with pinned-host copies of inputs and outputs"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": tensor_peak,
+                     "unit": "TFLOP/s", "frac": achieved / tensor_peak,
+                     "peak_source": f"{peak_kind}: 4 x bf16_tflops ({peaks['bf16_tflops']})",
+                     "traffic": traffic,
+                     "algorithmic_bytes": prob.algorithmic_bytes(),
+                     "hbm_frac": prob.algorithmic_bytes() / (ms_per_step * 1e-3) / 1e9
+                     / float(peaks["hbm_gbs"])},
+        "clocks": clk,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,131 @@
+/*
+ * nvfp4_group_gemm.h - C ABI of the B200 (sm_100a) NVFP4 block-scaled grouped GEMM.
+ *
+ * Plain pointers and sizes only; no CUDA or framework types appear in the
+ * signatures (streams are passed as `void*` holding a cudaStream_t, NULL = the
+ * legacy default stream). Every entry point returns an nvfp4_status code and
+ * never aborts the process. Launches are asynchronous on the given stream.
+ *
+ * Reference interfaces replaced (goldbar123467/NVFP4-Group-Gemm):
+ *   custom_kernel(data), 4-tuple grouped branch ... submission.py:788-858
+ *   run_single_gemm(...) + _fused_silu_gate(...) .. submission.py:742-785, 860-886, 707-710
+ *   compile_kernel(problem_sizes) ................. submission.py:715-739 (no JIT here:
+ *                                                   kernels are compiled ahead of time)
+ *   to_blocked(input_matrix) ...................... REFERENCE_IMPL.md:19-42
+ *   create_reordered_scale_factor_tensor(...) ..... REFERENCE_IMPL.md:89-137 (same bytes)
+ */
+#ifndef NVFP4_GROUP_GEMM_H_
+#define NVFP4_GROUP_GEMM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define NVFP4_API __attribute__((visibility("default")))
+#else
+#define NVFP4_API
+#endif
+
+#define NVFP4_ABI_VERSION 1
+
+typedef enum nvfp4_status {
+  NVFP4_OK = 0,
+  NVFP4_ERR_INVALID_ARGUMENT = 1,  /* null table, negative count, bad flags */
+  NVFP4_ERR_BAD_SHAPE = 2,         /* K % 256 != 0, K <= 0, N % 8 != 0, negative sizes */
+  NVFP4_ERR_MISALIGNED = 3,        /* a tensor base address is not 16-byte aligned */
+  NVFP4_ERR_NULL_POINTER = 4,      /* a tensor of a non-empty group is NULL */
+  NVFP4_ERR_WORKSPACE = 5,         /* workspace NULL, too small, or not 256-byte aligned */
+  NVFP4_ERR_CUDA = 6,              /* a CUDA runtime call or kernel launch failed */
+  NVFP4_ERR_DEVICE_TIMEOUT = 7,    /* a kernel gave up waiting (see nvfp4_workspace_check) */
+  NVFP4_ERR_UNSUPPORTED_DEVICE = 8,/* current device is not compute capability 10.0 */
+  NVFP4_ERR_DRIVER = 9             /* tensor-map encoder entry point unavailable */
+} nvfp4_status;
+
+/* Flags for nvfp4_grouped_gemm. */
+#define NVFP4_FLAG_GATED 0x1u     /* C = fp16(silu(fp16(a*A.B^T)) * fp16(a2*A.B2^T)) */
+#define NVFP4_FLAG_TILE_N128 0x2u /* force 128-column tiles (non-gated only) */
+#define NVFP4_FLAG_TILE_N256 0x4u /* force 256-column tiles (non-gated only) */
+#define NVFP4_FLAG_REUSE_DESCRIPTORS 0x8u /* workspace already holds this exact group table
+                                             (same pointers, sizes, scales, flags) from the
+                                             previous call on the same stream: skip rebuilding */
+
+/*
+ * One GEMM of the group. All matrices are row-major with K innermost ("K-major"),
+ * exactly the storage of the reference's tensors (L = 1):
+ *   a    : packed e2m1, [m, k/2] bytes     (float4_e2m1fn_x2 [M, K//2, 1]; low nibble = even k)
+ *   b    : packed e2m1, [n, k/2] bytes     (gate weights when NVFP4_FLAG_GATED)
+ *   b2   : packed e2m1, [n, k/2] bytes     (up weights; gated only, else NULL)
+ *   sfa  : E4M3 scales of a in the 128x4-blocked layout, ceil(m/128)*128 * k/16 bytes
+ *          (the storage of the reference's sfa_reordered tensor, = to_blocked(sfa))
+ *   sfb  : blocked E4M3 scales of b, ceil(n/128)*128 * k/16 bytes
+ *   sfb2 : blocked E4M3 scales of b2 (gated only)
+ *   c    : fp16 [m, n] output, written in place
+ *   alpha, alpha2 : per-tensor fp32 global scales of the (gate, up) products; 1.0 = none
+ * Constraints: k > 0 and k % 256 == 0; n % 8 == 0; every pointer 16-byte aligned.
+ * Groups with m == 0 or n == 0 are skipped (their pointers are not read).
+ */
+typedef struct nvfp4_group {
+  const void* a;
+  const void* b;
+  const void* b2;
+  const void* sfa;
+  const void* sfb;
+  const void* sfb2;
+  void* c;
+  int32_t m;
+  int32_t n;
+  int32_t k;
+  float alpha;
+  float alpha2;
+} nvfp4_group;
+
+/*
+ * Device workspace bytes needed for `num_groups` groups (group records, tensor
+ * maps and a device error word). The workspace is owned by the caller, must be
+ * 256-byte aligned, must not be shared by calls that may run concurrently, and
+ * may be reused by consecutive calls on one stream.
+ */
+NVFP4_API size_t nvfp4_workspace_size(int num_groups);
+
+/*
+ * Grouped GEMM over `num_groups` groups in one persistent launch (replaces
+ * custom_kernel's 4-tuple path, submission.py:804-858, and, with
+ * NVFP4_FLAG_GATED, the dual GEMM + SiLU path, submission.py:860-886).
+ * `groups` is a HOST array read before the call returns.
+ */
+NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsigned int flags,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Convert plain row-major E4M3 scales [rows, sf_cols] (row stride `ld` bytes)
+ * into the 128x4-blocked layout the kernel consumes; the output holds
+ * nvfp4_sf_blocked_size(rows, sf_cols) bytes, padding rows/columns written as 0.
+ * Bit-exact with to_blocked (REFERENCE_IMPL.md:19-42).
+ */
+NVFP4_API size_t nvfp4_sf_blocked_size(int rows, int sf_cols);
+NVFP4_API int nvfp4_sf_to_blocked(const void* plain, void* blocked, int rows, int sf_cols,
+                                  int64_t ld, void* stream);
+
+/*
+ * Synchronise `stream`, then read and clear the device error word of `workspace`.
+ * Returns NVFP4_ERR_DEVICE_TIMEOUT if a kernel using it gave up on a wait; the
+ * reason bits are stored to *device_error_bits when non-NULL.
+ */
+NVFP4_API int nvfp4_workspace_check(void* workspace, void* stream, unsigned int* device_error_bits);
+
+/* Human-readable text of a status code, and detail of the last error on this thread. */
+NVFP4_API const char* nvfp4_strerror(int status);
+NVFP4_API const char* nvfp4_last_error_detail(void);
+
+/* NVFP4_ABI_VERSION of the loaded library. */
+NVFP4_API int nvfp4_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVFP4_GROUP_GEMM_H_ */

@@ -1,0 +1,175 @@
+"""ctypes binding of the C ABI declared in ``include/nvfp4_group_gemm.h``.
+
+The shared library is the only compute path: if it is missing or cannot be
+loaded, every entry point raises instead of falling back to anything else.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import numpy as np
+
+from . import build as _build
+
+LIB_PATH = _build.LIB_PATH
+
+# Status codes (nvfp4_status).
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_BAD_SHAPE = 2
+ERR_MISALIGNED = 3
+ERR_NULL_POINTER = 4
+ERR_WORKSPACE = 5
+ERR_CUDA = 6
+ERR_DEVICE_TIMEOUT = 7
+ERR_UNSUPPORTED_DEVICE = 8
+ERR_DRIVER = 9
+
+# Flags (NVFP4_FLAG_*).
+FLAG_GATED = 0x1
+FLAG_TILE_N128 = 0x2
+FLAG_TILE_N256 = 0x4
+FLAG_REUSE_DESCRIPTORS = 0x8
+
+# Every symbol the public header declares; the library must export all of them.
+EXPORTED_SYMBOLS = (
+    "nvfp4_abi_version",
+    "nvfp4_strerror",
+    "nvfp4_last_error_detail",
+    "nvfp4_workspace_size",
+    "nvfp4_grouped_gemm",
+    "nvfp4_sf_blocked_size",
+    "nvfp4_sf_to_blocked",
+    "nvfp4_workspace_check",
+)
+
+
+class Nvfp4Group(ctypes.Structure):
+    """Mirror of ``nvfp4_group`` (80 bytes)."""
+
+    _fields_ = [
+        ("a", ctypes.c_void_p),
+        ("b", ctypes.c_void_p),
+        ("b2", ctypes.c_void_p),
+        ("sfa", ctypes.c_void_p),
+        ("sfb", ctypes.c_void_p),
+        ("sfb2", ctypes.c_void_p),
+        ("c", ctypes.c_void_p),
+        ("m", ctypes.c_int32),
+        ("n", ctypes.c_int32),
+        ("k", ctypes.c_int32),
+        ("alpha", ctypes.c_float),
+        ("alpha2", ctypes.c_float),
+    ]
+
+
+# The same record as a numpy structured dtype, so that a whole group table is
+# filled with a few vectorised column assignments instead of per-field ctypes calls.
+GROUP_DTYPE = np.dtype(
+    {
+        "names": [f[0] for f in Nvfp4Group._fields_],
+        "formats": ["<u8"] * 7 + ["<i4"] * 3 + ["<f4"] * 2,
+        "offsets": [getattr(Nvfp4Group, f[0]).offset for f in Nvfp4Group._fields_],
+        "itemsize": ctypes.sizeof(Nvfp4Group),
+    }
+)
+assert GROUP_DTYPE.itemsize == 80
+
+
+class Nvfp4Error(RuntimeError):
+    """A non-zero status returned by the native library."""
+
+    def __init__(self, status: int, message: str, detail: str = ""):
+        self.status = status
+        self.detail = detail
+        text = f"nvfp4 status {status}: {message}"
+        if detail:
+            text += f" ({detail})"
+        super().__init__(text)
+
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def load_library(path: str | None = None) -> ctypes.CDLL:
+    """Load (once) and return the native library, declaring argument types."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    with _lib_lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise ImportError(
+                f"native library {p} is missing; build it with "
+                "`python __graft_entry__.py build` (nvcc, sm_100a)"
+            )
+        lib = ctypes.CDLL(p)
+        vp, sz, i32, i64, u32 = (ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
+                                 ctypes.c_int64, ctypes.c_uint)
+        lib.nvfp4_abi_version.argtypes = []
+        lib.nvfp4_abi_version.restype = i32
+        lib.nvfp4_strerror.argtypes = [i32]
+        lib.nvfp4_strerror.restype = ctypes.c_char_p
+        lib.nvfp4_last_error_detail.argtypes = []
+        lib.nvfp4_last_error_detail.restype = ctypes.c_char_p
+        lib.nvfp4_workspace_size.argtypes = [i32]
+        lib.nvfp4_workspace_size.restype = sz
+        lib.nvfp4_grouped_gemm.argtypes = [vp, i32, u32, vp, sz, vp]
+        lib.nvfp4_grouped_gemm.restype = i32
+        lib.nvfp4_sf_blocked_size.argtypes = [i32, i32]
+        lib.nvfp4_sf_blocked_size.restype = sz
+        lib.nvfp4_sf_to_blocked.argtypes = [vp, vp, i32, i32, i64, vp]
+        lib.nvfp4_sf_to_blocked.restype = i32
+        lib.nvfp4_workspace_check.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint)]
+        lib.nvfp4_workspace_check.restype = i32
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def check(status: int, lib: ctypes.CDLL | None = None) -> None:
+    """Raise Nvfp4Error for a non-zero status (with the library's detail text)."""
+    if status == OK:
+        return
+    lib = lib or load_library()
+    msg = lib.nvfp4_strerror(status).decode()
+    detail = lib.nvfp4_last_error_detail().decode()
+    raise Nvfp4Error(status, msg, detail)
+
+
+def workspace_size(num_groups: int) -> int:
+    return int(load_library().nvfp4_workspace_size(num_groups))
+
+
+def sf_blocked_size(rows: int, sf_cols: int) -> int:
+    return int(load_library().nvfp4_sf_blocked_size(rows, sf_cols))
+
+
+def grouped_gemm_raw(table: np.ndarray, flags: int, workspace_ptr: int, workspace_bytes: int,
+                     stream_ptr: int) -> None:
+    """Call nvfp4_grouped_gemm on a GROUP_DTYPE table (host memory)."""
+    assert table.dtype == GROUP_DTYPE and table.flags["C_CONTIGUOUS"]
+    lib = load_library()
+    st = lib.nvfp4_grouped_gemm(table.ctypes.data, int(table.shape[0]), flags, workspace_ptr,
+                                workspace_bytes, stream_ptr)
+    check(st, lib)
+
+
+def sf_to_blocked_raw(plain_ptr: int, blocked_ptr: int, rows: int, sf_cols: int, ld: int,
+                      stream_ptr: int) -> None:
+    lib = load_library()
+    check(lib.nvfp4_sf_to_blocked(plain_ptr, blocked_ptr, rows, sf_cols, ld, stream_ptr), lib)
+
+
+def workspace_check(workspace_ptr: int, stream_ptr: int) -> int:
+    """Synchronise and return the device error bits (raises on timeout bits)."""
+    lib = load_library()
+    bits = ctypes.c_uint(0)
+    st = lib.nvfp4_workspace_check(workspace_ptr, stream_ptr, ctypes.byref(bits))
+    check(st, lib)
+    return int(bits.value)

@@ -1,0 +1,441 @@
+// Persistent, warp-specialised NVFP4 block-scaled grouped GEMM for sm_100a.
+//
+//   C_g[m, n] = fp16( alpha_g * sum_k  e2m1(A_g[m, k]) * sfa_g[m, k/16]
+//                                     * e2m1(B_g[n, k]) * sfb_g[n, k/16] )
+//
+// and, when GATED, the fused MoE gate/up form
+//
+//   C_g = fp16( silu(fp16(alpha_g * A_g Bgate_g^T)) * fp16(alpha2_g * A_g Bup_g^T) )
+//
+// which keeps the reference's rounding of the two projections to fp16 before the
+// SiLU product (submission.py:877-884, :707-710).
+//
+// One CTA per SM walks a static schedule of (group, m-tile, n-tile) work units;
+// inside the CTA:
+//   warp 0       TMA producer: A/B tiles by tensor map (128B swizzle), scale-factor
+//                blocks by plain bulk copies, into a STAGES-deep mbarrier ring
+//   warp 1       TMEM allocator + single-thread tcgen05 issuer: scale factors
+//                smem->TMEM (tcgen05.cp), 4 x tcgen05.mma kind::mxf4nvf4 per stage
+//   warps 2..5   epilogue: TMEM -> registers -> alpha / SiLU -> fp16 -> swizzled
+//                smem -> TMA store (out-of-range rows/columns clipped by the map)
+//
+// Every mbarrier wait is bounded in time: on timeout the CTA records the reason
+// in the workspace error word, drains its in-flight copies and MMAs, frees TMEM
+// and returns, so a malformed launch cannot hang the GPU.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "nvfp4_types.cuh"
+#include "sm100_ptx.cuh"
+
+namespace nvfp4 {
+
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s per wait
+constexpr int kNumThreads = 192;
+constexpr int kEpilogueWarp0 = 2;
+constexpr int kEpilogueWarps = 4;
+constexpr int kTmemCols = 512;
+
+template <int MMA_N, bool GATED, int STAGES>
+struct GemmConfig {
+  static_assert(MMA_N == 128 || MMA_N == 256, "MMA N must be 128 or 256");
+  static_assert(!GATED || MMA_N == 256, "gated tiles pair 128 gate + 128 up columns");
+  static constexpr int kOutN = GATED ? MMA_N / 2 : MMA_N;  // output columns per tile
+  static constexpr int kABytes = kBlockM * kRowBytesPerStage;
+  static constexpr int kBBytes = MMA_N * kRowBytesPerStage;
+  static constexpr int kSfaBytes = 4 * kSfBlockBytes;                 // 128 rows x 16 scales
+  static constexpr int kSfbBlocks = MMA_N / 128;
+  static constexpr int kSfbBytes = kSfbBlocks * 4 * kSfBlockBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  static constexpr int kAccStages = (MMA_N == 128) ? 2 : 1;
+  // TMEM columns: accumulators first, then one scale-factor slot per smem stage.
+  static constexpr int kSfaCols = 4 * 4;              // 4 MMAs x 4 columns (128 lanes x 4 B)
+  static constexpr int kSfbColsPerMma = MMA_N / 32;   // one column per 32 rows of B
+  static constexpr int kSfbCols = 4 * kSfbColsPerMma;
+  static constexpr int kSfColsPerStage = kSfaCols + kSfbCols;
+  static constexpr int kSfColBase = kAccStages * MMA_N;
+  static_assert(kSfColBase + STAGES * kSfColsPerStage <= kTmemCols, "TMEM over-subscribed");
+  static constexpr int kEpiBufBytes = 32 * 128;  // 32 rows x 64 fp16, one TMA store box
+  static constexpr int kEpiBufsPerWarp = 2;
+  static constexpr int kEpiBytes = kEpilogueWarps * kEpiBufsPerWarp * kEpiBufBytes;
+  static constexpr int kBarrierBytes = 8 * (2 * STAGES + 2 * kAccStages + 1) + 16;
+  static constexpr int kSmemBytes = 1024 /*alignment slack*/ + STAGES * kStageBytes + kEpiBytes +
+                                    kBarrierBytes;
+  static_assert(kSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
+  static constexpr uint32_t kIdesc = ptx::make_idesc_mxf4nvf4(kBlockM, MMA_N);
+  static constexpr int kNTilesPerOut = kOutN;  // output column span of one tile
+};
+
+// Bounded wait: true when the phase completed; false after a timeout (reason
+// recorded) or when another role of this CTA has already aborted.
+__device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity,
+                                           volatile uint32_t* abort_flag, uint32_t* error_bits,
+                                           uint32_t reason) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = ptx::globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 31u) == 0) {
+      if (*abort_flag) return false;
+      if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        *abort_flag = 1u;
+        atomicOr(error_bits, reason);
+        return false;
+      }
+    }
+  }
+}
+
+// Warp-wide bounded wait with one decision for all lanes (the epilogue's TMEM
+// loads are warp-collective, so lanes must never disagree about a timeout).
+// Lane 0 waits; once it has seen the phase complete, every lane re-probes the
+// same (already completed) phase to take its own acquire.
+__device__ __forceinline__ bool warp_wait_phase(uint64_t* bar, uint32_t parity,
+                                                volatile uint32_t* abort_flag,
+                                                uint32_t* error_bits, uint32_t reason, int lane) {
+  int ok = 1;
+  if (lane == 0) ok = wait_phase(bar, parity, abort_flag, error_bits, reason) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) {
+    for (uint32_t i = 0; i < (1u << 20) && !ptx::mbar_try_wait(bar, parity); ++i) {
+    }
+  }
+  return ok != 0;
+}
+
+// Locate the group owning `tile` (tiles are numbered group by group); `g` is a
+// cursor that only moves forward because every role walks its tiles in order.
+__device__ __forceinline__ int advance_group(const GroupDev* groups, int num_groups, int g,
+                                             int tile) {
+  while (g + 1 < num_groups && tile >= groups[g].tile_end) ++g;
+  return g;
+}
+
+template <int MMA_N, bool GATED, int STAGES>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    nvfp4_grouped_gemm_kernel(const __grid_constant__ GemmParams p) {
+  using Cfg = GemmConfig<MMA_N, GATED, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* stage_base = smem;
+  uint8_t* epi_base = smem + STAGES * Cfg::kStageBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_base + Cfg::kEpiBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* accf_bar = empty_bar + STAGES;
+  uint64_t* acce_bar = accf_bar + Cfg::kAccStages;
+  uint64_t* drain_bar = acce_bar + Cfg::kAccStages;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile uint32_t* abort_flag = tmem_holder + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(&full_bar[s], 1);
+      ptx::mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < Cfg::kAccStages; ++a) {
+      ptx::mbar_init(&accf_bar[a], 1);
+      ptx::mbar_init(&acce_bar[a], kEpilogueWarps);
+    }
+    ptx::mbar_init(drain_bar, 1);
+    *abort_flag = 0u;
+    ptx::fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_holder, kTmemCols);
+    ptx::tmem_relinquish_alloc_permit();
+  }
+  // The descriptor builder that ran just before this grid wrote the group
+  // records and tensor maps this kernel reads.
+  ptx::grid_dependency_wait();
+  ptx::tcgen05_fence_before_sync();
+  __syncthreads();
+  ptx::tcgen05_fence_after_sync();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const GroupDev* __restrict__ groups = p.groups;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (ptx::elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      int g = 0, acquired_g = -1;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x) {
+        g = advance_group(groups, p.num_groups, g, tile);
+        const GroupDev gd = groups[g];
+        const TmaDesc* maps = p.maps + static_cast<size_t>(g) * kMapsPerGroup;
+        if (g != acquired_g) {
+          ptx::tensormap_fence_acquire(&maps[kMapA]);
+          ptx::tensormap_fence_acquire(&maps[kMapB]);
+          if (GATED) ptx::tensormap_fence_acquire(&maps[kMapB2]);
+          acquired_g = g;
+        }
+        const int local = tile - gd.tile_start;
+        const int mt = local % gd.tiles_m;
+        const int nt = local / gd.tiles_m;
+        const int ktiles = gd.k / kBlockK;
+        const int rest_k = gd.k / 64;  // 4-scale column blocks along K
+        const int rest_n = (gd.n + 127) / 128;
+        // Scale-factor blocks of B for this tile (each 128 rows x 16 scales = 2 KiB per stage).
+        const uint8_t* sfb_blk0;
+        const uint8_t* sfb_blk1 = nullptr;
+        if (GATED) {
+          sfb_blk0 = gd.sfb + static_cast<size_t>(nt) * rest_k * kSfBlockBytes;
+          sfb_blk1 = gd.sfb2 + static_cast<size_t>(nt) * rest_k * kSfBlockBytes;
+        } else if (MMA_N == 256) {
+          sfb_blk0 = gd.sfb + static_cast<size_t>(2 * nt) * rest_k * kSfBlockBytes;
+          if (2 * nt + 1 < rest_n)
+            sfb_blk1 = gd.sfb + static_cast<size_t>(2 * nt + 1) * rest_k * kSfBlockBytes;
+        } else {
+          sfb_blk0 = gd.sfb + static_cast<size_t>(nt) * rest_k * kSfBlockBytes;
+        }
+        const uint8_t* sfa_blk = gd.sfa + static_cast<size_t>(mt) * rest_k * kSfBlockBytes;
+        const uint32_t tx = Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes +
+                            (sfb_blk1 != nullptr ? 2 : 1) * 4 * kSfBlockBytes;
+        for (int kt = 0; kt < ktiles; ++kt) {
+          if (!wait_phase(&empty_bar[stage], phase ^ 1u, abort_flag, p.error_bits,
+                          kDevErrProducerTimeout)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = stage_base + stage * Cfg::kStageBytes;
+          uint8_t* sB = sA + Cfg::kABytes;
+          uint8_t* sSFA = sB + Cfg::kBBytes;
+          uint8_t* sSFB = sSFA + Cfg::kSfaBytes;
+          ptx::mbar_arrive_expect_tx(&full_bar[stage], tx);
+          const int kx = kt * kRowBytesPerStage;
+          ptx::tma_load_2d(sA, &maps[kMapA], &full_bar[stage], kx, mt * kBlockM);
+          if (GATED) {
+            ptx::tma_load_2d(sB, &maps[kMapB], &full_bar[stage], kx, nt * 128);
+            ptx::tma_load_2d(sB + 128 * kRowBytesPerStage, &maps[kMapB2], &full_bar[stage], kx,
+                             nt * 128);
+          } else if (MMA_N == 256) {
+            ptx::tma_load_2d(sB, &maps[kMapB], &full_bar[stage], kx, nt * 256);
+            ptx::tma_load_2d(sB + 128 * kRowBytesPerStage, &maps[kMapB], &full_bar[stage], kx,
+                             nt * 256 + 128);
+          } else {
+            ptx::tma_load_2d(sB, &maps[kMapB], &full_bar[stage], kx, nt * 128);
+          }
+          const size_t sf_off = static_cast<size_t>(kt) * 4 * kSfBlockBytes;
+          ptx::bulk_load(sSFA, sfa_blk + sf_off, 4 * kSfBlockBytes, &full_bar[stage]);
+          ptx::bulk_load(sSFB, sfb_blk0 + sf_off, 4 * kSfBlockBytes, &full_bar[stage]);
+          if (sfb_blk1 != nullptr)
+            ptx::bulk_load(sSFB + 4 * kSfBlockBytes, sfb_blk1 + sf_off, 4 * kSfBlockBytes,
+                           &full_bar[stage]);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Make sure no copy into this CTA's shared memory is still in flight at exit:
+      // wait for the most recent fill of every stage (already complete on the normal path).
+      const uint32_t recent = issued < static_cast<uint32_t>(STAGES) ? issued : STAGES;
+      for (uint32_t i = 0; i < recent; ++i) {
+        const uint32_t n = issued - 1 - i;
+        const uint32_t s = n % STAGES;
+        const uint32_t ph = (n / STAGES) & 1u;
+        uint64_t t0 = ptx::globaltimer_ns();
+        while (!ptx::mbar_try_wait(&full_bar[s], ph)) {
+          if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            atomicOr(p.error_bits, kDevErrDrainTimeout);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (ptx::elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      int g = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x) {
+        g = advance_group(groups, p.num_groups, g, tile);
+        const int ktiles = groups[g].k / kBlockK;
+        if (!wait_phase(&acce_bar[acc], acc_phase ^ 1u, abort_flag, p.error_bits,
+                        kDevErrAccTimeout)) {
+          break;
+        }
+        ptx::tcgen05_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + acc * MMA_N;
+        for (int kt = 0; kt < ktiles; ++kt) {
+          if (!wait_phase(&full_bar[stage], phase, abort_flag, p.error_bits, kDevErrMmaTimeout)) {
+            ok = false;
+            break;
+          }
+          ptx::tcgen05_fence_after_sync();
+          const uint32_t sA = ptx::smem_u32(stage_base + stage * Cfg::kStageBytes);
+          const uint32_t sB = sA + Cfg::kABytes;
+          const uint32_t sSFA = sB + Cfg::kBBytes;
+          const uint32_t sSFB = sSFA + Cfg::kSfaBytes;
+          const uint32_t sfa_t = tmem_base + Cfg::kSfColBase + stage * Cfg::kSfColsPerStage;
+          const uint32_t sfb_t = sfa_t + Cfg::kSfaCols;
+          // Scale factors: each 512-byte block (128 rows x 4 scales) becomes 4 TMEM
+          // columns, replicated to all four lane quarters.
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb)
+            ptx::tmem_cp_32x128b_warpx4(sfa_t + 4 * kb,
+                                        ptx::make_sf_block_desc(sSFA + kb * kSfBlockBytes));
+#pragma unroll
+          for (int j = 0; j < Cfg::kSfbBlocks; ++j) {
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb)
+              ptx::tmem_cp_32x128b_warpx4(
+                  sfb_t + Cfg::kSfbColsPerMma * kb + 4 * j,
+                  ptx::make_sf_block_desc(sSFB + j * 4 * kSfBlockBytes + kb * kSfBlockBytes));
+          }
+          const uint64_t a_desc = ptx::make_sw128_kmajor_desc(sA);
+          const uint64_t b_desc = ptx::make_sw128_kmajor_desc(sB);
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb) {
+            // 64 e2m1 values = 32 bytes along K inside the 128-byte swizzle row.
+            ptx::mma_mxf4nvf4(d_tmem, a_desc + 2 * kb, b_desc + 2 * kb, Cfg::kIdesc,
+                              sfa_t + 4 * kb, sfb_t + Cfg::kSfbColsPerMma * kb,
+                              (kt | kb) != 0 ? 1u : 0u);
+          }
+          ptx::tcgen05_commit(&empty_bar[stage]);  // frees the smem stage when the MMAs finish
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        ptx::tcgen05_commit(&accf_bar[acc]);  // accumulator complete -> epilogue
+        if (++acc == Cfg::kAccStages) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Wait for every MMA / TMEM copy this thread issued before TMEM is freed.
+      ptx::tcgen05_commit(drain_bar);
+      uint64_t t0 = ptx::globaltimer_ns();
+      while (!ptx::mbar_try_wait(drain_bar, 0)) {
+        if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
+          atomicOr(p.error_bits, kDevErrDrainTimeout);
+          break;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int ew = warp - kEpilogueWarp0;   // 0..3
+    const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+    uint8_t* my_bufs = epi_base + ew * Cfg::kEpiBufsPerWarp * Cfg::kEpiBufBytes;
+    const uint32_t my_bufs_s = ptx::smem_u32(my_bufs);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    uint32_t stores = 0;
+    int g = 0, acquired_g = -1;
+    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
+      g = advance_group(groups, p.num_groups, g, tile);
+      const GroupDev gd = groups[g];
+      const TmaDesc* map_c = p.maps + static_cast<size_t>(g) * kMapsPerGroup + kMapC;
+      if (g != acquired_g) {
+        if (lane == 0) ptx::tensormap_fence_acquire(map_c);
+        acquired_g = g;
+      }
+      const int local = tile - gd.tile_start;
+      const int mt = local % gd.tiles_m;
+      const int nt = local / gd.tiles_m;
+      if (!warp_wait_phase(&accf_bar[acc], acc_phase, abort_flag, p.error_bits,
+                           kDevErrEpilogueTimeout, lane)) {
+        break;
+      }
+      ptx::tcgen05_fence_after_sync();
+      const int row0 = mt * kBlockM + 32 * quarter;
+      if (row0 < gd.m) {
+        const uint32_t t_acc =
+            tmem_base + (static_cast<uint32_t>(32 * quarter) << 16) + acc * MMA_N;
+#pragma unroll 1
+        for (int box = 0; box < Cfg::kOutN / 64; ++box) {
+          const uint32_t buf = my_bufs_s + (stores & 1u) * Cfg::kEpiBufBytes;
+          // The store that last read this buffer (two boxes ago) must be done with it.
+          if (lane == 0) ptx::bulk_wait_group_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const int col = box * 64 + half * 32;
+            uint32_t v[32];
+            ptx::tmem_ld_32x32b_x32(t_acc + col, v);
+            uint32_t packed[16];
+            if (GATED) {
+              uint32_t u[32];
+              ptx::tmem_ld_32x32b_x32(t_acc + 128 + col, u);
+              ptx::tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                float o[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const float gte = __half2float(
+                      __float2half_rn(__uint_as_float(v[2 * i + h]) * gd.alpha));
+                  const float up = __half2float(
+                      __float2half_rn(__uint_as_float(u[2 * i + h]) * gd.alpha2));
+                  o[h] = (gte / (1.0f + expf(-gte))) * up;
+                }
+                __half2 hv = __floats2half2_rn(o[0], o[1]);
+                packed[i] = *reinterpret_cast<uint32_t*>(&hv);
+              }
+            } else {
+              ptx::tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                __half2 hv = __floats2half2_rn(__uint_as_float(v[2 * i]) * gd.alpha,
+                                               __uint_as_float(v[2 * i + 1]) * gd.alpha);
+                packed[i] = *reinterpret_cast<uint32_t*>(&hv);
+              }
+            }
+            // Row `lane` of the 32 x 128 B box, 16-byte chunks XOR-swizzled by (row & 7)
+            // to match the map's 128B swizzle (and to spread the stores over all banks).
+            const uint32_t row_addr = buf + lane * 128;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint32_t chunk = static_cast<uint32_t>(half * 4 + c) ^ (lane & 7);
+              ptx::st_shared_v4(row_addr + chunk * 16, packed[4 * c], packed[4 * c + 1],
+                                packed[4 * c + 2], packed[4 * c + 3]);
+            }
+          }
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            ptx::tma_store_2d(map_c, my_bufs + (stores & 1u) * Cfg::kEpiBufBytes,
+                              nt * Cfg::kOutN + box * 64, row0);
+            ptx::bulk_commit_group();
+          }
+          ++stores;
+        }
+      }
+      ptx::tcgen05_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&acce_bar[acc]);
+      if (++acc == Cfg::kAccStages) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) ptx::bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  ptx::tcgen05_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tcgen05_fence_after_sync();
+    ptx::tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace nvfp4

@@ -1,0 +1,483 @@
+// C ABI implementation: host-side validation and scheduling, the device-side
+// group/tensor-map builder, the scale-factor layout converter, and the launch of
+// the persistent tcgen05 grouped GEMM.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/nvfp4_group_gemm.h"
+#include "grouped_gemm_kernel.cuh"
+#include "nvfp4_types.cuh"
+#include "sm100_ptx.cuh"
+
+namespace nvfp4 {
+
+// ============================================================================
+// Device-side group and tensor-map builder
+// ============================================================================
+// One warp per group: patch the two templates (e2m1 operand, fp16 output) with
+// the group's addresses, extents and row strides in shared memory, then copy
+// each map to the workspace with a release to the tensor-map proxy.
+__global__ void __launch_bounds__(128) nvfp4_build_descriptors_kernel(
+    const __grid_constant__ PrepParams p) {
+  __shared__ __align__(128) TmaDesc smaps[4][kMapsPerGroup];
+  // Let the dependent GEMM grid start its prologue (barrier init, TMEM
+  // allocation); it still waits for this grid to finish before reading.
+  ptx::grid_dependency_launch_dependents();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int gi = blockIdx.x * 4 + warp;
+  if (gi >= p.count) return;
+  const GroupIn& in = p.in[gi];
+  const int g = p.first_group + gi;
+  TmaDesc* sm = smaps[warp];
+  if (lane < 16) {
+    sm[kMapA].raw[lane] = p.tmpl_operand.raw[lane];
+    sm[kMapB].raw[lane] = p.tmpl_operand.raw[lane];
+    sm[kMapB2].raw[lane] = p.tmpl_operand.raw[lane];
+    sm[kMapC].raw[lane] = p.tmpl_output.raw[lane];
+  }
+  __syncwarp();
+  const bool active = in.m > 0 && in.n > 0;
+  if (lane == 0 && active) {
+    const uint32_t kbytes = static_cast<uint32_t>(in.k / 2);
+    ptx::tensormap_replace_address(&sm[kMapA], in.a);
+    ptx::tensormap_replace_dim<0>(&sm[kMapA], kbytes);
+    ptx::tensormap_replace_dim<1>(&sm[kMapA], static_cast<uint32_t>(in.m));
+    ptx::tensormap_replace_stride<0>(&sm[kMapA], kbytes);
+    ptx::tensormap_replace_address(&sm[kMapB], in.b);
+    ptx::tensormap_replace_dim<0>(&sm[kMapB], kbytes);
+    ptx::tensormap_replace_dim<1>(&sm[kMapB], static_cast<uint32_t>(in.n));
+    ptx::tensormap_replace_stride<0>(&sm[kMapB], kbytes);
+    if (p.gated) {
+      ptx::tensormap_replace_address(&sm[kMapB2], in.b2);
+      ptx::tensormap_replace_dim<0>(&sm[kMapB2], kbytes);
+      ptx::tensormap_replace_dim<1>(&sm[kMapB2], static_cast<uint32_t>(in.n));
+      ptx::tensormap_replace_stride<0>(&sm[kMapB2], kbytes);
+    }
+    ptx::tensormap_replace_address(&sm[kMapC], in.c);
+    ptx::tensormap_replace_dim<0>(&sm[kMapC], static_cast<uint32_t>(in.n));
+    ptx::tensormap_replace_dim<1>(&sm[kMapC], static_cast<uint32_t>(in.m));
+    ptx::tensormap_replace_stride<0>(&sm[kMapC], static_cast<uint64_t>(in.n) * 2u);
+  }
+  __syncwarp();
+  TmaDesc* out = p.maps_out + static_cast<size_t>(g) * kMapsPerGroup;
+#pragma unroll
+  for (int i = 0; i < kMapsPerGroup; ++i) ptx::tensormap_copy_release(&out[i], &sm[i]);
+  if (lane == 0) {
+    GroupDev d;
+    d.sfa = reinterpret_cast<const uint8_t*>(in.sfa);
+    d.sfb = reinterpret_cast<const uint8_t*>(in.sfb);
+    d.sfb2 = reinterpret_cast<const uint8_t*>(in.sfb2);
+    d.m = in.m;
+    d.n = in.n;
+    d.k = in.k;
+    d.tiles_m = in.tiles_m;
+    d.tile_start = in.tile_start;
+    d.tile_end = in.tile_end;
+    d.alpha = in.alpha;
+    d.alpha2 = in.alpha2;
+    p.groups_out[g] = d;
+  }
+}
+
+// ============================================================================
+// Scale-factor layout: plain [rows, cols] -> 128x4 blocks
+// ============================================================================
+// Output byte ((mm * rest_k + kk) * 32 + i0) * 16 + i1 * 4 + j holds
+// plain[mm*128 + i1*32 + i0][kk*4 + j] (zero outside the input), i.e. the
+// to_blocked permutation (REFERENCE_IMPL.md:19-42). One thread writes one
+// 16-byte row (i0) of a 512-byte block.
+__global__ void __launch_bounds__(256) nvfp4_sf_to_blocked_kernel(const uint8_t* __restrict__ plain,
+                                                                  uint8_t* __restrict__ blocked,
+                                                                  int rows, int cols, int64_t ld,
+                                                                  int rest_k, int64_t chunks) {
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < chunks;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int i0 = static_cast<int>(idx & 31);
+    const int64_t blk = idx >> 5;
+    const int kk = static_cast<int>(blk % rest_k);
+    const int64_t mm = blk / rest_k;
+    uint32_t w[4];
+#pragma unroll
+    for (int i1 = 0; i1 < 4; ++i1) {
+      const int64_t r = mm * 128 + i1 * 32 + i0;
+      uint32_t word = 0;
+      if (r < rows) {
+        const uint8_t* src = plain + r * ld;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = kk * 4 + j;
+          if (c < cols) word |= static_cast<uint32_t>(src[c]) << (8 * j);
+        }
+      }
+      w[i1] = word;
+    }
+    reinterpret_cast<uint4*>(blocked)[idx] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// ============================================================================
+// Host side
+// ============================================================================
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(NVFP4_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// Kernel variants: <MMA N, gated, stages>.
+using Kn128 = GemmConfig<128, false, 5>;
+using Kn256 = GemmConfig<256, false, 3>;
+using Kgated = GemmConfig<256, true, 3>;
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  std::once_flag once;
+  int status = NVFP4_OK;
+  int num_sms = 0;
+  std::string detail;
+};
+DeviceState g_dev[kMaxDevices];
+
+struct Templates {
+  std::once_flag once;
+  int status = NVFP4_OK;
+  std::string detail;
+  TmaDesc operand;
+  TmaDesc output;
+};
+Templates g_tmpl;
+
+void init_device(int dev, DeviceState& st) {
+  cudaDeviceProp prop;
+  cudaError_t e = cudaGetDeviceProperties(&prop, dev);
+  if (e != cudaSuccess) {
+    st.status = NVFP4_ERR_CUDA;
+    st.detail = std::string("cudaGetDeviceProperties: ") + cudaGetErrorString(e);
+    return;
+  }
+  if (prop.major != 10 || prop.minor != 0) {
+    st.status = NVFP4_ERR_UNSUPPORTED_DEVICE;
+    char buf[512];
+    snprintf(buf, sizeof(buf), "device %d is %.200s (sm_%d%d); this library is built for sm_100a",
+             dev, prop.name, prop.major, prop.minor);
+    st.detail = buf;
+    return;
+  }
+  st.num_sms = prop.multiProcessorCount;
+  struct {
+    const void* fn;
+    int smem;
+  } kernels[] = {
+      {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_kernel<128, false, 5>), Kn128::kSmemBytes},
+      {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_kernel<256, false, 3>), Kn256::kSmemBytes},
+      {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_kernel<256, true, 3>), Kgated::kSmemBytes},
+  };
+  for (auto& k : kernels) {
+    e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
+    if (e != cudaSuccess) {
+      st.status = NVFP4_ERR_CUDA;
+      st.detail = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+      return;
+    }
+  }
+}
+
+void init_templates(Templates& t) {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || fn == nullptr || q != cudaDriverEntryPointSuccess) {
+    t.status = NVFP4_ERR_DRIVER;
+    t.detail = "cuTensorMapEncodeTiled entry point not available from the driver";
+    return;
+  }
+  using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  EncodeFn encode = reinterpret_cast<EncodeFn>(fn);
+  // Templates carry everything that is the same for all groups (type, box, swizzle,
+  // fill); the builder kernel patches address, extents and row stride per group.
+  void* dummy = reinterpret_cast<void*>(static_cast<uintptr_t>(1) << 20);
+  {
+    CUtensorMap m;
+    cuuint64_t dims[2] = {4096, 4096};
+    cuuint64_t strides[1] = {4096};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kRowBytesPerStage), 128};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, dummy, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      t.status = NVFP4_ERR_DRIVER;
+      t.detail = "cuTensorMapEncodeTiled failed for the operand template";
+      return;
+    }
+    memcpy(&t.operand, &m, sizeof(TmaDesc));
+  }
+  {
+    CUtensorMap m;
+    cuuint64_t dims[2] = {4096, 4096};
+    cuuint64_t strides[1] = {4096 * 2};
+    cuuint32_t box[2] = {64, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dummy, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      t.status = NVFP4_ERR_DRIVER;
+      t.detail = "cuTensorMapEncodeTiled failed for the output template";
+      return;
+    }
+    memcpy(&t.output, &m, sizeof(TmaDesc));
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <int MMA_N, bool GATED, int STAGES>
+cudaError_t launch_gemm(const GemmParams& gp, int grid, cudaStream_t stream, bool after_prep) {
+  using Cfg = GemmConfig<MMA_N, GATED, STAGES>;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kNumThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = after_prep ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, nvfp4_grouped_gemm_kernel<MMA_N, GATED, STAGES>, gp);
+}
+
+}  // namespace
+}  // namespace nvfp4
+
+using namespace nvfp4;
+
+extern "C" {
+
+NVFP4_API int nvfp4_abi_version(void) { return NVFP4_ABI_VERSION; }
+
+NVFP4_API const char* nvfp4_strerror(int status) {
+  switch (status) {
+    case NVFP4_OK: return "success";
+    case NVFP4_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case NVFP4_ERR_BAD_SHAPE: return "unsupported problem shape";
+    case NVFP4_ERR_MISALIGNED: return "tensor address not 16-byte aligned";
+    case NVFP4_ERR_NULL_POINTER: return "null tensor pointer";
+    case NVFP4_ERR_WORKSPACE: return "workspace missing, too small or misaligned";
+    case NVFP4_ERR_CUDA: return "CUDA error";
+    case NVFP4_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case NVFP4_ERR_UNSUPPORTED_DEVICE: return "unsupported device (needs sm_100)";
+    case NVFP4_ERR_DRIVER: return "driver entry point unavailable";
+    default: return "unknown status";
+  }
+}
+
+NVFP4_API const char* nvfp4_last_error_detail(void) { return g_last_error.c_str(); }
+
+NVFP4_API size_t nvfp4_workspace_size(int num_groups) {
+  if (num_groups < 0) return 0;
+  return ws_total_bytes(num_groups);
+}
+
+NVFP4_API size_t nvfp4_sf_blocked_size(int rows, int sf_cols) {
+  if (rows <= 0 || sf_cols <= 0) return 0;
+  const size_t rest_m = (static_cast<size_t>(rows) + 127) / 128;
+  const size_t rest_k = (static_cast<size_t>(sf_cols) + 3) / 4;
+  return rest_m * rest_k * kSfBlockBytes;
+}
+
+NVFP4_API int nvfp4_sf_to_blocked(const void* plain, void* blocked, int rows, int sf_cols,
+                                  int64_t ld, void* stream) {
+  g_last_error.clear();
+  if (rows < 0 || sf_cols < 0) return fail(NVFP4_ERR_BAD_SHAPE, "rows=%d sf_cols=%d", rows, sf_cols);
+  if (rows == 0 || sf_cols == 0) return NVFP4_OK;
+  if (plain == nullptr || blocked == nullptr)
+    return fail(NVFP4_ERR_NULL_POINTER, "plain or blocked pointer is NULL");
+  if (ld < sf_cols) return fail(NVFP4_ERR_INVALID_ARGUMENT, "ld=%lld < sf_cols=%d",
+                                static_cast<long long>(ld), sf_cols);
+  if (!aligned16(blocked)) return fail(NVFP4_ERR_MISALIGNED, "blocked output not 16-byte aligned");
+  const int rest_m = (rows + 127) / 128;
+  const int rest_k = (sf_cols + 3) / 4;
+  const int64_t chunks = static_cast<int64_t>(rest_m) * rest_k * 32;
+  const int threads = 256;
+  int64_t blocks = (chunks + threads - 1) / threads;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  nvfp4_sf_to_blocked_kernel<<<static_cast<unsigned>(blocks), threads, 0,
+                               static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(plain), static_cast<uint8_t*>(blocked), rows, sf_cols, ld, rest_k,
+      chunks);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "sf_to_blocked launch");
+  return NVFP4_OK;
+}
+
+NVFP4_API int nvfp4_workspace_check(void* workspace, void* stream, unsigned int* device_error_bits) {
+  g_last_error.clear();
+  if (device_error_bits) *device_error_bits = 0;
+  if (workspace == nullptr) return fail(NVFP4_ERR_WORKSPACE, "workspace is NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  uint32_t bits = 0;
+  e = cudaMemcpy(&bits, workspace, sizeof(bits), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read workspace error word");
+  if (bits != 0) {
+    const uint32_t zero = 0;
+    e = cudaMemcpy(workspace, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "clear workspace error word");
+    if (device_error_bits) *device_error_bits = bits;
+    return fail(NVFP4_ERR_DEVICE_TIMEOUT, "device error bits 0x%x", bits);
+  }
+  return NVFP4_OK;
+}
+
+NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsigned int flags,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  const unsigned known = NVFP4_FLAG_GATED | NVFP4_FLAG_TILE_N128 | NVFP4_FLAG_TILE_N256 |
+                         NVFP4_FLAG_REUSE_DESCRIPTORS;
+  if (flags & ~known) return fail(NVFP4_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags & ~known);
+  if (num_groups < 0) return fail(NVFP4_ERR_INVALID_ARGUMENT, "num_groups=%d", num_groups);
+  if (num_groups == 0) return NVFP4_OK;
+  if (groups == nullptr) return fail(NVFP4_ERR_INVALID_ARGUMENT, "groups table is NULL");
+  const bool gated = (flags & NVFP4_FLAG_GATED) != 0;
+  if ((flags & NVFP4_FLAG_TILE_N128) && (flags & NVFP4_FLAG_TILE_N256))
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "TILE_N128 and TILE_N256 are exclusive");
+  if (gated && (flags & NVFP4_FLAG_TILE_N128))
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "gated launches use 128 gate + 128 up columns");
+  if (workspace == nullptr) return fail(NVFP4_ERR_WORKSPACE, "workspace is NULL");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(NVFP4_ERR_WORKSPACE, "workspace not 256-byte aligned");
+  if (workspace_bytes < ws_total_bytes(num_groups))
+    return fail(NVFP4_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes,
+                ws_total_bytes(num_groups));
+
+  // Tile width along N: 256-column MMAs unless asked otherwise.
+  const int mma_n = gated ? 256 : ((flags & NVFP4_FLAG_TILE_N128) ? 128 : 256);
+  const int out_n = gated ? 128 : mma_n;
+
+  std::vector<GroupIn> gin(static_cast<size_t>(num_groups));
+  int64_t total_tiles = 0;
+  for (int i = 0; i < num_groups; ++i) {
+    const nvfp4_group& gr = groups[i];
+    if (gr.m < 0 || gr.n < 0 || gr.k < 0)
+      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: negative size (m=%d n=%d k=%d)", i, gr.m, gr.n, gr.k);
+    GroupIn& d = gin[i];
+    memset(&d, 0, sizeof(d));
+    d.m = gr.m;
+    d.n = gr.n;
+    d.k = gr.k;
+    d.alpha = gr.alpha;
+    d.alpha2 = gr.alpha2;
+    const bool active = gr.m > 0 && gr.n > 0;
+    if (active) {
+      if (gr.k <= 0 || gr.k % kBlockK != 0)
+        return fail(NVFP4_ERR_BAD_SHAPE, "group %d: k=%d must be a positive multiple of 256", i, gr.k);
+      if (gr.n % 8 != 0)
+        return fail(NVFP4_ERR_BAD_SHAPE, "group %d: n=%d must be a multiple of 8", i, gr.n);
+      const void* ptrs[7] = {gr.a, gr.b, gr.b2, gr.sfa, gr.sfb, gr.sfb2, gr.c};
+      const char* names[7] = {"a", "b", "b2", "sfa", "sfb", "sfb2", "c"};
+      for (int j = 0; j < 7; ++j) {
+        if (!gated && (j == 2 || j == 5)) continue;
+        if (ptrs[j] == nullptr) return fail(NVFP4_ERR_NULL_POINTER, "group %d: %s is NULL", i, names[j]);
+        if (!aligned16(ptrs[j]))
+          return fail(NVFP4_ERR_MISALIGNED, "group %d: %s not 16-byte aligned", i, names[j]);
+      }
+      d.a = reinterpret_cast<uint64_t>(gr.a);
+      d.b = reinterpret_cast<uint64_t>(gr.b);
+      d.b2 = gated ? reinterpret_cast<uint64_t>(gr.b2) : 0;
+      d.sfa = reinterpret_cast<uint64_t>(gr.sfa);
+      d.sfb = reinterpret_cast<uint64_t>(gr.sfb);
+      d.sfb2 = gated ? reinterpret_cast<uint64_t>(gr.sfb2) : 0;
+      d.c = reinterpret_cast<uint64_t>(gr.c);
+      d.tiles_m = (gr.m + kBlockM - 1) / kBlockM;
+      const int tiles_n = (gr.n + out_n - 1) / out_n;
+      d.tile_start = static_cast<int32_t>(total_tiles);
+      total_tiles += static_cast<int64_t>(d.tiles_m) * tiles_n;
+      if (total_tiles > (int64_t{1} << 30))
+        return fail(NVFP4_ERR_BAD_SHAPE, "too many tiles (%lld)", static_cast<long long>(total_tiles));
+      d.tile_end = static_cast<int32_t>(total_tiles);
+    } else {
+      d.tiles_m = 1;
+      d.tile_start = d.tile_end = static_cast<int32_t>(total_tiles);
+    }
+  }
+  if (total_tiles == 0) return NVFP4_OK;
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_INVALID_ARGUMENT, "device %d", dev);
+  DeviceState& ds = g_dev[dev];
+  std::call_once(ds.once, init_device, dev, std::ref(ds));
+  if (ds.status != NVFP4_OK) return fail(ds.status, "%s", ds.detail.c_str());
+  std::call_once(g_tmpl.once, init_templates, std::ref(g_tmpl));
+  if (g_tmpl.status != NVFP4_OK) return fail(g_tmpl.status, "%s", g_tmpl.detail.c_str());
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  GroupDev* groups_dev = reinterpret_cast<GroupDev*>(ws + ws_groups_offset());
+  TmaDesc* maps_dev = reinterpret_cast<TmaDesc*>(ws + ws_maps_offset(num_groups));
+
+  const bool rebuild = (flags & NVFP4_FLAG_REUSE_DESCRIPTORS) == 0;
+  if (rebuild) {
+    static thread_local PrepParams pp;  // ~22 KB: too large for the stack of some callers
+    pp.tmpl_operand = g_tmpl.operand;
+    pp.tmpl_output = g_tmpl.output;
+    pp.groups_out = groups_dev;
+    pp.maps_out = maps_dev;
+    pp.gated = gated ? 1 : 0;
+    for (int first = 0; first < num_groups; first += kMaxGroupsPerPrepLaunch) {
+      const int count = std::min(kMaxGroupsPerPrepLaunch, num_groups - first);
+      pp.first_group = first;
+      pp.count = count;
+      memcpy(pp.in, &gin[first], sizeof(GroupIn) * count);
+      nvfp4_build_descriptors_kernel<<<(count + 3) / 4, 128, 0, s>>>(pp);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_fail(e, "descriptor builder launch");
+    }
+  }
+
+  GemmParams gp;
+  gp.groups = groups_dev;
+  gp.maps = maps_dev;
+  gp.error_bits = reinterpret_cast<uint32_t*>(ws);
+  gp.num_groups = num_groups;
+  gp.total_tiles = static_cast<int32_t>(total_tiles);
+  const int grid = static_cast<int>(std::min<int64_t>(total_tiles, ds.num_sms));
+  if (gated)
+    e = launch_gemm<256, true, 3>(gp, grid, s, rebuild);
+  else if (mma_n == 128)
+    e = launch_gemm<128, false, 5>(gp, grid, s, rebuild);
+  else
+    e = launch_gemm<256, false, 3>(gp, grid, s, rebuild);
+  if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
+  return NVFP4_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,96 @@
+// Types shared by the host launcher and the device kernels: the per-launch
+// workspace layout (group records + tensor maps + error word) and the kernel
+// parameter blocks.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+namespace nvfp4 {
+
+// Problem constants of the NVFP4 block-scaled format (16 e2m1 values share one
+// E4M3 scale; scale factors are stored in 128-row x 4-column blocks of 512 B).
+constexpr int kBlockM = 128;          // rows per tile (one tcgen05.mma M)
+constexpr int kBlockK = 256;          // K elements per pipeline stage (128 bytes per row)
+constexpr int kRowBytesPerStage = 128;
+constexpr int kMmaK = 64;             // K per tcgen05.mma kind::mxf4nvf4
+constexpr int kSfVec = 16;            // elements per scale factor
+constexpr int kSfBlockBytes = 512;    // one 128 x 4 scale-factor block
+constexpr int kMaxGroupsPerPrepLaunch = 256;
+
+// 128-byte opaque CUtensorMap image (the driver type requires 64-byte alignment).
+struct alignas(64) TmaDesc {
+  uint64_t raw[16];
+};
+static_assert(sizeof(TmaDesc) == 128, "tensor map image must be 128 bytes");
+
+// Tensor maps kept per group, in this order.
+enum : int { kMapA = 0, kMapB = 1, kMapB2 = 2, kMapC = 3, kMapsPerGroup = 4 };
+
+// One group as the device sees it (written by the descriptor builder).
+struct GroupDev {
+  const uint8_t* sfa;   // 128x4-blocked E4M3 scales of A
+  const uint8_t* sfb;   // blocked scales of B (gate weights when gated)
+  const uint8_t* sfb2;  // blocked scales of the up weights (gated only)
+  int32_t m, n, k;
+  int32_t tiles_m;
+  int32_t tile_start, tile_end;  // [start, end) in the launch-wide tile order
+  float alpha, alpha2;
+};
+static_assert(sizeof(GroupDev) <= 64, "group record must fit 64 bytes");
+
+// One group as the host hands it to the descriptor builder.
+struct GroupIn {
+  uint64_t a, b, b2, sfa, sfb, sfb2, c;
+  int32_t m, n, k;
+  int32_t tiles_m, tile_start, tile_end;
+  float alpha, alpha2;
+};
+
+struct WorkspaceHeader {
+  uint32_t error_bits;  // OR of device-side failure reasons (see kDevErr*)
+  uint32_t reserved[63];
+};
+static_assert(sizeof(WorkspaceHeader) == 256, "header is 256 bytes");
+
+// Device-side failure reasons (bit positions in WorkspaceHeader::error_bits).
+enum : uint32_t {
+  kDevErrProducerTimeout = 1u << 0,  // TMA producer gave up waiting for a free stage
+  kDevErrMmaTimeout = 1u << 1,       // MMA issuer gave up waiting for a loaded stage
+  kDevErrAccTimeout = 1u << 2,       // MMA issuer gave up waiting for a drained accumulator
+  kDevErrEpilogueTimeout = 1u << 3,  // epilogue gave up waiting for a finished accumulator
+  kDevErrDrainTimeout = 1u << 4,     // in-flight copies or MMAs did not finish at exit
+};
+
+// Workspace layout: header | GroupDev[G] (64 B each) | TmaDesc[G][4] (128 B aligned).
+__host__ __device__ inline size_t ws_groups_offset() { return sizeof(WorkspaceHeader); }
+__host__ __device__ inline size_t ws_maps_offset(int num_groups) {
+  size_t off = ws_groups_offset() + static_cast<size_t>(num_groups) * 64;
+  return (off + 127) & ~static_cast<size_t>(127);
+}
+__host__ __device__ inline size_t ws_total_bytes(int num_groups) {
+  return ws_maps_offset(num_groups) +
+         static_cast<size_t>(num_groups) * kMapsPerGroup * sizeof(TmaDesc);
+}
+
+struct PrepParams {
+  TmaDesc tmpl_operand;  // e2m1 operand map template: uint8, box 128 B x 128 rows, 128B swizzle
+  TmaDesc tmpl_output;   // fp16 output map template: box 64 x 32, 128B swizzle
+  GroupDev* groups_out;
+  TmaDesc* maps_out;
+  int32_t first_group;
+  int32_t count;
+  int32_t gated;
+  int32_t pad;
+  GroupIn in[kMaxGroupsPerPrepLaunch];
+};
+
+struct GemmParams {
+  const GroupDev* groups;
+  const TmaDesc* maps;
+  uint32_t* error_bits;
+  int32_t num_groups;
+  int32_t total_tiles;
+};
+
+}  // namespace nvfp4

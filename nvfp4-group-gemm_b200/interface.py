@@ -1,0 +1,293 @@
+"""Harness-facing entry points: ``custom_kernel(data)`` / ``solve(data)``.
+
+Mirrors the reference submission's interface (submission.py:788-891):
+
+* 4-tuple grouped form ``(abc_tensors, sfasfb_tensors, sfasfb_reordered_tensors,
+  problem_sizes)`` (REFERENCE_IMPL.md:52, submission.py:804-858): one grouped
+  launch; element 1 (plain CPU scales) is ignored exactly as the reference does;
+  each ``c`` is written in place and the list of ``c`` tensors is returned.
+* 10-tuple dual GEMM ``(a, b1, b2, sfa, sfb1, sfb2, sfa_perm, sfb1_perm,
+  sfb2_perm, c)`` (submission.py:860-886): ``c = silu(a@b1) * (a@b2)`` with the
+  two products rounded to fp16 first; here it is one fused launch.
+
+Extensions (no counterpart in the reference, which has no global scale and no
+grouped gated form):
+
+* an optional 5th element (or the ``global_scales`` keyword) holding one fp32
+  scale per group, or a (gate, up) pair per group when gated;
+* a grouped gated form: a 4-tuple whose ``abc_tensors`` entries are
+  ``(a, b_gate, b_up, c)`` and whose reordered scale entries are
+  ``(sfa, sfb_gate, sfb_up)``.
+
+Errors: malformed input raises ValueError before anything is launched; a
+failure reported by the native library raises ``Nvfp4Error`` (a RuntimeError).
+There is no CPU or library fallback.
+"""
+from __future__ import annotations
+
+import threading
+from typing import Sequence
+
+import numpy as np
+import torch
+
+from . import _native
+from .layout import blocked_sf_bytes, ceil_div
+
+input_t = tuple
+output_t = list
+
+_FP4_DTYPES = tuple(
+    d for d in (getattr(torch, "float4_e2m1fn_x2", None), torch.uint8, torch.int8) if d is not None
+)
+
+
+# ----------------------------------------------------------------------------
+# Workspace and descriptor-table cache (one per device and stream)
+# ----------------------------------------------------------------------------
+class _Workspace:
+    __slots__ = ("buf", "nbytes", "last_table", "last_flags")
+
+    def __init__(self):
+        self.buf = None
+        self.nbytes = 0
+        self.last_table = None
+        self.last_flags = None
+
+
+_ws_lock = threading.Lock()
+_workspaces: dict = {}
+
+
+def _workspace_for(device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> _Workspace:
+    key = (device.index, stream.cuda_stream)
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None:
+            ws = _workspaces[key] = _Workspace()
+    if ws.nbytes < nbytes:
+        size = max(nbytes, 2 * ws.nbytes, 1 << 16)
+        # Zero-filled: the first 4 bytes are the device error word.
+        ws.buf = torch.zeros(size, dtype=torch.uint8, device=device)
+        ws.nbytes = size
+        ws.last_table = None
+    return ws
+
+
+def check_device_errors(device: torch.device | int | None = None,
+                        stream: torch.cuda.Stream | None = None) -> int:
+    """Synchronise and return the device error bits of this stream's workspace."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index))
+    s = stream or torch.cuda.current_stream(dev)
+    ws = _workspaces.get((dev.index, s.cuda_stream))
+    if ws is None or ws.buf is None:
+        return 0
+    with torch.cuda.device(dev):
+        return _native.workspace_check(ws.buf.data_ptr(), s.cuda_stream)
+
+
+# ----------------------------------------------------------------------------
+# Validation helpers
+# ----------------------------------------------------------------------------
+def _as_2d_kmajor(t: torch.Tensor, rows: int, cols_bytes: int, name: str) -> torch.Tensor:
+    """Accept [rows, cols] or [rows, cols, 1] tensors with dense, row-major rows."""
+    if t.dim() == 3:
+        if t.shape[2] != 1:
+            raise ValueError(f"{name}: only L=1 is supported, got shape {tuple(t.shape)}")
+        t = t[:, :, 0]
+    if t.dim() != 2:
+        raise ValueError(f"{name}: expected [rows, cols(, 1)], got shape {tuple(t.shape)}")
+    if tuple(t.shape) != (rows, cols_bytes):
+        raise ValueError(f"{name}: expected shape ({rows}, {cols_bytes}), got {tuple(t.shape)}")
+    if rows > 0 and cols_bytes > 0 and (t.stride(1) != 1 or (rows > 1 and t.stride(0) != cols_bytes)):
+        raise ValueError(f"{name}: rows must be dense and K-major (strides {t.stride()})")
+    return t
+
+
+def _check_fp4(t: torch.Tensor, name: str) -> None:
+    if t.dtype not in _FP4_DTYPES:
+        raise ValueError(f"{name}: expected packed e2m1 (float4_e2m1fn_x2/uint8), got {t.dtype}")
+
+
+def _check_sf(t: torch.Tensor, rows: int, k: int, name: str) -> None:
+    if t.element_size() != 1:
+        raise ValueError(f"{name}: scale factors must be 1-byte E4M3 values, got {t.dtype}")
+    need = blocked_sf_bytes(rows, ceil_div(k, 16))
+    if t.numel() < need:
+        raise ValueError(f"{name}: holds {t.numel()} scale bytes, blocked layout needs {need}")
+
+
+# ----------------------------------------------------------------------------
+# Core grouped launch
+# ----------------------------------------------------------------------------
+def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
+                 sfa: Sequence[torch.Tensor], sfb: Sequence[torch.Tensor],
+                 c: Sequence[torch.Tensor], problem_sizes: Sequence[Sequence[int]],
+                 alpha: Sequence[float] | None = None,
+                 b2: Sequence[torch.Tensor] | None = None,
+                 sfb2: Sequence[torch.Tensor] | None = None,
+                 alpha2: Sequence[float] | None = None,
+                 tile_n: int | None = None,
+                 stream: torch.cuda.Stream | None = None,
+                 reuse_descriptors: bool = True) -> list:
+    """One grouped NVFP4 launch. Scale tensors are in the blocked layout.
+
+    ``problem_sizes`` holds (m, n, k[, l]) per group. When ``b2``/``sfb2`` are given
+    the launch is gated: ``c = fp16(silu(fp16(alpha*A.B^T)) * fp16(alpha2*A.B2^T))``.
+    """
+    G = len(problem_sizes)
+    if not (len(a) == len(b) == len(sfa) == len(sfb) == len(c) == G):
+        raise ValueError("a, b, sfa, sfb, c and problem_sizes must have one entry per group")
+    gated = b2 is not None
+    if gated and (sfb2 is None or len(b2) != G or len(sfb2) != G):
+        raise ValueError("gated launches need b2 and sfb2 for every group")
+    if G == 0:
+        return []
+    device = None
+    table = np.zeros(G, dtype=_native.GROUP_DTYPE)
+    ms = np.empty(G, dtype=np.int64)
+    ns = np.empty(G, dtype=np.int64)
+    ks = np.empty(G, dtype=np.int64)
+    for g, ps in enumerate(problem_sizes):
+        if len(ps) == 4 and int(ps[3]) != 1:
+            raise ValueError(f"group {g}: only L=1 is supported (problem size {tuple(ps)})")
+        m, n, k = int(ps[0]), int(ps[1]), int(ps[2])
+        ms[g], ns[g], ks[g] = m, n, k
+        if m < 0 or n < 0 or k < 0:
+            raise ValueError(f"group {g}: negative size {tuple(ps)}")
+        if m == 0 or n == 0:
+            continue
+        if k <= 0 or k % 256 != 0:
+            raise ValueError(f"group {g}: K={k} must be a positive multiple of 256")
+        if n % 8 != 0:
+            raise ValueError(f"group {g}: N={n} must be a multiple of 8")
+        tensors = [a[g], b[g], sfa[g], sfb[g], c[g]] + ([b2[g], sfb2[g]] if gated else [])
+        for t in tensors:
+            if not isinstance(t, torch.Tensor) or not t.is_cuda:
+                raise ValueError(f"group {g}: every tensor must be a CUDA tensor")
+            if device is None:
+                device = t.device
+            elif t.device != device:
+                raise ValueError(f"group {g}: tensors span devices {device} and {t.device}")
+        _check_fp4(a[g], f"a[{g}]")
+        _check_fp4(b[g], f"b[{g}]")
+        _as_2d_kmajor(a[g], m, k // 2, f"a[{g}]")
+        _as_2d_kmajor(b[g], n, k // 2, f"b[{g}]")
+        if c[g].dtype != torch.float16:
+            raise ValueError(f"c[{g}]: expected float16, got {c[g].dtype}")
+        _as_2d_kmajor(c[g], m, n, f"c[{g}]")
+        _check_sf(sfa[g], m, k, f"sfa[{g}]")
+        _check_sf(sfb[g], n, k, f"sfb[{g}]")
+        if gated:
+            _check_fp4(b2[g], f"b2[{g}]")
+            _as_2d_kmajor(b2[g], n, k // 2, f"b2[{g}]")
+            _check_sf(sfb2[g], n, k, f"sfb2[{g}]")
+    if device is None:  # every group empty
+        return list(c)
+    table["a"] = [t.data_ptr() for t in a]
+    table["b"] = [t.data_ptr() for t in b]
+    table["sfa"] = [t.data_ptr() for t in sfa]
+    table["sfb"] = [t.data_ptr() for t in sfb]
+    table["c"] = [t.data_ptr() for t in c]
+    if gated:
+        table["b2"] = [t.data_ptr() for t in b2]
+        table["sfb2"] = [t.data_ptr() for t in sfb2]
+    table["m"], table["n"], table["k"] = ms, ns, ks
+    table["alpha"] = 1.0 if alpha is None else np.asarray(alpha, dtype=np.float32)
+    table["alpha2"] = 1.0 if alpha2 is None else np.asarray(alpha2, dtype=np.float32)
+
+    flags = _native.FLAG_GATED if gated else 0
+    if tile_n is not None and not gated:
+        if tile_n == 128:
+            flags |= _native.FLAG_TILE_N128
+        elif tile_n == 256:
+            flags |= _native.FLAG_TILE_N256
+        else:
+            raise ValueError(f"tile_n must be 128 or 256, got {tile_n}")
+    s = stream or torch.cuda.current_stream(device)
+    ws = _workspace_for(device, s, _native.workspace_size(G))
+    call_flags = flags
+    if (reuse_descriptors and ws.last_flags == flags and ws.last_table is not None
+            and ws.last_table.shape == table.shape and np.array_equal(ws.last_table, table)):
+        call_flags |= _native.FLAG_REUSE_DESCRIPTORS
+    with torch.cuda.device(device):
+        _native.grouped_gemm_raw(table, call_flags, ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
+    ws.last_table = table
+    ws.last_flags = flags
+    return list(c)
+
+
+# ----------------------------------------------------------------------------
+# Reference-shaped entry points
+# ----------------------------------------------------------------------------
+def _split_scales(global_scales, G: int, gated: bool):
+    if global_scales is None:
+        return None, None
+    gs = global_scales.detach().cpu().tolist() if isinstance(global_scales, torch.Tensor) \
+        else list(global_scales)
+    if len(gs) != G:
+        raise ValueError(f"global_scales has {len(gs)} entries for {G} groups")
+    if gated:
+        pairs = [(float(x), float(x)) if np.isscalar(x) else (float(x[0]), float(x[1])) for x in gs]
+        return [p[0] for p in pairs], [p[1] for p in pairs]
+    return [float(x) for x in gs], None
+
+
+def custom_kernel(data: input_t, *, global_scales=None, tile_n: int | None = None,
+                  stream: torch.cuda.Stream | None = None) -> output_t:
+    """Drop-in replacement of the reference's ``custom_kernel`` (submission.py:788)."""
+    if not isinstance(data, (tuple, list)):
+        raise ValueError(f"unsupported input: expected a tuple, got {type(data).__name__}")
+    if len(data) == 10:
+        a, b1, b2, _sfa, _sfb1, _sfb2, sfa_p, sfb1_p, sfb2_p, c = data
+        if c.dim() == 3 and c.shape[2] != 1:
+            raise ValueError("only L=1 is supported")
+        m, n = int(c.shape[0]), int(c.shape[1])
+        k = int(a.shape[1]) * 2
+        alpha, alpha2 = _split_scales(global_scales, 1, True)
+        grouped_gemm([a], [b1], [sfa_p], [sfb1_p], [c], [(m, n, k, 1)], alpha=alpha,
+                     b2=[b2], sfb2=[sfb2_p], alpha2=alpha2, stream=stream)
+        return c
+    if len(data) not in (4, 5):
+        raise ValueError(f"unsupported input format with {len(data)} elements "
+                         "(expected the 4-tuple grouped form or the 10-tuple dual form)")
+    abc_tensors, _plain_sf, sf_reordered, problem_sizes = data[:4]
+    if len(data) == 5:
+        if global_scales is not None:
+            raise ValueError("global scales given twice")
+        global_scales = data[4]
+    G = len(problem_sizes)
+    if len(abc_tensors) != G or len(sf_reordered) != G:
+        raise ValueError("abc_tensors, sf tensors and problem_sizes differ in length")
+    if G == 0:
+        return []
+    gated = len(abc_tensors[0]) == 4
+    if gated:
+        a = [t[0] for t in abc_tensors]
+        b = [t[1] for t in abc_tensors]
+        b2 = [t[2] for t in abc_tensors]
+        c = [t[3] for t in abc_tensors]
+        if any(len(s) != 3 for s in sf_reordered):
+            raise ValueError("gated grouped form needs (sfa, sfb_gate, sfb_up) per group")
+        sfa = [s[0] for s in sf_reordered]
+        sfb = [s[1] for s in sf_reordered]
+        sfb2 = [s[2] for s in sf_reordered]
+    else:
+        if any(len(t) != 3 for t in abc_tensors):
+            raise ValueError("grouped form needs (a, b, c) per group")
+        a = [t[0] for t in abc_tensors]
+        b = [t[1] for t in abc_tensors]
+        c = [t[2] for t in abc_tensors]
+        sfa = [s[0] for s in sf_reordered]
+        sfb = [s[1] for s in sf_reordered]
+        b2 = sfb2 = None
+    alpha, alpha2 = _split_scales(global_scales, G, gated)
+    grouped_gemm(a, b, sfa, sfb, c, problem_sizes, alpha=alpha, b2=b2, sfb2=sfb2,
+                 alpha2=alpha2, tile_n=tile_n, stream=stream)
+    return list(c)
+
+
+def solve(data: input_t) -> output_t:
+    """Alias of custom_kernel (submission.py:889-891)."""
+    return custom_kernel(data)

@@ -1,0 +1,119 @@
+"""The C-ABI library loads and exports every declared symbol; host-side validation
+returns the documented status codes without launching anything (CPU only)."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+
+
+def _declared_symbols() -> set:
+    hdr = open(os.path.join(ROOT, "include", "nvfp4_group_gemm.h")).read()
+    return set(re.findall(r"NVFP4_API\s+[\w\s\*]+?\b(nvfp4_\w+)\s*\(", hdr))
+
+
+def test_header_declarations_match_binding(pkg):
+    assert _declared_symbols() == set(pkg._native.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg.load_library()
+    for name in _declared_symbols():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", pkg._native.LIB_PATH],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert _declared_symbols() <= exported
+    # Nothing else with C linkage leaks out besides the declared API.
+    assert {s for s in exported if s.startswith("nvfp4_")} == _declared_symbols()
+
+
+def test_struct_layout_matches_header(pkg):
+    N = pkg._native
+    assert ctypes.sizeof(N.Nvfp4Group) == 80
+    assert N.Nvfp4Group.m.offset == 56 and N.Nvfp4Group.alpha2.offset == 72
+    assert N.GROUP_DTYPE.itemsize == 80
+
+
+def test_version_and_strings(pkg):
+    lib = pkg.load_library()
+    assert lib.nvfp4_abi_version() == 1
+    assert lib.nvfp4_strerror(0) == b"success"
+    assert b"timed out" in lib.nvfp4_strerror(7)
+    assert lib.nvfp4_strerror(999) == b"unknown status"
+
+
+def test_size_queries(pkg):
+    N = pkg._native
+    assert N.workspace_size(0) == 256
+    assert N.workspace_size(8) == 256 + 8 * 64 + 8 * 4 * 128
+    assert N.sf_blocked_size(80, 32) == 1 * 8 * 512
+    assert N.sf_blocked_size(129, 5) == 2 * 2 * 512
+    assert N.sf_blocked_size(0, 4) == 0
+
+
+def _table(N, **kw):
+    t = np.zeros(1, dtype=N.GROUP_DTYPE)
+    base = dict(a=0x10000, b=0x20000, sfa=0x30000, sfb=0x40000, c=0x50000, m=128, n=256, k=512,
+                alpha=1.0, alpha2=1.0)
+    base.update(kw)
+    for k, v in base.items():
+        t[k] = v
+    return t
+
+
+@pytest.mark.parametrize("kw,flags,status", [
+    (dict(k=100), 0, 2),            # K not a multiple of 256
+    (dict(k=0), 0, 2),
+    (dict(n=100), 0, 2),            # N % 8
+    (dict(m=-1), 0, 2),
+    (dict(a=0), 0, 4),              # NULL operand of a non-empty group
+    (dict(c=0x50008), 0, 3),        # misaligned output
+    (dict(b2=0), 1, 4),             # gated without up weights
+    (dict(), 0x100, 1),             # unknown flag bit
+    (dict(), 0x2 | 0x4, 1),         # exclusive tile flags
+])
+def test_validation_errors_before_launch(pkg, kw, flags, status):
+    N = pkg._native
+    lib = pkg.load_library()
+    t = _table(N, **kw)
+    ws = ctypes.create_string_buffer(N.workspace_size(1) + 256)
+    ws_ptr = (ctypes.addressof(ws) + 255) & ~255
+    st = lib.nvfp4_grouped_gemm(t.ctypes.data, 1, flags, ws_ptr, N.workspace_size(1), None)
+    assert st == status, lib.nvfp4_last_error_detail()
+    assert lib.nvfp4_last_error_detail()
+
+
+def test_workspace_errors(pkg):
+    N = pkg._native
+    lib = pkg.load_library()
+    t = _table(N)
+    assert lib.nvfp4_grouped_gemm(t.ctypes.data, 1, 0, None, 1 << 20, None) == 5
+    assert lib.nvfp4_grouped_gemm(t.ctypes.data, 1, 0, 0x1000 + 8, 1 << 20, None) == 5
+    assert lib.nvfp4_grouped_gemm(t.ctypes.data, 1, 0, 0x1000, 16, None) == 5
+    assert lib.nvfp4_grouped_gemm(None, 1, 0, 0x1000, 1 << 20, None) == 1
+    assert lib.nvfp4_grouped_gemm(t.ctypes.data, -1, 0, 0x1000, 1 << 20, None) == 1
+    assert lib.nvfp4_grouped_gemm(None, 0, 0, None, 0, None) == 0   # empty launch is a no-op
+
+
+def test_empty_groups_launch_nothing(pkg):
+    """All groups empty -> success without touching the device (works on a CPU box)."""
+    N = pkg._native
+    lib = pkg.load_library()
+    t = _table(N, m=0, a=0, b=0, c=0, sfa=0, sfb=0)
+    assert lib.nvfp4_grouped_gemm(t.ctypes.data, 1, 0, 0x1000, N.workspace_size(1), None) == 0
+
+
+def test_sf_converter_validation(pkg):
+    lib = pkg.load_library()
+    assert lib.nvfp4_sf_to_blocked(None, None, 0, 4, 4, None) == 0
+    assert lib.nvfp4_sf_to_blocked(None, None, 4, 4, 4, None) == 4
+    assert lib.nvfp4_sf_to_blocked(0x1000, 0x2000, -1, 4, 4, None) == 2
+    assert lib.nvfp4_sf_to_blocked(0x1000, 0x2008, 4, 4, 4, None) == 3
+    assert lib.nvfp4_sf_to_blocked(0x1000, 0x2000, 4, 8, 4, None) == 1

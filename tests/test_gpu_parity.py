@@ -1,0 +1,284 @@
+"""Parity of the CUDA grouped GEMM with the CPU oracle and with the reference's arithmetic.
+
+Every test here calls the native library through the public entry points
+(``custom_kernel`` / ``grouped_gemm``, i.e. the C ABI) on a B200 and checks the
+fp16 outputs against the oracle (numpy restatement of ref_kernel) with the
+benchmark tolerance rtol = atol = 1e-2; cases drawn from the reference
+harness's distribution are also checked with the harness tolerance 1e-3
+(REFERENCE_IMPL.md:211-214).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden_case_names
+from oracle import nvfp4_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = dict(rtol=1e-2, atol=1e-2)          # benchmark tolerance
+HARNESS_TOL = dict(rtol=1e-3, atol=1e-3)  # reference harness tolerance
+
+
+def _np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().numpy()
+
+
+def _oracle_group(prob, g):
+    a, b = _np(prob.a[g]), _np(prob.b[g])
+    sfa, sfb = _np(prob.sfa_plain[g]), _np(prob.sfb_plain[g])
+    if prob.gated:
+        b2, sfb2 = _np(prob.b2[g]), _np(prob.sfb2_plain[g])
+        exp = O.ref_gated(a, b, b2, sfa, sfb, sfb2, prob.alpha[g], prob.alpha2[g])
+        ref32 = None
+    else:
+        ref32 = O.ref_gemm_fp32(a, b, sfa, sfb) * np.float32(prob.alpha[g])
+        exp = ref32.astype(np.float16)
+    return exp, ref32
+
+
+def check_problem(prob, tol=TOL, groups=None):
+    """Compare every (or the selected) group's kernel output with the oracle."""
+    torch.cuda.synchronize()
+    report = []
+    for g in (range(prob.num_groups) if groups is None else groups):
+        if prob.m[g] == 0:
+            continue
+        exp, ref32 = _oracle_group(prob, g)
+        res = O.compare_fp16(_np(prob.c[g]), exp, ref32, **tol)
+        report.append(res)
+        assert res["ok"], f"{prob.name} group {g} (m={prob.m[g]}): {res}"
+    return report
+
+
+def run_custom_kernel(pkg, prob, tile_n=None):
+    data = prob.reference_data()
+    scales = prob.global_scales()
+    if all(s == 1.0 or s == (1.0, 1.0) for s in scales):
+        scales = None
+    out = pkg.custom_kernel(data, global_scales=scales, tile_n=tile_n)
+    assert len(out) == prob.num_groups
+    for o, c in zip(out, prob.c):
+        assert o.data_ptr() == c.data_ptr()
+    return out
+
+
+# ----------------------------------------------------------------------------
+# Golden fixtures: the reference's own generator and to_blocked bytes
+# ----------------------------------------------------------------------------
+def _golden_problem(pkg, data, name):
+    from types import SimpleNamespace
+
+    G, gated = (int(x) for x in data[f"{name}/meta"])
+    sizes = data[f"{name}/sizes"]
+    alpha = [float(x) for x in data[f"{name}/alpha"]]
+    dev = torch.device("cuda")
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(dev)  # noqa: E731
+    p = SimpleNamespace(name=name, gated=bool(gated), m=[int(s[0]) for s in sizes],
+                        n=[int(s[1]) for s in sizes], k=[int(s[2]) for s in sizes], alpha=alpha,
+                        alpha2=[1.0] * G, num_groups=G)
+    p.a = [t(data[f"{name}/{g}/a"]) for g in range(G)]
+    p.b = [t(data[f"{name}/{g}/b"]) for g in range(G)]
+    p.sfa_plain = [data[f"{name}/{g}/sf_a"] for g in range(G)]
+    p.sfb_plain = [data[f"{name}/{g}/sf_b"] for g in range(G)]
+    # The kernel consumes the reference's reordered storage (== to_blocked bytes).
+    p.sfa = [t(data[f"{name}/{g}/reordered_a"]) for g in range(G)]
+    p.sfb = [t(data[f"{name}/{g}/reordered_b"]) for g in range(G)]
+    if gated:
+        p.b2 = [t(data[f"{name}/{g}/b2"]) for g in range(G)]
+        p.sfb2_plain = [data[f"{name}/{g}/sf_b2"] for g in range(G)]
+        p.sfb2 = [t(data[f"{name}/{g}/reordered_b2"]) for g in range(G)]
+    else:
+        p.b2 = p.sfb2 = p.sfb2_plain = None
+    p.c = [torch.full((int(s[0]), int(s[1])), float("nan"), dtype=torch.float16, device=dev)
+           for s in sizes]
+    return p
+
+
+@pytest.mark.parametrize("tile_n", [None, 128])
+def test_golden_cases_match_oracle_and_reference(pkg, golden_inputs, tile_n):
+    outputs = None
+    try:
+        import os
+
+        from conftest import GOLDEN_DIR
+        path = os.path.join(GOLDEN_DIR, "golden_outputs.npz")
+        outputs = np.load(path) if os.path.exists(path) else None
+    except Exception:
+        outputs = None
+    for name in golden_case_names(golden_inputs):
+        p = _golden_problem(pkg, golden_inputs, name)
+        if tile_n is not None and p.gated:
+            continue
+        pkg.grouped_gemm(p.a, p.b, p.sfa, p.sfb, p.c,
+                         [(m, n, k, 1) for m, n, k in zip(p.m, p.n, p.k)], alpha=p.alpha,
+                         b2=p.b2, sfb2=p.sfb2, alpha2=p.alpha2, tile_n=tile_n)
+        torch.cuda.synchronize()
+        for g in range(p.num_groups):
+            got = _np(p.c[g])
+            a, b = _np(p.a[g]), _np(p.b[g])
+            if p.gated:
+                exp = O.ref_gated(a, b, _np(p.b2[g]), p.sfa_plain[g], p.sfb_plain[g],
+                                  p.sfb2_plain[g])
+                ref32 = None
+            else:
+                ref32 = O.ref_gemm_fp32(a, b, p.sfa_plain[g], p.sfb_plain[g]) * np.float32(p.alpha[g])
+                exp = ref32.astype(np.float16)
+            tol = HARNESS_TOL if name.startswith("ref_") else TOL
+            res = O.compare_fp16(got, exp, ref32, **tol)
+            assert res["ok"], f"{name}[{g}] vs oracle: {res}"
+            if outputs is not None and f"{name}/{g}/c" in outputs.files:
+                res = O.compare_fp16(got, outputs[f"{name}/{g}/c"], ref32, **tol)
+                assert res["ok"], f"{name}[{g}] vs torch._scaled_mm: {res}"
+
+
+# ----------------------------------------------------------------------------
+# Seeded shapes: edge cases of the scheduler, the tiles and the epilogue
+# ----------------------------------------------------------------------------
+EDGE_SHAPES = [
+    # (name, m_list, n, k)
+    ("single_128x256x512", [128], 256, 512),
+    ("m1", [1], 256, 256),
+    ("m_ragged", [1, 127, 129, 255, 300], 384, 512),
+    ("n128_tail", [200], 384, 768),          # 256-wide tiles: last tile half out of range
+    ("n8", [64], 8, 256),
+    ("n136", [70], 136, 512),
+    ("k256", [128, 64], 512, 256),
+    ("empty_groups", [0, 64, 0, 0, 130, 0], 256, 512),
+    ("many_small", [3, 17, 0, 64, 9, 1, 128, 33] * 4, 256, 512),
+]
+
+
+@pytest.mark.parametrize("tile_n", [None, 128, 256])
+@pytest.mark.parametrize("shape", EDGE_SHAPES, ids=[s[0] for s in EDGE_SHAPES])
+def test_edge_shapes(pkg, shape, tile_n):
+    name, ms, n, k = shape
+    prob = pkg.workloads.make_problem(name, ms, n, k, seed=len(ms) * 7 + n + k, device="cuda",
+                                      alpha_range=(0.5, 2.0))
+    run_custom_kernel(pkg, prob, tile_n=tile_n)
+    check_problem(prob)
+
+
+@pytest.mark.parametrize("shape", [("gated_small", [96], 256, 512),
+                                   ("gated_ragged", [0, 1, 130, 257], 384, 768),
+                                   ("gated_n8", [40], 8, 256)], ids=lambda s: s[0])
+def test_gated_shapes(pkg, shape):
+    name, ms, n, k = shape
+    prob = pkg.workloads.make_problem(name, ms, n, k, gated=True, seed=99 + n, device="cuda",
+                                      alpha_range=(0.5, 2.0))
+    run_custom_kernel(pkg, prob)
+    check_problem(prob)
+
+
+def test_ten_tuple_dual_gemm_form(pkg):
+    """The reference's local 10-tuple form (submission.py:860-886) in one fused launch."""
+    prob = pkg.workloads.make_problem("ten", [256], 512, 1024, gated=True, seed=5,
+                                      device="cuda", distribution="reference")
+    d = prob.reference_data()
+    (a, b1, b2, c), = d[0]
+    (sfa, sfb1, sfb2), = d[2]
+    out = pkg.custom_kernel((a, b1, b2, None, None, None, sfa, sfb1, sfb2, c))
+    assert out.data_ptr() == c.data_ptr()
+    check_problem(prob, tol=HARNESS_TOL)
+
+
+def test_more_groups_than_one_builder_launch(pkg):
+    ms = [(i * 37) % 150 for i in range(300)]  # 300 groups -> two descriptor-builder launches
+    prob = pkg.workloads.make_problem("g300", ms, 128, 256, seed=3, device="cuda")
+    run_custom_kernel(pkg, prob)
+    check_problem(prob)
+
+
+@pytest.mark.parametrize("cfg", ["challenge3", "challenge4", "challenge1", "challenge2"])
+def test_challenge_shapes(pkg, cfg):
+    prob = pkg.workloads.make_config(cfg, seed=11, device="cuda")
+    run_custom_kernel(pkg, prob)
+    check_problem(prob, tol=HARNESS_TOL)
+
+
+def test_descriptor_reuse_and_rebuild(pkg):
+    p1 = pkg.workloads.make_problem("r1", [128, 200], 256, 512, seed=21, device="cuda")
+    run_custom_kernel(pkg, p1)
+    first = [c.clone() for c in p1.c]
+    for c in p1.c:
+        c.fill_(0)
+    run_custom_kernel(pkg, p1)             # same table -> descriptors reused
+    torch.cuda.synchronize()
+    for a, b in zip(first, p1.c):
+        assert torch.equal(a, b)
+    p2 = pkg.workloads.make_problem("r2", [64, 300], 256, 512, seed=22, device="cuda")
+    run_custom_kernel(pkg, p2)             # different table -> rebuilt
+    check_problem(p2)
+    assert pkg.check_device_errors() == 0
+
+
+# ----------------------------------------------------------------------------
+# Scale-factor converter: bit-exact
+# ----------------------------------------------------------------------------
+@pytest.mark.parametrize("rows,cols", [(1, 1), (80, 32), (128, 4), (129, 5), (257, 448), (4096, 448)])
+def test_sf_to_blocked_bit_exact(pkg, rows, cols):
+    rng = np.random.default_rng(rows * 1000 + cols)
+    plain = rng.integers(0, 256, (rows, cols), dtype=np.uint8)
+    out = pkg.sf_to_blocked(torch.from_numpy(plain).cuda())
+    torch.cuda.synchronize()
+    assert np.array_equal(_np(out), O.to_blocked(plain))
+
+
+def test_sf_to_blocked_matches_reference_golden(pkg, golden_inputs):
+    for key in golden_inputs.files:
+        if "/sf_" not in key:
+            continue
+        plain = golden_inputs[key]
+        blocked = golden_inputs[key.replace("/sf_", "/blocked_")]
+        out = pkg.sf_to_blocked(torch.from_numpy(plain).cuda())
+        torch.cuda.synchronize()
+        assert np.array_equal(_np(out), blocked), key
+
+
+# ----------------------------------------------------------------------------
+# Benchmark configurations at full size
+# ----------------------------------------------------------------------------
+def test_cfg1_cpu_reference_config(pkg):
+    prob = pkg.workloads.make_config("cfg1", seed=1, device="cuda")
+    run_custom_kernel(pkg, prob)
+    check_problem(prob)
+
+
+def test_cfg2_full_size(pkg):
+    prob = pkg.workloads.make_config("cfg2", seed=2, device="cuda")
+    run_custom_kernel(pkg, prob)
+    check_problem(prob)
+    assert pkg.check_device_errors() == 0
+
+
+def test_cfg4_skewed_full_size(pkg):
+    prob = pkg.workloads.make_config("cfg4", seed=4, device="cuda")
+    assert 0 in prob.m or min(prob.m) <= 16
+    run_custom_kernel(pkg, prob)
+    check_problem(prob)
+
+
+def test_cfg3_gated_full_size(pkg):
+    prob = pkg.workloads.make_config("cfg3", seed=3, device="cuda")
+    run_custom_kernel(pkg, prob)
+    check_problem(prob)
+
+
+def test_cfg5_gated_checksum_subset(pkg):
+    """Full cfg5 launch (256 experts); oracle on a spread of experts (size-independent check)."""
+    prob = pkg.workloads.make_config("cfg5", seed=5, device="cuda")
+    run_custom_kernel(pkg, prob)
+    check_problem(prob, groups=[0, 1, 63, 128, 200, 255])
+    # every output element was written (the buffers were prefilled with randn; finite check
+    # plus a recomputation of two experts in a second launch must agree bit for bit)
+    sub = pkg.workloads.make_config("cfg5", seed=5, device="cuda")
+    keep = [3, 250]
+    pkg.grouped_gemm([sub.a[g] for g in keep], [sub.b[g] for g in keep],
+                     [sub.sfa[g] for g in keep], [sub.sfb[g] for g in keep],
+                     [sub.c[g] for g in keep], [sub.problem_sizes()[g] for g in keep],
+                     b2=[sub.b2[g] for g in keep], sfb2=[sub.sfb2[g] for g in keep])
+    torch.cuda.synchronize()
+    for i, g in enumerate(keep):
+        assert torch.equal(sub.c[g], prob.c[g])
