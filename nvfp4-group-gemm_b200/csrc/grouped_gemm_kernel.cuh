@@ -150,9 +150,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     ptx::tmem_alloc(tmem_holder, kTmemCols);
     ptx::tmem_relinquish_alloc_permit();
   }
-  // The descriptor builder that ran just before this grid wrote the group
-  // records and tensor maps this kernel reads.
-  ptx::grid_dependency_wait();
   ptx::tcgen05_fence_before_sync();
   __syncthreads();
   ptx::tcgen05_fence_after_sync();

@@ -1,14 +1,17 @@
-// C ABI implementation: host-side validation and scheduling, the device-side
-// group/tensor-map builder, the scale-factor layout converter, and the launch of
-// the persistent tcgen05 grouped GEMM.
+// C ABI implementation: host-side validation and scheduling, tensor-map encoding
+// (driver encoder, cached per tensor) and upload into the workspace, the
+// scale-factor layout converter, and the launch of the persistent tcgen05
+// grouped GEMM.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "../../include/nvfp4_group_gemm.h"
@@ -19,72 +22,23 @@
 namespace nvfp4 {
 
 // ============================================================================
-// Device-side group and tensor-map builder
+// Descriptor upload
 // ============================================================================
-// One warp per group: patch the two templates (e2m1 operand, fp16 output) with
-// the group's addresses, extents and row strides in shared memory, then copy
-// each map to the workspace with a release to the tensor-map proxy.
-__global__ void __launch_bounds__(128) nvfp4_build_descriptors_kernel(
-    const __grid_constant__ PrepParams p) {
-  __shared__ __align__(128) TmaDesc smaps[4][kMapsPerGroup];
-  // Let the dependent GEMM grid start its prologue (barrier init, TMEM
-  // allocation); it still waits for this grid to finish before reading.
-  ptx::grid_dependency_launch_dependents();
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int gi = blockIdx.x * 4 + warp;
+// Copies host-encoded group records and tensor maps (carried in the kernel's
+// parameter block) into the workspace, then releases the maps to the
+// tensor-map proxy. One warp per group: each lane moves 16 bytes of the 512
+// bytes of maps; lane 0 also writes the record.
+__global__ void __launch_bounds__(32) nvfp4_upload_descriptors_kernel(
+    const __grid_constant__ UploadParams p) {
+  const int gi = blockIdx.x;
+  const int lane = threadIdx.x;
   if (gi >= p.count) return;
-  const GroupIn& in = p.in[gi];
   const int g = p.first_group + gi;
-  TmaDesc* sm = smaps[warp];
-  if (lane < 16) {
-    sm[kMapA].raw[lane] = p.tmpl_operand.raw[lane];
-    sm[kMapB].raw[lane] = p.tmpl_operand.raw[lane];
-    sm[kMapB2].raw[lane] = p.tmpl_operand.raw[lane];
-    sm[kMapC].raw[lane] = p.tmpl_output.raw[lane];
-  }
-  __syncwarp();
-  const bool active = in.m > 0 && in.n > 0;
-  if (lane == 0 && active) {
-    const uint32_t kbytes = static_cast<uint32_t>(in.k / 2);
-    ptx::tensormap_replace_address(&sm[kMapA], in.a);
-    ptx::tensormap_replace_dim<0>(&sm[kMapA], kbytes);
-    ptx::tensormap_replace_dim<1>(&sm[kMapA], static_cast<uint32_t>(in.m));
-    ptx::tensormap_replace_stride<0>(&sm[kMapA], kbytes);
-    ptx::tensormap_replace_address(&sm[kMapB], in.b);
-    ptx::tensormap_replace_dim<0>(&sm[kMapB], kbytes);
-    ptx::tensormap_replace_dim<1>(&sm[kMapB], static_cast<uint32_t>(in.n));
-    ptx::tensormap_replace_stride<0>(&sm[kMapB], kbytes);
-    if (p.gated) {
-      ptx::tensormap_replace_address(&sm[kMapB2], in.b2);
-      ptx::tensormap_replace_dim<0>(&sm[kMapB2], kbytes);
-      ptx::tensormap_replace_dim<1>(&sm[kMapB2], static_cast<uint32_t>(in.n));
-      ptx::tensormap_replace_stride<0>(&sm[kMapB2], kbytes);
-    }
-    ptx::tensormap_replace_address(&sm[kMapC], in.c);
-    ptx::tensormap_replace_dim<0>(&sm[kMapC], static_cast<uint32_t>(in.n));
-    ptx::tensormap_replace_dim<1>(&sm[kMapC], static_cast<uint32_t>(in.m));
-    ptx::tensormap_replace_stride<0>(&sm[kMapC], static_cast<uint64_t>(in.n) * 2u);
-  }
-  __syncwarp();
-  TmaDesc* out = p.maps_out + static_cast<size_t>(g) * kMapsPerGroup;
-#pragma unroll
-  for (int i = 0; i < kMapsPerGroup; ++i) ptx::tensormap_copy_release(&out[i], &sm[i]);
-  if (lane == 0) {
-    GroupDev d;
-    d.sfa = reinterpret_cast<const uint8_t*>(in.sfa);
-    d.sfb = reinterpret_cast<const uint8_t*>(in.sfb);
-    d.sfb2 = reinterpret_cast<const uint8_t*>(in.sfb2);
-    d.m = in.m;
-    d.n = in.n;
-    d.k = in.k;
-    d.tiles_m = in.tiles_m;
-    d.tile_start = in.tile_start;
-    d.tile_end = in.tile_end;
-    d.alpha = in.alpha;
-    d.alpha2 = in.alpha2;
-    p.groups_out[g] = d;
-  }
+  const uint4* src = reinterpret_cast<const uint4*>(&p.maps[gi][0]);
+  uint4* dst = reinterpret_cast<uint4*>(p.maps_out + static_cast<size_t>(g) * kMapsPerGroup);
+  dst[lane] = src[lane];  // 32 lanes x 16 B = 4 maps x 128 B
+  if (lane == 0) p.groups_out[g] = p.rec[gi];
+  ptx::tensormap_fence_release();
 }
 
 // ============================================================================
@@ -159,14 +113,85 @@ struct DeviceState {
 };
 DeviceState g_dev[kMaxDevices];
 
-struct Templates {
+// cuTensorMapEncodeTiled, resolved once through the runtime (no libcuda link).
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                              const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+struct Encoder {
   std::once_flag once;
-  int status = NVFP4_OK;
-  std::string detail;
-  TmaDesc operand;
-  TmaDesc output;
+  EncodeFn fn = nullptr;
 };
-Templates g_tmpl;
+Encoder g_encoder;
+
+void init_encoder(Encoder& e) {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) e.fn = reinterpret_cast<EncodeFn>(fn);
+}
+
+// Encoded maps are cached by (kind, address, rows, row bytes): weights keep
+// their maps across calls, so steady-state calls encode only what changed.
+struct MapKey {
+  uint64_t addr;
+  uint32_t rows;
+  uint32_t row_bytes;
+  uint32_t kind;
+  bool operator==(const MapKey& o) const {
+    return addr == o.addr && rows == o.rows && row_bytes == o.row_bytes && kind == o.kind;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = k.addr * 0x9E3779B97F4A7C15ull;
+    h ^= (static_cast<uint64_t>(k.rows) << 32 | k.row_bytes) + 0x632BE59BD9B4E019ull + (h << 6);
+    return static_cast<size_t>(h ^ (static_cast<uint64_t>(k.kind) << 61));
+  }
+};
+std::mutex g_map_cache_mu;
+std::unordered_map<MapKey, TmaDesc, MapKeyHash> g_map_cache;
+constexpr size_t kMapCacheMax = 1 << 14;
+
+enum : uint32_t { kKindOperand = 0, kKindOutput = 1 };
+
+// e2m1 operand [rows, row_bytes] (uint8 view): box 128 B x 128 rows, 128B swizzle,
+// zero fill outside the tensor. fp16 output [rows, cols]: box 64 x 32, 128B swizzle.
+bool encode_map(uint32_t kind, const void* addr, uint32_t rows, uint32_t row_elems, TmaDesc* out) {
+  const MapKey key{reinterpret_cast<uint64_t>(addr), rows, row_elems, kind};
+  {
+    std::lock_guard<std::mutex> lk(g_map_cache_mu);
+    auto it = g_map_cache.find(key);
+    if (it != g_map_cache.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  CUtensorMap m;
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r;
+  if (kind == kKindOperand) {
+    cuuint64_t dims[2] = {row_elems, rows};
+    cuuint64_t strides[1] = {row_elems};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kRowBytesPerStage), static_cast<cuuint32_t>(kBlockM)};
+    r = g_encoder.fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(addr), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[2] = {row_elems, rows};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_elems) * 2u};
+    cuuint32_t box[2] = {64, 32};
+    r = g_encoder.fn(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(addr), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  if (r != CUDA_SUCCESS) return false;
+  memcpy(out, &m, sizeof(TmaDesc));
+  std::lock_guard<std::mutex> lk(g_map_cache_mu);
+  if (g_map_cache.size() >= kMapCacheMax) g_map_cache.clear();
+  g_map_cache.emplace(key, *out);
+  return true;
+}
 
 void init_device(int dev, DeviceState& st) {
   cudaDeviceProp prop;
@@ -203,73 +228,14 @@ void init_device(int dev, DeviceState& st) {
   }
 }
 
-void init_templates(Templates& t) {
-  void* fn = nullptr;
-  cudaDriverEntryPointQueryResult q;
-  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-  if (e != cudaSuccess || fn == nullptr || q != cudaDriverEntryPointSuccess) {
-    t.status = NVFP4_ERR_DRIVER;
-    t.detail = "cuTensorMapEncodeTiled entry point not available from the driver";
-    return;
-  }
-  using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-  EncodeFn encode = reinterpret_cast<EncodeFn>(fn);
-  // Templates carry everything that is the same for all groups (type, box, swizzle,
-  // fill); the builder kernel patches address, extents and row stride per group.
-  void* dummy = reinterpret_cast<void*>(static_cast<uintptr_t>(1) << 20);
-  {
-    CUtensorMap m;
-    cuuint64_t dims[2] = {4096, 4096};
-    cuuint64_t strides[1] = {4096};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(kRowBytesPerStage), 128};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, dummy, dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      t.status = NVFP4_ERR_DRIVER;
-      t.detail = "cuTensorMapEncodeTiled failed for the operand template";
-      return;
-    }
-    memcpy(&t.operand, &m, sizeof(TmaDesc));
-  }
-  {
-    CUtensorMap m;
-    cuuint64_t dims[2] = {4096, 4096};
-    cuuint64_t strides[1] = {4096 * 2};
-    cuuint32_t box[2] = {64, 32};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dummy, dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      t.status = NVFP4_ERR_DRIVER;
-      t.detail = "cuTensorMapEncodeTiled failed for the output template";
-      return;
-    }
-    memcpy(&t.output, &m, sizeof(TmaDesc));
-  }
-}
-
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 template <int MMA_N, bool GATED, int STAGES>
-cudaError_t launch_gemm(const GemmParams& gp, int grid, cudaStream_t stream, bool after_prep) {
+cudaError_t launch_gemm(const GemmParams& gp, int grid, cudaStream_t stream) {
   using Cfg = GemmConfig<MMA_N, GATED, STAGES>;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(kNumThreads, 1, 1);
-  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = after_prep ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, nvfp4_grouped_gemm_kernel<MMA_N, GATED, STAGES>, gp);
+  nvfp4_grouped_gemm_kernel<MMA_N, GATED, STAGES>
+      <<<grid, kNumThreads, Cfg::kSmemBytes, stream>>>(gp);
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -381,51 +347,44 @@ NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsi
   const int mma_n = gated ? 256 : ((flags & NVFP4_FLAG_TILE_N128) ? 128 : 256);
   const int out_n = gated ? 128 : mma_n;
 
-  std::vector<GroupIn> gin(static_cast<size_t>(num_groups));
+  // Host-side schedule: tiles are numbered group by group, m-tile fastest.
+  std::vector<GroupDev> rec(static_cast<size_t>(num_groups));
   int64_t total_tiles = 0;
   for (int i = 0; i < num_groups; ++i) {
     const nvfp4_group& gr = groups[i];
     if (gr.m < 0 || gr.n < 0 || gr.k < 0)
       return fail(NVFP4_ERR_BAD_SHAPE, "group %d: negative size (m=%d n=%d k=%d)", i, gr.m, gr.n, gr.k);
-    GroupIn& d = gin[i];
+    GroupDev& d = rec[i];
     memset(&d, 0, sizeof(d));
     d.m = gr.m;
     d.n = gr.n;
     d.k = gr.k;
     d.alpha = gr.alpha;
     d.alpha2 = gr.alpha2;
-    const bool active = gr.m > 0 && gr.n > 0;
-    if (active) {
-      if (gr.k <= 0 || gr.k % kBlockK != 0)
-        return fail(NVFP4_ERR_BAD_SHAPE, "group %d: k=%d must be a positive multiple of 256", i, gr.k);
-      if (gr.n % 8 != 0)
-        return fail(NVFP4_ERR_BAD_SHAPE, "group %d: n=%d must be a multiple of 8", i, gr.n);
-      const void* ptrs[7] = {gr.a, gr.b, gr.b2, gr.sfa, gr.sfb, gr.sfb2, gr.c};
-      const char* names[7] = {"a", "b", "b2", "sfa", "sfb", "sfb2", "c"};
-      for (int j = 0; j < 7; ++j) {
-        if (!gated && (j == 2 || j == 5)) continue;
-        if (ptrs[j] == nullptr) return fail(NVFP4_ERR_NULL_POINTER, "group %d: %s is NULL", i, names[j]);
-        if (!aligned16(ptrs[j]))
-          return fail(NVFP4_ERR_MISALIGNED, "group %d: %s not 16-byte aligned", i, names[j]);
-      }
-      d.a = reinterpret_cast<uint64_t>(gr.a);
-      d.b = reinterpret_cast<uint64_t>(gr.b);
-      d.b2 = gated ? reinterpret_cast<uint64_t>(gr.b2) : 0;
-      d.sfa = reinterpret_cast<uint64_t>(gr.sfa);
-      d.sfb = reinterpret_cast<uint64_t>(gr.sfb);
-      d.sfb2 = gated ? reinterpret_cast<uint64_t>(gr.sfb2) : 0;
-      d.c = reinterpret_cast<uint64_t>(gr.c);
-      d.tiles_m = (gr.m + kBlockM - 1) / kBlockM;
-      const int tiles_n = (gr.n + out_n - 1) / out_n;
-      d.tile_start = static_cast<int32_t>(total_tiles);
-      total_tiles += static_cast<int64_t>(d.tiles_m) * tiles_n;
-      if (total_tiles > (int64_t{1} << 30))
-        return fail(NVFP4_ERR_BAD_SHAPE, "too many tiles (%lld)", static_cast<long long>(total_tiles));
-      d.tile_end = static_cast<int32_t>(total_tiles);
-    } else {
-      d.tiles_m = 1;
-      d.tile_start = d.tile_end = static_cast<int32_t>(total_tiles);
+    d.tiles_m = 1;
+    d.tile_start = d.tile_end = static_cast<int32_t>(total_tiles);
+    if (gr.m == 0 || gr.n == 0) continue;
+    if (gr.k <= 0 || gr.k % kBlockK != 0)
+      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: k=%d must be a positive multiple of 256", i, gr.k);
+    if (gr.n % 8 != 0)
+      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: n=%d must be a multiple of 8", i, gr.n);
+    const void* ptrs[7] = {gr.a, gr.b, gr.b2, gr.sfa, gr.sfb, gr.sfb2, gr.c};
+    const char* names[7] = {"a", "b", "b2", "sfa", "sfb", "sfb2", "c"};
+    for (int j = 0; j < 7; ++j) {
+      if (!gated && (j == 2 || j == 5)) continue;
+      if (ptrs[j] == nullptr) return fail(NVFP4_ERR_NULL_POINTER, "group %d: %s is NULL", i, names[j]);
+      if (!aligned16(ptrs[j]))
+        return fail(NVFP4_ERR_MISALIGNED, "group %d: %s not 16-byte aligned", i, names[j]);
     }
+    d.sfa = static_cast<const uint8_t*>(gr.sfa);
+    d.sfb = static_cast<const uint8_t*>(gr.sfb);
+    d.sfb2 = gated ? static_cast<const uint8_t*>(gr.sfb2) : nullptr;
+    d.tiles_m = (gr.m + kBlockM - 1) / kBlockM;
+    const int tiles_n = (gr.n + out_n - 1) / out_n;
+    total_tiles += static_cast<int64_t>(d.tiles_m) * tiles_n;
+    if (total_tiles > (int64_t{1} << 30))
+      return fail(NVFP4_ERR_BAD_SHAPE, "too many tiles (%lld)", static_cast<long long>(total_tiles));
+    d.tile_end = static_cast<int32_t>(total_tiles);
   }
   if (total_tiles == 0) return NVFP4_OK;
 
@@ -436,30 +395,40 @@ NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsi
   DeviceState& ds = g_dev[dev];
   std::call_once(ds.once, init_device, dev, std::ref(ds));
   if (ds.status != NVFP4_OK) return fail(ds.status, "%s", ds.detail.c_str());
-  std::call_once(g_tmpl.once, init_templates, std::ref(g_tmpl));
-  if (g_tmpl.status != NVFP4_OK) return fail(g_tmpl.status, "%s", g_tmpl.detail.c_str());
+  std::call_once(g_encoder.once, init_encoder, std::ref(g_encoder));
+  if (g_encoder.fn == nullptr)
+    return fail(NVFP4_ERR_DRIVER, "cuTensorMapEncodeTiled entry point not available from the driver");
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   GroupDev* groups_dev = reinterpret_cast<GroupDev*>(ws + ws_groups_offset());
   TmaDesc* maps_dev = reinterpret_cast<TmaDesc*>(ws + ws_maps_offset(num_groups));
 
-  const bool rebuild = (flags & NVFP4_FLAG_REUSE_DESCRIPTORS) == 0;
-  if (rebuild) {
-    static thread_local PrepParams pp;  // ~22 KB: too large for the stack of some callers
-    pp.tmpl_operand = g_tmpl.operand;
-    pp.tmpl_output = g_tmpl.output;
-    pp.groups_out = groups_dev;
-    pp.maps_out = maps_dev;
-    pp.gated = gated ? 1 : 0;
-    for (int first = 0; first < num_groups; first += kMaxGroupsPerPrepLaunch) {
-      const int count = std::min(kMaxGroupsPerPrepLaunch, num_groups - first);
-      pp.first_group = first;
-      pp.count = count;
-      memcpy(pp.in, &gin[first], sizeof(GroupIn) * count);
-      nvfp4_build_descriptors_kernel<<<(count + 3) / 4, 128, 0, s>>>(pp);
+  if ((flags & NVFP4_FLAG_REUSE_DESCRIPTORS) == 0) {
+    static thread_local UploadParams up;  // ~23 KB: kept off the caller's stack
+    up.groups_out = groups_dev;
+    up.maps_out = maps_dev;
+    for (int first = 0; first < num_groups; first += kGroupsPerUpload) {
+      const int count = std::min(kGroupsPerUpload, num_groups - first);
+      up.first_group = first;
+      up.count = count;
+      for (int gi = 0; gi < count; ++gi) {
+        const int i = first + gi;
+        const nvfp4_group& gr = groups[i];
+        up.rec[gi] = rec[i];
+        TmaDesc* mp = up.maps[gi];
+        memset(mp, 0, sizeof(TmaDesc) * kMapsPerGroup);
+        if (rec[i].tile_end == rec[i].tile_start) continue;  // empty group: maps never read
+        const uint32_t kb = static_cast<uint32_t>(gr.k / 2);
+        bool ok = encode_map(kKindOperand, gr.a, gr.m, kb, &mp[kMapA]) &&
+                  encode_map(kKindOperand, gr.b, gr.n, kb, &mp[kMapB]) &&
+                  (!gated || encode_map(kKindOperand, gr.b2, gr.n, kb, &mp[kMapB2])) &&
+                  encode_map(kKindOutput, gr.c, gr.m, gr.n, &mp[kMapC]);
+        if (!ok) return fail(NVFP4_ERR_DRIVER, "group %d: cuTensorMapEncodeTiled rejected a tensor", i);
+      }
+      nvfp4_upload_descriptors_kernel<<<count, 32, 0, s>>>(up);
       e = cudaGetLastError();
-      if (e != cudaSuccess) return cuda_fail(e, "descriptor builder launch");
+      if (e != cudaSuccess) return cuda_fail(e, "descriptor upload launch");
     }
   }
 
@@ -471,11 +440,11 @@ NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsi
   gp.total_tiles = static_cast<int32_t>(total_tiles);
   const int grid = static_cast<int>(std::min<int64_t>(total_tiles, ds.num_sms));
   if (gated)
-    e = launch_gemm<256, true, 3>(gp, grid, s, rebuild);
+    e = launch_gemm<256, true, 3>(gp, grid, s);
   else if (mma_n == 128)
-    e = launch_gemm<128, false, 5>(gp, grid, s, rebuild);
+    e = launch_gemm<128, false, 5>(gp, grid, s);
   else
-    e = launch_gemm<256, false, 3>(gp, grid, s, rebuild);
+    e = launch_gemm<256, false, 3>(gp, grid, s);
   if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
   return NVFP4_OK;
 }

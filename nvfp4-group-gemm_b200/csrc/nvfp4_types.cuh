@@ -16,7 +16,8 @@ constexpr int kRowBytesPerStage = 128;
 constexpr int kMmaK = 64;             // K per tcgen05.mma kind::mxf4nvf4
 constexpr int kSfVec = 16;            // elements per scale factor
 constexpr int kSfBlockBytes = 512;    // one 128 x 4 scale-factor block
-constexpr int kMaxGroupsPerPrepLaunch = 256;
+// Groups whose records and tensor maps one upload launch carries in its parameters.
+constexpr int kGroupsPerUpload = 40;
 
 // 128-byte opaque CUtensorMap image (the driver type requires 64-byte alignment).
 struct alignas(64) TmaDesc {
@@ -38,14 +39,6 @@ struct GroupDev {
   float alpha, alpha2;
 };
 static_assert(sizeof(GroupDev) <= 64, "group record must fit 64 bytes");
-
-// One group as the host hands it to the descriptor builder.
-struct GroupIn {
-  uint64_t a, b, b2, sfa, sfb, sfb2, c;
-  int32_t m, n, k;
-  int32_t tiles_m, tile_start, tile_end;
-  float alpha, alpha2;
-};
 
 struct WorkspaceHeader {
   uint32_t error_bits;  // OR of device-side failure reasons (see kDevErr*)
@@ -73,17 +66,17 @@ __host__ __device__ inline size_t ws_total_bytes(int num_groups) {
          static_cast<size_t>(num_groups) * kMapsPerGroup * sizeof(TmaDesc);
 }
 
-struct PrepParams {
-  TmaDesc tmpl_operand;  // e2m1 operand map template: uint8, box 128 B x 128 rows, 128B swizzle
-  TmaDesc tmpl_output;   // fp16 output map template: box 64 x 32, 128B swizzle
+// Parameter block of the descriptor upload kernel: host-encoded records and
+// tensor maps of up to kGroupsPerUpload groups (about 23 KB of kernel parameters).
+struct UploadParams {
+  TmaDesc maps[kGroupsPerUpload][kMapsPerGroup];
+  GroupDev rec[kGroupsPerUpload];
   GroupDev* groups_out;
   TmaDesc* maps_out;
   int32_t first_group;
   int32_t count;
-  int32_t gated;
-  int32_t pad;
-  GroupIn in[kMaxGroupsPerPrepLaunch];
 };
+static_assert(sizeof(UploadParams) <= 32000, "kernel parameter block too large");
 
 struct GemmParams {
   const GroupDev* groups;

@@ -1,6 +1,6 @@
 // Inline-PTX building blocks for sm_100a: mbarriers, TMA (tiled + bulk), tcgen05
 // (TMEM alloc, block-scaled MMA, smem->TMEM copy, TMEM->register loads) and
-// device-side tensor-map patching.
+// tensor-map proxy fences.
 //
 // Everything here is a thin, documented wrapper around one PTX instruction (or a
 // short fixed sequence of them). Bit layouts of the shared-memory matrix
@@ -35,15 +35,6 @@ __device__ __forceinline__ bool elect_one() {
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(pred));
   return pred != 0;
-}
-
-// Programmatic dependent launch: wait until the preceding grid in the stream
-// has completed and its memory is visible.
-__device__ __forceinline__ void grid_dependency_wait() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-__device__ __forceinline__ void grid_dependency_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -145,38 +136,9 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// ---------------------------------------------------------------------------
-// Device-side tensor-map patching (template map in shared memory)
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void tensormap_replace_address(void* smem_map, uint64_t addr) {
-  asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;" ::"r"(
-                   smem_u32(smem_map)),
-               "l"(addr)
-               : "memory");
-}
-template <int DIM>
-__device__ __forceinline__ void tensormap_replace_dim(void* smem_map, uint32_t size) {
-  asm volatile("tensormap.replace.tile.global_dim.shared::cta.b1024.b32 [%0], %1, %2;" ::"r"(
-                   smem_u32(smem_map)),
-               "n"(DIM), "r"(size)
-               : "memory");
-}
-// Byte stride of dimension DIM+1 (the innermost dimension is implicitly dense).
-template <int DIM>
-__device__ __forceinline__ void tensormap_replace_stride(void* smem_map, uint64_t stride_bytes) {
-  asm volatile("tensormap.replace.tile.global_stride.shared::cta.b1024.b64 [%0], %1, %2;" ::"r"(
-                   smem_u32(smem_map)),
-               "n"(DIM), "l"(stride_bytes)
-               : "memory");
-}
-// Warp-wide: copy a 128-byte map from shared to global memory and release it to
-// the tensor-map proxy.
-__device__ __forceinline__ void tensormap_copy_release(void* gmem_map, const void* smem_map) {
-  asm volatile(
-      "tensormap.cp_fenceproxy.global.shared::cta.tensormap::generic.release.gpu.sync.aligned"
-      " [%0], [%1], 128;" ::"l"(reinterpret_cast<uint64_t>(gmem_map)),
-      "r"(smem_u32(smem_map))
-      : "memory");
+// Release side of tensor maps written to global memory with generic stores.
+__device__ __forceinline__ void tensormap_fence_release() {
+  asm volatile("fence.proxy.tensormap::generic.release.gpu;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------
