@@ -121,6 +121,39 @@ NVFP4_API int nvfp4_workspace_check(void* workspace, void* stream, unsigned int*
 NVFP4_API const char* nvfp4_strerror(int status);
 NVFP4_API const char* nvfp4_last_error_detail(void);
 
+/*
+ * Allocation-free variant of nvfp4_grouped_gemm. No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory where they run the GEMM:
+ * frameworks that own all device memory through their own pool allocator and
+ * forbid other allocations, plugins loaded into a host application that only
+ * hands them their input and output buffers, and latency-critical paths that
+ * cannot afford cudaMalloc's implicit device synchronisation. Instead of a caller-provided
+ * workspace it uses a scratch array compiled into the library
+ * (nvfp4_workspace_size(NVFP4_NOALLOC_MAX_GROUPS) bytes, about 288 KiB, held on
+ * every GPU that loads the library until the process exits). It calls no
+ * cudaMalloc/cudaFree and no allocating library routine.
+ *
+ * - num_groups above NVFP4_NOALLOC_MAX_GROUPS is rejected with
+ *   NVFP4_ERR_INVALID_ARGUMENT (use nvfp4_grouped_gemm with a workspace instead).
+ * - The first call on a device looks up the device address of the scratch array
+ *   (cudaGetSymbolAddress) with that device current; make that first call before
+ *   any stream capture.
+ * - Every call on a device shares the one scratch array, which keeps the last
+ *   call's contents (the device error word is cleared at the start of each call).
+ *   Calls that can overlap on the GPU - on different streams, or from different
+ *   threads without ordering - race on it and must not be issued.
+ * - NVFP4_FLAG_REUSE_DESCRIPTORS means the scratch array holds this exact group
+ *   table from the previous call on the device.
+ * - Device-side wait timeouts are recorded in the scratch array's error word and
+ *   are not reported back; use nvfp4_grouped_gemm + nvfp4_workspace_check when
+ *   they are needed.
+ * Arguments, flags, outputs and other status codes are as in nvfp4_grouped_gemm.
+ */
+#define NVFP4_NOALLOC_MAX_GROUPS 512
+NVFP4_API int nvfp4_grouped_gemm_noalloc(const nvfp4_group* groups, int num_groups,
+                                         unsigned int flags, void* stream);
+
 /* NVFP4_ABI_VERSION of the loaded library. */
 NVFP4_API int nvfp4_abi_version(void);
 

@@ -43,7 +43,11 @@ EXPORTED_SYMBOLS = (
     "nvfp4_sf_blocked_size",
     "nvfp4_sf_to_blocked",
     "nvfp4_workspace_check",
+    "nvfp4_grouped_gemm_noalloc",
 )
+
+# Largest group count nvfp4_grouped_gemm_noalloc accepts (NVFP4_NOALLOC_MAX_GROUPS).
+NOALLOC_MAX_GROUPS = 512
 
 
 class Nvfp4Group(ctypes.Structure):
@@ -127,6 +131,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_sf_to_blocked.restype = i32
         lib.nvfp4_workspace_check.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint)]
         lib.nvfp4_workspace_check.restype = i32
+        lib.nvfp4_grouped_gemm_noalloc.argtypes = [vp, i32, u32, vp]
+        lib.nvfp4_grouped_gemm_noalloc.restype = i32
         if path is None:
             _lib = lib
         return lib

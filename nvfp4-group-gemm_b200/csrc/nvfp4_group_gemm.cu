@@ -157,16 +157,8 @@ enum : uint32_t { kKindOperand = 0, kKindOutput = 1 };
 
 // e2m1 operand [rows, row_bytes] (uint8 view): box 128 B x 128 rows, 128B swizzle,
 // zero fill outside the tensor. fp16 output [rows, cols]: box 64 x 32, 128B swizzle.
-bool encode_map(uint32_t kind, const void* addr, uint32_t rows, uint32_t row_elems, TmaDesc* out) {
-  const MapKey key{reinterpret_cast<uint64_t>(addr), rows, row_elems, kind};
-  {
-    std::lock_guard<std::mutex> lk(g_map_cache_mu);
-    auto it = g_map_cache.find(key);
-    if (it != g_map_cache.end()) {
-      *out = it->second;
-      return true;
-    }
-  }
+bool encode_map_uncached(uint32_t kind, const void* addr, uint32_t rows, uint32_t row_elems,
+                         TmaDesc* out) {
   CUtensorMap m;
   cuuint32_t estr[2] = {1, 1};
   CUresult r;
@@ -187,6 +179,20 @@ bool encode_map(uint32_t kind, const void* addr, uint32_t rows, uint32_t row_ele
   }
   if (r != CUDA_SUCCESS) return false;
   memcpy(out, &m, sizeof(TmaDesc));
+  return true;
+}
+
+bool encode_map(uint32_t kind, const void* addr, uint32_t rows, uint32_t row_elems, TmaDesc* out) {
+  const MapKey key{reinterpret_cast<uint64_t>(addr), rows, row_elems, kind};
+  {
+    std::lock_guard<std::mutex> lk(g_map_cache_mu);
+    auto it = g_map_cache.find(key);
+    if (it != g_map_cache.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  if (!encode_map_uncached(kind, addr, rows, row_elems, out)) return false;
   std::lock_guard<std::mutex> lk(g_map_cache_mu);
   if (g_map_cache.size() >= kMapCacheMax) g_map_cache.clear();
   g_map_cache.emplace(key, *out);
@@ -450,3 +456,168 @@ NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsi
 }
 
 }  // extern "C"
+
+// ============================================================================
+// Allocation-free entry point
+// ============================================================================
+// Some callers cannot allocate device memory at the point where they run the
+// GEMM: frameworks whose memory is owned by their own pool allocator and that
+// forbid other device allocations, plugins loaded into a host that only hands
+// them the input and output buffers, and latency-critical paths that cannot
+// afford the device synchronisation cudaMalloc may imply. For them this entry
+// point takes its scratch space (group records, tensor maps and the device error
+// word) from a fixed-size array compiled into the library instead of a
+// caller-provided workspace. Limits and sharing rules are documented with the
+// declaration in nvfp4_group_gemm.h.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = ws_total_bytes(NVFP4_NOALLOC_MAX_GROUPS);
+
+// One copy per GPU that loads the library, kept until the process exits.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocState {
+  std::once_flag once;
+  cudaError_t status = cudaSuccess;
+  void* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+};
+NoAllocState g_noalloc[kMaxDevices];
+
+// Runs once per device, with that device current: the host-side symbol is only a
+// stand-in, so the kernel must be given the device address looked up here.
+void init_noalloc(NoAllocState& st) {
+  st.status = cudaGetSymbolAddress(&st.scratch, g_noalloc_scratch);
+  if (st.status != cudaSuccess) st.scratch = nullptr;
+}
+
+}  // namespace
+
+extern "C" NVFP4_API int nvfp4_grouped_gemm_noalloc(const nvfp4_group* groups, int num_groups,
+                                                    unsigned int flags, void* stream) {
+  g_last_error.clear();
+  const unsigned known = NVFP4_FLAG_GATED | NVFP4_FLAG_TILE_N128 | NVFP4_FLAG_TILE_N256 |
+                         NVFP4_FLAG_REUSE_DESCRIPTORS;
+  if (flags & ~known) return fail(NVFP4_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags & ~known);
+  if (num_groups < 0) return fail(NVFP4_ERR_INVALID_ARGUMENT, "num_groups=%d", num_groups);
+  if (num_groups > NVFP4_NOALLOC_MAX_GROUPS)
+    return fail(NVFP4_ERR_INVALID_ARGUMENT,
+                "num_groups=%d exceeds the %d groups the built-in scratch array holds; "
+                "use nvfp4_grouped_gemm with a caller-provided workspace",
+                num_groups, NVFP4_NOALLOC_MAX_GROUPS);
+  if (num_groups == 0) return NVFP4_OK;
+  if (groups == nullptr) return fail(NVFP4_ERR_INVALID_ARGUMENT, "groups table is NULL");
+  const bool gated = (flags & NVFP4_FLAG_GATED) != 0;
+  if ((flags & NVFP4_FLAG_TILE_N128) && (flags & NVFP4_FLAG_TILE_N256))
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "TILE_N128 and TILE_N256 are exclusive");
+  if (gated && (flags & NVFP4_FLAG_TILE_N128))
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "gated launches use 128 gate + 128 up columns");
+  const int mma_n = gated ? 256 : ((flags & NVFP4_FLAG_TILE_N128) ? 128 : 256);
+  const int out_n = gated ? 128 : mma_n;
+
+  // Fixed-size host staging (no heap use on this path).
+  static thread_local GroupDev rec[NVFP4_NOALLOC_MAX_GROUPS];
+  int64_t total_tiles = 0;
+  for (int i = 0; i < num_groups; ++i) {
+    const nvfp4_group& gr = groups[i];
+    if (gr.m < 0 || gr.n < 0 || gr.k < 0)
+      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: negative size (m=%d n=%d k=%d)", i, gr.m, gr.n, gr.k);
+    GroupDev& d = rec[i];
+    memset(&d, 0, sizeof(d));
+    d.m = gr.m;
+    d.n = gr.n;
+    d.k = gr.k;
+    d.alpha = gr.alpha;
+    d.alpha2 = gr.alpha2;
+    d.tiles_m = 1;
+    d.tile_start = d.tile_end = static_cast<int32_t>(total_tiles);
+    if (gr.m == 0 || gr.n == 0) continue;
+    if (gr.k <= 0 || gr.k % kBlockK != 0)
+      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: k=%d must be a positive multiple of 256", i, gr.k);
+    if (gr.n % 8 != 0)
+      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: n=%d must be a multiple of 8", i, gr.n);
+    const void* ptrs[7] = {gr.a, gr.b, gr.b2, gr.sfa, gr.sfb, gr.sfb2, gr.c};
+    const char* names[7] = {"a", "b", "b2", "sfa", "sfb", "sfb2", "c"};
+    for (int j = 0; j < 7; ++j) {
+      if (!gated && (j == 2 || j == 5)) continue;
+      if (ptrs[j] == nullptr) return fail(NVFP4_ERR_NULL_POINTER, "group %d: %s is NULL", i, names[j]);
+      if (!aligned16(ptrs[j]))
+        return fail(NVFP4_ERR_MISALIGNED, "group %d: %s not 16-byte aligned", i, names[j]);
+    }
+    d.sfa = static_cast<const uint8_t*>(gr.sfa);
+    d.sfb = static_cast<const uint8_t*>(gr.sfb);
+    d.sfb2 = gated ? static_cast<const uint8_t*>(gr.sfb2) : nullptr;
+    d.tiles_m = (gr.m + kBlockM - 1) / kBlockM;
+    total_tiles += static_cast<int64_t>(d.tiles_m) * ((gr.n + out_n - 1) / out_n);
+    if (total_tiles > (int64_t{1} << 30))
+      return fail(NVFP4_ERR_BAD_SHAPE, "too many tiles (%lld)", static_cast<long long>(total_tiles));
+    d.tile_end = static_cast<int32_t>(total_tiles);
+  }
+  if (total_tiles == 0) return NVFP4_OK;
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_INVALID_ARGUMENT, "device %d", dev);
+  DeviceState& ds = g_dev[dev];
+  std::call_once(ds.once, init_device, dev, std::ref(ds));
+  if (ds.status != NVFP4_OK) return fail(ds.status, "%s", ds.detail.c_str());
+  std::call_once(g_encoder.once, init_encoder, std::ref(g_encoder));
+  if (g_encoder.fn == nullptr)
+    return fail(NVFP4_ERR_DRIVER, "cuTensorMapEncodeTiled entry point not available from the driver");
+  NoAllocState& na = g_noalloc[dev];
+  std::call_once(na.once, init_noalloc, std::ref(na));
+  if (na.scratch == nullptr) return cuda_fail(na.status, "cudaGetSymbolAddress(scratch)");
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(na.scratch);
+  GroupDev* groups_dev = reinterpret_cast<GroupDev*>(ws + ws_groups_offset());
+  TmaDesc* maps_dev = reinterpret_cast<TmaDesc*>(ws + ws_maps_offset(num_groups));
+
+  // The device error word keeps whatever the previous call left: start this call at zero.
+  e = cudaMemsetAsync(ws, 0, sizeof(uint32_t), s);
+  if (e != cudaSuccess) return cuda_fail(e, "clear scratch error word");
+
+  if ((flags & NVFP4_FLAG_REUSE_DESCRIPTORS) == 0) {
+    static thread_local UploadParams up;
+    up.groups_out = groups_dev;
+    up.maps_out = maps_dev;
+    for (int first = 0; first < num_groups; first += kGroupsPerUpload) {
+      const int count = std::min(kGroupsPerUpload, num_groups - first);
+      up.first_group = first;
+      up.count = count;
+      for (int gi = 0; gi < count; ++gi) {
+        const int i = first + gi;
+        const nvfp4_group& gr = groups[i];
+        up.rec[gi] = rec[i];
+        TmaDesc* mp = up.maps[gi];
+        memset(mp, 0, sizeof(TmaDesc) * kMapsPerGroup);
+        if (rec[i].tile_end == rec[i].tile_start) continue;
+        const uint32_t kb = static_cast<uint32_t>(gr.k / 2);
+        bool ok = encode_map_uncached(kKindOperand, gr.a, gr.m, kb, &mp[kMapA]) &&
+                  encode_map_uncached(kKindOperand, gr.b, gr.n, kb, &mp[kMapB]) &&
+                  (!gated || encode_map_uncached(kKindOperand, gr.b2, gr.n, kb, &mp[kMapB2])) &&
+                  encode_map_uncached(kKindOutput, gr.c, gr.m, gr.n, &mp[kMapC]);
+        if (!ok) return fail(NVFP4_ERR_DRIVER, "group %d: cuTensorMapEncodeTiled rejected a tensor", i);
+      }
+      nvfp4_upload_descriptors_kernel<<<count, 32, 0, s>>>(up);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_fail(e, "descriptor upload launch");
+    }
+  }
+
+  GemmParams gp;
+  gp.groups = groups_dev;
+  gp.maps = maps_dev;
+  gp.error_bits = reinterpret_cast<uint32_t*>(ws);
+  gp.num_groups = num_groups;
+  gp.total_tiles = static_cast<int32_t>(total_tiles);
+  const int grid = static_cast<int>(std::min<int64_t>(total_tiles, ds.num_sms));
+  if (gated)
+    e = launch_gemm<256, true, 3>(gp, grid, s);
+  else if (mma_n == 128)
+    e = launch_gemm<128, false, 5>(gp, grid, s);
+  else
+    e = launch_gemm<256, false, 3>(gp, grid, s);
+  if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
+  return NVFP4_OK;
+}

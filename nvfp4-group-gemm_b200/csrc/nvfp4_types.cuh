@@ -56,12 +56,12 @@ enum : uint32_t {
 };
 
 // Workspace layout: header | GroupDev[G] (64 B each) | TmaDesc[G][4] (128 B aligned).
-__host__ __device__ inline size_t ws_groups_offset() { return sizeof(WorkspaceHeader); }
-__host__ __device__ inline size_t ws_maps_offset(int num_groups) {
-  size_t off = ws_groups_offset() + static_cast<size_t>(num_groups) * 64;
-  return (off + 127) & ~static_cast<size_t>(127);
+__host__ __device__ constexpr size_t ws_groups_offset() { return sizeof(WorkspaceHeader); }
+__host__ __device__ constexpr size_t ws_maps_offset(int num_groups) {
+  return (ws_groups_offset() + static_cast<size_t>(num_groups) * 64 + 127) &
+         ~static_cast<size_t>(127);
 }
-__host__ __device__ inline size_t ws_total_bytes(int num_groups) {
+__host__ __device__ constexpr size_t ws_total_bytes(int num_groups) {
   return ws_maps_offset(num_groups) +
          static_cast<size_t>(num_groups) * kMapsPerGroup * sizeof(TmaDesc);
 }
