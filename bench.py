@@ -235,8 +235,10 @@ def main():
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
+    t_host = time.perf_counter()
     for _ in range(args.steps):
         step()
+    host_us = (time.perf_counter() - t_host) / args.steps * 1e6
     ev1.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
@@ -301,6 +303,7 @@ def main():
         "warmup": max(args.warmup, 3),
         "ms_per_step": ms_per_step,
         "us_per_call": ms_per_step * 1e3,
+        "host_us_per_call": host_us,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,

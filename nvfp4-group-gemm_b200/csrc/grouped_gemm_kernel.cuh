@@ -36,6 +36,10 @@ constexpr int kNumThreads = 192;
 constexpr int kEpilogueWarp0 = 2;
 constexpr int kEpilogueWarps = 4;
 constexpr int kTmemCols = 512;
+// k-tiles the producer warms in L2 ahead of its TMA loads. CTAs that share an A or B
+// tile walk K in lockstep, so without this every one of them waits on the same DRAM
+// miss at every k-step; the prefetch turns those misses into L2 hits.
+constexpr int kL2PrefetchKTiles = 6;
 
 template <int MMA_N, bool GATED, int STAGES>
 struct GemmConfig {
@@ -197,7 +201,27 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const uint8_t* sfa_blk = gd.sfa + static_cast<size_t>(mt) * rest_k * kSfBlockBytes;
         const uint32_t tx = Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes +
                             (sfb_blk1 != nullptr ? 2 : 1) * 4 * kSfBlockBytes;
+        // L2 warm-up of k-tile `kp` of this tile (A, B halves, scale blocks).
+        auto prefetch_ktile = [&](int kp) {
+          const int px = kp * kRowBytesPerStage;
+          const size_t psf = static_cast<size_t>(kp) * 4 * kSfBlockBytes;
+          ptx::tma_prefetch_l2_2d(&maps[kMapA], px, mt * kBlockM);
+          if (GATED) {
+            ptx::tma_prefetch_l2_2d(&maps[kMapB], px, nt * 128);
+            ptx::tma_prefetch_l2_2d(&maps[kMapB2], px, nt * 128);
+          } else if (MMA_N == 256) {
+            ptx::tma_prefetch_l2_2d(&maps[kMapB], px, nt * 256);
+            ptx::tma_prefetch_l2_2d(&maps[kMapB], px, nt * 256 + 128);
+          } else {
+            ptx::tma_prefetch_l2_2d(&maps[kMapB], px, nt * 128);
+          }
+          ptx::bulk_prefetch_l2(sfa_blk + psf, 4 * kSfBlockBytes);
+          ptx::bulk_prefetch_l2(sfb_blk0 + psf, 4 * kSfBlockBytes);
+          if (sfb_blk1 != nullptr) ptx::bulk_prefetch_l2(sfb_blk1 + psf, 4 * kSfBlockBytes);
+        };
+        for (int kp = 0; kp < kL2PrefetchKTiles && kp < ktiles; ++kp) prefetch_ktile(kp);
         for (int kt = 0; kt < ktiles; ++kt) {
+          if (kt + kL2PrefetchKTiles < ktiles) prefetch_ktile(kt + kL2PrefetchKTiles);
           if (!wait_phase(&empty_bar[stage], phase ^ 1u, abort_flag, p.error_bits,
                           kDevErrProducerTimeout)) {
             ok = false;
@@ -353,25 +377,40 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
       ptx::tcgen05_fence_after_sync();
       const int row0 = mt * kBlockM + 32 * quarter;
+      bool released = false;
       if (row0 < gd.m) {
         const uint32_t t_acc =
             tmem_base + (static_cast<uint32_t>(32 * quarter) << 16) + acc * MMA_N;
 #pragma unroll 1
         for (int box = 0; box < Cfg::kOutN / 64; ++box) {
           const uint32_t buf = my_bufs_s + (stores & 1u) * Cfg::kEpiBufBytes;
-          // The store that last read this buffer (two boxes ago) must be done with it.
+          // 64 output columns: issue every TMEM load of the box, then wait once.
+          uint32_t v0[32], v1[32];
+          ptx::tmem_ld_32x32b_x32(t_acc + box * 64, v0);
+          ptx::tmem_ld_32x32b_x32(t_acc + box * 64 + 32, v1);
+          uint32_t u0[32], u1[32];
+          if (GATED) {
+            ptx::tmem_ld_32x32b_x32(t_acc + 128 + box * 64, u0);
+            ptx::tmem_ld_32x32b_x32(t_acc + 128 + box * 64 + 32, u1);
+          }
+          ptx::tmem_ld_wait();
+          if (box == Cfg::kOutN / 64 - 1) {
+            // Every TMEM read of this tile has landed: hand the accumulator back to the
+            // MMA issuer before converting and storing the last box.
+            ptx::tcgen05_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&acce_bar[acc]);
+            released = true;
+          }
+          // The store that last read this staging buffer (two boxes ago) must be done with it.
           if (lane == 0) ptx::bulk_wait_group_read<1>();
           __syncwarp();
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
-            const int col = box * 64 + half * 32;
-            uint32_t v[32];
-            ptx::tmem_ld_32x32b_x32(t_acc + col, v);
+            const uint32_t* v = half ? v1 : v0;
             uint32_t packed[16];
             if (GATED) {
-              uint32_t u[32];
-              ptx::tmem_ld_32x32b_x32(t_acc + 128 + col, u);
-              ptx::tmem_ld_wait();
+              const uint32_t* u = half ? u1 : u0;
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
                 float o[2];
@@ -387,7 +426,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                 packed[i] = *reinterpret_cast<uint32_t*>(&hv);
               }
             } else {
-              ptx::tmem_ld_wait();
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
                 __half2 hv = __floats2half2_rn(__uint_as_float(v[2 * i]) * gd.alpha,
@@ -415,9 +453,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           ++stores;
         }
       }
-      ptx::tcgen05_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&acce_bar[acc]);
+      if (!released) {
+        ptx::tcgen05_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&acce_bar[acc]);
+      }
       if (++acc == Cfg::kAccStages) {
         acc = 0;
         acc_phase ^= 1u;

@@ -121,6 +121,22 @@ __device__ __forceinline__ void bulk_wait_group() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Warm L2 with one box of a 2-D tensor map (no shared-memory destination, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* desc, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(desc)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
+// Warm L2 with a contiguous range (16-byte aligned, bytes % 16 == 0).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                   reinterpret_cast<uint64_t>(gmem_src)),
+               "r"(bytes)
+               : "memory");
+}
+
 // Contiguous global -> shared copy; both addresses 16-byte aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes,
                                           uint64_t* bar) {

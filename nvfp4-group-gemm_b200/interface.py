@@ -46,13 +46,14 @@ _FP4_DTYPES = tuple(
 # Workspace and descriptor-table cache (one per device and stream)
 # ----------------------------------------------------------------------------
 class _Workspace:
-    __slots__ = ("buf", "nbytes", "last_table", "last_flags")
+    __slots__ = ("buf", "nbytes", "last_table", "last_flags", "last_sig")
 
     def __init__(self):
         self.buf = None
         self.nbytes = 0
         self.last_table = None
         self.last_flags = None
+        self.last_sig = None
 
 
 _ws_lock = threading.Lock()
@@ -71,6 +72,7 @@ def _workspace_for(device: torch.device, stream: torch.cuda.Stream, nbytes: int)
         ws.buf = torch.zeros(size, dtype=torch.uint8, device=device)
         ws.nbytes = size
         ws.last_table = None
+        ws.last_sig = None
     return ws
 
 
@@ -140,6 +142,30 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
     if not (len(a) == len(b) == len(sfa) == len(sfb) == len(c) == G):
         raise ValueError("a, b, sfa, sfb, c and problem_sizes must have one entry per group")
     gated = b2 is not None
+    # Fast path: the same tensor objects at the same addresses, sizes, scales and tile
+    # choice as the previous call on this stream were validated then, and the workspace
+    # still holds their descriptors -> launch directly.
+    sig = None
+    if reuse_descriptors and G > 0 and isinstance(c[0], torch.Tensor) and c[0].is_cuda:
+        lists = (a, b, sfa, sfb, c) + ((b2, sfb2) if gated else ())
+        try:
+            sig = (tuple(id(t) for lst in lists for t in lst),
+                   tuple(t.data_ptr() for lst in lists for t in lst),
+                   tuple(tuple(ps) for ps in problem_sizes),
+                   None if alpha is None else tuple(alpha),
+                   None if alpha2 is None else tuple(alpha2), tile_n, gated)
+        except (AttributeError, TypeError):
+            sig = None
+        if sig is not None:
+            device = c[0].device
+            s = stream or torch.cuda.current_stream(device)
+            ws = _workspaces.get((device.index, s.cuda_stream))
+            if ws is not None and ws.last_sig == sig and ws.last_table is not None:
+                with torch.cuda.device(device):
+                    _native.grouped_gemm_raw(ws.last_table,
+                                             ws.last_flags | _native.FLAG_REUSE_DESCRIPTORS,
+                                             ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
+                return list(c)
     if gated and (sfb2 is None or len(b2) != G or len(sfb2) != G):
         raise ValueError("gated launches need b2 and sfb2 for every group")
     if G == 0:
@@ -215,6 +241,7 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
         _native.grouped_gemm_raw(table, call_flags, ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
     ws.last_table = table
     ws.last_flags = flags
+    ws.last_sig = sig
     return list(c)
 
 
