@@ -52,14 +52,19 @@ struct GemmConfig {
   static constexpr int kSfbBlocks = MMA_N / 128;
   static constexpr int kSfbBytes = kSfbBlocks * 4 * kSfBlockBytes;
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
-  static constexpr int kAccStages = (MMA_N == 128) ? 2 : 1;
-  // TMEM columns: accumulators first, then one scale-factor slot per smem stage.
+  // Two accumulator stages. At MMA_N = 256 they overlap by one 64-column epilogue box
+  // (stage 1 starts at column 192): the epilogue drains that shared box first and
+  // releases it, so the next tile's MMAs start while the other three boxes drain.
+  static constexpr bool kOverlapAcc = (MMA_N == 256);
+  static constexpr int kAccStages = 2;
+  static constexpr int kAccStride = kOverlapAcc ? MMA_N - 64 : MMA_N;
+  // Scale factors: one TMEM slot above the accumulators. tcgen05.cp and tcgen05.mma
+  // issued by one thread execute in order, so a slot is reused safely every k-tile.
   static constexpr int kSfaCols = 4 * 4;              // 4 MMAs x 4 columns (128 lanes x 4 B)
   static constexpr int kSfbColsPerMma = MMA_N / 32;   // one column per 32 rows of B
   static constexpr int kSfbCols = 4 * kSfbColsPerMma;
-  static constexpr int kSfColsPerStage = kSfaCols + kSfbCols;
-  static constexpr int kSfColBase = kAccStages * MMA_N;
-  static_assert(kSfColBase + STAGES * kSfColsPerStage <= kTmemCols, "TMEM over-subscribed");
+  static constexpr int kSfColBase = kAccStride + MMA_N;
+  static_assert(kSfColBase + kSfaCols + kSfbCols <= kTmemCols, "TMEM over-subscribed");
   static constexpr int kEpiBufBytes = 32 * 128;  // 32 rows x 64 fp16, one TMA store box
   static constexpr int kEpiBufsPerWarp = 2;
   static constexpr int kEpiBytes = kEpilogueWarps * kEpiBufsPerWarp * kEpiBufBytes;
@@ -279,19 +284,25 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (ptx::elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
+      // Parity to wait for on acce_bar[s] before tile t (stage s = t & 1) may write its
+      // accumulator. Overlapped stages: tile t needs tile t-1's shared box drained
+      // (arrived on acce_bar[t & 1] by the epilogue of tile t-1); the first tile passes.
+      // Plain double buffer: tile t needs tile t-2 drained; the first two tiles pass.
+      uint32_t acc_parity = Cfg::kOverlapAcc ? 0x1u : 0x3u;  // bit s: parity for stage s
+      uint32_t local = 0;
       int g = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x) {
+      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x, ++local) {
         g = advance_group(groups, p.num_groups, g, tile);
         const int ktiles = groups[g].k / kBlockK;
-        if (!wait_phase(&acce_bar[acc], acc_phase ^ 1u, abort_flag, p.error_bits,
+        const int acc = static_cast<int>(local & 1u);
+        if (!wait_phase(&acce_bar[acc], (acc_parity >> acc) & 1u, abort_flag, p.error_bits,
                         kDevErrAccTimeout)) {
           break;
         }
+        acc_parity ^= 1u << acc;
         ptx::tcgen05_fence_after_sync();
-        const uint32_t d_tmem = tmem_base + acc * MMA_N;
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
         for (int kt = 0; kt < ktiles; ++kt) {
           if (!wait_phase(&full_bar[stage], phase, abort_flag, p.error_bits, kDevErrMmaTimeout)) {
             ok = false;
@@ -302,7 +313,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const uint32_t sB = sA + Cfg::kABytes;
           const uint32_t sSFA = sB + Cfg::kBBytes;
           const uint32_t sSFB = sSFA + Cfg::kSfaBytes;
-          const uint32_t sfa_t = tmem_base + Cfg::kSfColBase + stage * Cfg::kSfColsPerStage;
+          const uint32_t sfa_t = tmem_base + Cfg::kSfColBase;
           const uint32_t sfb_t = sfa_t + Cfg::kSfaCols;
           // Scale factors: each 512-byte block (128 rows x 4 scales) becomes 4 TMEM
           // columns, replicated to all four lane quarters.
@@ -335,10 +346,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         if (!ok) break;
         ptx::tcgen05_commit(&accf_bar[acc]);  // accumulator complete -> epilogue
-        if (++acc == Cfg::kAccStages) {
-          acc = 0;
-          acc_phase ^= 1u;
-        }
       }
       // Wait for every MMA / TMEM copy this thread issued before TMEM is freed.
       ptx::tcgen05_commit(drain_bar);
@@ -356,11 +363,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const int quarter = warp & 3;           // TMEM lane quarter this warp may access
     uint8_t* my_bufs = epi_base + ew * Cfg::kEpiBufsPerWarp * Cfg::kEpiBufBytes;
     const uint32_t my_bufs_s = ptx::smem_u32(my_bufs);
-    int acc = 0;
-    uint32_t acc_phase = 0;
+    uint32_t full_parity = 0;  // bit s: parity to wait for on accf_bar[s]
     uint32_t stores = 0;
+    uint32_t local = 0;
     int g = 0, acquired_g = -1;
-    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
+    constexpr int kBoxes = Cfg::kOutN / 64;
+    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++local) {
       g = advance_group(groups, p.num_groups, g, tile);
       const GroupDev gd = groups[g];
       const TmaDesc* map_c = p.maps + static_cast<size_t>(g) * kMapsPerGroup + kMapC;
@@ -368,21 +376,29 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if (lane == 0) ptx::tensormap_fence_acquire(map_c);
         acquired_g = g;
       }
-      const int local = tile - gd.tile_start;
-      const int mt = local % gd.tiles_m;
-      const int nt = local / gd.tiles_m;
-      if (!warp_wait_phase(&accf_bar[acc], acc_phase, abort_flag, p.error_bits,
+      const int tl = tile - gd.tile_start;
+      const int mt = tl % gd.tiles_m;
+      const int nt = tl / gd.tiles_m;
+      const int acc = static_cast<int>(local & 1u);
+      if (!warp_wait_phase(&accf_bar[acc], (full_parity >> acc) & 1u, abort_flag, p.error_bits,
                            kDevErrEpilogueTimeout, lane)) {
         break;
       }
+      full_parity ^= 1u << acc;
       ptx::tcgen05_fence_after_sync();
+      // Which barrier hands this accumulator (or its shared box) back to the MMA issuer.
+      uint64_t* release_bar = Cfg::kOverlapAcc ? &acce_bar[acc ^ 1] : &acce_bar[acc];
+      // With overlapped stages the box holding TMEM columns [192, 256) goes first:
+      // stage 0 -> its last box (up-projection half of box 1 when gated), stage 1 -> box 0.
+      const int first_box = (Cfg::kOverlapAcc && acc == 0) ? kBoxes - 1 : 0;
       const int row0 = mt * kBlockM + 32 * quarter;
       bool released = false;
       if (row0 < gd.m) {
-        const uint32_t t_acc =
-            tmem_base + (static_cast<uint32_t>(32 * quarter) << 16) + acc * MMA_N;
+        const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(32 * quarter) << 16) +
+                               acc * Cfg::kAccStride;
 #pragma unroll 1
-        for (int box = 0; box < Cfg::kOutN / 64; ++box) {
+        for (int bi = 0; bi < kBoxes; ++bi) {
+          const int box = (first_box + bi) % kBoxes;
           const uint32_t buf = my_bufs_s + (stores & 1u) * Cfg::kEpiBufBytes;
           // 64 output columns: issue every TMEM load of the box, then wait once.
           uint32_t v0[32], v1[32];
@@ -394,12 +410,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             ptx::tmem_ld_32x32b_x32(t_acc + 128 + box * 64 + 32, u1);
           }
           ptx::tmem_ld_wait();
-          if (box == Cfg::kOutN / 64 - 1) {
-            // Every TMEM read of this tile has landed: hand the accumulator back to the
-            // MMA issuer before converting and storing the last box.
+          if (Cfg::kOverlapAcc ? bi == 0 : bi == kBoxes - 1) {
             ptx::tcgen05_fence_before_sync();
             __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(&acce_bar[acc]);
+            if (lane == 0) ptx::mbar_arrive(release_bar);
             released = true;
           }
           // The store that last read this staging buffer (two boxes ago) must be done with it.
@@ -416,11 +430,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                 float o[2];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
+                  // Gate and up are rounded to fp16 first, as the reference's two-GEMM
+                  // path does; SiLU and the product are fp32.
                   const float gte = __half2float(
                       __float2half_rn(__uint_as_float(v[2 * i + h]) * gd.alpha));
                   const float up = __half2float(
                       __float2half_rn(__uint_as_float(u[2 * i + h]) * gd.alpha2));
-                  o[h] = (gte / (1.0f + expf(-gte))) * up;
+                  o[h] = __fdividef(gte, 1.0f + __expf(-gte)) * up;
                 }
                 __half2 hv = __floats2half2_rn(o[0], o[1]);
                 packed[i] = *reinterpret_cast<uint32_t*>(&hv);
@@ -456,11 +472,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (!released) {
         ptx::tcgen05_fence_before_sync();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&acce_bar[acc]);
-      }
-      if (++acc == Cfg::kAccStages) {
-        acc = 0;
-        acc_phase ^= 1u;
+        if (lane == 0) ptx::mbar_arrive(release_bar);
       }
     }
     if (lane == 0) ptx::bulk_wait_group<0>();
