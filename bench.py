@@ -48,6 +48,7 @@ def parse_args():
     ap.add_argument("--config", default="cfg2")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tile-n", type=int, default=None)
+    ap.add_argument("--cta", default=None, choices=[None, "pair", "single"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
@@ -210,7 +211,7 @@ def main():
     def step():
         pkg.grouped_gemm(prob.a, prob.b, prob.sfa, prob.sfb, prob.c, sizes, alpha=prob.alpha,
                          b2=prob.b2, sfb2=prob.sfb2, alpha2=prob.alpha2, tile_n=args.tile_n,
-                         stream=stream)
+                         stream=stream, cta=args.cta)
 
     def barrier():
         if world > 1:
@@ -261,7 +262,8 @@ def main():
     def e2e_step():
         for h, d in zip(host_in, dev_in):
             d.copy_(h, non_blocking=True)
-        pkg.custom_kernel(data, global_scales=scales, tile_n=args.tile_n, stream=stream)
+        pkg.custom_kernel(data, global_scales=scales, tile_n=args.tile_n, stream=stream,
+                          cta=args.cta)
         for h, c in zip(host_out, prob.c):
             h.copy_(c, non_blocking=True)
 

@@ -52,6 +52,10 @@ typedef enum nvfp4_status {
 #define NVFP4_FLAG_REUSE_DESCRIPTORS 0x8u /* workspace already holds this exact group table
                                              (same pointers, sizes, scales, flags) from the
                                              previous call on the same stream: skip rebuilding */
+#define NVFP4_FLAG_CTA_PAIR 0x10u   /* force 256-row tiles on CTA pairs (tcgen05 cta_group::2) */
+#define NVFP4_FLAG_SINGLE_CTA 0x20u /* force 128-row tiles on single CTAs.
+                                       Default: CTA pairs when the non-empty groups average
+                                       at least 192 rows, single CTAs otherwise */
 
 /*
  * One GEMM of the group. All matrices are row-major with K innermost ("K-major"),
@@ -85,7 +89,7 @@ typedef struct nvfp4_group {
 
 /*
  * Device workspace bytes needed for `num_groups` groups (group records, tensor
- * maps and a device error word). The workspace is owned by the caller, must be
+ * maps and a device error word): 256 + 1088 * num_groups, rounded up to 128. The workspace is owned by the caller, must be
  * 256-byte aligned, must not be shared by calls that may run concurrently, and
  * may be reused by consecutive calls on one stream.
  */
@@ -130,7 +134,7 @@ NVFP4_API const char* nvfp4_last_error_detail(void);
  * hands them their input and output buffers, and latency-critical paths that
  * cannot afford cudaMalloc's implicit device synchronisation. Instead of a caller-provided
  * workspace it uses a scratch array compiled into the library
- * (nvfp4_workspace_size(NVFP4_NOALLOC_MAX_GROUPS) bytes, about 288 KiB, held on
+ * (nvfp4_workspace_size(NVFP4_NOALLOC_MAX_GROUPS) bytes, about 544 KiB, held on
  * every GPU that loads the library until the process exits). It calls no
  * cudaMalloc/cudaFree and no allocating library routine.
  *

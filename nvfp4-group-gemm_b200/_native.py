@@ -32,6 +32,8 @@ FLAG_GATED = 0x1
 FLAG_TILE_N128 = 0x2
 FLAG_TILE_N256 = 0x4
 FLAG_REUSE_DESCRIPTORS = 0x8
+FLAG_CTA_PAIR = 0x10
+FLAG_SINGLE_CTA = 0x20
 
 # Every symbol the public header declares; the library must export all of them.
 EXPORTED_SYMBOLS = (

@@ -1,0 +1,438 @@
+// CTA-pair (cta_group::2) variant of the persistent NVFP4 grouped GEMM.
+//
+// A cluster of two CTAs on two SMs computes one 256 x 256 tile per step (gated:
+// 256 rows x 128 output columns, the MMA's 256 B rows being 128 gate + 128 up rows):
+//
+//   CTA r (r = 0, 1) loads the 128 A rows [256 mt + 128 r, +128) and one half of the
+//   256 B rows, plus the scale factors of its A rows and of all 256 B rows; the even
+//   CTA issues tcgen05.mma.cta_group::2 (M = 256, N = 256), which reads A and B from
+//   both CTAs' shared memory and writes each CTA's 128 accumulator rows into that
+//   CTA's TMEM. Per SM this halves the B bytes per MMA compared with a 128 x 256 tile
+//   on one SM, which is what lets the mainloop keep the tensor pipe fed.
+//
+// Synchronisation between the two CTAs (no multicast anywhere):
+//   full[s]   even CTA; one arrive.expect_tx (both CTAs' bytes) by its producer, and
+//             every load of both CTAs completes its bytes there (cta_group::2 TMA)
+//   empty[s]  each CTA; the even CTA's MMA commit frees its own, and its producer
+//             forwards each release to the odd CTA with a remote arrive
+//   accf[a]   each CTA; MMA commit on the even CTA, forwarded to the odd CTA by the
+//             even CTA's epilogue
+//   acce[a]   even CTA; the 8 epilogue warps of both CTAs release accumulators there
+// All waits are bounded (same timeout/abort scheme as the single-CTA kernel); a
+// final cluster barrier keeps both CTAs alive until every cross-CTA access is done.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "grouped_gemm_kernel.cuh"
+#include "nvfp4_types.cuh"
+#include "sm100_ptx.cuh"
+
+namespace nvfp4 {
+
+template <bool GATED, int STAGES>
+struct PairConfig {
+  static constexpr int kMmaN = 256;
+  static constexpr int kOutN = GATED ? 128 : 256;  // output columns per tile
+  static constexpr int kABytes = 128 * kRowBytesPerStage;
+  static constexpr int kBBytes = 128 * kRowBytesPerStage;  // this CTA's half of B
+  static constexpr int kSfaBytes = 4 * kSfBlockBytes;       // this CTA's 128 A rows
+  static constexpr int kSfbBytes = 2 * 4 * kSfBlockBytes;   // all 256 B rows
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  static constexpr uint32_t kPairTxBytes = 2u * kStageBytes;  // both CTAs, every stage
+  // Overlapped accumulator stages (stride 192 columns) and one scale-factor slot.
+  static constexpr int kAccStride = kMmaN - 64;
+  static constexpr int kSfColBase = kAccStride + kMmaN;
+  static constexpr int kSfaCols = 16;
+  static constexpr int kSfbColsPerMma = kMmaN / 32;
+  static_assert(kSfColBase + kSfaCols + 4 * kSfbColsPerMma <= kTmemCols, "TMEM over-subscribed");
+  static constexpr int kEpiBufBytes = 32 * 128;
+  static constexpr int kEpiBufsPerWarp = 2;
+  static constexpr int kEpiBytes = kEpilogueWarps * kEpiBufsPerWarp * kEpiBufBytes;
+  static constexpr int kBarrierBytes = 8 * (2 * STAGES + 2 * 2 + 1) + 16;
+  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kEpiBytes + kBarrierBytes;
+  static_assert(kSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
+  static constexpr uint32_t kIdesc = ptx::make_idesc_mxf4nvf4(256, kMmaN);
+  static constexpr uint32_t kEpilogueArrivals = 2 * kEpilogueWarps;
+};
+
+// Bounded wait with cluster-scope acquire (barriers that the other CTA arrives on).
+__device__ __forceinline__ bool wait_phase_cluster(uint64_t* bar, uint32_t parity,
+                                                   volatile uint32_t* abort_flag,
+                                                   uint32_t* error_bits, uint32_t reason) {
+  if (ptx::mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = ptx::globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (ptx::mbar_try_wait_cluster(bar, parity)) return true;
+    if ((++spins & 31u) == 0) {
+      if (*abort_flag) return false;
+      if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        *abort_flag = 1u;
+        atomicOr(error_bits, reason);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ bool warp_wait_phase_cluster(uint64_t* bar, uint32_t parity,
+                                                        volatile uint32_t* abort_flag,
+                                                        uint32_t* error_bits, uint32_t reason,
+                                                        int lane) {
+  int ok = 1;
+  if (lane == 0) ok = wait_phase_cluster(bar, parity, abort_flag, error_bits, reason) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) {
+    for (uint32_t i = 0; i < (1u << 20) && !ptx::mbar_try_wait_cluster(bar, parity); ++i) {
+    }
+  }
+  return ok != 0;
+}
+
+template <bool GATED, int STAGES>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    nvfp4_grouped_gemm_pair_kernel(const __grid_constant__ GemmParams p) {
+  using Cfg = PairConfig<GATED, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* stage_base = smem;
+  uint8_t* epi_base = smem + STAGES * Cfg::kStageBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_base + Cfg::kEpiBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* accf_bar = empty_bar + STAGES;
+  uint64_t* acce_bar = accf_bar + 2;
+  uint64_t* drain_bar = acce_bar + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile uint32_t* abort_flag = tmem_holder + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = ptx::cluster_ctarank();  // 0: issues the MMAs
+  const bool leader = rank == 0;
+  const int cluster = static_cast<int>(blockIdx.x >> 1);
+  const int num_clusters = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(&full_bar[s], 1);
+      ptx::mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&accf_bar[a], 1);
+      ptx::mbar_init(&acce_bar[a], Cfg::kEpilogueArrivals);
+    }
+    ptx::mbar_init(drain_bar, 1);
+    *abort_flag = 0u;
+    ptx::fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc_pair(tmem_holder, kTmemCols);
+    ptx::tmem_relinquish_alloc_permit_pair();
+  }
+  // Barriers of both CTAs initialised and TMEM allocated in both before any
+  // cross-CTA arrive, load completion or MMA.
+  ptx::tcgen05_fence_before_sync();
+  ptx::cluster_sync_all();
+  ptx::tcgen05_fence_after_sync();
+  const uint32_t tmem_base = *tmem_holder;
+  const GroupDev* __restrict__ groups = p.groups;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (ptx::elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      int g = 0, acquired_g = -1;
+      bool ok = true;
+      for (int tile = cluster; ok && tile < p.total_tiles; tile += num_clusters) {
+        g = advance_group(groups, p.num_groups, g, tile);
+        const GroupDev gd = groups[g];
+        const TmaDesc* maps = p.maps + static_cast<size_t>(g) * kMapsPerGroup;
+        if (g != acquired_g) {
+          ptx::tensormap_fence_acquire(&maps[kMapA]);
+          ptx::tensormap_fence_acquire(&maps[kMapB]);
+          ptx::tensormap_fence_acquire(&maps[kMapSfa]);
+          ptx::tensormap_fence_acquire(&maps[kMapSfb]);
+          if (GATED) {
+            ptx::tensormap_fence_acquire(&maps[kMapB2]);
+            ptx::tensormap_fence_acquire(&maps[kMapSfb2]);
+          }
+          acquired_g = g;
+        }
+        const int local = tile - gd.tile_start;
+        const int mt = local % gd.tiles_m;
+        const int nt = local / gd.tiles_m;
+        const int ktiles = gd.k / kBlockK;
+        const int rest_k = gd.k / 64;
+        const int row_a = mt * 256 + 128 * static_cast<int>(rank);
+        // This CTA's half of the MMA's B rows.
+        const TmaDesc* map_b = (GATED && rank == 1) ? &maps[kMapB2] : &maps[kMapB];
+        const int row_b = GATED ? nt * 128 : nt * 256 + 128 * static_cast<int>(rank);
+        // Scale blocks (in 8-byte elements of the 1-D maps; a block out of range reads as 0).
+        const int sfa_x0 = (2 * mt + static_cast<int>(rank)) * rest_k * 64;
+        const TmaDesc* map_sfb1 = GATED ? &maps[kMapSfb2] : &maps[kMapSfb];
+        const int sfb0_x0 = (GATED ? nt : 2 * nt) * rest_k * 64;
+        const int sfb1_x0 = (GATED ? nt : 2 * nt + 1) * rest_k * 64;
+        auto prefetch_ktile = [&](int kp) {
+          ptx::tma_prefetch_l2_2d(&maps[kMapA], kp * kRowBytesPerStage, row_a);
+          ptx::tma_prefetch_l2_2d(map_b, kp * kRowBytesPerStage, row_b);
+          ptx::tma_prefetch_l2_1d(&maps[kMapSfa], sfa_x0 + kp * 256);
+          ptx::tma_prefetch_l2_1d(&maps[kMapSfb], sfb0_x0 + kp * 256);
+          ptx::tma_prefetch_l2_1d(map_sfb1, sfb1_x0 + kp * 256);
+        };
+        for (int kp = 0; kp < kL2PrefetchKTiles && kp < ktiles; ++kp) prefetch_ktile(kp);
+        for (int kt = 0; kt < ktiles; ++kt) {
+          if (kt + kL2PrefetchKTiles < ktiles) prefetch_ktile(kt + kL2PrefetchKTiles);
+          if (!wait_phase_cluster(&empty_bar[stage], phase ^ 1u, abort_flag, p.error_bits,
+                                  kDevErrProducerTimeout)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_leader = ptx::mapa_shared(ptx::smem_u32(&full_bar[stage]), 0);
+          if (leader) {
+            // The MMAs that read this stage have finished: let the odd CTA refill its
+            // half too (from the second use of the stage on; the first use is free).
+            if (issued >= static_cast<uint32_t>(STAGES))
+              ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&empty_bar[stage]), 1));
+            ptx::mbar_arrive_expect_tx(&full_bar[stage], Cfg::kPairTxBytes);
+          }
+          uint8_t* sA = stage_base + stage * Cfg::kStageBytes;
+          uint8_t* sB = sA + Cfg::kABytes;
+          uint8_t* sSFA = sB + Cfg::kBBytes;
+          uint8_t* sSFB = sSFA + Cfg::kSfaBytes;
+          const int kx = kt * kRowBytesPerStage;
+          ptx::tma_load_2d_pair(sA, &maps[kMapA], full_leader, kx, row_a);
+          ptx::tma_load_2d_pair(sB, map_b, full_leader, kx, row_b);
+          ptx::tma_load_1d_pair(sSFA, &maps[kMapSfa], full_leader, sfa_x0 + kt * 256);
+          ptx::tma_load_1d_pair(sSFB, &maps[kMapSfb], full_leader, sfb0_x0 + kt * 256);
+          ptx::tma_load_1d_pair(sSFB + 4 * kSfBlockBytes, map_sfb1, full_leader,
+                                sfb1_x0 + kt * 256);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (leader) {
+        // Every fill of both CTAs completes on these barriers: wait for the most recent
+        // fill of each stage before the cluster may exit.
+        const uint32_t recent = issued < static_cast<uint32_t>(STAGES) ? issued : STAGES;
+        for (uint32_t i = 0; i < recent; ++i) {
+          const uint32_t n = issued - 1 - i;
+          const uint32_t s = n % STAGES;
+          const uint32_t ph = (n / STAGES) & 1u;
+          const uint64_t t0 = ptx::globaltimer_ns();
+          while (!ptx::mbar_try_wait_cluster(&full_bar[s], ph)) {
+            if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
+              atomicOr(p.error_bits, kDevErrDrainTimeout);
+              break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (even CTA)
+    if (leader && ptx::elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t acc_parity = 0x1u;  // overlapped stages: only the first tile passes freely
+      uint32_t local = 0;
+      int g = 0;
+      bool ok = true;
+      for (int tile = cluster; ok && tile < p.total_tiles; tile += num_clusters, ++local) {
+        g = advance_group(groups, p.num_groups, g, tile);
+        const int ktiles = groups[g].k / kBlockK;
+        const int acc = static_cast<int>(local & 1u);
+        if (!wait_phase_cluster(&acce_bar[acc], (acc_parity >> acc) & 1u, abort_flag,
+                                p.error_bits, kDevErrAccTimeout)) {
+          break;
+        }
+        acc_parity ^= 1u << acc;
+        ptx::tcgen05_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
+        for (int kt = 0; kt < ktiles; ++kt) {
+          if (!wait_phase_cluster(&full_bar[stage], phase, abort_flag, p.error_bits,
+                                  kDevErrMmaTimeout)) {
+            ok = false;
+            break;
+          }
+          ptx::tcgen05_fence_after_sync();
+          const uint32_t sA = ptx::smem_u32(stage_base + stage * Cfg::kStageBytes);
+          const uint32_t sB = sA + Cfg::kABytes;
+          const uint32_t sSFA = sB + Cfg::kBBytes;
+          const uint32_t sSFB = sSFA + Cfg::kSfaBytes;
+          const uint32_t sfa_t = tmem_base + Cfg::kSfColBase;
+          const uint32_t sfb_t = sfa_t + Cfg::kSfaCols;
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb)
+            ptx::tmem_cp_32x128b_warpx4_pair(sfa_t + 4 * kb,
+                                             ptx::make_sf_block_desc(sSFA + kb * kSfBlockBytes));
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb)
+              ptx::tmem_cp_32x128b_warpx4_pair(
+                  sfb_t + Cfg::kSfbColsPerMma * kb + 4 * j,
+                  ptx::make_sf_block_desc(sSFB + j * 4 * kSfBlockBytes + kb * kSfBlockBytes));
+          }
+          const uint64_t a_desc = ptx::make_sw128_kmajor_desc(sA);
+          const uint64_t b_desc = ptx::make_sw128_kmajor_desc(sB);
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb) {
+            ptx::mma_mxf4nvf4_pair(d_tmem, a_desc + 2 * kb, b_desc + 2 * kb, Cfg::kIdesc,
+                                   sfa_t + 4 * kb, sfb_t + Cfg::kSfbColsPerMma * kb,
+                                   (kt | kb) != 0 ? 1u : 0u);
+          }
+          ptx::tcgen05_commit_pair(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        ptx::tcgen05_commit_pair(&accf_bar[acc]);
+      }
+      ptx::tcgen05_commit_pair(drain_bar);
+      const uint64_t t0 = ptx::globaltimer_ns();
+      while (!ptx::mbar_try_wait(drain_bar, 0)) {
+        if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
+          atomicOr(p.error_bits, kDevErrDrainTimeout);
+          break;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    const int ew = warp - kEpilogueWarp0;
+    const int quarter = warp & 3;
+    uint8_t* my_bufs = epi_base + ew * Cfg::kEpiBufsPerWarp * Cfg::kEpiBufBytes;
+    const uint32_t my_bufs_s = ptx::smem_u32(my_bufs);
+    uint32_t full_parity = 0;
+    uint32_t stores = 0;
+    uint32_t local = 0;
+    int g = 0, acquired_g = -1;
+    constexpr int kBoxes = Cfg::kOutN / 64;
+    for (int tile = cluster; tile < p.total_tiles; tile += num_clusters, ++local) {
+      g = advance_group(groups, p.num_groups, g, tile);
+      const GroupDev gd = groups[g];
+      const TmaDesc* map_c = p.maps + static_cast<size_t>(g) * kMapsPerGroup + kMapC;
+      if (g != acquired_g) {
+        if (lane == 0) ptx::tensormap_fence_acquire(map_c);
+        acquired_g = g;
+      }
+      const int tl = tile - gd.tile_start;
+      const int mt = tl % gd.tiles_m;
+      const int nt = tl / gd.tiles_m;
+      const int acc = static_cast<int>(local & 1u);
+      if (!warp_wait_phase_cluster(&accf_bar[acc], (full_parity >> acc) & 1u, abort_flag,
+                                   p.error_bits, kDevErrEpilogueTimeout, lane)) {
+        break;
+      }
+      full_parity ^= 1u << acc;
+      if (leader && warp == kEpilogueWarp0 && lane == 0) {
+        // Accumulators of both CTAs are complete: tell the odd CTA's epilogue.
+        ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&accf_bar[acc]), 1));
+      }
+      ptx::tcgen05_fence_after_sync();
+      const uint32_t release_bar = ptx::mapa_shared(ptx::smem_u32(&acce_bar[acc ^ 1]), 0);
+      const int first_box = (acc == 0) ? kBoxes - 1 : 0;
+      const int row0 = mt * 256 + 128 * static_cast<int>(rank) + 32 * quarter;
+      bool released = false;
+      if (row0 < gd.m) {
+        const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(32 * quarter) << 16) +
+                               acc * Cfg::kAccStride;
+#pragma unroll 1
+        for (int bi = 0; bi < kBoxes; ++bi) {
+          const int box = (first_box + bi) % kBoxes;
+          const uint32_t buf = my_bufs_s + (stores & 1u) * Cfg::kEpiBufBytes;
+          uint32_t v0[32], v1[32];
+          ptx::tmem_ld_32x32b_x32(t_acc + box * 64, v0);
+          ptx::tmem_ld_32x32b_x32(t_acc + box * 64 + 32, v1);
+          uint32_t u0[32], u1[32];
+          if (GATED) {
+            ptx::tmem_ld_32x32b_x32(t_acc + 128 + box * 64, u0);
+            ptx::tmem_ld_32x32b_x32(t_acc + 128 + box * 64 + 32, u1);
+          }
+          ptx::tmem_ld_wait();
+          if (bi == 0) {
+            // The box shared by both accumulator stages is drained: the next tile's
+            // MMAs may start.
+            ptx::tcgen05_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive_cluster(release_bar);
+            released = true;
+          }
+          if (lane == 0) ptx::bulk_wait_group_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const uint32_t* v = half ? v1 : v0;
+            uint32_t packed[16];
+            if (GATED) {
+              const uint32_t* u = half ? u1 : u0;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                float o[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const float gte = __half2float(
+                      __float2half_rn(__uint_as_float(v[2 * i + h]) * gd.alpha));
+                  const float up = __half2float(
+                      __float2half_rn(__uint_as_float(u[2 * i + h]) * gd.alpha2));
+                  o[h] = __fdividef(gte, 1.0f + __expf(-gte)) * up;
+                }
+                __half2 hv = __floats2half2_rn(o[0], o[1]);
+                packed[i] = *reinterpret_cast<uint32_t*>(&hv);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                __half2 hv = __floats2half2_rn(__uint_as_float(v[2 * i]) * gd.alpha,
+                                               __uint_as_float(v[2 * i + 1]) * gd.alpha);
+                packed[i] = *reinterpret_cast<uint32_t*>(&hv);
+              }
+            }
+            const uint32_t row_addr = buf + lane * 128;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint32_t chunk = static_cast<uint32_t>(half * 4 + c) ^ (lane & 7);
+              ptx::st_shared_v4(row_addr + chunk * 16, packed[4 * c], packed[4 * c + 1],
+                                packed[4 * c + 2], packed[4 * c + 3]);
+            }
+          }
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            ptx::tma_store_2d(map_c, my_bufs + (stores & 1u) * Cfg::kEpiBufBytes,
+                              nt * Cfg::kOutN + box * 64, row0);
+            ptx::bulk_commit_group();
+          }
+          ++stores;
+        }
+      }
+      if (!released) {
+        ptx::tcgen05_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive_cluster(release_bar);
+      }
+    }
+    if (lane == 0) ptx::bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  // Keep both CTAs resident until every remote arrive, load completion and MMA that
+  // touches the other CTA is done, then free the pair's TMEM.
+  ptx::tcgen05_fence_before_sync();
+  ptx::cluster_sync_all();
+  if (warp == 1) {
+    ptx::tcgen05_fence_after_sync();
+    ptx::tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace nvfp4

@@ -16,6 +16,7 @@
 
 #include "../../include/nvfp4_group_gemm.h"
 #include "grouped_gemm_kernel.cuh"
+#include "grouped_gemm_pair_kernel.cuh"
 #include "nvfp4_types.cuh"
 #include "sm100_ptx.cuh"
 
@@ -26,8 +27,8 @@ namespace nvfp4 {
 // ============================================================================
 // Copies host-encoded group records and tensor maps (carried in the kernel's
 // parameter block) into the workspace, then releases the maps to the
-// tensor-map proxy. One warp per group: each lane moves 16 bytes of the 512
-// bytes of maps; lane 0 also writes the record.
+// tensor-map proxy. One warp per group moves the group's 1 KiB of maps in 16-byte
+// pieces; lane 0 also writes the record.
 __global__ void __launch_bounds__(32) nvfp4_upload_descriptors_kernel(
     const __grid_constant__ UploadParams p) {
   const int gi = blockIdx.x;
@@ -36,7 +37,8 @@ __global__ void __launch_bounds__(32) nvfp4_upload_descriptors_kernel(
   const int g = p.first_group + gi;
   const uint4* src = reinterpret_cast<const uint4*>(&p.maps[gi][0]);
   uint4* dst = reinterpret_cast<uint4*>(p.maps_out + static_cast<size_t>(g) * kMapsPerGroup);
-  dst[lane] = src[lane];  // 32 lanes x 16 B = 4 maps x 128 B
+#pragma unroll
+  for (int i = lane; i < kMapsPerGroup * 8; i += 32) dst[i] = src[i];  // 8 maps x 128 B
   if (lane == 0) p.groups_out[g] = p.rec[gi];
   ptx::tensormap_fence_release();
 }
@@ -98,10 +100,13 @@ int cuda_fail(cudaError_t e, const char* what) {
   return fail(NVFP4_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
-// Kernel variants: <MMA N, gated, stages>.
+// Kernel variants. Single CTA: <MMA N, gated, stages>; CTA pair: <gated, stages>.
 using Kn128 = GemmConfig<128, false, 5>;
 using Kn256 = GemmConfig<256, false, 3>;
 using Kgated = GemmConfig<256, true, 3>;
+constexpr int kPairStages = 5;
+using Kpair = PairConfig<false, kPairStages>;
+using KpairGated = PairConfig<true, kPairStages>;
 
 constexpr int kMaxDevices = 64;
 
@@ -109,94 +114,30 @@ struct DeviceState {
   std::once_flag once;
   int status = NVFP4_OK;
   int num_sms = 0;
+  int pair_clusters = 0;        // CTA pairs that can be resident at once (plain pair kernel)
+  int pair_clusters_gated = 0;  // same for the gated pair kernel
   std::string detail;
 };
 DeviceState g_dev[kMaxDevices];
 
-// cuTensorMapEncodeTiled, resolved once through the runtime (no libcuda link).
-using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                              const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-struct Encoder {
-  std::once_flag once;
-  EncodeFn fn = nullptr;
-};
-Encoder g_encoder;
-
-void init_encoder(Encoder& e) {
-  void* fn = nullptr;
-  cudaDriverEntryPointQueryResult q;
-  cudaError_t err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-  if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) e.fn = reinterpret_cast<EncodeFn>(fn);
-}
-
-// Encoded maps are cached by (kind, address, rows, row bytes): weights keep
-// their maps across calls, so steady-state calls encode only what changed.
-struct MapKey {
-  uint64_t addr;
-  uint32_t rows;
-  uint32_t row_bytes;
-  uint32_t kind;
-  bool operator==(const MapKey& o) const {
-    return addr == o.addr && rows == o.rows && row_bytes == o.row_bytes && kind == o.kind;
+int max_pair_clusters(const void* fn, int smem, int num_sms) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_sms, 1, 1);
+  cfg.blockDim = dim3(kNumThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();  // clear the error; fall back to pairs of all SMs
+    n = num_sms / 2;
   }
-};
-struct MapKeyHash {
-  size_t operator()(const MapKey& k) const {
-    uint64_t h = k.addr * 0x9E3779B97F4A7C15ull;
-    h ^= (static_cast<uint64_t>(k.rows) << 32 | k.row_bytes) + 0x632BE59BD9B4E019ull + (h << 6);
-    return static_cast<size_t>(h ^ (static_cast<uint64_t>(k.kind) << 61));
-  }
-};
-std::mutex g_map_cache_mu;
-std::unordered_map<MapKey, TmaDesc, MapKeyHash> g_map_cache;
-constexpr size_t kMapCacheMax = 1 << 14;
-
-enum : uint32_t { kKindOperand = 0, kKindOutput = 1 };
-
-// e2m1 operand [rows, row_bytes] (uint8 view): box 128 B x 128 rows, 128B swizzle,
-// zero fill outside the tensor. fp16 output [rows, cols]: box 64 x 32, 128B swizzle.
-bool encode_map_uncached(uint32_t kind, const void* addr, uint32_t rows, uint32_t row_elems,
-                         TmaDesc* out) {
-  CUtensorMap m;
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r;
-  if (kind == kKindOperand) {
-    cuuint64_t dims[2] = {row_elems, rows};
-    cuuint64_t strides[1] = {row_elems};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(kRowBytesPerStage), static_cast<cuuint32_t>(kBlockM)};
-    r = g_encoder.fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(addr), dims, strides,
-                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  } else {
-    cuuint64_t dims[2] = {row_elems, rows};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_elems) * 2u};
-    cuuint32_t box[2] = {64, 32};
-    r = g_encoder.fn(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(addr), dims, strides,
-                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  }
-  if (r != CUDA_SUCCESS) return false;
-  memcpy(out, &m, sizeof(TmaDesc));
-  return true;
-}
-
-bool encode_map(uint32_t kind, const void* addr, uint32_t rows, uint32_t row_elems, TmaDesc* out) {
-  const MapKey key{reinterpret_cast<uint64_t>(addr), rows, row_elems, kind};
-  {
-    std::lock_guard<std::mutex> lk(g_map_cache_mu);
-    auto it = g_map_cache.find(key);
-    if (it != g_map_cache.end()) {
-      *out = it->second;
-      return true;
-    }
-  }
-  if (!encode_map_uncached(kind, addr, rows, row_elems, out)) return false;
-  std::lock_guard<std::mutex> lk(g_map_cache_mu);
-  if (g_map_cache.size() >= kMapCacheMax) g_map_cache.clear();
-  g_map_cache.emplace(key, *out);
-  return true;
+  return n;
 }
 
 void init_device(int dev, DeviceState& st) {
@@ -223,6 +164,10 @@ void init_device(int dev, DeviceState& st) {
       {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_kernel<128, false, 5>), Kn128::kSmemBytes},
       {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_kernel<256, false, 3>), Kn256::kSmemBytes},
       {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_kernel<256, true, 3>), Kgated::kSmemBytes},
+      {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_pair_kernel<false, kPairStages>),
+       Kpair::kSmemBytes},
+      {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_pair_kernel<true, kPairStages>),
+       KpairGated::kSmemBytes},
   };
   for (auto& k : kernels) {
     e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
@@ -232,16 +177,289 @@ void init_device(int dev, DeviceState& st) {
       return;
     }
   }
+  st.pair_clusters = max_pair_clusters(kernels[3].fn, kernels[3].smem, st.num_sms);
+  st.pair_clusters_gated = max_pair_clusters(kernels[4].fn, kernels[4].smem, st.num_sms);
+}
+
+// cuTensorMapEncodeTiled, resolved once through the runtime (no libcuda link).
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                              const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+struct Encoder {
+  std::once_flag once;
+  EncodeFn fn = nullptr;
+};
+Encoder g_encoder;
+
+void init_encoder(Encoder& e) {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) e.fn = reinterpret_cast<EncodeFn>(fn);
+}
+
+// Encoded maps are cached by (kind, address, rows, row elements): weights keep
+// their maps across calls, so steady-state calls encode only what changed.
+struct MapKey {
+  uint64_t addr;
+  uint32_t rows;
+  uint32_t row_bytes;
+  uint32_t kind;
+  bool operator==(const MapKey& o) const {
+    return addr == o.addr && rows == o.rows && row_bytes == o.row_bytes && kind == o.kind;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = k.addr * 0x9E3779B97F4A7C15ull;
+    h ^= (static_cast<uint64_t>(k.rows) << 32 | k.row_bytes) + 0x632BE59BD9B4E019ull + (h << 6);
+    return static_cast<size_t>(h ^ (static_cast<uint64_t>(k.kind) << 61));
+  }
+};
+std::mutex g_map_cache_mu;
+std::unordered_map<MapKey, TmaDesc, MapKeyHash> g_map_cache;
+constexpr size_t kMapCacheMax = 1 << 14;
+
+enum : uint32_t { kKindOperand = 0, kKindOutput = 1, kKindScales = 2 };
+
+// kKindOperand: e2m1 operand [rows, row_elems bytes] (uint8 view), box 128 B x 128 rows,
+//   128B swizzle, zero fill outside the tensor.
+// kKindOutput:  fp16 output [rows, row_elems], box 64 x 32, 128B swizzle.
+// kKindScales:  blocked scale bytes as row_elems 8-byte elements (1-D), box 256
+//   elements = one 2-KiB k-tile chunk of a 128-row block, zero fill outside.
+bool encode_map_uncached(uint32_t kind, const void* addr, uint32_t rows, uint32_t row_elems,
+                         TmaDesc* out) {
+  CUtensorMap m;
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r;
+  if (kind == kKindOperand) {
+    cuuint64_t dims[2] = {row_elems, rows};
+    cuuint64_t strides[1] = {row_elems};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kRowBytesPerStage), static_cast<cuuint32_t>(kBlockM)};
+    r = g_encoder.fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(addr), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else if (kind == kKindOutput) {
+    cuuint64_t dims[2] = {row_elems, rows};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_elems) * 2u};
+    cuuint32_t box[2] = {64, 32};
+    r = g_encoder.fn(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(addr), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[1] = {row_elems};
+    cuuint64_t strides[1] = {0};  // rank 1: no strides are read
+    cuuint32_t box[1] = {256};
+    r = g_encoder.fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 1, const_cast<void*>(addr), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  if (r != CUDA_SUCCESS) return false;
+  memcpy(out, &m, sizeof(TmaDesc));
+  return true;
+}
+
+bool encode_map(uint32_t kind, const void* addr, uint32_t rows, uint32_t row_elems, TmaDesc* out,
+                bool use_cache) {
+  if (!use_cache) return encode_map_uncached(kind, addr, rows, row_elems, out);
+  const MapKey key{reinterpret_cast<uint64_t>(addr), rows, row_elems, kind};
+  {
+    std::lock_guard<std::mutex> lk(g_map_cache_mu);
+    auto it = g_map_cache.find(key);
+    if (it != g_map_cache.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  if (!encode_map_uncached(kind, addr, rows, row_elems, out)) return false;
+  std::lock_guard<std::mutex> lk(g_map_cache_mu);
+  if (g_map_cache.size() >= kMapCacheMax) g_map_cache.clear();
+  g_map_cache.emplace(key, *out);
+  return true;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 template <int MMA_N, bool GATED, int STAGES>
-cudaError_t launch_gemm(const GemmParams& gp, int grid, cudaStream_t stream) {
+cudaError_t launch_single(const GemmParams& gp, int grid, cudaStream_t stream) {
   using Cfg = GemmConfig<MMA_N, GATED, STAGES>;
   nvfp4_grouped_gemm_kernel<MMA_N, GATED, STAGES>
       <<<grid, kNumThreads, Cfg::kSmemBytes, stream>>>(gp);
   return cudaGetLastError();
+}
+
+template <bool GATED>
+cudaError_t launch_pair(const GemmParams& gp, int clusters, cudaStream_t stream) {
+  using Cfg = PairConfig<GATED, kPairStages>;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.blockDim = dim3(kNumThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, nvfp4_grouped_gemm_pair_kernel<GATED, kPairStages>, gp);
+}
+
+// Shared implementation of both grouped entry points: validate, schedule, encode
+// and upload descriptors into `ws`, launch. `rec` holds num_groups records of host
+// scratch; `use_cache` selects the cached tensor-map encoder.
+int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int flags, uint8_t* ws,
+                      cudaStream_t s, GroupDev* rec, bool use_cache) {
+  const bool gated = (flags & NVFP4_FLAG_GATED) != 0;
+  // Tile shape: CTA pairs (256-row tiles) when the groups are tall enough to fill
+  // them, single CTAs (128-row tiles) otherwise; 256 MMA columns unless asked otherwise.
+  bool pair = false;
+  if ((flags & NVFP4_FLAG_TILE_N128) == 0 && (flags & NVFP4_FLAG_SINGLE_CTA) == 0) {
+    if (flags & NVFP4_FLAG_CTA_PAIR) {
+      pair = true;
+    } else {
+      int64_t rows = 0, active = 0;
+      for (int i = 0; i < num_groups; ++i)
+        if (groups[i].m > 0 && groups[i].n > 0) {
+          rows += groups[i].m;
+          ++active;
+        }
+      pair = active > 0 && rows >= 192 * active;
+    }
+  }
+  const int mma_n = gated ? 256 : ((flags & NVFP4_FLAG_TILE_N128) ? 128 : 256);
+  const int out_n = gated ? 128 : mma_n;
+  const int tile_m = pair ? 256 : kBlockM;
+
+  int64_t total_tiles = 0;
+  for (int i = 0; i < num_groups; ++i) {
+    const nvfp4_group& gr = groups[i];
+    if (gr.m < 0 || gr.n < 0 || gr.k < 0)
+      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: negative size (m=%d n=%d k=%d)", i, gr.m, gr.n, gr.k);
+    GroupDev& d = rec[i];
+    memset(&d, 0, sizeof(d));
+    d.m = gr.m;
+    d.n = gr.n;
+    d.k = gr.k;
+    d.alpha = gr.alpha;
+    d.alpha2 = gr.alpha2;
+    d.tiles_m = 1;
+    d.tile_start = d.tile_end = static_cast<int32_t>(total_tiles);
+    if (gr.m == 0 || gr.n == 0) continue;
+    if (gr.k <= 0 || gr.k % kBlockK != 0)
+      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: k=%d must be a positive multiple of 256", i, gr.k);
+    if (gr.n % 8 != 0)
+      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: n=%d must be a multiple of 8", i, gr.n);
+    const void* ptrs[7] = {gr.a, gr.b, gr.b2, gr.sfa, gr.sfb, gr.sfb2, gr.c};
+    const char* names[7] = {"a", "b", "b2", "sfa", "sfb", "sfb2", "c"};
+    for (int j = 0; j < 7; ++j) {
+      if (!gated && (j == 2 || j == 5)) continue;
+      if (ptrs[j] == nullptr) return fail(NVFP4_ERR_NULL_POINTER, "group %d: %s is NULL", i, names[j]);
+      if (!aligned16(ptrs[j]))
+        return fail(NVFP4_ERR_MISALIGNED, "group %d: %s not 16-byte aligned", i, names[j]);
+    }
+    d.sfa = static_cast<const uint8_t*>(gr.sfa);
+    d.sfb = static_cast<const uint8_t*>(gr.sfb);
+    d.sfb2 = gated ? static_cast<const uint8_t*>(gr.sfb2) : nullptr;
+    d.tiles_m = (gr.m + tile_m - 1) / tile_m;
+    total_tiles += static_cast<int64_t>(d.tiles_m) * ((gr.n + out_n - 1) / out_n);
+    if (total_tiles > (int64_t{1} << 30))
+      return fail(NVFP4_ERR_BAD_SHAPE, "too many tiles (%lld)", static_cast<long long>(total_tiles));
+    d.tile_end = static_cast<int32_t>(total_tiles);
+  }
+  if (total_tiles == 0) return NVFP4_OK;
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_INVALID_ARGUMENT, "device %d", dev);
+  DeviceState& ds = g_dev[dev];
+  std::call_once(ds.once, init_device, dev, std::ref(ds));
+  if (ds.status != NVFP4_OK) return fail(ds.status, "%s", ds.detail.c_str());
+  std::call_once(g_encoder.once, init_encoder, std::ref(g_encoder));
+  if (g_encoder.fn == nullptr)
+    return fail(NVFP4_ERR_DRIVER, "cuTensorMapEncodeTiled entry point not available from the driver");
+
+  GroupDev* groups_dev = reinterpret_cast<GroupDev*>(ws + ws_groups_offset());
+  TmaDesc* maps_dev = reinterpret_cast<TmaDesc*>(ws + ws_maps_offset(num_groups));
+
+  if ((flags & NVFP4_FLAG_REUSE_DESCRIPTORS) == 0) {
+    static thread_local UploadParams up;  // ~26 KB: kept off the caller's stack
+    up.groups_out = groups_dev;
+    up.maps_out = maps_dev;
+    for (int first = 0; first < num_groups; first += kGroupsPerUpload) {
+      const int count = std::min(kGroupsPerUpload, num_groups - first);
+      up.first_group = first;
+      up.count = count;
+      for (int gi = 0; gi < count; ++gi) {
+        const int i = first + gi;
+        const nvfp4_group& gr = groups[i];
+        up.rec[gi] = rec[i];
+        TmaDesc* mp = up.maps[gi];
+        memset(mp, 0, sizeof(TmaDesc) * kMapsPerGroup);
+        if (rec[i].tile_end == rec[i].tile_start) continue;  // empty group: maps never read
+        const uint32_t kb = static_cast<uint32_t>(gr.k / 2);
+        // Blocked scale bytes of an R-row operand, in 8-byte elements.
+        const uint32_t sfa_e = static_cast<uint32_t>(((gr.m + 127) / 128) * (gr.k / 64) * 64);
+        const uint32_t sfb_e = static_cast<uint32_t>(((gr.n + 127) / 128) * (gr.k / 64) * 64);
+        bool ok = encode_map(kKindOperand, gr.a, gr.m, kb, &mp[kMapA], use_cache) &&
+                  encode_map(kKindOperand, gr.b, gr.n, kb, &mp[kMapB], use_cache) &&
+                  encode_map(kKindOutput, gr.c, gr.m, gr.n, &mp[kMapC], use_cache) &&
+                  encode_map(kKindScales, gr.sfa, 1, sfa_e, &mp[kMapSfa], use_cache) &&
+                  encode_map(kKindScales, gr.sfb, 1, sfb_e, &mp[kMapSfb], use_cache) &&
+                  (!gated ||
+                   (encode_map(kKindOperand, gr.b2, gr.n, kb, &mp[kMapB2], use_cache) &&
+                    encode_map(kKindScales, gr.sfb2, 1, sfb_e, &mp[kMapSfb2], use_cache)));
+        if (!ok) return fail(NVFP4_ERR_DRIVER, "group %d: cuTensorMapEncodeTiled rejected a tensor", i);
+      }
+      nvfp4_upload_descriptors_kernel<<<count, 32, 0, s>>>(up);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_fail(e, "descriptor upload launch");
+    }
+  }
+
+  GemmParams gp;
+  gp.groups = groups_dev;
+  gp.maps = maps_dev;
+  gp.error_bits = reinterpret_cast<uint32_t*>(ws);
+  gp.num_groups = num_groups;
+  gp.total_tiles = static_cast<int32_t>(total_tiles);
+  if (pair) {
+    const int max_clusters = gated ? ds.pair_clusters_gated : ds.pair_clusters;
+    const int clusters = static_cast<int>(std::min<int64_t>(total_tiles, max_clusters));
+    e = gated ? launch_pair<true>(gp, clusters, s) : launch_pair<false>(gp, clusters, s);
+  } else {
+    const int grid = static_cast<int>(std::min<int64_t>(total_tiles, ds.num_sms));
+    if (gated)
+      e = launch_single<256, true, 3>(gp, grid, s);
+    else if (mma_n == 128)
+      e = launch_single<128, false, 5>(gp, grid, s);
+    else
+      e = launch_single<256, false, 3>(gp, grid, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
+  return NVFP4_OK;
+}
+
+int check_common_args(const nvfp4_group* groups, int num_groups, unsigned int flags) {
+  const unsigned known = NVFP4_FLAG_GATED | NVFP4_FLAG_TILE_N128 | NVFP4_FLAG_TILE_N256 |
+                         NVFP4_FLAG_REUSE_DESCRIPTORS | NVFP4_FLAG_CTA_PAIR |
+                         NVFP4_FLAG_SINGLE_CTA;
+  if (flags & ~known) return fail(NVFP4_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags & ~known);
+  if (num_groups < 0) return fail(NVFP4_ERR_INVALID_ARGUMENT, "num_groups=%d", num_groups);
+  if (num_groups > 0 && groups == nullptr)
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "groups table is NULL");
+  if ((flags & NVFP4_FLAG_TILE_N128) && (flags & NVFP4_FLAG_TILE_N256))
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "TILE_N128 and TILE_N256 are exclusive");
+  if ((flags & NVFP4_FLAG_CTA_PAIR) && (flags & NVFP4_FLAG_SINGLE_CTA))
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "CTA_PAIR and SINGLE_CTA are exclusive");
+  if ((flags & NVFP4_FLAG_CTA_PAIR) && (flags & NVFP4_FLAG_TILE_N128))
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "CTA pairs use 256-column tiles");
+  if ((flags & NVFP4_FLAG_GATED) && (flags & NVFP4_FLAG_TILE_N128))
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "gated launches use 128 gate + 128 up columns");
+  return NVFP4_OK;
 }
 
 }  // namespace
@@ -331,128 +549,17 @@ NVFP4_API int nvfp4_workspace_check(void* workspace, void* stream, unsigned int*
 NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsigned int flags,
                                  void* workspace, size_t workspace_bytes, void* stream) {
   g_last_error.clear();
-  const unsigned known = NVFP4_FLAG_GATED | NVFP4_FLAG_TILE_N128 | NVFP4_FLAG_TILE_N256 |
-                         NVFP4_FLAG_REUSE_DESCRIPTORS;
-  if (flags & ~known) return fail(NVFP4_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags & ~known);
-  if (num_groups < 0) return fail(NVFP4_ERR_INVALID_ARGUMENT, "num_groups=%d", num_groups);
-  if (num_groups == 0) return NVFP4_OK;
-  if (groups == nullptr) return fail(NVFP4_ERR_INVALID_ARGUMENT, "groups table is NULL");
-  const bool gated = (flags & NVFP4_FLAG_GATED) != 0;
-  if ((flags & NVFP4_FLAG_TILE_N128) && (flags & NVFP4_FLAG_TILE_N256))
-    return fail(NVFP4_ERR_INVALID_ARGUMENT, "TILE_N128 and TILE_N256 are exclusive");
-  if (gated && (flags & NVFP4_FLAG_TILE_N128))
-    return fail(NVFP4_ERR_INVALID_ARGUMENT, "gated launches use 128 gate + 128 up columns");
+  int st = check_common_args(groups, num_groups, flags);
+  if (st != NVFP4_OK || num_groups == 0) return st;
   if (workspace == nullptr) return fail(NVFP4_ERR_WORKSPACE, "workspace is NULL");
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return fail(NVFP4_ERR_WORKSPACE, "workspace not 256-byte aligned");
   if (workspace_bytes < ws_total_bytes(num_groups))
     return fail(NVFP4_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes,
                 ws_total_bytes(num_groups));
-
-  // Tile width along N: 256-column MMAs unless asked otherwise.
-  const int mma_n = gated ? 256 : ((flags & NVFP4_FLAG_TILE_N128) ? 128 : 256);
-  const int out_n = gated ? 128 : mma_n;
-
-  // Host-side schedule: tiles are numbered group by group, m-tile fastest.
   std::vector<GroupDev> rec(static_cast<size_t>(num_groups));
-  int64_t total_tiles = 0;
-  for (int i = 0; i < num_groups; ++i) {
-    const nvfp4_group& gr = groups[i];
-    if (gr.m < 0 || gr.n < 0 || gr.k < 0)
-      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: negative size (m=%d n=%d k=%d)", i, gr.m, gr.n, gr.k);
-    GroupDev& d = rec[i];
-    memset(&d, 0, sizeof(d));
-    d.m = gr.m;
-    d.n = gr.n;
-    d.k = gr.k;
-    d.alpha = gr.alpha;
-    d.alpha2 = gr.alpha2;
-    d.tiles_m = 1;
-    d.tile_start = d.tile_end = static_cast<int32_t>(total_tiles);
-    if (gr.m == 0 || gr.n == 0) continue;
-    if (gr.k <= 0 || gr.k % kBlockK != 0)
-      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: k=%d must be a positive multiple of 256", i, gr.k);
-    if (gr.n % 8 != 0)
-      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: n=%d must be a multiple of 8", i, gr.n);
-    const void* ptrs[7] = {gr.a, gr.b, gr.b2, gr.sfa, gr.sfb, gr.sfb2, gr.c};
-    const char* names[7] = {"a", "b", "b2", "sfa", "sfb", "sfb2", "c"};
-    for (int j = 0; j < 7; ++j) {
-      if (!gated && (j == 2 || j == 5)) continue;
-      if (ptrs[j] == nullptr) return fail(NVFP4_ERR_NULL_POINTER, "group %d: %s is NULL", i, names[j]);
-      if (!aligned16(ptrs[j]))
-        return fail(NVFP4_ERR_MISALIGNED, "group %d: %s not 16-byte aligned", i, names[j]);
-    }
-    d.sfa = static_cast<const uint8_t*>(gr.sfa);
-    d.sfb = static_cast<const uint8_t*>(gr.sfb);
-    d.sfb2 = gated ? static_cast<const uint8_t*>(gr.sfb2) : nullptr;
-    d.tiles_m = (gr.m + kBlockM - 1) / kBlockM;
-    const int tiles_n = (gr.n + out_n - 1) / out_n;
-    total_tiles += static_cast<int64_t>(d.tiles_m) * tiles_n;
-    if (total_tiles > (int64_t{1} << 30))
-      return fail(NVFP4_ERR_BAD_SHAPE, "too many tiles (%lld)", static_cast<long long>(total_tiles));
-    d.tile_end = static_cast<int32_t>(total_tiles);
-  }
-  if (total_tiles == 0) return NVFP4_OK;
-
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_INVALID_ARGUMENT, "device %d", dev);
-  DeviceState& ds = g_dev[dev];
-  std::call_once(ds.once, init_device, dev, std::ref(ds));
-  if (ds.status != NVFP4_OK) return fail(ds.status, "%s", ds.detail.c_str());
-  std::call_once(g_encoder.once, init_encoder, std::ref(g_encoder));
-  if (g_encoder.fn == nullptr)
-    return fail(NVFP4_ERR_DRIVER, "cuTensorMapEncodeTiled entry point not available from the driver");
-
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  GroupDev* groups_dev = reinterpret_cast<GroupDev*>(ws + ws_groups_offset());
-  TmaDesc* maps_dev = reinterpret_cast<TmaDesc*>(ws + ws_maps_offset(num_groups));
-
-  if ((flags & NVFP4_FLAG_REUSE_DESCRIPTORS) == 0) {
-    static thread_local UploadParams up;  // ~23 KB: kept off the caller's stack
-    up.groups_out = groups_dev;
-    up.maps_out = maps_dev;
-    for (int first = 0; first < num_groups; first += kGroupsPerUpload) {
-      const int count = std::min(kGroupsPerUpload, num_groups - first);
-      up.first_group = first;
-      up.count = count;
-      for (int gi = 0; gi < count; ++gi) {
-        const int i = first + gi;
-        const nvfp4_group& gr = groups[i];
-        up.rec[gi] = rec[i];
-        TmaDesc* mp = up.maps[gi];
-        memset(mp, 0, sizeof(TmaDesc) * kMapsPerGroup);
-        if (rec[i].tile_end == rec[i].tile_start) continue;  // empty group: maps never read
-        const uint32_t kb = static_cast<uint32_t>(gr.k / 2);
-        bool ok = encode_map(kKindOperand, gr.a, gr.m, kb, &mp[kMapA]) &&
-                  encode_map(kKindOperand, gr.b, gr.n, kb, &mp[kMapB]) &&
-                  (!gated || encode_map(kKindOperand, gr.b2, gr.n, kb, &mp[kMapB2])) &&
-                  encode_map(kKindOutput, gr.c, gr.m, gr.n, &mp[kMapC]);
-        if (!ok) return fail(NVFP4_ERR_DRIVER, "group %d: cuTensorMapEncodeTiled rejected a tensor", i);
-      }
-      nvfp4_upload_descriptors_kernel<<<count, 32, 0, s>>>(up);
-      e = cudaGetLastError();
-      if (e != cudaSuccess) return cuda_fail(e, "descriptor upload launch");
-    }
-  }
-
-  GemmParams gp;
-  gp.groups = groups_dev;
-  gp.maps = maps_dev;
-  gp.error_bits = reinterpret_cast<uint32_t*>(ws);
-  gp.num_groups = num_groups;
-  gp.total_tiles = static_cast<int32_t>(total_tiles);
-  const int grid = static_cast<int>(std::min<int64_t>(total_tiles, ds.num_sms));
-  if (gated)
-    e = launch_gemm<256, true, 3>(gp, grid, s);
-  else if (mma_n == 128)
-    e = launch_gemm<128, false, 5>(gp, grid, s);
-  else
-    e = launch_gemm<256, false, 3>(gp, grid, s);
-  if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
-  return NVFP4_OK;
+  return grouped_gemm_impl(groups, num_groups, flags, static_cast<uint8_t*>(workspace),
+                           static_cast<cudaStream_t>(stream), rec.data(), /*use_cache=*/true);
 }
 
 }  // extern "C"
@@ -495,129 +602,29 @@ void init_noalloc(NoAllocState& st) {
 extern "C" NVFP4_API int nvfp4_grouped_gemm_noalloc(const nvfp4_group* groups, int num_groups,
                                                     unsigned int flags, void* stream) {
   g_last_error.clear();
-  const unsigned known = NVFP4_FLAG_GATED | NVFP4_FLAG_TILE_N128 | NVFP4_FLAG_TILE_N256 |
-                         NVFP4_FLAG_REUSE_DESCRIPTORS;
-  if (flags & ~known) return fail(NVFP4_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags & ~known);
-  if (num_groups < 0) return fail(NVFP4_ERR_INVALID_ARGUMENT, "num_groups=%d", num_groups);
+  int st = check_common_args(groups, num_groups, flags);
+  if (st != NVFP4_OK) return st;
   if (num_groups > NVFP4_NOALLOC_MAX_GROUPS)
     return fail(NVFP4_ERR_INVALID_ARGUMENT,
                 "num_groups=%d exceeds the %d groups the built-in scratch array holds; "
                 "use nvfp4_grouped_gemm with a caller-provided workspace",
                 num_groups, NVFP4_NOALLOC_MAX_GROUPS);
   if (num_groups == 0) return NVFP4_OK;
-  if (groups == nullptr) return fail(NVFP4_ERR_INVALID_ARGUMENT, "groups table is NULL");
-  const bool gated = (flags & NVFP4_FLAG_GATED) != 0;
-  if ((flags & NVFP4_FLAG_TILE_N128) && (flags & NVFP4_FLAG_TILE_N256))
-    return fail(NVFP4_ERR_INVALID_ARGUMENT, "TILE_N128 and TILE_N256 are exclusive");
-  if (gated && (flags & NVFP4_FLAG_TILE_N128))
-    return fail(NVFP4_ERR_INVALID_ARGUMENT, "gated launches use 128 gate + 128 up columns");
-  const int mma_n = gated ? 256 : ((flags & NVFP4_FLAG_TILE_N128) ? 128 : 256);
-  const int out_n = gated ? 128 : mma_n;
-
-  // Fixed-size host staging (no heap use on this path).
-  static thread_local GroupDev rec[NVFP4_NOALLOC_MAX_GROUPS];
-  int64_t total_tiles = 0;
-  for (int i = 0; i < num_groups; ++i) {
-    const nvfp4_group& gr = groups[i];
-    if (gr.m < 0 || gr.n < 0 || gr.k < 0)
-      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: negative size (m=%d n=%d k=%d)", i, gr.m, gr.n, gr.k);
-    GroupDev& d = rec[i];
-    memset(&d, 0, sizeof(d));
-    d.m = gr.m;
-    d.n = gr.n;
-    d.k = gr.k;
-    d.alpha = gr.alpha;
-    d.alpha2 = gr.alpha2;
-    d.tiles_m = 1;
-    d.tile_start = d.tile_end = static_cast<int32_t>(total_tiles);
-    if (gr.m == 0 || gr.n == 0) continue;
-    if (gr.k <= 0 || gr.k % kBlockK != 0)
-      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: k=%d must be a positive multiple of 256", i, gr.k);
-    if (gr.n % 8 != 0)
-      return fail(NVFP4_ERR_BAD_SHAPE, "group %d: n=%d must be a multiple of 8", i, gr.n);
-    const void* ptrs[7] = {gr.a, gr.b, gr.b2, gr.sfa, gr.sfb, gr.sfb2, gr.c};
-    const char* names[7] = {"a", "b", "b2", "sfa", "sfb", "sfb2", "c"};
-    for (int j = 0; j < 7; ++j) {
-      if (!gated && (j == 2 || j == 5)) continue;
-      if (ptrs[j] == nullptr) return fail(NVFP4_ERR_NULL_POINTER, "group %d: %s is NULL", i, names[j]);
-      if (!aligned16(ptrs[j]))
-        return fail(NVFP4_ERR_MISALIGNED, "group %d: %s not 16-byte aligned", i, names[j]);
-    }
-    d.sfa = static_cast<const uint8_t*>(gr.sfa);
-    d.sfb = static_cast<const uint8_t*>(gr.sfb);
-    d.sfb2 = gated ? static_cast<const uint8_t*>(gr.sfb2) : nullptr;
-    d.tiles_m = (gr.m + kBlockM - 1) / kBlockM;
-    total_tiles += static_cast<int64_t>(d.tiles_m) * ((gr.n + out_n - 1) / out_n);
-    if (total_tiles > (int64_t{1} << 30))
-      return fail(NVFP4_ERR_BAD_SHAPE, "too many tiles (%lld)", static_cast<long long>(total_tiles));
-    d.tile_end = static_cast<int32_t>(total_tiles);
-  }
-  if (total_tiles == 0) return NVFP4_OK;
 
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_INVALID_ARGUMENT, "device %d", dev);
-  DeviceState& ds = g_dev[dev];
-  std::call_once(ds.once, init_device, dev, std::ref(ds));
-  if (ds.status != NVFP4_OK) return fail(ds.status, "%s", ds.detail.c_str());
-  std::call_once(g_encoder.once, init_encoder, std::ref(g_encoder));
-  if (g_encoder.fn == nullptr)
-    return fail(NVFP4_ERR_DRIVER, "cuTensorMapEncodeTiled entry point not available from the driver");
   NoAllocState& na = g_noalloc[dev];
   std::call_once(na.once, init_noalloc, std::ref(na));
   if (na.scratch == nullptr) return cuda_fail(na.status, "cudaGetSymbolAddress(scratch)");
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(na.scratch);
-  GroupDev* groups_dev = reinterpret_cast<GroupDev*>(ws + ws_groups_offset());
-  TmaDesc* maps_dev = reinterpret_cast<TmaDesc*>(ws + ws_maps_offset(num_groups));
-
   // The device error word keeps whatever the previous call left: start this call at zero.
   e = cudaMemsetAsync(ws, 0, sizeof(uint32_t), s);
   if (e != cudaSuccess) return cuda_fail(e, "clear scratch error word");
-
-  if ((flags & NVFP4_FLAG_REUSE_DESCRIPTORS) == 0) {
-    static thread_local UploadParams up;
-    up.groups_out = groups_dev;
-    up.maps_out = maps_dev;
-    for (int first = 0; first < num_groups; first += kGroupsPerUpload) {
-      const int count = std::min(kGroupsPerUpload, num_groups - first);
-      up.first_group = first;
-      up.count = count;
-      for (int gi = 0; gi < count; ++gi) {
-        const int i = first + gi;
-        const nvfp4_group& gr = groups[i];
-        up.rec[gi] = rec[i];
-        TmaDesc* mp = up.maps[gi];
-        memset(mp, 0, sizeof(TmaDesc) * kMapsPerGroup);
-        if (rec[i].tile_end == rec[i].tile_start) continue;
-        const uint32_t kb = static_cast<uint32_t>(gr.k / 2);
-        bool ok = encode_map_uncached(kKindOperand, gr.a, gr.m, kb, &mp[kMapA]) &&
-                  encode_map_uncached(kKindOperand, gr.b, gr.n, kb, &mp[kMapB]) &&
-                  (!gated || encode_map_uncached(kKindOperand, gr.b2, gr.n, kb, &mp[kMapB2])) &&
-                  encode_map_uncached(kKindOutput, gr.c, gr.m, gr.n, &mp[kMapC]);
-        if (!ok) return fail(NVFP4_ERR_DRIVER, "group %d: cuTensorMapEncodeTiled rejected a tensor", i);
-      }
-      nvfp4_upload_descriptors_kernel<<<count, 32, 0, s>>>(up);
-      e = cudaGetLastError();
-      if (e != cudaSuccess) return cuda_fail(e, "descriptor upload launch");
-    }
-  }
-
-  GemmParams gp;
-  gp.groups = groups_dev;
-  gp.maps = maps_dev;
-  gp.error_bits = reinterpret_cast<uint32_t*>(ws);
-  gp.num_groups = num_groups;
-  gp.total_tiles = static_cast<int32_t>(total_tiles);
-  const int grid = static_cast<int>(std::min<int64_t>(total_tiles, ds.num_sms));
-  if (gated)
-    e = launch_gemm<256, true, 3>(gp, grid, s);
-  else if (mma_n == 128)
-    e = launch_gemm<128, false, 5>(gp, grid, s);
-  else
-    e = launch_gemm<256, false, 3>(gp, grid, s);
-  if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
-  return NVFP4_OK;
+  // Fixed-size host staging and uncached encoding: no heap use on this path.
+  static thread_local GroupDev rec[NVFP4_NOALLOC_MAX_GROUPS];
+  return grouped_gemm_impl(groups, num_groups, flags, ws, s, rec, /*use_cache=*/false);
 }

@@ -17,7 +17,7 @@ constexpr int kMmaK = 64;             // K per tcgen05.mma kind::mxf4nvf4
 constexpr int kSfVec = 16;            // elements per scale factor
 constexpr int kSfBlockBytes = 512;    // one 128 x 4 scale-factor block
 // Groups whose records and tensor maps one upload launch carries in its parameters.
-constexpr int kGroupsPerUpload = 40;
+constexpr int kGroupsPerUpload = 24;
 
 // 128-byte opaque CUtensorMap image (the driver type requires 64-byte alignment).
 struct alignas(64) TmaDesc {
@@ -25,8 +25,13 @@ struct alignas(64) TmaDesc {
 };
 static_assert(sizeof(TmaDesc) == 128, "tensor map image must be 128 bytes");
 
-// Tensor maps kept per group, in this order.
-enum : int { kMapA = 0, kMapB = 1, kMapB2 = 2, kMapC = 3, kMapsPerGroup = 4 };
+// Tensor maps kept per group, in this order. The scale-factor maps are 1-D views of
+// the blocked scale bytes as 8-byte elements (one box = 256 elements = one 2-KiB k-tile
+// chunk of a 128-row block); the CTA-pair kernel loads scales through them.
+enum : int {
+  kMapA = 0, kMapB = 1, kMapB2 = 2, kMapC = 3, kMapSfa = 4, kMapSfb = 5, kMapSfb2 = 6,
+  kMapsPerGroup = 8
+};
 
 // One group as the device sees it (written by the descriptor builder).
 struct GroupDev {
@@ -55,7 +60,7 @@ enum : uint32_t {
   kDevErrDrainTimeout = 1u << 4,     // in-flight copies or MMAs did not finish at exit
 };
 
-// Workspace layout: header | GroupDev[G] (64 B each) | TmaDesc[G][4] (128 B aligned).
+// Workspace layout: header | GroupDev[G] (64 B each) | TmaDesc[G][8] (128 B aligned).
 __host__ __device__ constexpr size_t ws_groups_offset() { return sizeof(WorkspaceHeader); }
 __host__ __device__ constexpr size_t ws_maps_offset(int num_groups) {
   return (ws_groups_offset() + static_cast<size_t>(num_groups) * 64 + 127) &
@@ -67,7 +72,7 @@ __host__ __device__ constexpr size_t ws_total_bytes(int num_groups) {
 }
 
 // Parameter block of the descriptor upload kernel: host-encoded records and
-// tensor maps of up to kGroupsPerUpload groups (about 23 KB of kernel parameters).
+// tensor maps of up to kGroupsPerUpload groups (about 26 KB of kernel parameters).
 struct UploadParams {
   TmaDesc maps[kGroupsPerUpload][kMapsPerGroup];
   GroupDev rec[kGroupsPerUpload];

@@ -132,12 +132,18 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
                  alpha2: Sequence[float] | None = None,
                  tile_n: int | None = None,
                  stream: torch.cuda.Stream | None = None,
-                 reuse_descriptors: bool = True) -> list:
+                 reuse_descriptors: bool = True,
+                 cta: str | None = None) -> list:
     """One grouped NVFP4 launch. Scale tensors are in the blocked layout.
 
     ``problem_sizes`` holds (m, n, k[, l]) per group. When ``b2``/``sfb2`` are given
     the launch is gated: ``c = fp16(silu(fp16(alpha*A.B^T)) * fp16(alpha2*A.B2^T))``.
+    ``cta`` forces 256-row tiles on CTA pairs (``"pair"``) or 128-row tiles on single
+    CTAs (``"single"``); by default the library picks pairs when the groups average
+    at least 192 rows. ``tile_n`` (128 or 256) applies to single-CTA tiles.
     """
+    if cta not in (None, "pair", "single"):
+        raise ValueError(f"cta must be None, 'pair' or 'single', got {cta!r}")
     G = len(problem_sizes)
     if not (len(a) == len(b) == len(sfa) == len(sfb) == len(c) == G):
         raise ValueError("a, b, sfa, sfb, c and problem_sizes must have one entry per group")
@@ -153,7 +159,7 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
                    tuple(t.data_ptr() for lst in lists for t in lst),
                    tuple(tuple(ps) for ps in problem_sizes),
                    None if alpha is None else tuple(alpha),
-                   None if alpha2 is None else tuple(alpha2), tile_n, gated)
+                   None if alpha2 is None else tuple(alpha2), tile_n, gated, cta)
         except (AttributeError, TypeError):
             sig = None
         if sig is not None:
@@ -224,6 +230,12 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
     table["alpha2"] = 1.0 if alpha2 is None else np.asarray(alpha2, dtype=np.float32)
 
     flags = _native.FLAG_GATED if gated else 0
+    if cta == "pair":
+        flags |= _native.FLAG_CTA_PAIR
+    elif cta == "single":
+        flags |= _native.FLAG_SINGLE_CTA
+    if tile_n == 128 and cta == "pair":
+        raise ValueError("CTA pairs use 256-column tiles")
     if tile_n is not None and not gated:
         if tile_n == 128:
             flags |= _native.FLAG_TILE_N128
@@ -262,7 +274,7 @@ def _split_scales(global_scales, G: int, gated: bool):
 
 
 def custom_kernel(data: input_t, *, global_scales=None, tile_n: int | None = None,
-                  stream: torch.cuda.Stream | None = None) -> output_t:
+                  stream: torch.cuda.Stream | None = None, cta: str | None = None) -> output_t:
     """Drop-in replacement of the reference's ``custom_kernel`` (submission.py:788)."""
     if not isinstance(data, (tuple, list)):
         raise ValueError(f"unsupported input: expected a tuple, got {type(data).__name__}")
@@ -274,7 +286,7 @@ def custom_kernel(data: input_t, *, global_scales=None, tile_n: int | None = Non
         k = int(a.shape[1]) * 2
         alpha, alpha2 = _split_scales(global_scales, 1, True)
         grouped_gemm([a], [b1], [sfa_p], [sfb1_p], [c], [(m, n, k, 1)], alpha=alpha,
-                     b2=[b2], sfb2=[sfb2_p], alpha2=alpha2, stream=stream)
+                     b2=[b2], sfb2=[sfb2_p], alpha2=alpha2, stream=stream, cta=cta)
         return c
     if len(data) not in (4, 5):
         raise ValueError(f"unsupported input format with {len(data)} elements "
@@ -311,7 +323,7 @@ def custom_kernel(data: input_t, *, global_scales=None, tile_n: int | None = Non
         b2 = sfb2 = None
     alpha, alpha2 = _split_scales(global_scales, G, gated)
     grouped_gemm(a, b, sfa, sfb, c, problem_sizes, alpha=alpha, b2=b2, sfb2=sfb2,
-                 alpha2=alpha2, tile_n=tile_n, stream=stream)
+                 alpha2=alpha2, tile_n=tile_n, stream=stream, cta=cta)
     return list(c)
 
 

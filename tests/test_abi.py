@@ -52,7 +52,8 @@ def test_version_and_strings(pkg):
 def test_size_queries(pkg):
     N = pkg._native
     assert N.workspace_size(0) == 256
-    assert N.workspace_size(8) == 256 + 8 * 64 + 8 * 4 * 128
+    assert N.workspace_size(8) == 256 + 8 * 64 + 8 * 8 * 128
+    assert N.workspace_size(3) == 512 + 3 * 8 * 128  # records padded to 128 bytes
     assert N.sf_blocked_size(80, 32) == 1 * 8 * 512
     assert N.sf_blocked_size(129, 5) == 2 * 2 * 512
     assert N.sf_blocked_size(0, 4) == 0
@@ -77,6 +78,8 @@ def _table(N, **kw):
     (dict(c=0x50008), 0, 3),        # misaligned output
     (dict(b2=0), 1, 4),             # gated without up weights
     (dict(), 0x100, 1),             # unknown flag bit
+    (dict(), 0x10 | 0x20, 1),       # exclusive CTA modes
+    (dict(), 0x10 | 0x2, 1),        # pairs need 256-column tiles
     (dict(), 0x2 | 0x4, 1),         # exclusive tile flags
 ])
 def test_validation_errors_before_launch(pkg, kw, flags, status):

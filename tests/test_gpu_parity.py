@@ -53,12 +53,18 @@ def check_problem(prob, tol=TOL, groups=None):
     return report
 
 
-def run_custom_kernel(pkg, prob, tile_n=None):
+# (tile_n, cta) of every kernel variant: library default, single CTA with 128- and
+# 256-column tiles, CTA pair with 256 x 256 tiles.
+VARIANTS = [(None, None), (128, "single"), (256, "single"), (None, "pair")]
+VARIANT_IDS = ["auto", "single128", "single256", "pair"]
+
+
+def run_custom_kernel(pkg, prob, tile_n=None, cta=None):
     data = prob.reference_data()
     scales = prob.global_scales()
     if all(s == 1.0 or s == (1.0, 1.0) for s in scales):
         scales = None
-    out = pkg.custom_kernel(data, global_scales=scales, tile_n=tile_n)
+    out = pkg.custom_kernel(data, global_scales=scales, tile_n=tile_n, cta=cta)
     assert len(out) == prob.num_groups
     for o, c in zip(out, prob.c):
         assert o.data_ptr() == c.data_ptr()
@@ -97,8 +103,8 @@ def _golden_problem(pkg, data, name):
     return p
 
 
-@pytest.mark.parametrize("tile_n", [None, 128])
-def test_golden_cases_match_oracle_and_reference(pkg, golden_inputs, tile_n):
+@pytest.mark.parametrize("tile_n,cta", VARIANTS, ids=VARIANT_IDS)
+def test_golden_cases_match_oracle_and_reference(pkg, golden_inputs, tile_n, cta):
     outputs = None
     try:
         import os
@@ -114,7 +120,7 @@ def test_golden_cases_match_oracle_and_reference(pkg, golden_inputs, tile_n):
             continue
         pkg.grouped_gemm(p.a, p.b, p.sfa, p.sfb, p.c,
                          [(m, n, k, 1) for m, n, k in zip(p.m, p.n, p.k)], alpha=p.alpha,
-                         b2=p.b2, sfb2=p.sfb2, alpha2=p.alpha2, tile_n=tile_n)
+                         b2=p.b2, sfb2=p.sfb2, alpha2=p.alpha2, tile_n=tile_n, cta=cta)
         torch.cuda.synchronize()
         for g in range(p.num_groups):
             got = _np(p.c[g])
@@ -151,24 +157,27 @@ EDGE_SHAPES = [
 ]
 
 
-@pytest.mark.parametrize("tile_n", [None, 128, 256])
+@pytest.mark.parametrize("tile_n,cta", VARIANTS, ids=VARIANT_IDS)
 @pytest.mark.parametrize("shape", EDGE_SHAPES, ids=[s[0] for s in EDGE_SHAPES])
-def test_edge_shapes(pkg, shape, tile_n):
+def test_edge_shapes(pkg, shape, tile_n, cta):
     name, ms, n, k = shape
     prob = pkg.workloads.make_problem(name, ms, n, k, seed=len(ms) * 7 + n + k, device="cuda",
                                       alpha_range=(0.5, 2.0))
-    run_custom_kernel(pkg, prob, tile_n=tile_n)
+    run_custom_kernel(pkg, prob, tile_n=tile_n, cta=cta)
     check_problem(prob)
 
 
-@pytest.mark.parametrize("shape", [("gated_small", [96], 256, 512),
-                                   ("gated_ragged", [0, 1, 130, 257], 384, 768),
-                                   ("gated_n8", [40], 8, 256)], ids=lambda s: s[0])
-def test_gated_shapes(pkg, shape):
+GATED_SHAPES = [("gated_small", [96], 256, 512), ("gated_ragged", [0, 1, 130, 257], 384, 768),
+                ("gated_n8", [40], 8, 256), ("gated_tall", [512, 300], 256, 1024)]
+
+
+@pytest.mark.parametrize("cta", [None, "single", "pair"])
+@pytest.mark.parametrize("shape", GATED_SHAPES, ids=lambda s: s[0])
+def test_gated_shapes(pkg, shape, cta):
     name, ms, n, k = shape
     prob = pkg.workloads.make_problem(name, ms, n, k, gated=True, seed=99 + n, device="cuda",
                                       alpha_range=(0.5, 2.0))
-    run_custom_kernel(pkg, prob)
+    run_custom_kernel(pkg, prob, cta=cta)
     check_problem(prob)
 
 
@@ -184,10 +193,11 @@ def test_ten_tuple_dual_gemm_form(pkg):
     check_problem(prob, tol=HARNESS_TOL)
 
 
-def test_more_groups_than_one_builder_launch(pkg):
-    ms = [(i * 37) % 150 for i in range(300)]  # 300 groups -> two descriptor-builder launches
+@pytest.mark.parametrize("cta", [None, "pair"])
+def test_many_groups_several_upload_launches(pkg, cta):
+    ms = [(i * 37) % 150 for i in range(300)]  # 300 groups -> 13 descriptor-upload launches
     prob = pkg.workloads.make_problem("g300", ms, 128, 256, seed=3, device="cuda")
-    run_custom_kernel(pkg, prob)
+    run_custom_kernel(pkg, prob, cta=cta)
     check_problem(prob)
 
 
@@ -246,9 +256,10 @@ def test_cfg1_cpu_reference_config(pkg):
     check_problem(prob)
 
 
-def test_cfg2_full_size(pkg):
+@pytest.mark.parametrize("cta", ["pair", "single"])
+def test_cfg2_full_size(pkg, cta):
     prob = pkg.workloads.make_config("cfg2", seed=2, device="cuda")
-    run_custom_kernel(pkg, prob)
+    run_custom_kernel(pkg, prob, cta=cta)
     check_problem(prob)
     assert pkg.check_device_errors() == 0
 
@@ -260,9 +271,10 @@ def test_cfg4_skewed_full_size(pkg):
     check_problem(prob)
 
 
-def test_cfg3_gated_full_size(pkg):
+@pytest.mark.parametrize("cta", ["pair", "single"])
+def test_cfg3_gated_full_size(pkg, cta):
     prob = pkg.workloads.make_config("cfg3", seed=3, device="cuda")
-    run_custom_kernel(pkg, prob)
+    run_custom_kernel(pkg, prob, cta=cta)
     check_problem(prob)
 
 
