@@ -56,40 +56,6 @@ struct PairConfig {
   static constexpr uint32_t kEpilogueArrivals = 2 * kEpilogueWarps;
 };
 
-// Bounded wait with cluster-scope acquire (barriers that the other CTA arrives on).
-__device__ __forceinline__ bool wait_phase_cluster(uint64_t* bar, uint32_t parity,
-                                                   volatile uint32_t* abort_flag,
-                                                   uint32_t* error_bits, uint32_t reason) {
-  if (ptx::mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = ptx::globaltimer_ns();
-  uint32_t spins = 0;
-  while (true) {
-    if (ptx::mbar_try_wait_cluster(bar, parity)) return true;
-    if ((++spins & 31u) == 0) {
-      if (*abort_flag) return false;
-      if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
-        *abort_flag = 1u;
-        atomicOr(error_bits, reason);
-        return false;
-      }
-    }
-  }
-}
-
-__device__ __forceinline__ bool warp_wait_phase_cluster(uint64_t* bar, uint32_t parity,
-                                                        volatile uint32_t* abort_flag,
-                                                        uint32_t* error_bits, uint32_t reason,
-                                                        int lane) {
-  int ok = 1;
-  if (lane == 0) ok = wait_phase_cluster(bar, parity, abort_flag, error_bits, reason) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  if (ok) {
-    for (uint32_t i = 0; i < (1u << 20) && !ptx::mbar_try_wait_cluster(bar, parity); ++i) {
-    }
-  }
-  return ok != 0;
-}
-
 template <bool GATED, int STAGES>
 __global__ void __launch_bounds__(kNumThreads, 1)
     nvfp4_grouped_gemm_pair_kernel(const __grid_constant__ GemmParams p) {
@@ -186,7 +152,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         for (int kp = 0; kp < kL2PrefetchKTiles && kp < ktiles; ++kp) prefetch_ktile(kp);
         for (int kt = 0; kt < ktiles; ++kt) {
           if (kt + kL2PrefetchKTiles < ktiles) prefetch_ktile(kt + kL2PrefetchKTiles);
-          if (!wait_phase_cluster(&empty_bar[stage], phase ^ 1u, abort_flag, p.error_bits,
+          if (!wait_phase(&empty_bar[stage], phase ^ 1u, abort_flag, p.error_bits,
                                   kDevErrProducerTimeout)) {
             ok = false;
             break;
@@ -226,7 +192,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const uint32_t s = n % STAGES;
           const uint32_t ph = (n / STAGES) & 1u;
           const uint64_t t0 = ptx::globaltimer_ns();
-          while (!ptx::mbar_try_wait_cluster(&full_bar[s], ph)) {
+          while (!ptx::mbar_try_wait(&full_bar[s], ph)) {
             if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
               atomicOr(p.error_bits, kDevErrDrainTimeout);
               break;
@@ -248,7 +214,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         g = advance_group(groups, p.num_groups, g, tile);
         const int ktiles = groups[g].k / kBlockK;
         const int acc = static_cast<int>(local & 1u);
-        if (!wait_phase_cluster(&acce_bar[acc], (acc_parity >> acc) & 1u, abort_flag,
+        if (!wait_phase(&acce_bar[acc], (acc_parity >> acc) & 1u, abort_flag,
                                 p.error_bits, kDevErrAccTimeout)) {
           break;
         }
@@ -256,7 +222,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         ptx::tcgen05_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
         for (int kt = 0; kt < ktiles; ++kt) {
-          if (!wait_phase_cluster(&full_bar[stage], phase, abort_flag, p.error_bits,
+          if (!wait_phase(&full_bar[stage], phase, abort_flag, p.error_bits,
                                   kDevErrMmaTimeout)) {
             ok = false;
             break;
@@ -329,7 +295,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const int mt = tl % gd.tiles_m;
       const int nt = tl / gd.tiles_m;
       const int acc = static_cast<int>(local & 1u);
-      if (!warp_wait_phase_cluster(&accf_bar[acc], (full_parity >> acc) & 1u, abort_flag,
+      if (!warp_wait_phase(&accf_bar[acc], (full_parity >> acc) & 1u, abort_flag,
                                    p.error_bits, kDevErrEpilogueTimeout, lane)) {
         break;
       }

@@ -314,23 +314,12 @@ __device__ __forceinline__ void cluster_sync_all() {
                    "memory");
 }
 
-// Arrive on an mbarrier of another CTA of the cluster (shared::cluster address).
+// Arrive on an mbarrier of a CTA of this cluster (shared::cluster address; may be
+// this CTA's own barrier). Default (CTA-scope) semantics: the barriers order the
+// tcgen05 / TMA work of the pair, not generic-memory data, so no cluster-scope
+// fence is needed on either side.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
-
-// Probe with cluster-scope acquire (for barriers that other CTAs arrive on).
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // Tiled loads of a CTA pair: the data lands in this CTA's shared memory, the
