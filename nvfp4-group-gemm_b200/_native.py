@@ -108,7 +108,9 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
     with _lib_lock:
         if _lib is not None and path is None:
             return _lib
-        p = path or LIB_PATH
+        # NVFP4_LIBRARY selects another build of the same library (same ABI), e.g. one
+        # compiled with different tuning constants.
+        p = path or os.environ.get("NVFP4_LIBRARY") or LIB_PATH
         if not os.path.exists(p):
             raise ImportError(
                 f"native library {p} is missing; build it with "

@@ -40,6 +40,12 @@ constexpr int kTmemCols = 512;
 // tile walk K in lockstep, so without this every one of them waits on the same DRAM
 // miss at every k-step; the prefetch turns those misses into L2 hits.
 constexpr int kL2PrefetchKTiles = 6;
+// Which producers warm L2: 0 none, 1 one per shared tile (B by the CTAs on the first
+// m-tile of a group, A by those on its first n-tile), 2 every producer for its own tiles.
+#ifndef NVFP4_L2_PREFETCH
+#define NVFP4_L2_PREFETCH 1
+#endif
+constexpr int kL2PrefetchMode = NVFP4_L2_PREFETCH;
 
 template <int MMA_N, bool GATED, int STAGES>
 struct GemmConfig {
@@ -207,26 +213,34 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const uint32_t tx = Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes +
                             (sfb_blk1 != nullptr ? 2 : 1) * 4 * kSfBlockBytes;
         // L2 warm-up of k-tile `kp` of this tile (A, B halves, scale blocks).
+        const bool warm_a = kL2PrefetchMode == 2 || (kL2PrefetchMode == 1 && nt == 0);
+        const bool warm_b = kL2PrefetchMode == 2 || (kL2PrefetchMode == 1 && mt == 0);
         auto prefetch_ktile = [&](int kp) {
           const int px = kp * kRowBytesPerStage;
           const size_t psf = static_cast<size_t>(kp) * 4 * kSfBlockBytes;
-          ptx::tma_prefetch_l2_2d(&maps[kMapA], px, mt * kBlockM);
-          if (GATED) {
-            ptx::tma_prefetch_l2_2d(&maps[kMapB], px, nt * 128);
-            ptx::tma_prefetch_l2_2d(&maps[kMapB2], px, nt * 128);
-          } else if (MMA_N == 256) {
-            ptx::tma_prefetch_l2_2d(&maps[kMapB], px, nt * 256);
-            ptx::tma_prefetch_l2_2d(&maps[kMapB], px, nt * 256 + 128);
-          } else {
-            ptx::tma_prefetch_l2_2d(&maps[kMapB], px, nt * 128);
+          if (warm_a) {
+            ptx::tma_prefetch_l2_2d(&maps[kMapA], px, mt * kBlockM);
+            ptx::bulk_prefetch_l2(sfa_blk + psf, 4 * kSfBlockBytes);
           }
-          ptx::bulk_prefetch_l2(sfa_blk + psf, 4 * kSfBlockBytes);
-          ptx::bulk_prefetch_l2(sfb_blk0 + psf, 4 * kSfBlockBytes);
-          if (sfb_blk1 != nullptr) ptx::bulk_prefetch_l2(sfb_blk1 + psf, 4 * kSfBlockBytes);
+          if (warm_b) {
+            if (GATED) {
+              ptx::tma_prefetch_l2_2d(&maps[kMapB], px, nt * 128);
+              ptx::tma_prefetch_l2_2d(&maps[kMapB2], px, nt * 128);
+            } else if (MMA_N == 256) {
+              ptx::tma_prefetch_l2_2d(&maps[kMapB], px, nt * 256);
+              ptx::tma_prefetch_l2_2d(&maps[kMapB], px, nt * 256 + 128);
+            } else {
+              ptx::tma_prefetch_l2_2d(&maps[kMapB], px, nt * 128);
+            }
+            ptx::bulk_prefetch_l2(sfb_blk0 + psf, 4 * kSfBlockBytes);
+            if (sfb_blk1 != nullptr) ptx::bulk_prefetch_l2(sfb_blk1 + psf, 4 * kSfBlockBytes);
+          }
         };
-        for (int kp = 0; kp < kL2PrefetchKTiles && kp < ktiles; ++kp) prefetch_ktile(kp);
+        if (warm_a || warm_b)
+          for (int kp = 0; kp < kL2PrefetchKTiles && kp < ktiles; ++kp) prefetch_ktile(kp);
         for (int kt = 0; kt < ktiles; ++kt) {
-          if (kt + kL2PrefetchKTiles < ktiles) prefetch_ktile(kt + kL2PrefetchKTiles);
+          if ((warm_a || warm_b) && kt + kL2PrefetchKTiles < ktiles)
+            prefetch_ktile(kt + kL2PrefetchKTiles);
           if (!wait_phase(&empty_bar[stage], phase ^ 1u, abort_flag, p.error_bits,
                           kDevErrProducerTimeout)) {
             ok = false;

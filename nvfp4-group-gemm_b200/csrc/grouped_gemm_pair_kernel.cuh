@@ -137,21 +137,30 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         // This CTA's half of the MMA's B rows.
         const TmaDesc* map_b = (GATED && rank == 1) ? &maps[kMapB2] : &maps[kMapB];
         const int row_b = GATED ? nt * 128 : nt * 256 + 128 * static_cast<int>(rank);
-        // Scale blocks (in 8-byte elements of the 1-D maps; a block out of range reads as 0).
-        const int sfa_x0 = (2 * mt + static_cast<int>(rank)) * rest_k * 64;
+        // Scale blocks, in 128-byte rows of the scale maps (16 rows = one k-tile of a
+        // 128-row block; a block out of range reads as 0).
+        const int sfa_y0 = (2 * mt + static_cast<int>(rank)) * rest_k * 4;
         const TmaDesc* map_sfb1 = GATED ? &maps[kMapSfb2] : &maps[kMapSfb];
-        const int sfb0_x0 = (GATED ? nt : 2 * nt) * rest_k * 64;
-        const int sfb1_x0 = (GATED ? nt : 2 * nt + 1) * rest_k * 64;
+        const int sfb0_y0 = (GATED ? nt : 2 * nt) * rest_k * 4;
+        const int sfb1_y0 = (GATED ? nt : 2 * nt + 1) * rest_k * 4;
+        const bool warm_a = kL2PrefetchMode == 2 || (kL2PrefetchMode == 1 && nt == 0);
+        const bool warm_b = kL2PrefetchMode == 2 || (kL2PrefetchMode == 1 && mt == 0);
         auto prefetch_ktile = [&](int kp) {
-          ptx::tma_prefetch_l2_2d(&maps[kMapA], kp * kRowBytesPerStage, row_a);
-          ptx::tma_prefetch_l2_2d(map_b, kp * kRowBytesPerStage, row_b);
-          ptx::tma_prefetch_l2_1d(&maps[kMapSfa], sfa_x0 + kp * 256);
-          ptx::tma_prefetch_l2_1d(&maps[kMapSfb], sfb0_x0 + kp * 256);
-          ptx::tma_prefetch_l2_1d(map_sfb1, sfb1_x0 + kp * 256);
+          if (warm_a) {
+            ptx::tma_prefetch_l2_2d(&maps[kMapA], kp * kRowBytesPerStage, row_a);
+            ptx::tma_prefetch_l2_2d(&maps[kMapSfa], 0, sfa_y0 + kp * 16);
+          }
+          if (warm_b) {
+            ptx::tma_prefetch_l2_2d(map_b, kp * kRowBytesPerStage, row_b);
+            ptx::tma_prefetch_l2_2d(&maps[kMapSfb], 0, sfb0_y0 + kp * 16);
+            ptx::tma_prefetch_l2_2d(map_sfb1, 0, sfb1_y0 + kp * 16);
+          }
         };
-        for (int kp = 0; kp < kL2PrefetchKTiles && kp < ktiles; ++kp) prefetch_ktile(kp);
+        if (warm_a || warm_b)
+          for (int kp = 0; kp < kL2PrefetchKTiles && kp < ktiles; ++kp) prefetch_ktile(kp);
         for (int kt = 0; kt < ktiles; ++kt) {
-          if (kt + kL2PrefetchKTiles < ktiles) prefetch_ktile(kt + kL2PrefetchKTiles);
+          if ((warm_a || warm_b) && kt + kL2PrefetchKTiles < ktiles)
+            prefetch_ktile(kt + kL2PrefetchKTiles);
           if (!wait_phase(&empty_bar[stage], phase ^ 1u, abort_flag, p.error_bits,
                                   kDevErrProducerTimeout)) {
             ok = false;
@@ -172,10 +181,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const int kx = kt * kRowBytesPerStage;
           ptx::tma_load_2d_pair(sA, &maps[kMapA], full_leader, kx, row_a);
           ptx::tma_load_2d_pair(sB, map_b, full_leader, kx, row_b);
-          ptx::tma_load_1d_pair(sSFA, &maps[kMapSfa], full_leader, sfa_x0 + kt * 256);
-          ptx::tma_load_1d_pair(sSFB, &maps[kMapSfb], full_leader, sfb0_x0 + kt * 256);
-          ptx::tma_load_1d_pair(sSFB + 4 * kSfBlockBytes, map_sfb1, full_leader,
-                                sfb1_x0 + kt * 256);
+          ptx::tma_load_2d_pair(sSFA, &maps[kMapSfa], full_leader, 0, sfa_y0 + kt * 16);
+          ptx::tma_load_2d_pair(sSFB, &maps[kMapSfb], full_leader, 0, sfb0_y0 + kt * 16);
+          ptx::tma_load_2d_pair(sSFB + 4 * kSfBlockBytes, map_sfb1, full_leader, 0,
+                                sfb1_y0 + kt * 16);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;

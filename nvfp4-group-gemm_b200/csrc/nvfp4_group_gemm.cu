@@ -226,8 +226,8 @@ enum : uint32_t { kKindOperand = 0, kKindOutput = 1, kKindScales = 2 };
 // kKindOperand: e2m1 operand [rows, row_elems bytes] (uint8 view), box 128 B x 128 rows,
 //   128B swizzle, zero fill outside the tensor.
 // kKindOutput:  fp16 output [rows, row_elems], box 64 x 32, 128B swizzle.
-// kKindScales:  blocked scale bytes as row_elems 8-byte elements (1-D), box 256
-//   elements = one 2-KiB k-tile chunk of a 128-row block, zero fill outside.
+// kKindScales:  blocked scale bytes as `rows` rows of 128 bytes, box 128 B x 16 rows =
+//   one 2-KiB k-tile chunk of a 128-row block, zero fill outside.
 bool encode_map_uncached(uint32_t kind, const void* addr, uint32_t rows, uint32_t row_elems,
                          TmaDesc* out) {
   CUtensorMap m;
@@ -248,10 +248,10 @@ bool encode_map_uncached(uint32_t kind, const void* addr, uint32_t rows, uint32_
                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   } else {
-    cuuint64_t dims[1] = {row_elems};
-    cuuint64_t strides[1] = {0};  // rank 1: no strides are read
-    cuuint32_t box[1] = {256};
-    r = g_encoder.fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 1, const_cast<void*>(addr), dims, strides,
+    cuuint64_t dims[2] = {128, rows};
+    cuuint64_t strides[1] = {128};
+    cuuint32_t box[2] = {128, 16};
+    r = g_encoder.fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(addr), dims, strides,
                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   }
@@ -401,17 +401,17 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
         memset(mp, 0, sizeof(TmaDesc) * kMapsPerGroup);
         if (rec[i].tile_end == rec[i].tile_start) continue;  // empty group: maps never read
         const uint32_t kb = static_cast<uint32_t>(gr.k / 2);
-        // Blocked scale bytes of an R-row operand, in 8-byte elements.
-        const uint32_t sfa_e = static_cast<uint32_t>(((gr.m + 127) / 128) * (gr.k / 64) * 64);
-        const uint32_t sfb_e = static_cast<uint32_t>(((gr.n + 127) / 128) * (gr.k / 64) * 64);
+        // Blocked scale bytes of an R-row operand, in rows of 128 bytes.
+        const uint32_t sfa_rows = static_cast<uint32_t>(((gr.m + 127) / 128) * (gr.k / 64) * 4);
+        const uint32_t sfb_rows = static_cast<uint32_t>(((gr.n + 127) / 128) * (gr.k / 64) * 4);
         bool ok = encode_map(kKindOperand, gr.a, gr.m, kb, &mp[kMapA], use_cache) &&
                   encode_map(kKindOperand, gr.b, gr.n, kb, &mp[kMapB], use_cache) &&
                   encode_map(kKindOutput, gr.c, gr.m, gr.n, &mp[kMapC], use_cache) &&
-                  encode_map(kKindScales, gr.sfa, 1, sfa_e, &mp[kMapSfa], use_cache) &&
-                  encode_map(kKindScales, gr.sfb, 1, sfb_e, &mp[kMapSfb], use_cache) &&
+                  encode_map(kKindScales, gr.sfa, sfa_rows, 128, &mp[kMapSfa], use_cache) &&
+                  encode_map(kKindScales, gr.sfb, sfb_rows, 128, &mp[kMapSfb], use_cache) &&
                   (!gated ||
                    (encode_map(kKindOperand, gr.b2, gr.n, kb, &mp[kMapB2], use_cache) &&
-                    encode_map(kKindScales, gr.sfb2, 1, sfb_e, &mp[kMapSfb2], use_cache)));
+                    encode_map(kKindScales, gr.sfb2, sfb_rows, 128, &mp[kMapSfb2], use_cache)));
         if (!ok) return fail(NVFP4_ERR_DRIVER, "group %d: cuTensorMapEncodeTiled rejected a tensor", i);
       }
       nvfp4_upload_descriptors_kernel<<<count, 32, 0, s>>>(up);

@@ -25,9 +25,9 @@ struct alignas(64) TmaDesc {
 };
 static_assert(sizeof(TmaDesc) == 128, "tensor map image must be 128 bytes");
 
-// Tensor maps kept per group, in this order. The scale-factor maps are 1-D views of
-// the blocked scale bytes as 8-byte elements (one box = 256 elements = one 2-KiB k-tile
-// chunk of a 128-row block); the CTA-pair kernel loads scales through them.
+// Tensor maps kept per group, in this order. The scale-factor maps view the blocked
+// scale bytes as rows of 128 bytes (one box = 16 rows = one 2-KiB k-tile chunk of a
+// 128-row block); the CTA-pair kernel loads scales through them.
 enum : int {
   kMapA = 0, kMapB = 1, kMapB2 = 2, kMapC = 3, kMapSfa = 4, kMapSfb = 5, kMapSfb2 = 6,
   kMapsPerGroup = 8
