@@ -55,7 +55,8 @@ typedef enum nvfp4_status {
 #define NVFP4_FLAG_CTA_PAIR 0x10u   /* force 256-row tiles on CTA pairs (tcgen05 cta_group::2) */
 #define NVFP4_FLAG_SINGLE_CTA 0x20u /* force 128-row tiles on single CTAs.
                                        Default: CTA pairs when the non-empty groups average
-                                       at least 192 rows, single CTAs otherwise */
+                                       at least 192 rows, or at least 96 rows with
+                                       K >= 4096; single CTAs otherwise */
 
 /*
  * One GEMM of the group. All matrices are row-major with K innermost ("K-major"),

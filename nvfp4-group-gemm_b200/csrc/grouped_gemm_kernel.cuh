@@ -42,10 +42,17 @@ constexpr int kTmemCols = 512;
 constexpr int kL2PrefetchKTiles = 6;
 // Which producers warm L2: 0 none, 1 one per shared tile (B by the CTAs on the first
 // m-tile of a group, A by those on its first n-tile), 2 every producer for its own tiles.
-#ifndef NVFP4_L2_PREFETCH
-#define NVFP4_L2_PREFETCH 1
+// Measured on cfg2 (G=8, 1024 x 4096 x 7168): single-CTA tiles 108.8 / 119.1 / 133.3 us
+// with modes 1 / 0 / 2; CTA-pair tiles 97.0 / 96.3 / 111.4 us (their deeper ring needs no
+// warm-up, and every prefetch is an extra L2 request).
+#ifndef NVFP4_L2_PREFETCH_SINGLE
+#define NVFP4_L2_PREFETCH_SINGLE 1
 #endif
-constexpr int kL2PrefetchMode = NVFP4_L2_PREFETCH;
+#ifndef NVFP4_L2_PREFETCH_PAIR
+#define NVFP4_L2_PREFETCH_PAIR 0
+#endif
+constexpr int kL2PrefetchMode = NVFP4_L2_PREFETCH_SINGLE;
+constexpr int kL2PrefetchModePair = NVFP4_L2_PREFETCH_PAIR;
 
 template <int MMA_N, bool GATED, int STAGES>
 struct GemmConfig {

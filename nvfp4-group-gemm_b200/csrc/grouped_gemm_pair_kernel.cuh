@@ -143,8 +143,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const TmaDesc* map_sfb1 = GATED ? &maps[kMapSfb2] : &maps[kMapSfb];
         const int sfb0_y0 = (GATED ? nt : 2 * nt) * rest_k * 4;
         const int sfb1_y0 = (GATED ? nt : 2 * nt + 1) * rest_k * 4;
-        const bool warm_a = kL2PrefetchMode == 2 || (kL2PrefetchMode == 1 && nt == 0);
-        const bool warm_b = kL2PrefetchMode == 2 || (kL2PrefetchMode == 1 && mt == 0);
+        const bool warm_a = kL2PrefetchModePair == 2 || (kL2PrefetchModePair == 1 && nt == 0);
+        const bool warm_b = kL2PrefetchModePair == 2 || (kL2PrefetchModePair == 1 && mt == 0);
         auto prefetch_ktile = [&](int kp) {
           if (warm_a) {
             ptx::tma_prefetch_l2_2d(&maps[kMapA], kp * kRowBytesPerStage, row_a);

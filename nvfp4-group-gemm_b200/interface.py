@@ -140,7 +140,8 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
     the launch is gated: ``c = fp16(silu(fp16(alpha*A.B^T)) * fp16(alpha2*A.B2^T))``.
     ``cta`` forces 256-row tiles on CTA pairs (``"pair"``) or 128-row tiles on single
     CTAs (``"single"``); by default the library picks pairs when the groups average
-    at least 192 rows. ``tile_n`` (128 or 256) applies to single-CTA tiles.
+    at least 192 rows (96 with K >= 4096). ``tile_n`` (128 or 256) applies to
+    single-CTA tiles.
     """
     if cta not in (None, "pair", "single"):
         raise ValueError(f"cta must be None, 'pair' or 'single', got {cta!r}")
