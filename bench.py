@@ -229,8 +229,21 @@ def main():
         step()
     torch.cuda.synchronize(dev)
     barrier()
+    # Clocks are sampled every 200 ms across a load window that contains the timed
+    # region: ~1 s of back-to-back calls before it and ~0.5 s after it, so that the
+    # samples show the clock the timed calls ran at (the timed region itself is short).
     clocks = ClockSampler(local_rank, enabled=not args.no_clocks)
-    time.sleep(0.3 if not args.no_clocks else 0.0)
+
+    def sustain(seconds: float) -> None:
+        if args.no_clocks:
+            return
+        t_end = time.perf_counter() + seconds
+        while time.perf_counter() < t_end:
+            for _ in range(50):
+                step()
+            torch.cuda.synchronize(dev)
+
+    sustain(1.0)
     barrier()
     torch.cuda.synchronize(dev)
     ev0 = torch.cuda.Event(enable_timing=True)
@@ -243,6 +256,7 @@ def main():
     ev1.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
+    sustain(0.5)
     clk = clocks.stop()
     ms_total = max_over_ranks(ev0.elapsed_time(ev1))
     ms_per_step = ms_total / args.steps
@@ -294,7 +308,7 @@ def main():
     peaks, peak_kind = load_peaks()
     tensor_peak = FP4_PER_BF16 * float(peaks["bf16_tflops"])
     achieved = flops_rank / (ms_per_step * 1e-3) / 1e12
-    kernel_tag = "gated" if prob.gated else f"n{args.tile_n or 256}"
+    kernel_tag = args.cta or ("single" if args.tile_n else "auto")
     traffic = load_traffic(kernel_tag, args.config)
     line = {
         "metric": f"NVFP4 grouped GEMM TFLOP/s ({args.config})",
@@ -317,7 +331,7 @@ def main():
                    "input_bytes_per_gpu": prob.input_bytes(),
                    "l2": "inputs larger than L2 (126 MB); no flush",
                    "parallelism": f"ep{world} (experts sharded, no data-path collective)"},
-        "gpu_launches": args.steps,  # one persistent GEMM kernel per call (descriptors reused)
+        "gpu_launches": args.steps,  # one persistent GEMM kernel per timed call (descriptors reused)
         "device_error_bits": errors,
         "e2e": {"value": flops_rank * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
