@@ -53,6 +53,11 @@ typedef enum nvfp4_status {
                                              (same pointers, sizes, scales, flags) from the
                                              previous call on the same stream: skip rebuilding */
 #define NVFP4_FLAG_CTA_PAIR 0x10u   /* force 256-row tiles on CTA pairs (tcgen05 cta_group::2) */
+#define NVFP4_FLAG_DIAG_SKIP_MMA 0x40u /* diagnostic, for testing failure detection only: the
+                                          MMA issuer issues nothing, so the kernel's bounded
+                                          waits run out (about 2 s), it records the reason in
+                                          the workspace error word and exits cleanly; the
+                                          output is not written */
 #define NVFP4_FLAG_SINGLE_CTA 0x20u /* force 128-row tiles on single CTAs.
                                        Default: CTA pairs when the non-empty groups average
                                        at least 192 rows, or at least 96 rows with

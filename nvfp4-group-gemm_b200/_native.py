@@ -34,6 +34,14 @@ FLAG_TILE_N256 = 0x4
 FLAG_REUSE_DESCRIPTORS = 0x8
 FLAG_CTA_PAIR = 0x10
 FLAG_SINGLE_CTA = 0x20
+FLAG_DIAG_SKIP_MMA = 0x40
+
+# Device error bits (WorkspaceHeader::error_bits).
+DEV_ERR_PRODUCER_TIMEOUT = 1 << 0
+DEV_ERR_MMA_TIMEOUT = 1 << 1
+DEV_ERR_ACC_TIMEOUT = 1 << 2
+DEV_ERR_EPILOGUE_TIMEOUT = 1 << 3
+DEV_ERR_DRAIN_TIMEOUT = 1 << 4
 
 # Every symbol the public header declares; the library must export all of them.
 EXPORTED_SYMBOLS = (

@@ -312,7 +312,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t acc_parity = Cfg::kOverlapAcc ? 0x1u : 0x3u;  // bit s: parity for stage s
       uint32_t local = 0;
       int g = 0;
-      bool ok = true;
+      bool ok = p.diag_skip_mma == 0;
       for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x, ++local) {
         g = advance_group(groups, p.num_groups, g, tile);
         const int ktiles = groups[g].k / kBlockK;

@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t acc_parity = 0x1u;  // overlapped stages: only the first tile passes freely
       uint32_t local = 0;
       int g = 0;
-      bool ok = true;
+      bool ok = p.diag_skip_mma == 0;
       for (int tile = cluster; ok && tile < p.total_tiles; tile += num_clusters, ++local) {
         g = advance_group(groups, p.num_groups, g, tile);
         const int ktiles = groups[g].k / kBlockK;

@@ -431,6 +431,7 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
   gp.error_bits = reinterpret_cast<uint32_t*>(ws);
   gp.num_groups = num_groups;
   gp.total_tiles = static_cast<int32_t>(total_tiles);
+  gp.diag_skip_mma = (flags & NVFP4_FLAG_DIAG_SKIP_MMA) ? 1 : 0;
   if (pair) {
     const int max_clusters = gated ? ds.pair_clusters_gated : ds.pair_clusters;
     const int clusters = static_cast<int>(std::min<int64_t>(total_tiles, max_clusters));
@@ -451,7 +452,7 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
 int check_common_args(const nvfp4_group* groups, int num_groups, unsigned int flags) {
   const unsigned known = NVFP4_FLAG_GATED | NVFP4_FLAG_TILE_N128 | NVFP4_FLAG_TILE_N256 |
                          NVFP4_FLAG_REUSE_DESCRIPTORS | NVFP4_FLAG_CTA_PAIR |
-                         NVFP4_FLAG_SINGLE_CTA;
+                         NVFP4_FLAG_SINGLE_CTA | NVFP4_FLAG_DIAG_SKIP_MMA;
   if (flags & ~known) return fail(NVFP4_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags & ~known);
   if (num_groups < 0) return fail(NVFP4_ERR_INVALID_ARGUMENT, "num_groups=%d", num_groups);
   if (num_groups > 0 && groups == nullptr)

@@ -89,6 +89,7 @@ struct GemmParams {
   uint32_t* error_bits;
   int32_t num_groups;
   int32_t total_tiles;
+  int32_t diag_skip_mma;  // NVFP4_FLAG_DIAG_SKIP_MMA: the MMA issuer does no work
 };
 
 }  // namespace nvfp4
