@@ -89,10 +89,19 @@ class ClockSampler:
         if not enabled:
             return
         try:
+            import torch
+
+            # nvidia-smi numbers GPUs physically; the UUID names this process's device
+            # whatever CUDA_VISIBLE_DEVICES maps it to.
+            ident = str(gpu_index)
+            uuid = getattr(torch.cuda.get_device_properties(gpu_index), "uuid", None)
+            if uuid is not None:
+                u = str(uuid)
+                ident = u if u.startswith("GPU-") else f"GPU-{u}"
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", f"--id={ident}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
