@@ -13,7 +13,9 @@ Our arm (default):
     copies the operands from pinned host memory, calls custom_kernel and copies
     the fp16 outputs back.
   * `roofline`: the grouped-GEMM kernel against the dense FP4 tensor peak derived
-    from MEASURED_PEAKS.json (4 x the measured cuBLAS bf16 figure).
+    from MEASURED_PEAKS.json (4 x the measured cuBLAS bf16 figure: the sustained one for
+    `value`, which is timed after a 1 s load window with the clocks sampled around it;
+    `burst` reports the same calls timed right after warm-up against the burst figure).
   * `cpu_baseline`: the CPU oracle (numpy restatement of the reference's
     ref_kernel) on the full configuration, rank 0 at N=1 only.
 With N GPUs each rank runs its own set of experts of the same shape (weak scaling;
@@ -238,6 +240,23 @@ def main():
         step()
     torch.cuda.synchronize(dev)
     barrier()
+
+    def timed(n: int) -> float:
+        """Device time of n back-to-back calls (ms), max over ranks."""
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1))
+
+    # Burst: right after warm-up, before the GPU reaches its power limit.
+    burst_ms = timed(args.steps) / args.steps
     # Clocks are sampled every 200 ms across a load window that contains the timed
     # region: ~1 s of back-to-back calls before it and ~0.5 s after it, so that the
     # samples show the clock the timed calls ran at (the timed region itself is short).
@@ -315,8 +334,13 @@ def main():
         return
 
     peaks, peak_kind = load_peaks()
-    tensor_peak = FP4_PER_BF16 * float(peaks["bf16_tflops"])
+    # `value` is timed inside a sustained-load window (the clocks above describe it), so
+    # its roofline uses the sustained bf16 figure; the burst timing uses the burst one.
+    sustained_key = "bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks else "bf16_tflops"
+    tensor_peak = FP4_PER_BF16 * float(peaks[sustained_key])
+    burst_peak = FP4_PER_BF16 * float(peaks["bf16_tflops"])
     achieved = flops_rank / (ms_per_step * 1e-3) / 1e12
+    burst_tflops = flops_rank / (burst_ms * 1e-3) / 1e12
     kernel_tag = args.cta or ("single" if args.tile_n else "auto")
     traffic = load_traffic(kernel_tag, args.config)
     line = {
@@ -345,9 +369,13 @@ def main():
         "e2e": {"value": flops_rank * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "custom_kernel(data) with pinned-host copies of inputs and outputs"},
+        "burst": {"us_per_call": burst_ms * 1e3, "tflops_per_gpu": burst_tflops,
+                  "frac_of_burst_peak": burst_tflops / burst_peak,
+                  "note": "timed right after warm-up, before the power limit engages"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": tensor_peak,
                      "unit": "TFLOP/s", "frac": achieved / tensor_peak,
-                     "peak_source": f"{peak_kind}: 4 x bf16_tflops ({peaks['bf16_tflops']})",
+                     "peak_source": f"{peak_kind}: 4 x {sustained_key} "
+                                    f"({peaks[sustained_key]}; timed under sustained load)",
                      "traffic": traffic,
                      "algorithmic_bytes": prob.algorithmic_bytes(),
                      "hbm_frac": prob.algorithmic_bytes() / (ms_per_step * 1e-3) / 1e9
