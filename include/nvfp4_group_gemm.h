@@ -95,7 +95,7 @@ typedef struct nvfp4_group {
 
 /*
  * Device workspace bytes needed for `num_groups` groups (group records, tensor
- * maps and a device error word): 256 + 80 * num_groups rounded up to 128, plus
+ * maps and a device error word): 256 + 64 * num_groups rounded up to 128, plus
  * 1024 * num_groups. The workspace is owned by the caller, must be
  * 256-byte aligned, must not be shared by calls that may run concurrently, and
  * may be reused by consecutive calls on one stream.
@@ -141,7 +141,7 @@ NVFP4_API const char* nvfp4_last_error_detail(void);
  * hands them their input and output buffers, and latency-critical paths that
  * cannot afford cudaMalloc's implicit device synchronisation. Instead of a caller-provided
  * workspace it uses a scratch array compiled into the library
- * (nvfp4_workspace_size(NVFP4_NOALLOC_MAX_GROUPS) bytes, about 552 KiB, held on
+ * (nvfp4_workspace_size(NVFP4_NOALLOC_MAX_GROUPS) bytes, about 544 KiB, held on
  * every GPU that loads the library until the process exits). It calls no
  * cudaMalloc/cudaFree and no allocating library routine.
  *

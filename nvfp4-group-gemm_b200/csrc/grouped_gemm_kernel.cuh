@@ -53,13 +53,6 @@ constexpr int kL2PrefetchKTiles = 6;
 #endif
 constexpr int kL2PrefetchMode = NVFP4_L2_PREFETCH_SINGLE;
 constexpr int kL2PrefetchModePair = NVFP4_L2_PREFETCH_PAIR;
-// Whole-row warm-up: at the start of each tile the single-CTA producer prefetches every
-// B row of the tile in one contiguous bulk prefetch (K/2 bytes per row), so DRAM serves
-// long runs instead of 128-byte slices at the row stride.
-#ifndef NVFP4_ROW_PREFETCH
-#define NVFP4_ROW_PREFETCH 0
-#endif
-constexpr bool kRowPrefetch = NVFP4_ROW_PREFETCH != 0;
 
 template <int MMA_N, bool GATED, int STAGES>
 struct GemmConfig {
@@ -250,19 +243,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (sfb_blk1 != nullptr) ptx::bulk_prefetch_l2(sfb_blk1 + psf, 4 * kSfBlockBytes);
           }
         };
-        if (kRowPrefetch && gd.b_ptr != nullptr) {
-          const uint32_t row_bytes = static_cast<uint32_t>(gd.k / 2);
-          const int rows_here = GATED ? 128 : MMA_N;
-          const int row0_b = GATED ? nt * 128 : nt * MMA_N;
-          for (int r = 0; r < rows_here; ++r) {
-            if (row0_b + r >= gd.n) break;
-            ptx::bulk_prefetch_l2(gd.b_ptr + static_cast<size_t>(row0_b + r) * row_bytes,
-                                  row_bytes);
-            if (GATED)
-              ptx::bulk_prefetch_l2(gd.b2_ptr + static_cast<size_t>(row0_b + r) * row_bytes,
-                                    row_bytes);
-          }
-        }
         if (warm_a || warm_b)
           for (int kp = 0; kp < kL2PrefetchKTiles && kp < ktiles; ++kp) prefetch_ktile(kp);
         for (int kt = 0; kt < ktiles; ++kt) {

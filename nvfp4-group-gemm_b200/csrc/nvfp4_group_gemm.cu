@@ -368,8 +368,6 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
     d.sfa = static_cast<const uint8_t*>(gr.sfa);
     d.sfb = static_cast<const uint8_t*>(gr.sfb);
     d.sfb2 = gated ? static_cast<const uint8_t*>(gr.sfb2) : nullptr;
-    d.b_ptr = static_cast<const uint8_t*>(gr.b);
-    d.b2_ptr = gated ? static_cast<const uint8_t*>(gr.b2) : nullptr;
     d.tiles_m = (gr.m + tile_m - 1) / tile_m;
     total_tiles += static_cast<int64_t>(d.tiles_m) * ((gr.n + out_n - 1) / out_n);
     if (total_tiles > (int64_t{1} << 30))

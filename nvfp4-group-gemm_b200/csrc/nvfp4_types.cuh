@@ -38,14 +38,12 @@ struct GroupDev {
   const uint8_t* sfa;   // 128x4-blocked E4M3 scales of A
   const uint8_t* sfb;   // blocked scales of B (gate weights when gated)
   const uint8_t* sfb2;  // blocked scales of the up weights (gated only)
-  const uint8_t* b_ptr;   // B (gate) rows, for L2 warm-up
-  const uint8_t* b2_ptr;  // up rows (gated only)
   int32_t m, n, k;
   int32_t tiles_m;
   int32_t tile_start, tile_end;  // [start, end) in the launch-wide tile order
   float alpha, alpha2;
 };
-static_assert(sizeof(GroupDev) <= 80, "group record must fit its workspace slot");
+static_assert(sizeof(GroupDev) <= 64, "group record must fit its workspace slot");
 
 struct WorkspaceHeader {
   uint32_t error_bits;  // OR of device-side failure reasons (see kDevErr*)
@@ -62,10 +60,10 @@ enum : uint32_t {
   kDevErrDrainTimeout = 1u << 4,     // in-flight copies or MMAs did not finish at exit
 };
 
-// Workspace layout: header | GroupDev[G] (80 B each) | TmaDesc[G][8] (128 B aligned).
+// Workspace layout: header | GroupDev[G] (64 B each) | TmaDesc[G][8] (128 B aligned).
 __host__ __device__ constexpr size_t ws_groups_offset() { return sizeof(WorkspaceHeader); }
 __host__ __device__ constexpr size_t ws_maps_offset(int num_groups) {
-  return (ws_groups_offset() + static_cast<size_t>(num_groups) * 80 + 127) &
+  return (ws_groups_offset() + static_cast<size_t>(num_groups) * 64 + 127) &
          ~static_cast<size_t>(127);
 }
 __host__ __device__ constexpr size_t ws_total_bytes(int num_groups) {

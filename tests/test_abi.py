@@ -52,7 +52,7 @@ def test_version_and_strings(pkg):
 def test_size_queries(pkg):
     N = pkg._native
     assert N.workspace_size(0) == 256
-    assert N.workspace_size(8) == 256 + 8 * 80 + 8 * 8 * 128
+    assert N.workspace_size(8) == 256 + 8 * 64 + 8 * 8 * 128
     assert N.workspace_size(3) == 512 + 3 * 8 * 128  # records padded to 128 bytes
     assert N.sf_blocked_size(80, 32) == 1 * 8 * 512
     assert N.sf_blocked_size(129, 5) == 2 * 2 * 512
