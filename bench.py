@@ -39,6 +39,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 PEAK_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_BYTES = 126 * 1000 * 1000
 FP4_PER_BF16 = 4.0  # dense FP4 : dense BF16 tensor throughput on B200 (9 : 2.25 PFLOP/s)
 
 
@@ -241,19 +242,43 @@ def main():
     torch.cuda.synchronize(dev)
     barrier()
 
-    def timed(n: int) -> float:
-        """Device time of n back-to-back calls (ms), max over ranks."""
-        barrier()
-        torch.cuda.synchronize(dev)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+    # Inputs smaller than L2 would be served from it on back-to-back calls: for those
+    # configurations a 256 MiB buffer is rewritten before every timed call, outside the
+    # events that bracket the call.
+    flush_l2 = prob.input_bytes() < L2_BYTES
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if flush_l2 else None
+
+    def run_timed(n: int) -> float:
+        """Device time (ms) of n calls on this rank: one event pair around all of them,
+        or, with the L2 flush, one pair per call with the flush between the pairs."""
+        if not flush_l2:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(n):
+                step()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            return e0.elapsed_time(e1)
+        pairs = []
         for _ in range(n):
+            flush_buf.fill_(1)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
             step()
-        e1.record(stream)
+            e1.record(stream)
+            pairs.append((e0, e1))
         torch.cuda.synchronize(dev)
+        return sum(a.elapsed_time(b) for a, b in pairs)
+
+    def timed(n: int) -> float:
+        """Device time of n calls (ms), max over ranks."""
         barrier()
-        return max_over_ranks(e0.elapsed_time(e1))
+        torch.cuda.synchronize(dev)
+        ms = run_timed(n)
+        barrier()
+        return max_over_ranks(ms)
 
     # Burst: right after warm-up, before the GPU reaches its power limit.
     burst_ms = timed(args.steps) / args.steps
@@ -274,19 +299,13 @@ def main():
     sustain(1.0)
     barrier()
     torch.cuda.synchronize(dev)
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
     t_host = time.perf_counter()
-    for _ in range(args.steps):
-        step()
+    ms_rank = run_timed(args.steps)
     host_us = (time.perf_counter() - t_host) / args.steps * 1e6
-    ev1.record(stream)
-    torch.cuda.synchronize(dev)
     barrier()
     sustain(0.5)
     clk = clocks.stop()
-    ms_total = max_over_ranks(ev0.elapsed_time(ev1))
+    ms_total = max_over_ranks(ms_rank)
     ms_per_step = ms_total / args.steps
     errors = pkg.check_device_errors(dev, stream)
     flops_rank = prob.flops()
@@ -312,6 +331,8 @@ def main():
     e2e_step()
     torch.cuda.synchronize(dev)
     barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     for _ in range(e2e_steps):
         e2e_step()
@@ -341,6 +362,13 @@ def main():
     burst_peak = FP4_PER_BF16 * float(peaks["bf16_tflops"])
     achieved = flops_rank / (ms_per_step * 1e-3) / 1e12
     burst_tflops = flops_rank / (burst_ms * 1e-3) / 1e12
+    # Roofline: tensor-bound when the arithmetic intensity (FLOPs per algorithmic HBM
+    # byte) exceeds the ridge of the measured peaks, HBM-bound otherwise.
+    alg_bytes = prob.algorithmic_bytes()
+    hbm_peak = float(peaks["hbm_gbs"])
+    hbm_gbs = alg_bytes / (ms_per_step * 1e-3) / 1e9
+    ridge = tensor_peak * 1e12 / (hbm_peak * 1e9)
+    hbm_bound = flops_rank / alg_bytes < ridge
     kernel_tag = args.cta or ("single" if args.tile_n else "auto")
     traffic = load_traffic(kernel_tag, args.config)
     line = {
@@ -362,7 +390,9 @@ def main():
                    "m_per_group": prob.m if len(prob.m) <= 16 else f"{sum(prob.m)} rows",
                    "n": prob.n, "k": prob.k, "gated": prob.gated,
                    "input_bytes_per_gpu": prob.input_bytes(),
-                   "l2": "inputs larger than L2 (126 MB); no flush",
+                   "l2": ("inputs smaller than L2 (126 MB): 256 MiB flush before every timed "
+                          "call, outside its events" if flush_l2 else
+                          "inputs larger than L2 (126 MB); no flush"),
                    "parallelism": f"ep{world} (experts sharded, no data-path collective)"},
         "gpu_launches": args.steps,  # one persistent GEMM kernel per timed call (descriptors reused)
         "device_error_bits": errors,
@@ -371,15 +401,20 @@ def main():
                 "api": "custom_kernel(data) with pinned-host copies of inputs and outputs"},
         "burst": {"us_per_call": burst_ms * 1e3, "tflops_per_gpu": burst_tflops,
                   "frac_of_burst_peak": burst_tflops / burst_peak,
+                  "hbm_frac": alg_bytes / (burst_ms * 1e-3) / 1e9 / hbm_peak,
                   "note": "timed right after warm-up, before the power limit engages"},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": tensor_peak,
-                     "unit": "TFLOP/s", "frac": achieved / tensor_peak,
-                     "peak_source": f"{peak_kind}: 4 x {sustained_key} "
-                                    f"({peaks[sustained_key]}; timed under sustained load)",
-                     "traffic": traffic,
-                     "algorithmic_bytes": prob.algorithmic_bytes(),
-                     "hbm_frac": prob.algorithmic_bytes() / (ms_per_step * 1e-3) / 1e9
-                     / float(peaks["hbm_gbs"])},
+        "roofline": ({"bound": "hbm", "achieved": hbm_gbs, "peak": hbm_peak, "unit": "GB/s",
+                      "frac": hbm_gbs / hbm_peak,
+                      "peak_source": f"{peak_kind}: hbm_gbs (copy bandwidth)",
+                      "traffic": traffic, "algorithmic_bytes": alg_bytes,
+                      "tensor_frac": achieved / tensor_peak}
+                     if hbm_bound else
+                     {"bound": "tensor", "achieved": achieved, "peak": tensor_peak,
+                      "unit": "TFLOP/s", "frac": achieved / tensor_peak,
+                      "peak_source": f"{peak_kind}: 4 x {sustained_key} "
+                                     f"({peaks[sustained_key]}; timed under sustained load)",
+                      "traffic": traffic, "algorithmic_bytes": alg_bytes,
+                      "hbm_frac": hbm_gbs / hbm_peak}),
         "clocks": clk,
     }
     if cpu is not None:

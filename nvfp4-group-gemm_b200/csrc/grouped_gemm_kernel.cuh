@@ -39,7 +39,21 @@ constexpr int kTmemCols = 512;
 // k-tiles the producer warms in L2 ahead of its TMA loads. CTAs that share an A or B
 // tile walk K in lockstep, so without this every one of them waits on the same DRAM
 // miss at every k-step; the prefetch turns those misses into L2 hits.
-constexpr int kL2PrefetchKTiles = 6;
+#ifndef NVFP4_L2_PREFETCH_KTILES
+#define NVFP4_L2_PREFETCH_KTILES 6
+#endif
+constexpr int kL2PrefetchKTiles = NVFP4_L2_PREFETCH_KTILES;
+// Groups whose tile_end values are staged in shared memory (see advance_group).
+constexpr int kSmemGroups = 512;
+constexpr int kTileEndBytes = kSmemGroups * 4;
+// Dynamic tile schedule: after its first tile (blockIdx.x) a CTA claims each next tile
+// from a launch-wide counter, kClaimLeadKTiles k-tiles before it finishes issuing the
+// loads of its current one, so that CTAs whose tiles ran faster take more of them.
+// The producer hands each claimed (tile, group, K) to the MMA issuer and the epilogue
+// through a ring of kSchedSlots shared-memory slots.
+constexpr int kSchedSlots = 4;
+constexpr int kClaimLeadKTiles = 3;
+constexpr uint32_t kSchedConsumers = 1 + kEpilogueWarps;  // MMA issuer + epilogue warps
 // Which producers warm L2: 0 none, 1 one per shared tile (B by the CTAs on the first
 // m-tile of a group, A by those on its first n-tile), 2 every producer for its own tiles.
 // Measured on cfg2 (G=8, 1024 x 4096 x 7168): single-CTA tiles 108.8 / 119.1 / 133.3 us
@@ -81,9 +95,12 @@ struct GemmConfig {
   static constexpr int kEpiBufBytes = 32 * 128;  // 32 rows x 64 fp16, one TMA store box
   static constexpr int kEpiBufsPerWarp = 2;
   static constexpr int kEpiBytes = kEpilogueWarps * kEpiBufsPerWarp * kEpiBufBytes;
-  static constexpr int kBarrierBytes = 8 * (2 * STAGES + 2 * kAccStages + 1) + 16;
+  // mbarriers (stage ring, accumulators, drain, tile-schedule ring), TMEM address and
+  // abort flag, tile-schedule slots.
+  static constexpr int kBarrierBytes =
+      8 * (2 * STAGES + 2 * kAccStages + 1 + 2 * kSchedSlots) + 16 + 16 * kSchedSlots;
   static constexpr int kSmemBytes = 1024 /*alignment slack*/ + STAGES * kStageBytes + kEpiBytes +
-                                    kBarrierBytes;
+                                    kBarrierBytes + kTileEndBytes;
   static_assert(kSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
   static constexpr uint32_t kIdesc = ptx::make_idesc_mxf4nvf4(kBlockM, MMA_N);
   static constexpr int kNTilesPerOut = kOutN;  // output column span of one tile
@@ -127,12 +144,46 @@ __device__ __forceinline__ bool warp_wait_phase(uint64_t* bar, uint32_t parity,
   return ok != 0;
 }
 
-// Locate the group owning `tile` (tiles are numbered group by group); `g` is a
-// cursor that only moves forward because every role walks its tiles in order.
-__device__ __forceinline__ int advance_group(const GroupDev* groups, int num_groups, int g,
-                                             int tile) {
-  while (g + 1 < num_groups && tile >= groups[g].tile_end) ++g;
-  return g;
+// Tile -> group lookup. Tiles are numbered group by group and every CTA meets its
+// tiles in increasing order, so the lookup starts from the previous answer `g`.
+// Launches of up to kSmemGroups groups first copy each group's tile_end into shared
+// memory (one parallel load at kernel start) and search that copy; larger launches
+// search the records in global memory. A CTA passes ~grid/tiles-per-group groups
+// between two of its tiles (about 20 for 64 groups of 7 tiles): a linear walk cost
+// one dependent load per group and stalled the start of every tile, so the lookup
+// checks the current group and otherwise bisects the rest.
+__device__ __forceinline__ void stage_tile_ends(int32_t* ends, const GroupDev* groups,
+                                                int num_groups) {
+  if (num_groups <= kSmemGroups)
+    for (int i = threadIdx.x; i < num_groups; i += blockDim.x) ends[i] = groups[i].tile_end;
+}
+
+__device__ __forceinline__ int advance_group(const int32_t* ends, const GroupDev* groups,
+                                             int num_groups, int g, int tile) {
+  const bool in_smem = num_groups <= kSmemGroups;
+  auto end_of = [&](int i) { return in_smem ? ends[i] : groups[i].tile_end; };
+  if (g + 1 >= num_groups || tile < end_of(g)) return g;
+  // First group in (g, num_groups - 1] whose tile_end exceeds `tile` (tile_end is
+  // non-decreasing); the last group when none does.
+  int lo = g + 1, hi = num_groups - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (tile >= end_of(mid)) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
+
+// Dynamic schedule bookkeeping in the workspace header: counter[0] hands out tiles,
+// counter[1] counts CTAs that have finished. The last CTA to finish sets both back to
+// zero, so the next launch on the same workspace starts from zero without a memset.
+// Every CTA calls this once, after all of its roles are done with counter[0].
+__device__ __forceinline__ void release_tile_counter(uint32_t* counter) {
+  __threadfence();
+  if (atomicAdd(&counter[1], 1u) == gridDim.x - 1) {
+    __threadfence();
+    atomicExch(&counter[0], 0u);
+    atomicExch(&counter[1], 0u);
+  }
 }
 
 template <int MMA_N, bool GATED, int STAGES>
@@ -149,11 +200,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint64_t* accf_bar = empty_bar + STAGES;
   uint64_t* acce_bar = accf_bar + Cfg::kAccStages;
   uint64_t* drain_bar = acce_bar + Cfg::kAccStages;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* sched_full = drain_bar + 1;
+  uint64_t* sched_empty = sched_full + kSchedSlots;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sched_empty + kSchedSlots);
   volatile uint32_t* abort_flag = tmem_holder + 1;
+  // Slot i: {tile, group, K, unused}; a tile >= total_tiles marks the end of the schedule.
+  volatile int32_t* sched_info = reinterpret_cast<volatile int32_t*>(tmem_holder + 4);
+  int32_t* tile_ends = const_cast<int32_t*>(sched_info + 4 * kSchedSlots);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const GroupDev* __restrict__ groups = p.groups;
+  stage_tile_ends(tile_ends, groups, p.num_groups);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -165,6 +223,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       ptx::mbar_init(&acce_bar[a], kEpilogueWarps);
     }
     ptx::mbar_init(drain_bar, 1);
+    for (int i = 0; i < kSchedSlots; ++i) {
+      ptx::mbar_init(&sched_full[i], 1);
+      ptx::mbar_init(&sched_empty[i], kSchedConsumers);
+    }
     *abort_flag = 0u;
     ptx::fence_mbarrier_init();
   }
@@ -177,26 +239,35 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   ptx::tcgen05_fence_after_sync();
   const uint32_t tmem_base = *tmem_holder;
 
-  const GroupDev* __restrict__ groups = p.groups;
-
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (ptx::elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued = 0;
-      int g = 0, acquired_g = -1;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x) {
-        g = advance_group(groups, p.num_groups, g, tile);
-        const GroupDev gd = groups[g];
+      auto acquire_maps = [&](int grp) {
+        const TmaDesc* m = p.maps + static_cast<size_t>(grp) * kMapsPerGroup;
+        ptx::tensormap_fence_acquire(&m[kMapA]);
+        ptx::tensormap_fence_acquire(&m[kMapB]);
+        if (GATED) ptx::tensormap_fence_acquire(&m[kMapB2]);
+      };
+      int tile = blockIdx.x;  // grid <= total_tiles: every CTA has a first tile
+      int g = advance_group(tile_ends, groups, p.num_groups, 0, tile);
+      GroupDev gd = groups[g];
+      acquire_maps(g);
+      for (uint32_t seq = 0;; ++seq) {
+        // Publish this CTA's seq-th tile (or the end marker) to the MMA issuer and epilogue.
+        const int slot = static_cast<int>(seq % kSchedSlots);
+        if (!wait_phase(&sched_empty[slot], ((seq / kSchedSlots) & 1u) ^ 1u, abort_flag,
+                        p.error_bits, kDevErrProducerTimeout))
+          break;
+        sched_info[4 * slot + 0] = tile;
+        sched_info[4 * slot + 1] = g;
+        sched_info[4 * slot + 2] = gd.k;
+        ptx::mbar_arrive(&sched_full[slot]);
+        if (tile >= p.total_tiles) break;
         const TmaDesc* maps = p.maps + static_cast<size_t>(g) * kMapsPerGroup;
-        if (g != acquired_g) {
-          ptx::tensormap_fence_acquire(&maps[kMapA]);
-          ptx::tensormap_fence_acquire(&maps[kMapB]);
-          if (GATED) ptx::tensormap_fence_acquire(&maps[kMapB2]);
-          acquired_g = g;
-        }
         const int local = tile - gd.tile_start;
         const int mt = local % gd.tiles_m;
         const int nt = local / gd.tiles_m;
@@ -219,9 +290,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const uint8_t* sfa_blk = gd.sfa + static_cast<size_t>(mt) * rest_k * kSfBlockBytes;
         const uint32_t tx = Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes +
                             (sfb_blk1 != nullptr ? 2 : 1) * 4 * kSfBlockBytes;
-        // L2 warm-up of k-tile `kp` of this tile (A, B halves, scale blocks).
-        const bool warm_a = kL2PrefetchMode == 2 || (kL2PrefetchMode == 1 && nt == 0);
-        const bool warm_b = kL2PrefetchMode == 2 || (kL2PrefetchMode == 1 && mt == 0);
+        // L2 warm-up of k-tile `kp` of this tile (A, B halves, scale blocks). In mode 1 only
+        // operands that other CTAs also read are warmed (A when the group has several
+        // n-tiles, B when it has several m-tiles): every prefetch box is TMA work, and on
+        // weight-streaming shapes (one m-tile per group) warming unshared B only delayed
+        // the loads behind it.
+        const int tiles_n = (gd.tile_end - gd.tile_start) / gd.tiles_m;
+        const bool warm_a =
+            kL2PrefetchMode == 2 || (kL2PrefetchMode == 1 && nt == 0 && tiles_n > 1);
+        const bool warm_b =
+            kL2PrefetchMode == 2 || (kL2PrefetchMode == 1 && mt == 0 && gd.tiles_m > 1);
         auto prefetch_ktile = [&](int kp) {
           const int px = kp * kRowBytesPerStage;
           const size_t psf = static_cast<size_t>(kp) * 4 * kSfBlockBytes;
@@ -243,10 +321,25 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (sfb_blk1 != nullptr) ptx::bulk_prefetch_l2(sfb_blk1 + psf, 4 * kSfBlockBytes);
           }
         };
-        if (warm_a || warm_b)
-          for (int kp = 0; kp < kL2PrefetchKTiles && kp < ktiles; ++kp) prefetch_ktile(kp);
+        const int claim_kt = ktiles > kClaimLeadKTiles ? ktiles - kClaimLeadKTiles : 0;
+        int next_tile = p.total_tiles;
+        int g_next = g;
+        GroupDev next_gd = gd;
+        bool resolved = false;
+        auto claim_next = [&]() -> int {
+          if (p.dynamic_schedule)
+            return static_cast<int>(gridDim.x + atomicAdd(p.tile_counter, 1u));
+          return tile + static_cast<int>(gridDim.x);
+        };
+        auto resolve_next = [&]() {
+          resolved = true;
+          if (next_tile >= p.total_tiles) return;
+          g_next = advance_group(tile_ends, groups, p.num_groups, g, next_tile);
+          next_gd = groups[g_next];
+          if (g_next != g) acquire_maps(g_next);
+        };
         for (int kt = 0; kt < ktiles; ++kt) {
-          if ((warm_a || warm_b) && kt + kL2PrefetchKTiles < ktiles)
+          if ((warm_a || warm_b) && kt > 0 && kt + kL2PrefetchKTiles < ktiles)
             prefetch_ktile(kt + kL2PrefetchKTiles);
           if (!wait_phase(&empty_bar[stage], phase ^ 1u, abort_flag, p.error_bits,
                           kDevErrProducerTimeout)) {
@@ -277,12 +370,27 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           if (sfb_blk1 != nullptr)
             ptx::bulk_load(sSFB + 4 * kSfBlockBytes, sfb_blk1 + sf_off, 4 * kSfBlockBytes,
                            &full_bar[stage]);
+          // The first warm-up prefetches go behind the tile's first loads, which would
+          // otherwise wait for the TMA unit to work through them.
+          if (kt == 0 && (warm_a || warm_b))
+            for (int kp = 1; kp <= kL2PrefetchKTiles && kp < ktiles; ++kp) prefetch_ktile(kp);
+          // Claim the next tile a few k-tiles before the end of this one; one k-tile
+          // later (the claim's atomic has returned by then) look up its group, load its
+          // record and acquire its tensor maps (about a microsecond per group switch),
+          // all behind loads already in flight.
+          if (kt == claim_kt) next_tile = claim_next();
+          if (kt == claim_kt + 1) resolve_next();
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
+        if (!ok) break;
+        if (!resolved) resolve_next();
+        tile = next_tile;
+        g = g_next;
+        gd = next_gd;
       }
       // Make sure no copy into this CTA's shared memory is still in flight at exit:
       // wait for the most recent fill of every stage (already complete on the normal path).
@@ -310,12 +418,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // (arrived on acce_bar[t & 1] by the epilogue of tile t-1); the first tile passes.
       // Plain double buffer: tile t needs tile t-2 drained; the first two tiles pass.
       uint32_t acc_parity = Cfg::kOverlapAcc ? 0x1u : 0x3u;  // bit s: parity for stage s
-      uint32_t local = 0;
-      int g = 0;
       bool ok = p.diag_skip_mma == 0;
-      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x, ++local) {
-        g = advance_group(groups, p.num_groups, g, tile);
-        const int ktiles = groups[g].k / kBlockK;
+      for (uint32_t local = 0; ok; ++local) {
+        // This CTA's local-th tile, as published by the producer.
+        const int slot = static_cast<int>(local % kSchedSlots);
+        if (!wait_phase(&sched_full[slot], (local / kSchedSlots) & 1u, abort_flag, p.error_bits,
+                        kDevErrMmaTimeout))
+          break;
+        const int tile = sched_info[4 * slot + 0];
+        const int ktiles = sched_info[4 * slot + 2] / kBlockK;
+        ptx::mbar_arrive(&sched_empty[slot]);
+        if (tile >= p.total_tiles) break;
         const int acc = static_cast<int>(local & 1u);
         if (!wait_phase(&acce_bar[acc], (acc_parity >> acc) & 1u, abort_flag, p.error_bits,
                         kDevErrAccTimeout)) {
@@ -386,27 +499,36 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const uint32_t my_bufs_s = ptx::smem_u32(my_bufs);
     uint32_t full_parity = 0;  // bit s: parity to wait for on accf_bar[s]
     uint32_t stores = 0;
-    uint32_t local = 0;
-    int g = 0, acquired_g = -1;
+    int acquired_g = -1;
     constexpr int kBoxes = Cfg::kOutN / 64;
-    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++local) {
-      g = advance_group(groups, p.num_groups, g, tile);
+    for (uint32_t local = 0;; ++local) {
+      // This CTA's local-th tile, as published by the producer.
+      const int slot = static_cast<int>(local % kSchedSlots);
+      if (!warp_wait_phase(&sched_full[slot], (local / kSchedSlots) & 1u, abort_flag,
+                           p.error_bits, kDevErrEpilogueTimeout, lane))
+        break;
+      const int tile = sched_info[4 * slot + 0];
+      const int g = sched_info[4 * slot + 1];
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&sched_empty[slot]);
+      if (tile >= p.total_tiles) break;
       const GroupDev gd = groups[g];
       const TmaDesc* map_c = p.maps + static_cast<size_t>(g) * kMapsPerGroup + kMapC;
       if (g != acquired_g) {
         if (lane == 0) ptx::tensormap_fence_acquire(map_c);
         acquired_g = g;
       }
-      const int tl = tile - gd.tile_start;
-      const int mt = tl % gd.tiles_m;
-      const int nt = tl / gd.tiles_m;
       const int acc = static_cast<int>(local & 1u);
+      // The group record's load is in flight while the accumulator is awaited.
       if (!warp_wait_phase(&accf_bar[acc], (full_parity >> acc) & 1u, abort_flag, p.error_bits,
                            kDevErrEpilogueTimeout, lane)) {
         break;
       }
       full_parity ^= 1u << acc;
       ptx::tcgen05_fence_after_sync();
+      const int tl = tile - gd.tile_start;
+      const int mt = tl % gd.tiles_m;
+      const int nt = tl / gd.tiles_m;
       // Which barrier hands this accumulator (or its shared box) back to the MMA issuer.
       uint64_t* release_bar = Cfg::kOverlapAcc ? &acce_bar[acc ^ 1] : &acce_bar[acc];
       // With overlapped stages the box holding TMEM columns [192, 256) goes first:
@@ -506,6 +628,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     ptx::tcgen05_fence_after_sync();
     ptx::tmem_dealloc(tmem_base, kTmemCols);
   }
+  if (threadIdx.x == 0 && p.dynamic_schedule) release_tile_counter(p.tile_counter);
 }
 
 }  // namespace nvfp4

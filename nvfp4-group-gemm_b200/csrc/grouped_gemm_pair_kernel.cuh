@@ -50,7 +50,8 @@ struct PairConfig {
   static constexpr int kEpiBufsPerWarp = 2;
   static constexpr int kEpiBytes = kEpilogueWarps * kEpiBufsPerWarp * kEpiBufBytes;
   static constexpr int kBarrierBytes = 8 * (2 * STAGES + 2 * 2 + 1) + 16;
-  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kEpiBytes + kBarrierBytes;
+  static constexpr int kSmemBytes =
+      1024 + STAGES * kStageBytes + kEpiBytes + kBarrierBytes + kTileEndBytes;
   static_assert(kSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
   static constexpr uint32_t kIdesc = ptx::make_idesc_mxf4nvf4(256, kMmaN);
   static constexpr uint32_t kEpilogueArrivals = 2 * kEpilogueWarps;
@@ -72,9 +73,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint64_t* drain_bar = acce_bar + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile uint32_t* abort_flag = tmem_holder + 1;
+  int32_t* tile_ends = reinterpret_cast<int32_t*>(tmem_holder + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const GroupDev* __restrict__ groups = p.groups;
+  stage_tile_ends(tile_ends, groups, p.num_groups);  // ordered by the cluster barrier below
   const uint32_t rank = ptx::cluster_ctarank();  // 0: issues the MMAs
   const bool leader = rank == 0;
   const int cluster = static_cast<int>(blockIdx.x >> 1);
@@ -103,7 +107,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   ptx::cluster_sync_all();
   ptx::tcgen05_fence_after_sync();
   const uint32_t tmem_base = *tmem_holder;
-  const GroupDev* __restrict__ groups = p.groups;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -111,21 +114,30 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued = 0;
-      int g = 0, acquired_g = -1;
+      int acquired_g = -1;
       bool ok = true;
+      // The record of the next tile's group is loaded while this tile's loads are issued.
+      int g = advance_group(tile_ends, groups, p.num_groups, 0, cluster);
+      GroupDev next_gd = groups[g];
       for (int tile = cluster; ok && tile < p.total_tiles; tile += num_clusters) {
-        g = advance_group(groups, p.num_groups, g, tile);
-        const GroupDev gd = groups[g];
+        const GroupDev gd = next_gd;
+        const int g_next = advance_group(tile_ends, groups, p.num_groups, g, tile + num_clusters);
+        next_gd = groups[g_next];
         const TmaDesc* maps = p.maps + static_cast<size_t>(g) * kMapsPerGroup;
-        if (g != acquired_g) {
-          ptx::tensormap_fence_acquire(&maps[kMapA]);
-          ptx::tensormap_fence_acquire(&maps[kMapB]);
-          ptx::tensormap_fence_acquire(&maps[kMapSfa]);
-          ptx::tensormap_fence_acquire(&maps[kMapSfb]);
+        // Tensor maps of a group are acquired before its first loads: here for the CTA's
+        // first tile, and otherwise behind the previous tile's first loads (below).
+        auto acquire_maps = [&](const TmaDesc* m) {
+          ptx::tensormap_fence_acquire(&m[kMapA]);
+          ptx::tensormap_fence_acquire(&m[kMapB]);
+          ptx::tensormap_fence_acquire(&m[kMapSfa]);
+          ptx::tensormap_fence_acquire(&m[kMapSfb]);
           if (GATED) {
-            ptx::tensormap_fence_acquire(&maps[kMapB2]);
-            ptx::tensormap_fence_acquire(&maps[kMapSfb2]);
+            ptx::tensormap_fence_acquire(&m[kMapB2]);
+            ptx::tensormap_fence_acquire(&m[kMapSfb2]);
           }
+        };
+        if (g != acquired_g) {
+          acquire_maps(maps);
           acquired_g = g;
         }
         const int local = tile - gd.tile_start;
@@ -185,12 +197,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           ptx::tma_load_2d_pair(sSFB, &maps[kMapSfb], full_leader, 0, sfb0_y0 + kt * 16);
           ptx::tma_load_2d_pair(sSFB + 4 * kSfBlockBytes, map_sfb1, full_leader, 0,
                                 sfb1_y0 + kt * 16);
+          if (kt == 0 && g_next != acquired_g) {
+            acquire_maps(p.maps + static_cast<size_t>(g_next) * kMapsPerGroup);
+            acquired_g = g_next;
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
+        g = g_next;
       }
       if (leader) {
         // Every fill of both CTAs completes on these barriers: wait for the most recent
@@ -217,11 +234,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t phase = 0;
       uint32_t acc_parity = 0x1u;  // overlapped stages: only the first tile passes freely
       uint32_t local = 0;
-      int g = 0;
       bool ok = p.diag_skip_mma == 0;
+      int g = advance_group(tile_ends, groups, p.num_groups, 0, cluster);
+      int next_k = groups[g].k;
       for (int tile = cluster; ok && tile < p.total_tiles; tile += num_clusters, ++local) {
-        g = advance_group(groups, p.num_groups, g, tile);
-        const int ktiles = groups[g].k / kBlockK;
+        const int ktiles = next_k / kBlockK;
+        g = advance_group(tile_ends, groups, p.num_groups, g, tile + num_clusters);
+        next_k = groups[g].k;
         const int acc = static_cast<int>(local & 1u);
         if (!wait_phase(&acce_bar[acc], (acc_parity >> acc) & 1u, abort_flag,
                                 p.error_bits, kDevErrAccTimeout)) {
@@ -290,11 +309,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     uint32_t full_parity = 0;
     uint32_t stores = 0;
     uint32_t local = 0;
-    int g = 0, acquired_g = -1;
+    int acquired_g = -1;
     constexpr int kBoxes = Cfg::kOutN / 64;
+    int g_next = advance_group(tile_ends, groups, p.num_groups, 0, cluster);
+    GroupDev next_gd = groups[g_next];
     for (int tile = cluster; tile < p.total_tiles; tile += num_clusters, ++local) {
-      g = advance_group(groups, p.num_groups, g, tile);
-      const GroupDev gd = groups[g];
+      const GroupDev gd = next_gd;
+      const int g = g_next;
+      g_next = advance_group(tile_ends, groups, p.num_groups, g, tile + num_clusters);
+      next_gd = groups[g_next];
       const TmaDesc* map_c = p.maps + static_cast<size_t>(g) * kMapsPerGroup + kMapC;
       if (g != acquired_g) {
         if (lane == 0) ptx::tensormap_fence_acquire(map_c);

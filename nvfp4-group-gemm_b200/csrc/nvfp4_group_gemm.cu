@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdarg>
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 #include <algorithm>
@@ -281,6 +282,13 @@ bool encode_map(uint32_t kind, const void* addr, uint32_t rows, uint32_t row_ele
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Single-CTA launches hand out tiles dynamically (see kClaimLeadKTiles); building with
+// -DNVFP4_DYNAMIC_SCHEDULE=0 restores the static round-robin order.
+#ifndef NVFP4_DYNAMIC_SCHEDULE
+#define NVFP4_DYNAMIC_SCHEDULE 1
+#endif
+constexpr bool kDynamicSchedule = NVFP4_DYNAMIC_SCHEDULE != 0;
+
 template <int MMA_N, bool GATED, int STAGES>
 cudaError_t launch_single(const GemmParams& gp, int grid, cudaStream_t stream) {
   using Cfg = GemmConfig<MMA_N, GATED, STAGES>;
@@ -432,6 +440,8 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
   gp.num_groups = num_groups;
   gp.total_tiles = static_cast<int32_t>(total_tiles);
   gp.diag_skip_mma = (flags & NVFP4_FLAG_DIAG_SKIP_MMA) ? 1 : 0;
+  gp.dynamic_schedule = (!pair && kDynamicSchedule) ? 1 : 0;
+  gp.tile_counter = reinterpret_cast<WorkspaceHeader*>(ws)->tile_counter;
   if (pair) {
     const int max_clusters = gated ? ds.pair_clusters_gated : ds.pair_clusters;
     const int clusters = static_cast<int>(std::min<int64_t>(total_tiles, max_clusters));
@@ -627,8 +637,9 @@ extern "C" NVFP4_API int nvfp4_grouped_gemm_noalloc(const nvfp4_group* groups, i
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(na.scratch);
-  // The device error word keeps whatever the previous call left: start this call at zero.
-  e = cudaMemsetAsync(ws, 0, sizeof(uint32_t), s);
+  // The device error word keeps whatever the previous call left: start this call at zero,
+  // together with the tile-schedule counters (which every completed launch leaves at zero).
+  e = cudaMemsetAsync(ws, 0, offsetof(WorkspaceHeader, reserved), s);
   if (e != cudaSuccess) return cuda_fail(e, "clear scratch error word");
   // Fixed-size host staging and uncached encoding: no heap use on this path.
   static thread_local GroupDev rec[NVFP4_NOALLOC_MAX_GROUPS];

@@ -46,8 +46,9 @@ struct GroupDev {
 static_assert(sizeof(GroupDev) <= 64, "group record must fit its workspace slot");
 
 struct WorkspaceHeader {
-  uint32_t error_bits;  // OR of device-side failure reasons (see kDevErr*)
-  uint32_t reserved[63];
+  uint32_t error_bits;        // OR of device-side failure reasons (see kDevErr*)
+  uint32_t tile_counter[2];   // dynamic tile schedule: next tile, finished CTAs (0 between launches)
+  uint32_t reserved[61];
 };
 static_assert(sizeof(WorkspaceHeader) == 256, "header is 256 bytes");
 
@@ -90,6 +91,8 @@ struct GemmParams {
   int32_t num_groups;
   int32_t total_tiles;
   int32_t diag_skip_mma;  // NVFP4_FLAG_DIAG_SKIP_MMA: the MMA issuer does no work
+  int32_t dynamic_schedule;  // single-CTA kernel: claim tiles from tile_counter after the first
+  uint32_t* tile_counter;    // WorkspaceHeader::tile_counter
 };
 
 }  // namespace nvfp4
