@@ -62,6 +62,10 @@ typedef enum nvfp4_status {
                                        Default: CTA pairs when the non-empty groups average
                                        at least 192 rows, or at least 96 rows with
                                        K >= 4096; single CTAs otherwise */
+#define NVFP4_FLAG_WEIGHT_STATIONARY 0x80u /* force the weight-stationary kernel (non-gated
+                                              only): tiles of 128 weight rows x 64 token
+                                              rows, computed as C^T so that small groups
+                                              carry no padding rows */
 
 /*
  * One GEMM of the group. All matrices are row-major with K innermost ("K-major"),

@@ -3,19 +3,20 @@
 Public API:
   custom_kernel(data) / solve(data)   harness entry points (submission.py:788-891)
   grouped_gemm(...)                   explicit grouped launch (blocked scales)
+  GroupedGemmPlan(...).run()          the same launch prepared once, run repeatedly
   sf_to_blocked / plain_to_blocked    scale-factor layout conversion
   workloads                           seeded synthetic benchmark problems
   expert_parallel                     expert sharding + output all-gather
 """
 from . import _native, expert_parallel, layout, workloads
 from ._native import Nvfp4Error, load_library
-from .interface import (check_device_errors, custom_kernel, grouped_gemm, input_t, output_t,
-                        solve)
+from .interface import (GroupedGemmPlan, check_device_errors, custom_kernel, grouped_gemm,
+                        input_t, output_t, solve)
 from .layout import (blocked_as_reordered, blocked_sf_bytes, blocked_to_plain, plain_to_blocked,
                      sf_to_blocked)
 
 __all__ = [
-    "Nvfp4Error", "blocked_as_reordered", "blocked_sf_bytes", "blocked_to_plain",
+    "GroupedGemmPlan", "Nvfp4Error", "blocked_as_reordered", "blocked_sf_bytes", "blocked_to_plain",
     "check_device_errors", "custom_kernel", "expert_parallel", "grouped_gemm", "input_t",
     "layout", "load_library", "output_t", "plain_to_blocked", "sf_to_blocked", "solve",
     "workloads",

@@ -35,6 +35,7 @@ FLAG_REUSE_DESCRIPTORS = 0x8
 FLAG_CTA_PAIR = 0x10
 FLAG_SINGLE_CTA = 0x20
 FLAG_DIAG_SKIP_MMA = 0x40
+FLAG_WEIGHT_STATIONARY = 0x80
 
 # Device error bits (WorkspaceHeader::error_bits).
 DEV_ERR_PRODUCER_TIMEOUT = 1 << 0

@@ -211,7 +211,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const GroupDev* __restrict__ groups = p.groups;
-  stage_tile_ends(tile_ends, groups, p.num_groups);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -234,6 +233,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     ptx::tmem_alloc(tmem_holder, kTmemCols);
     ptx::tmem_relinquish_alloc_permit();
   }
+  // Everything above is local to the CTA. Group records, tensor maps, operands and the
+  // tile counter may come from the previous kernels in the stream: wait for them here,
+  // then let the next launch be scheduled onto SMs as this grid's CTAs retire.
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  stage_tile_ends(tile_ends, groups, p.num_groups);
   ptx::tcgen05_fence_before_sync();
   __syncthreads();
   ptx::tcgen05_fence_after_sync();

@@ -78,7 +78,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const GroupDev* __restrict__ groups = p.groups;
-  stage_tile_ends(tile_ends, groups, p.num_groups);  // ordered by the cluster barrier below
   const uint32_t rank = ptx::cluster_ctarank();  // 0: issues the MMAs
   const bool leader = rank == 0;
   const int cluster = static_cast<int>(blockIdx.x >> 1);
@@ -101,6 +100,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     ptx::tmem_alloc_pair(tmem_holder, kTmemCols);
     ptx::tmem_relinquish_alloc_permit_pair();
   }
+  // Local set-up above; data written by earlier kernels in the stream is read only after
+  // this wait. The next launch may then be scheduled as this grid's CTAs retire.
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  stage_tile_ends(tile_ends, groups, p.num_groups);  // ordered by the cluster barrier below
   // Barriers of both CTAs initialised and TMEM allocated in both before any
   // cross-CTA arrive, load completion or MMA.
   ptx::tcgen05_fence_before_sync();

@@ -18,6 +18,7 @@
 #include "../../include/nvfp4_group_gemm.h"
 #include "grouped_gemm_kernel.cuh"
 #include "grouped_gemm_pair_kernel.cuh"
+#include "grouped_gemm_swap_kernel.cuh"
 #include "nvfp4_types.cuh"
 #include "sm100_ptx.cuh"
 
@@ -108,6 +109,8 @@ using Kgated = GemmConfig<256, true, 3>;
 constexpr int kPairStages = 5;
 using Kpair = PairConfig<false, kPairStages>;
 using KpairGated = PairConfig<true, kPairStages>;
+constexpr int kSwapStages = 7;
+using Kswap = SwapConfig<kSwapStages>;
 
 constexpr int kMaxDevices = 64;
 
@@ -169,6 +172,8 @@ void init_device(int dev, DeviceState& st) {
        Kpair::kSmemBytes},
       {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_pair_kernel<true, kPairStages>),
        KpairGated::kSmemBytes},
+      {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_swap_kernel<kSwapStages>),
+       Kswap::kSmemBytes},
   };
   for (auto& k : kernels) {
     e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
@@ -222,10 +227,10 @@ std::mutex g_map_cache_mu;
 std::unordered_map<MapKey, TmaDesc, MapKeyHash> g_map_cache;
 constexpr size_t kMapCacheMax = 1 << 14;
 
-enum : uint32_t { kKindOperand = 0, kKindOutput = 1, kKindScales = 2 };
+enum : uint32_t { kKindOperand = 0, kKindOutput = 1, kKindScales = 2, kKindOperand64 = 3 };
 
 // kKindOperand: e2m1 operand [rows, row_elems bytes] (uint8 view), box 128 B x 128 rows,
-//   128B swizzle, zero fill outside the tensor.
+//   128B swizzle, zero fill outside the tensor; kKindOperand64: the same with 64-row boxes.
 // kKindOutput:  fp16 output [rows, row_elems], box 64 x 32, 128B swizzle.
 // kKindScales:  blocked scale bytes as `rows` rows of 128 bytes, box 128 B x 16 rows =
 //   one 2-KiB k-tile chunk of a 128-row block, zero fill outside.
@@ -234,10 +239,11 @@ bool encode_map_uncached(uint32_t kind, const void* addr, uint32_t rows, uint32_
   CUtensorMap m;
   cuuint32_t estr[2] = {1, 1};
   CUresult r;
-  if (kind == kKindOperand) {
+  if (kind == kKindOperand || kind == kKindOperand64) {
     cuuint64_t dims[2] = {row_elems, rows};
     cuuint64_t strides[1] = {row_elems};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(kRowBytesPerStage), static_cast<cuuint32_t>(kBlockM)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kRowBytesPerStage),
+                         static_cast<cuuint32_t>(kind == kKindOperand ? kBlockM : 64)};
     r = g_encoder.fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(addr), dims, strides,
                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -289,30 +295,62 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 #endif
 constexpr bool kDynamicSchedule = NVFP4_DYNAMIC_SCHEDULE != 0;
 
+// Non-gated launches whose non-empty groups average at most this many rows use the
+// weight-stationary kernel. Off by default: on the shapes measured (64 experts, N = 1536,
+// K = 4096, 8 and 64 rows per expert on average) the single-CTA row tiles were as fast
+// or faster (43.3 vs 44.2 us and 55 vs 59 us per call), both being bound by the weight
+// stream; the kernel stays available through NVFP4_FLAG_WEIGHT_STATIONARY.
+#ifndef NVFP4_SWAP_MAX_AVG_ROWS
+#define NVFP4_SWAP_MAX_AVG_ROWS 0
+#endif
+constexpr int kSwapMaxAvgRows = NVFP4_SWAP_MAX_AVG_ROWS;
+
+// GEMM kernels are launched with programmatic stream serialization: a launch may be
+// scheduled while the previous kernel in the stream is still finishing, and waits
+// (griddepcontrol.wait) before reading anything that kernel may have written.
+#ifndef NVFP4_PDL
+#define NVFP4_PDL 1
+#endif
+
+template <typename Kernel>
+cudaError_t launch_gemm(Kernel kernel, const GemmParams& gp, int grid, int smem, int cluster,
+                        cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kNumThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (NVFP4_PDL) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, gp);
+}
+
 template <int MMA_N, bool GATED, int STAGES>
 cudaError_t launch_single(const GemmParams& gp, int grid, cudaStream_t stream) {
   using Cfg = GemmConfig<MMA_N, GATED, STAGES>;
-  nvfp4_grouped_gemm_kernel<MMA_N, GATED, STAGES>
-      <<<grid, kNumThreads, Cfg::kSmemBytes, stream>>>(gp);
-  return cudaGetLastError();
+  return launch_gemm(nvfp4_grouped_gemm_kernel<MMA_N, GATED, STAGES>, gp, grid, Cfg::kSmemBytes,
+                     1, stream);
 }
 
 template <bool GATED>
 cudaError_t launch_pair(const GemmParams& gp, int clusters, cudaStream_t stream) {
   using Cfg = PairConfig<GATED, kPairStages>;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * clusters, 1, 1);
-  cfg.blockDim = dim3(kNumThreads, 1, 1);
-  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, nvfp4_grouped_gemm_pair_kernel<GATED, kPairStages>, gp);
+  return launch_gemm(nvfp4_grouped_gemm_pair_kernel<GATED, kPairStages>, gp, 2 * clusters,
+                     Cfg::kSmemBytes, 2, stream);
 }
 
 // Shared implementation of both grouped entry points: validate, schedule, encode
@@ -324,7 +362,8 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
   // Tile shape: CTA pairs (256-row tiles) when the groups are tall enough to fill
   // them, single CTAs (128-row tiles) otherwise; 256 MMA columns unless asked otherwise.
   bool pair = false;
-  if ((flags & NVFP4_FLAG_TILE_N128) == 0 && (flags & NVFP4_FLAG_SINGLE_CTA) == 0) {
+  bool swap = (flags & NVFP4_FLAG_WEIGHT_STATIONARY) != 0;
+  if (!swap && (flags & NVFP4_FLAG_TILE_N128) == 0 && (flags & NVFP4_FLAG_SINGLE_CTA) == 0) {
     if (flags & NVFP4_FLAG_CTA_PAIR) {
       pair = true;
     } else {
@@ -340,11 +379,15 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
           max_k = std::max(max_k, groups[i].k);
         }
       pair = active > 0 && (rows >= 192 * active || (rows >= 96 * active && max_k >= 4096));
+      // Small groups: weight-stationary tiles carry no padding rows (non-gated launches
+      // without a forced tile width).
+      swap = !pair && !gated && (flags & NVFP4_FLAG_TILE_N256) == 0 && active > 0 &&
+             rows <= static_cast<int64_t>(kSwapMaxAvgRows) * active;
     }
   }
   const int mma_n = gated ? 256 : ((flags & NVFP4_FLAG_TILE_N128) ? 128 : 256);
-  const int out_n = gated ? 128 : mma_n;
-  const int tile_m = pair ? 256 : kBlockM;
+  const int out_n = swap ? 128 : (gated ? 128 : mma_n);
+  const int tile_m = swap ? Kswap::kTokens : (pair ? 256 : kBlockM);
 
   int64_t total_tiles = 0;
   for (int i = 0; i < num_groups; ++i) {
@@ -376,6 +419,7 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
     d.sfa = static_cast<const uint8_t*>(gr.sfa);
     d.sfb = static_cast<const uint8_t*>(gr.sfb);
     d.sfb2 = gated ? static_cast<const uint8_t*>(gr.sfb2) : nullptr;
+    d.c = static_cast<uint8_t*>(gr.c);
     d.tiles_m = (gr.m + tile_m - 1) / tile_m;
     total_tiles += static_cast<int64_t>(d.tiles_m) * ((gr.n + out_n - 1) / out_n);
     if (total_tiles > (int64_t{1} << 30))
@@ -424,7 +468,8 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
                   encode_map(kKindScales, gr.sfb, sfb_rows, 128, &mp[kMapSfb], use_cache) &&
                   (!gated ||
                    (encode_map(kKindOperand, gr.b2, gr.n, kb, &mp[kMapB2], use_cache) &&
-                    encode_map(kKindScales, gr.sfb2, sfb_rows, 128, &mp[kMapSfb2], use_cache)));
+                    encode_map(kKindScales, gr.sfb2, sfb_rows, 128, &mp[kMapSfb2], use_cache))) &&
+                  (!swap || encode_map(kKindOperand64, gr.a, gr.m, kb, &mp[kMapA64], use_cache));
         if (!ok) return fail(NVFP4_ERR_DRIVER, "group %d: cuTensorMapEncodeTiled rejected a tensor", i);
       }
       nvfp4_upload_descriptors_kernel<<<count, 32, 0, s>>>(up);
@@ -440,9 +485,13 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
   gp.num_groups = num_groups;
   gp.total_tiles = static_cast<int32_t>(total_tiles);
   gp.diag_skip_mma = (flags & NVFP4_FLAG_DIAG_SKIP_MMA) ? 1 : 0;
-  gp.dynamic_schedule = (!pair && kDynamicSchedule) ? 1 : 0;
+  gp.dynamic_schedule = (!pair && kDynamicSchedule) ? 1 : 0;  // single-CTA kernels only
   gp.tile_counter = reinterpret_cast<WorkspaceHeader*>(ws)->tile_counter;
-  if (pair) {
+  if (swap) {
+    const int grid = static_cast<int>(std::min<int64_t>(total_tiles, ds.num_sms));
+    e = launch_gemm(nvfp4_grouped_gemm_swap_kernel<kSwapStages>, gp, grid, Kswap::kSmemBytes, 1,
+                    s);
+  } else if (pair) {
     const int max_clusters = gated ? ds.pair_clusters_gated : ds.pair_clusters;
     const int clusters = static_cast<int>(std::min<int64_t>(total_tiles, max_clusters));
     e = gated ? launch_pair<true>(gp, clusters, s) : launch_pair<false>(gp, clusters, s);
@@ -462,7 +511,8 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
 int check_common_args(const nvfp4_group* groups, int num_groups, unsigned int flags) {
   const unsigned known = NVFP4_FLAG_GATED | NVFP4_FLAG_TILE_N128 | NVFP4_FLAG_TILE_N256 |
                          NVFP4_FLAG_REUSE_DESCRIPTORS | NVFP4_FLAG_CTA_PAIR |
-                         NVFP4_FLAG_SINGLE_CTA | NVFP4_FLAG_DIAG_SKIP_MMA;
+                         NVFP4_FLAG_SINGLE_CTA | NVFP4_FLAG_DIAG_SKIP_MMA |
+                         NVFP4_FLAG_WEIGHT_STATIONARY;
   if (flags & ~known) return fail(NVFP4_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags & ~known);
   if (num_groups < 0) return fail(NVFP4_ERR_INVALID_ARGUMENT, "num_groups=%d", num_groups);
   if (num_groups > 0 && groups == nullptr)
@@ -475,6 +525,11 @@ int check_common_args(const nvfp4_group* groups, int num_groups, unsigned int fl
     return fail(NVFP4_ERR_INVALID_ARGUMENT, "CTA pairs use 256-column tiles");
   if ((flags & NVFP4_FLAG_GATED) && (flags & NVFP4_FLAG_TILE_N128))
     return fail(NVFP4_ERR_INVALID_ARGUMENT, "gated launches use 128 gate + 128 up columns");
+  if ((flags & NVFP4_FLAG_WEIGHT_STATIONARY) &&
+      (flags & (NVFP4_FLAG_GATED | NVFP4_FLAG_TILE_N128 | NVFP4_FLAG_TILE_N256 |
+                NVFP4_FLAG_CTA_PAIR | NVFP4_FLAG_SINGLE_CTA)))
+    return fail(NVFP4_ERR_INVALID_ARGUMENT,
+                "the weight-stationary kernel is non-gated with its own tile shape");
   return NVFP4_OK;
 }
 

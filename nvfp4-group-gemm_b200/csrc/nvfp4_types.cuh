@@ -28,9 +28,10 @@ static_assert(sizeof(TmaDesc) == 128, "tensor map image must be 128 bytes");
 // Tensor maps kept per group, in this order. The scale-factor maps view the blocked
 // scale bytes as rows of 128 bytes (one box = 16 rows = one 2-KiB k-tile chunk of a
 // 128-row block); the CTA-pair kernel loads scales through them.
+// kMapA64 views A like kMapA with a 64-row box (the weight-stationary kernel's token tiles).
 enum : int {
   kMapA = 0, kMapB = 1, kMapB2 = 2, kMapC = 3, kMapSfa = 4, kMapSfb = 5, kMapSfb2 = 6,
-  kMapsPerGroup = 8
+  kMapA64 = 7, kMapsPerGroup = 8
 };
 
 // One group as the device sees it (written by the descriptor builder).
@@ -38,12 +39,13 @@ struct GroupDev {
   const uint8_t* sfa;   // 128x4-blocked E4M3 scales of A
   const uint8_t* sfb;   // blocked scales of B (gate weights when gated)
   const uint8_t* sfb2;  // blocked scales of the up weights (gated only)
+  uint8_t* c;           // fp16 output (the weight-stationary kernel stores without a map)
   int32_t m, n, k;
   int32_t tiles_m;
   int32_t tile_start, tile_end;  // [start, end) in the launch-wide tile order
   float alpha, alpha2;
 };
-static_assert(sizeof(GroupDev) <= 64, "group record must fit its workspace slot");
+static_assert(sizeof(GroupDev) == 64, "group record must fill its 64-byte workspace slot");
 
 struct WorkspaceHeader {
   uint32_t error_bits;        // OR of device-side failure reasons (see kDevErr*)

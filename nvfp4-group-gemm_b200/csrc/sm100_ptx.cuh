@@ -165,6 +165,21 @@ __device__ __forceinline__ void tensormap_fence_release() {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch
+// ---------------------------------------------------------------------------
+// Blocks until every grid this one depends on (the previous kernel in the stream, when
+// launched with programmatic stream serialization) has completed and its memory
+// operations are visible; returns at once when there is no such grid.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Lets the next grid in the stream (if launched with programmatic stream serialization)
+// be scheduled before this one completes; it still waits in griddep_wait for our results.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // tcgen05: TMEM allocation
 // ---------------------------------------------------------------------------
 // Warp-wide. Writes the TMEM base address (lane 0, first column) to *smem_dst.

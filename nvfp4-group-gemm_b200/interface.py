@@ -123,60 +123,22 @@ def _check_sf(t: torch.Tensor, rows: int, k: int, name: str) -> None:
 # ----------------------------------------------------------------------------
 # Core grouped launch
 # ----------------------------------------------------------------------------
-def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
-                 sfa: Sequence[torch.Tensor], sfb: Sequence[torch.Tensor],
-                 c: Sequence[torch.Tensor], problem_sizes: Sequence[Sequence[int]],
-                 alpha: Sequence[float] | None = None,
-                 b2: Sequence[torch.Tensor] | None = None,
-                 sfb2: Sequence[torch.Tensor] | None = None,
-                 alpha2: Sequence[float] | None = None,
-                 tile_n: int | None = None,
-                 stream: torch.cuda.Stream | None = None,
-                 reuse_descriptors: bool = True,
-                 cta: str | None = None) -> list:
-    """One grouped NVFP4 launch. Scale tensors are in the blocked layout.
+def _prepare(a, b, sfa, sfb, c, problem_sizes, alpha, b2, sfb2, alpha2, tile_n, cta):
+    """Validate one grouped launch and build its group table.
 
-    ``problem_sizes`` holds (m, n, k[, l]) per group. When ``b2``/``sfb2`` are given
-    the launch is gated: ``c = fp16(silu(fp16(alpha*A.B^T)) * fp16(alpha2*A.B2^T))``.
-    ``cta`` forces 256-row tiles on CTA pairs (``"pair"``) or 128-row tiles on single
-    CTAs (``"single"``); by default the library picks pairs when the groups average
-    at least 192 rows (96 with K >= 4096). ``tile_n`` (128 or 256) applies to
-    single-CTA tiles.
+    Returns ``(table, flags, device)``, or None when there is nothing to launch (no
+    groups, or every group empty). Raises ValueError on malformed input.
     """
-    if cta not in (None, "pair", "single"):
-        raise ValueError(f"cta must be None, 'pair' or 'single', got {cta!r}")
+    if cta not in (None, "pair", "single", "weights"):
+        raise ValueError(f"cta must be None, 'pair', 'single' or 'weights', got {cta!r}")
     G = len(problem_sizes)
     if not (len(a) == len(b) == len(sfa) == len(sfb) == len(c) == G):
         raise ValueError("a, b, sfa, sfb, c and problem_sizes must have one entry per group")
     gated = b2 is not None
-    # Fast path: the same tensor objects at the same addresses, sizes, scales and tile
-    # choice as the previous call on this stream were validated then, and the workspace
-    # still holds their descriptors -> launch directly.
-    sig = None
-    if reuse_descriptors and G > 0 and isinstance(c[0], torch.Tensor) and c[0].is_cuda:
-        lists = (a, b, sfa, sfb, c) + ((b2, sfb2) if gated else ())
-        try:
-            sig = (tuple(id(t) for lst in lists for t in lst),
-                   tuple(t.data_ptr() for lst in lists for t in lst),
-                   tuple(tuple(ps) for ps in problem_sizes),
-                   None if alpha is None else tuple(alpha),
-                   None if alpha2 is None else tuple(alpha2), tile_n, gated, cta)
-        except (AttributeError, TypeError):
-            sig = None
-        if sig is not None:
-            device = c[0].device
-            s = stream or torch.cuda.current_stream(device)
-            ws = _workspaces.get((device.index, s.cuda_stream))
-            if ws is not None and ws.last_sig == sig and ws.last_table is not None:
-                with torch.cuda.device(device):
-                    _native.grouped_gemm_raw(ws.last_table,
-                                             ws.last_flags | _native.FLAG_REUSE_DESCRIPTORS,
-                                             ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
-                return list(c)
     if gated and (sfb2 is None or len(b2) != G or len(sfb2) != G):
         raise ValueError("gated launches need b2 and sfb2 for every group")
     if G == 0:
-        return []
+        return None
     device = None
     table = np.zeros(G, dtype=_native.GROUP_DTYPE)
     ms = np.empty(G, dtype=np.int64)
@@ -217,7 +179,7 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
             _as_2d_kmajor(b2[g], n, k // 2, f"b2[{g}]")
             _check_sf(sfb2[g], n, k, f"sfb2[{g}]")
     if device is None:  # every group empty
-        return list(c)
+        return None
     table["a"] = [t.data_ptr() for t in a]
     table["b"] = [t.data_ptr() for t in b]
     table["sfa"] = [t.data_ptr() for t in sfa]
@@ -235,6 +197,12 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
         flags |= _native.FLAG_CTA_PAIR
     elif cta == "single":
         flags |= _native.FLAG_SINGLE_CTA
+    elif cta == "weights":
+        if gated:
+            raise ValueError("the weight-stationary kernel is non-gated")
+        if tile_n is not None:
+            raise ValueError("the weight-stationary kernel has its own tile shape")
+        flags |= _native.FLAG_WEIGHT_STATIONARY
     if tile_n == 128 and cta == "pair":
         raise ValueError("CTA pairs use 256-column tiles")
     if tile_n is not None and not gated:
@@ -244,6 +212,64 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
             flags |= _native.FLAG_TILE_N256
         else:
             raise ValueError(f"tile_n must be 128 or 256, got {tile_n}")
+    return table, flags, device
+
+
+def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
+                 sfa: Sequence[torch.Tensor], sfb: Sequence[torch.Tensor],
+                 c: Sequence[torch.Tensor], problem_sizes: Sequence[Sequence[int]],
+                 alpha: Sequence[float] | None = None,
+                 b2: Sequence[torch.Tensor] | None = None,
+                 sfb2: Sequence[torch.Tensor] | None = None,
+                 alpha2: Sequence[float] | None = None,
+                 tile_n: int | None = None,
+                 stream: torch.cuda.Stream | None = None,
+                 reuse_descriptors: bool = True,
+                 cta: str | None = None) -> list:
+    """One grouped NVFP4 launch. Scale tensors are in the blocked layout.
+
+    ``problem_sizes`` holds (m, n, k[, l]) per group. When ``b2``/``sfb2`` are given
+    the launch is gated: ``c = fp16(silu(fp16(alpha*A.B^T)) * fp16(alpha2*A.B2^T))``.
+    ``cta`` forces 256-row tiles on CTA pairs (``"pair"``), 128-row tiles on single
+    CTAs (``"single"``) or the weight-stationary kernel's 128-weight-row x 64-token
+    tiles (``"weights"``, non-gated only); by default the library picks pairs when the
+    groups average at least 192 rows (96 with K >= 4096) and single CTAs otherwise.
+    ``tile_n`` (128 or 256) applies to single-CTA tiles.
+    """
+    if cta not in (None, "pair", "single", "weights"):
+        raise ValueError(f"cta must be None, 'pair', 'single' or 'weights', got {cta!r}")
+    G = len(problem_sizes)
+    if not (len(a) == len(b) == len(sfa) == len(sfb) == len(c) == G):
+        raise ValueError("a, b, sfa, sfb, c and problem_sizes must have one entry per group")
+    gated = b2 is not None
+    # Fast path: the same tensor objects at the same addresses, sizes, scales and tile
+    # choice as the previous call on this stream were validated then, and the workspace
+    # still holds their descriptors -> launch directly.
+    sig = None
+    if reuse_descriptors and G > 0 and isinstance(c[0], torch.Tensor) and c[0].is_cuda:
+        lists = (a, b, sfa, sfb, c) + ((b2, sfb2) if gated else ())
+        try:
+            sig = (tuple(id(t) for lst in lists for t in lst),
+                   tuple(t.data_ptr() for lst in lists for t in lst),
+                   tuple(tuple(ps) for ps in problem_sizes),
+                   None if alpha is None else tuple(alpha),
+                   None if alpha2 is None else tuple(alpha2), tile_n, gated, cta)
+        except (AttributeError, TypeError):
+            sig = None
+        if sig is not None:
+            device = c[0].device
+            s = stream or torch.cuda.current_stream(device)
+            ws = _workspaces.get((device.index, s.cuda_stream))
+            if ws is not None and ws.last_sig == sig and ws.last_table is not None:
+                with torch.cuda.device(device):
+                    _native.grouped_gemm_raw(ws.last_table,
+                                             ws.last_flags | _native.FLAG_REUSE_DESCRIPTORS,
+                                             ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
+                return list(c)
+    prepared = _prepare(a, b, sfa, sfb, c, problem_sizes, alpha, b2, sfb2, alpha2, tile_n, cta)
+    if prepared is None:
+        return list(c)
+    table, flags, device = prepared
     s = stream or torch.cuda.current_stream(device)
     ws = _workspace_for(device, s, _native.workspace_size(G))
     call_flags = flags
@@ -256,6 +282,63 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
     ws.last_flags = flags
     ws.last_sig = sig
     return list(c)
+
+
+class GroupedGemmPlan:
+    """A grouped launch validated once and then run many times on the same tensors.
+
+    For callers that issue the same grouped GEMM repeatedly over fixed buffers (an
+    MoE layer's expert weights and its activation and output slabs): the group table
+    is checked and built once, the first run uploads the tensor maps, and every
+    later run is a single library call that reuses them
+    (``NVFP4_FLAG_REUSE_DESCRIPTORS``), with no per-tensor Python work. Arguments
+    are those of :func:`grouped_gemm`. The tensors must keep their storage (same
+    addresses and shapes) while the plan is used; their contents may change between
+    runs. Runs of one plan share its workspace, so they must be ordered on the GPU
+    (one stream, or synchronised streams).
+    """
+
+    def __init__(self, a, b, sfa, sfb, c, problem_sizes, *, alpha=None, b2=None, sfb2=None,
+                 alpha2=None, tile_n=None, cta=None):
+        prepared = _prepare(a, b, sfa, sfb, c, problem_sizes, alpha, b2, sfb2, alpha2, tile_n,
+                            cta)
+        self.outputs = list(c)
+        self._keep = (a, b, sfa, sfb, c, b2, sfb2)  # the table holds their addresses
+        self._table = None
+        if prepared is None:
+            return
+        self._table, self._flags, self.device = prepared
+        self._nbytes = _native.workspace_size(len(problem_sizes))
+        # Zero-filled: the first 4 bytes are the device error word.
+        self._ws = torch.zeros(self._nbytes, dtype=torch.uint8, device=self.device)
+        self._lib = _native.load_library()
+        self._uploaded = False
+
+    def run(self, stream: torch.cuda.Stream | None = None) -> list:
+        """Launch on ``stream`` (default: the current stream); returns the outputs."""
+        if self._table is None:
+            return self.outputs
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        flags = self._flags | (_native.FLAG_REUSE_DESCRIPTORS if self._uploaded else 0)
+        args = (self._table.ctypes.data, int(self._table.shape[0]), flags, self._ws.data_ptr(),
+                self._nbytes, s)
+        if torch.cuda.current_device() == self.device.index:
+            st = self._lib.nvfp4_grouped_gemm(*args)
+        else:
+            with torch.cuda.device(self.device):
+                st = self._lib.nvfp4_grouped_gemm(*args)
+        _native.check(st, self._lib)
+        self._uploaded = True
+        return self.outputs
+
+    def check_device_errors(self, stream: torch.cuda.Stream | None = None) -> int:
+        """Synchronise and return the device error bits of this plan's runs (raises
+        ``Nvfp4Error`` when a kernel gave up waiting)."""
+        if self._table is None:
+            return 0
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        with torch.cuda.device(self.device):
+            return _native.workspace_check(self._ws.data_ptr(), s)
 
 
 # ----------------------------------------------------------------------------

@@ -81,6 +81,10 @@ def _table(N, **kw):
     (dict(), 0x10 | 0x20, 1),       # exclusive CTA modes
     (dict(), 0x10 | 0x2, 1),        # pairs need 256-column tiles
     (dict(), 0x2 | 0x4, 1),         # exclusive tile flags
+    (dict(), 0x80 | 0x1, 1),        # weight-stationary tiles are non-gated
+    (dict(), 0x80 | 0x10, 1),       # ... and exclusive with the other tile shapes
+    (dict(), 0x80 | 0x2, 1),
+    (dict(k=100), 0x80, 2),         # shape checks apply to every kernel
 ])
 def test_validation_errors_before_launch(pkg, kw, flags, status):
     N = pkg._native

@@ -54,9 +54,9 @@ def check_problem(prob, tol=TOL, groups=None):
 
 
 # (tile_n, cta) of every kernel variant: library default, single CTA with 128- and
-# 256-column tiles, CTA pair with 256 x 256 tiles.
-VARIANTS = [(None, None), (128, "single"), (256, "single"), (None, "pair")]
-VARIANT_IDS = ["auto", "single128", "single256", "pair"]
+# 256-column tiles, CTA pair with 256 x 256 tiles, weight-stationary 128 x 64 tiles.
+VARIANTS = [(None, None), (128, "single"), (256, "single"), (None, "pair"), (None, "weights")]
+VARIANT_IDS = ["auto", "single128", "single256", "pair", "weights"]
 
 
 def run_custom_kernel(pkg, prob, tile_n=None, cta=None):
@@ -116,7 +116,7 @@ def test_golden_cases_match_oracle_and_reference(pkg, golden_inputs, tile_n, cta
         outputs = None
     for name in golden_case_names(golden_inputs):
         p = _golden_problem(pkg, golden_inputs, name)
-        if tile_n is not None and p.gated:
+        if (tile_n is not None or cta == "weights") and p.gated:
             continue
         pkg.grouped_gemm(p.a, p.b, p.sfa, p.sfb, p.c,
                          [(m, n, k, 1) for m, n, k in zip(p.m, p.n, p.k)], alpha=p.alpha,
@@ -193,7 +193,7 @@ def test_ten_tuple_dual_gemm_form(pkg):
     check_problem(prob, tol=HARNESS_TOL)
 
 
-@pytest.mark.parametrize("cta", [None, "pair"])
+@pytest.mark.parametrize("cta", [None, "pair", "weights"])
 def test_many_groups_several_upload_launches(pkg, cta):
     ms = [(i * 37) % 150 for i in range(300)]  # 300 groups -> 13 descriptor-upload launches
     prob = pkg.workloads.make_problem("g300", ms, 128, 256, seed=3, device="cuda")
@@ -201,11 +201,38 @@ def test_many_groups_several_upload_launches(pkg, cta):
     check_problem(prob)
 
 
+@pytest.mark.parametrize("cta", [None, "weights"])
 @pytest.mark.parametrize("cfg", ["challenge3", "challenge4", "challenge1", "challenge2"])
-def test_challenge_shapes(pkg, cfg):
+def test_challenge_shapes(pkg, cfg, cta):
     prob = pkg.workloads.make_config(cfg, seed=11, device="cuda")
-    run_custom_kernel(pkg, prob)
+    run_custom_kernel(pkg, prob, cta=cta)
     check_problem(prob, tol=HARNESS_TOL)
+
+
+@pytest.mark.parametrize("cta", [None, "single", "pair", "weights"])
+def test_prepared_plan_runs_repeatedly(pkg, cta):
+    """A GroupedGemmPlan reuses its descriptors; new input contents show up in the output."""
+    prob = pkg.workloads.make_problem("plan", [5, 0, 130, 64], 384, 512, seed=31, device="cuda",
+                                      alpha_range=(0.5, 2.0))
+    sizes = prob.problem_sizes()
+    plan = pkg.GroupedGemmPlan(prob.a, prob.b, prob.sfa, prob.sfb, prob.c, sizes,
+                               alpha=prob.alpha, cta=cta)
+    out = plan.run()
+    assert [o.data_ptr() for o in out] == [c.data_ptr() for c in prob.c]
+    check_problem(prob)
+    # Same storage, new contents: the second run must see them.
+    other = pkg.workloads.make_problem("plan2", [5, 0, 130, 64], 384, 512, seed=32,
+                                       device="cuda", alpha_range=(0.5, 2.0))
+    for dst, src in zip(prob.a + prob.b + prob.sfa + prob.sfb,
+                        other.a + other.b + other.sfa + other.sfb):
+        dst.copy_(src)
+    prob.sfa_plain, prob.sfb_plain = other.sfa_plain, other.sfb_plain
+    for c in prob.c:
+        c.fill_(float("nan"))
+    plan.run()
+    torch.cuda.synchronize()
+    check_problem(prob)
+    assert plan.check_device_errors() == 0
 
 
 def test_descriptor_reuse_and_rebuild(pkg):
@@ -264,10 +291,11 @@ def test_cfg2_full_size(pkg, cta):
     assert pkg.check_device_errors() == 0
 
 
-def test_cfg4_skewed_full_size(pkg):
+@pytest.mark.parametrize("cta", [None, "single", "pair", "weights"])
+def test_cfg4_skewed_full_size(pkg, cta):
     prob = pkg.workloads.make_config("cfg4", seed=4, device="cuda")
     assert 0 in prob.m or min(prob.m) <= 16
-    run_custom_kernel(pkg, prob)
+    run_custom_kernel(pkg, prob, cta=cta)
     check_problem(prob)
 
 
