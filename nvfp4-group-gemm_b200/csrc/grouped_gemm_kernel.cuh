@@ -68,8 +68,13 @@ constexpr uint32_t kSchedConsumers = 1 + kEpilogueWarps;  // MMA issuer + epilog
 constexpr int kL2PrefetchMode = NVFP4_L2_PREFETCH_SINGLE;
 constexpr int kL2PrefetchModePair = NVFP4_L2_PREFETCH_PAIR;
 
-template <int MMA_N, bool GATED, int STAGES>
+// DIRECT: the epilogue stores C from registers (16 bytes per lane, one row per lane)
+// instead of staging 64-column boxes in shared memory for TMA stores. That frees the
+// 32 KiB of staging space for a fourth pipeline stage at MMA_N = 256, for launches whose
+// run time is the weight stream (groups of at most a few hundred rows).
+template <int MMA_N, bool GATED, int STAGES, bool DIRECT = false>
 struct GemmConfig {
+  static constexpr bool kDirectStore = DIRECT;
   static_assert(MMA_N == 128 || MMA_N == 256, "MMA N must be 128 or 256");
   static_assert(!GATED || MMA_N == 256, "gated tiles pair 128 gate + 128 up columns");
   static constexpr int kOutN = GATED ? MMA_N / 2 : MMA_N;  // output columns per tile
@@ -94,7 +99,7 @@ struct GemmConfig {
   static_assert(kSfColBase + kSfaCols + kSfbCols <= kTmemCols, "TMEM over-subscribed");
   static constexpr int kEpiBufBytes = 32 * 128;  // 32 rows x 64 fp16, one TMA store box
   static constexpr int kEpiBufsPerWarp = 2;
-  static constexpr int kEpiBytes = kEpilogueWarps * kEpiBufsPerWarp * kEpiBufBytes;
+  static constexpr int kEpiBytes = DIRECT ? 0 : kEpilogueWarps * kEpiBufsPerWarp * kEpiBufBytes;
   // mbarriers (stage ring, accumulators, drain, tile-schedule ring), TMEM address and
   // abort flag, tile-schedule slots.
   static constexpr int kBarrierBytes =
@@ -186,10 +191,10 @@ __device__ __forceinline__ void release_tile_counter(uint32_t* counter) {
   }
 }
 
-template <int MMA_N, bool GATED, int STAGES>
+template <int MMA_N, bool GATED, int STAGES, bool DIRECT = false>
 __global__ void __launch_bounds__(kNumThreads, 1)
     nvfp4_grouped_gemm_kernel(const __grid_constant__ GemmParams p) {
-  using Cfg = GemmConfig<MMA_N, GATED, STAGES>;
+  using Cfg = GemmConfig<MMA_N, GATED, STAGES, DIRECT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -519,7 +524,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (tile >= p.total_tiles) break;
       const GroupDev gd = groups[g];
       const TmaDesc* map_c = p.maps + static_cast<size_t>(g) * kMapsPerGroup + kMapC;
-      if (g != acquired_g) {
+      if (!DIRECT && g != acquired_g) {
         if (lane == 0) ptx::tensormap_fence_acquire(map_c);
         acquired_g = g;
       }
@@ -564,9 +569,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (lane == 0) ptx::mbar_arrive(release_bar);
             released = true;
           }
-          // The store that last read this staging buffer (two boxes ago) must be done with it.
-          if (lane == 0) ptx::bulk_wait_group_read<1>();
-          __syncwarp();
+          if (!DIRECT) {
+            // The store that last read this staging buffer (two boxes ago) must be done with it.
+            if (lane == 0) ptx::bulk_wait_group_read<1>();
+            __syncwarp();
+          }
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             const uint32_t* v = half ? v1 : v0;
@@ -597,24 +604,42 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                 packed[i] = *reinterpret_cast<uint32_t*>(&hv);
               }
             }
-            // Row `lane` of the 32 x 128 B box, 16-byte chunks XOR-swizzled by (row & 7)
-            // to match the map's 128B swizzle (and to spread the stores over all banks).
-            const uint32_t row_addr = buf + lane * 128;
+            if (DIRECT) {
+              // Row row0 + lane, columns [col, col + 32): four 16-byte stores (N is a
+              // multiple of 8, so a chunk is either inside the row or past its end).
+              const int row = row0 + lane;
+              const int col = nt * Cfg::kOutN + box * 64 + half * 32;
+              if (row < gd.m) {
+                uint4* dst = reinterpret_cast<uint4*>(
+                    gd.c + (static_cast<size_t>(row) * gd.n + col) * sizeof(__half));
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const uint32_t chunk = static_cast<uint32_t>(half * 4 + c) ^ (lane & 7);
-              ptx::st_shared_v4(row_addr + chunk * 16, packed[4 * c], packed[4 * c + 1],
-                                packed[4 * c + 2], packed[4 * c + 3]);
+                for (int c = 0; c < 4; ++c)
+                  if (col + 8 * c < gd.n)
+                    dst[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
+                                        packed[4 * c + 3]);
+              }
+            } else {
+              // Row `lane` of the 32 x 128 B box, 16-byte chunks XOR-swizzled by (row & 7)
+              // to match the map's 128B swizzle (and to spread the stores over all banks).
+              const uint32_t row_addr = buf + lane * 128;
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                const uint32_t chunk = static_cast<uint32_t>(half * 4 + c) ^ (lane & 7);
+                ptx::st_shared_v4(row_addr + chunk * 16, packed[4 * c], packed[4 * c + 1],
+                                  packed[4 * c + 2], packed[4 * c + 3]);
+              }
             }
           }
-          ptx::fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            ptx::tma_store_2d(map_c, my_bufs + (stores & 1u) * Cfg::kEpiBufBytes,
-                              nt * Cfg::kOutN + box * 64, row0);
-            ptx::bulk_commit_group();
+          if (!DIRECT) {
+            ptx::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              ptx::tma_store_2d(map_c, my_bufs + (stores & 1u) * Cfg::kEpiBufBytes,
+                                nt * Cfg::kOutN + box * 64, row0);
+              ptx::bulk_commit_group();
+            }
+            ++stores;
           }
-          ++stores;
         }
       }
       if (!released) {

@@ -106,6 +106,7 @@ int cuda_fail(cudaError_t e, const char* what) {
 using Kn128 = GemmConfig<128, false, 5>;
 using Kn256 = GemmConfig<256, false, 3>;
 using Kgated = GemmConfig<256, true, 3>;
+using Kstream = GemmConfig<256, false, 4, true>;  // weight-streaming shapes
 constexpr int kPairStages = 5;
 using Kpair = PairConfig<false, kPairStages>;
 using KpairGated = PairConfig<true, kPairStages>;
@@ -168,6 +169,8 @@ void init_device(int dev, DeviceState& st) {
       {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_kernel<128, false, 5>), Kn128::kSmemBytes},
       {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_kernel<256, false, 3>), Kn256::kSmemBytes},
       {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_kernel<256, true, 3>), Kgated::kSmemBytes},
+      {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_kernel<256, false, 4, true>),
+       Kstream::kSmemBytes},
       {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_pair_kernel<false, kPairStages>),
        Kpair::kSmemBytes},
       {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_pair_kernel<true, kPairStages>),
@@ -183,8 +186,12 @@ void init_device(int dev, DeviceState& st) {
       return;
     }
   }
-  st.pair_clusters = max_pair_clusters(kernels[3].fn, kernels[3].smem, st.num_sms);
-  st.pair_clusters_gated = max_pair_clusters(kernels[4].fn, kernels[4].smem, st.num_sms);
+  st.pair_clusters = max_pair_clusters(
+      reinterpret_cast<const void*>(&nvfp4_grouped_gemm_pair_kernel<false, kPairStages>),
+      Kpair::kSmemBytes, st.num_sms);
+  st.pair_clusters_gated = max_pair_clusters(
+      reinterpret_cast<const void*>(&nvfp4_grouped_gemm_pair_kernel<true, kPairStages>),
+      KpairGated::kSmemBytes, st.num_sms);
 }
 
 // cuTensorMapEncodeTiled, resolved once through the runtime (no libcuda link).
@@ -305,6 +312,18 @@ constexpr bool kDynamicSchedule = NVFP4_DYNAMIC_SCHEDULE != 0;
 #endif
 constexpr int kSwapMaxAvgRows = NVFP4_SWAP_MAX_AVG_ROWS;
 
+// Non-gated 128 x 256 single-CTA launches whose non-empty groups average at most this
+// many rows are bound by the weight stream: they use the variant with four pipeline
+// stages and register-direct output stores (their C writes are small). Measured per
+// call, 4 vs 3 stages: 64 experts x N 1536 x K 4096 with 64 rows each 52.0 vs 53.1 us,
+// with 8 rows each 42.0 vs 44.0 us; but 8 groups of 128 rows, N 7168, K 2048, 34.6 vs
+// 32.0 us (there the row-per-lane stores of the larger C cost more than the deeper ring
+// gains). Taller groups keep the three-stage variant whose TMA stores write whole rows.
+#ifndef NVFP4_STREAM_MAX_AVG_ROWS
+#define NVFP4_STREAM_MAX_AVG_ROWS 64
+#endif
+constexpr int kStreamMaxAvgRows = NVFP4_STREAM_MAX_AVG_ROWS;
+
 // GEMM kernels are launched with programmatic stream serialization: a launch may be
 // scheduled while the previous kernel in the stream is still finishing, and waits
 // (griddepcontrol.wait) before reading anything that kernel may have written.
@@ -339,11 +358,11 @@ cudaError_t launch_gemm(Kernel kernel, const GemmParams& gp, int grid, int smem,
   return cudaLaunchKernelEx(&cfg, kernel, gp);
 }
 
-template <int MMA_N, bool GATED, int STAGES>
+template <int MMA_N, bool GATED, int STAGES, bool DIRECT = false>
 cudaError_t launch_single(const GemmParams& gp, int grid, cudaStream_t stream) {
-  using Cfg = GemmConfig<MMA_N, GATED, STAGES>;
-  return launch_gemm(nvfp4_grouped_gemm_kernel<MMA_N, GATED, STAGES>, gp, grid, Cfg::kSmemBytes,
-                     1, stream);
+  using Cfg = GemmConfig<MMA_N, GATED, STAGES, DIRECT>;
+  return launch_gemm(nvfp4_grouped_gemm_kernel<MMA_N, GATED, STAGES, DIRECT>, gp, grid,
+                     Cfg::kSmemBytes, 1, stream);
 }
 
 template <bool GATED>
@@ -361,6 +380,14 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
   const bool gated = (flags & NVFP4_FLAG_GATED) != 0;
   // Tile shape: CTA pairs (256-row tiles) when the groups are tall enough to fill
   // them, single CTAs (128-row tiles) otherwise; 256 MMA columns unless asked otherwise.
+  int64_t rows = 0, active = 0;  // rows and count of the non-empty groups
+  int max_k = 0;
+  for (int i = 0; i < num_groups; ++i)
+    if (groups[i].m > 0 && groups[i].n > 0) {
+      rows += groups[i].m;
+      ++active;
+      max_k = std::max(max_k, groups[i].k);
+    }
   bool pair = false;
   bool swap = (flags & NVFP4_FLAG_WEIGHT_STATIONARY) != 0;
   if (!swap && (flags & NVFP4_FLAG_TILE_N128) == 0 && (flags & NVFP4_FLAG_SINGLE_CTA) == 0) {
@@ -370,14 +397,6 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
       // Pairs pay off when the groups fill most of a 256-row tile, or when K is long
       // enough that the halved B traffic outweighs the padding of 128-255-row groups
       // (measured: G=8, M 64-248, K=7168 -> 39 vs 48 us; same M, K=2048 -> 32 vs 30 us).
-      int64_t rows = 0, active = 0;
-      int max_k = 0;
-      for (int i = 0; i < num_groups; ++i)
-        if (groups[i].m > 0 && groups[i].n > 0) {
-          rows += groups[i].m;
-          ++active;
-          max_k = std::max(max_k, groups[i].k);
-        }
       pair = active > 0 && (rows >= 192 * active || (rows >= 96 * active && max_k >= 4096));
       // Small groups: weight-stationary tiles carry no padding rows (non-gated launches
       // without a forced tile width).
@@ -501,6 +520,8 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
       e = launch_single<256, true, 3>(gp, grid, s);
     else if (mma_n == 128)
       e = launch_single<128, false, 5>(gp, grid, s);
+    else if (rows <= static_cast<int64_t>(kStreamMaxAvgRows) * active)
+      e = launch_single<256, false, 4, true>(gp, grid, s);  // weight-streaming shapes
     else
       e = launch_single<256, false, 3>(gp, grid, s);
   }

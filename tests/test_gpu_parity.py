@@ -154,6 +154,7 @@ EDGE_SHAPES = [
     ("k256", [128, 64], 512, 256),
     ("empty_groups", [0, 64, 0, 0, 130, 0], 256, 512),
     ("many_small", [3, 17, 0, 64, 9, 1, 128, 33] * 4, 256, 512),
+    ("tall_ragged", [700, 513], 264, 512),   # tall groups: staged-store single-CTA tiles
 ]
 
 
