@@ -55,6 +55,8 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--experts", default=None,
+                    help="START:STOP - run only this contiguous expert shard of the configuration")
     return ap.parse_args()
 
 
@@ -216,7 +218,11 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
 
     # Each rank owns its own experts (seed = rank): weak scaling, no data-path collective.
-    prob = pkg.workloads.make_config(args.config, seed=rank, device=dev)
+    shard = None
+    if args.experts:
+        start, stop = (int(x) for x in args.experts.split(":"))
+        shard = slice(start, stop)
+    prob = pkg.workloads.make_config(args.config, seed=rank, device=dev, experts=shard)
     stream = torch.cuda.current_stream(dev)
     sizes = prob.problem_sizes()
 
@@ -398,7 +404,8 @@ def main():
         "vs_baseline": None,
         "dtype": "e2m1xe4m3->f32->f16",
         "data": "synthetic (seeded; e2m1 codes uniform over 16, E4M3 scales 2^U{-4..3})",
-        "config": {"workload": args.config, "groups_per_gpu": prob.num_groups,
+        "config": {"workload": args.config + (f"[experts {args.experts}]" if args.experts else ""),
+                   "groups_per_gpu": prob.num_groups,
                    "m_per_group": prob.m if len(prob.m) <= 16 else f"{sum(prob.m)} rows",
                    "n": prob.n, "k": prob.k, "gated": prob.gated,
                    "input_bytes_per_gpu": prob.input_bytes(),
