@@ -326,6 +326,38 @@ def main():
     ms_total = max_over_ranks(ms_rank)
     ms_per_step = ms_total / args.steps
     errors = plan.check_device_errors(stream)
+
+    # ---------------------------------------------------------------- with the output gather (N > 1)
+    # The same calls followed by the NCCL all-gather that gives every rank every expert's
+    # fp16 output (expert_parallel.all_gather_expert_outputs); timed the same way.
+    gather = None
+    if world > 1:
+        rows_all = [None] * world
+        dist.all_gather_object(rows_all, list(prob.m))
+        rows_flat = [m for r in rows_all for m in r]
+
+        def gather_step():
+            plan.run(stream)
+            pkg.expert_parallel.all_gather_expert_outputs(prob.c, rows_flat, prob.n)
+
+        for _ in range(3):
+            gather_step()
+        torch.cuda.synchronize(dev)
+        barrier()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(args.steps):
+            gather_step()
+        g1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        g_ms = max_over_ranks(g0.elapsed_time(g1)) / args.steps
+        gather = {"value": prob.flops() * world / (g_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                  "ms_per_step": g_ms,
+                  "gather_bytes_received_per_rank": int(sum(rows_flat) * prob.n * 2
+                                                        - sum(prob.m) * prob.n * 2),
+                  "what": "GEMM + NCCL all-gather of every expert's fp16 output to every rank"}
     flops_rank = prob.flops()
     value = flops_rank * world / (ms_per_step * 1e-3) / 1e12
 
@@ -437,6 +469,8 @@ def main():
                       "hbm_frac": hbm_gbs / hbm_peak}),
         "clocks": clk,
     }
+    if gather is not None:
+        line["with_gather"] = gather
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
