@@ -55,6 +55,9 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--op", default="gemm", choices=["gemm", "quantize"],
+                    help="gemm: the grouped GEMM (default); quantize: the NVFP4 activation "
+                         "quantiser on the configuration's A rows (bf16 [sum M_g, K])")
     ap.add_argument("--experts", default=None,
                     help="START:STOP - run only this contiguous expert shard of the configuration")
     return ap.parse_args()
@@ -196,8 +199,115 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_quantize(args):
+    """The activation quantiser over the configuration's A rows, one JSON line (rank 0)."""
+    import numpy as np
+    import torch
+
+    import submission
+
+    pkg = submission.load_package()
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    if args.impl == "reference":
+        from oracle import nvfp4_quant_oracle as Q
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    ms, n, k, gated, _ = pkg.workloads.config_rows(args.config, seed=0)
+    rows = int(sum(ms))
+    g = torch.Generator(device="cpu").manual_seed(0)
+    xh = (torch.randn((rows, k), generator=g) * 2.0).to(torch.bfloat16)
+    alg = rows * k * 2 + rows * k // 2 + pkg.blocked_sf_bytes(rows, k // 16)
+    sg = float(xh.abs().amax().float()) / (6 * 448)
+    line = {"metric": f"NVFP4 quantiser GB/s ({args.config} A rows, bf16 [{rows}, {k}])",
+            "unit": "GB/s", "n_gpus": 1, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16->e2m1+e4m3", "data": "synthetic (seeded N(0, 4))",
+            "config": {"workload": f"quantize:{args.config}", "rows": rows, "cols": k}}
+    if args.impl == "reference":
+        sample = max(1, min(rows, (1 << 22) // k))
+        xs = xh[:sample].float().numpy()
+        t0 = time.perf_counter()
+        Q.quantize_nvfp4_blocked(xs, sg)
+        dt = time.perf_counter() - t0
+        v = sample * (k * 2 + k // 2 + k // 16) / dt / 1e9
+        line.update({"impl": "reference", "value": v, "steps": 1, "warmup": 0,
+                     "cpu_baseline": {"value": v, "unit": "GB/s", "cores": 1, "kind": "port",
+                                      "sample": f"{sample} rows through the numpy oracle, {dt:.2f} s"},
+                     "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                             "d2h_bytes_per_step": 0}})
+        print(json.dumps(line), flush=True)
+        return
+    x = xh.to(dev)
+    packed = torch.empty((rows, k // 2), dtype=torch.uint8, device=dev)
+    sf = torch.empty(pkg.blocked_sf_bytes(rows, k // 16), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if rows * k * 2 < L2_BYTES else None
+
+    def timed(n_steps):
+        pairs = []
+        for _ in range(n_steps):
+            if flush is not None:
+                flush.fill_(1)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            pkg.quantize(x, sg, packed=packed, sf=sf, stream=stream)
+            e1.record(stream)
+            pairs.append((e0, e1))
+        torch.cuda.synchronize(dev)
+        return sum(a.elapsed_time(b) for a, b in pairs) / n_steps
+
+    for _ in range(max(args.warmup, 3)):
+        pkg.quantize(x, sg, packed=packed, sf=sf, stream=stream)
+    ms_step = timed(args.steps)
+    # End to end: bf16 rows from pinned host memory, quantise, codes and scales back.
+    xp = xh.pin_memory()
+    hp = torch.empty(packed.shape, dtype=torch.uint8).pin_memory()
+    hs = torch.empty(sf.shape, dtype=torch.uint8).pin_memory()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(3):
+        x.copy_(xp, non_blocking=True)
+        pkg.quantize(x, sg, packed=packed, sf=sf, stream=stream)
+        hp.copy_(packed, non_blocking=True)
+        hs.copy_(sf, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / 3
+    peaks, kind = load_peaks()
+    gbs = alg / (ms_step * 1e-3) / 1e9
+    sample = max(1, min(rows, (1 << 21) // k))
+    from oracle import nvfp4_quant_oracle as Q
+    xs = xh[:sample].float().numpy()
+    t0 = time.perf_counter()
+    Q.quantize_nvfp4_blocked(xs, sg)
+    dt = time.perf_counter() - t0
+    line.update({
+        "value": gbs, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_step,
+        "us_per_call": ms_step * 1e3, "gpu_launches": args.steps,
+        "config": dict(line["config"], l2=("inputs smaller than L2: 256 MiB flush before every "
+                                           "timed call" if flush is not None else
+                                           "inputs larger than L2 (126 MB); no flush")),
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": float(peaks["hbm_gbs"]),
+                     "unit": "GB/s", "frac": gbs / float(peaks["hbm_gbs"]),
+                     "peak_source": f"{kind}: hbm_gbs", "traffic": None,
+                     "algorithmic_bytes": alg},
+        "e2e": {"value": alg / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": int(xp.numel() * 2),
+                "d2h_bytes_per_step": int(hp.numel() + hs.numel())},
+        "cpu_baseline": {"value": sample * (k * 2 + k // 2 + k // 16) / dt / 1e9, "unit": "GB/s",
+                         "cores": 1, "kind": "port",
+                         "sample": f"{sample} rows through the numpy oracle, {dt:.2f} s"},
+    })
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.op == "quantize":
+        return run_quantize(args)
     if args.impl == "reference":
         return run_reference(args)
 

@@ -126,6 +126,27 @@ NVFP4_API int nvfp4_sf_to_blocked(const void* plain, void* blocked, int rows, in
                                   int64_t ld, void* stream);
 
 /*
+ * NVFP4 activation quantiser: x [rows, cols] (bf16 or fp16, row stride `ld` elements)
+ * -> packed e2m1 [rows, cols/2] (row stride `packed_ld` bytes; element 2i in the low
+ * nibble) and E4M3 scales per 16 elements, written in the 128x4-blocked layout that
+ * nvfp4_group.sfa expects (nvfp4_sf_blocked_size(rows, cols/16) bytes; padding rows 0).
+ * Per 16-element block: sf = E4M3(amax / (6 * global_scale)) and
+ * q = E2M1(x * (1 / (value(sf) * global_scale))), every step rounded to nearest even and
+ * saturated, so x ~= value(q) * value(sf) * global_scale; pass global_scale =
+ * amax(|x|) / (6 * 448) and fold it into the GEMM's alpha. The reference has no
+ * counterpart: its inputs arrive already quantised (REFERENCE_IMPL.md:143-205 generates
+ * e2m1 codes and scales directly); this produces the GEMM's A operand from activations.
+ * Requirements: cols a positive multiple of 64; x, packed and sf_blocked 16-byte aligned;
+ * ld a multiple of 8 elements, packed_ld a multiple of 16 bytes; global_scale finite > 0;
+ * inputs finite. Asynchronous on `stream`.
+ */
+#define NVFP4_DTYPE_BF16 0
+#define NVFP4_DTYPE_FP16 1
+NVFP4_API int nvfp4_quantize(const void* x, int rows, int cols, int64_t ld, int dtype,
+                             float global_scale, void* packed, int64_t packed_ld, void* sf_blocked,
+                             void* stream);
+
+/*
  * Synchronise `stream`, then read and clear the device error word of `workspace`.
  * Returns NVFP4_ERR_DEVICE_TIMEOUT if a kernel using it gave up on a wait; the
  * reason bits are stored to *device_error_bits when non-NULL.

@@ -55,7 +55,12 @@ EXPORTED_SYMBOLS = (
     "nvfp4_sf_to_blocked",
     "nvfp4_workspace_check",
     "nvfp4_grouped_gemm_noalloc",
+    "nvfp4_quantize",
 )
+
+# Input dtypes of nvfp4_quantize (NVFP4_DTYPE_*).
+DTYPE_BF16 = 0
+DTYPE_FP16 = 1
 
 # Largest group count nvfp4_grouped_gemm_noalloc accepts (NVFP4_NOALLOC_MAX_GROUPS).
 NOALLOC_MAX_GROUPS = 512
@@ -146,6 +151,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_workspace_check.restype = i32
         lib.nvfp4_grouped_gemm_noalloc.argtypes = [vp, i32, u32, vp]
         lib.nvfp4_grouped_gemm_noalloc.restype = i32
+        lib.nvfp4_quantize.argtypes = [vp, i32, i32, i64, i32, ctypes.c_float, vp, i64, vp, vp]
+        lib.nvfp4_quantize.restype = i32
         if path is None:
             _lib = lib
         return lib
@@ -177,6 +184,14 @@ def grouped_gemm_raw(table: np.ndarray, flags: int, workspace_ptr: int, workspac
     st = lib.nvfp4_grouped_gemm(table.ctypes.data, int(table.shape[0]), flags, workspace_ptr,
                                 workspace_bytes, stream_ptr)
     check(st, lib)
+
+
+def quantize_raw(x_ptr: int, rows: int, cols: int, ld: int, dtype: int, global_scale: float,
+                 packed_ptr: int, packed_ld: int, sf_ptr: int, stream_ptr: int) -> None:
+    """Call nvfp4_quantize (device pointers, row strides in elements / bytes)."""
+    lib = load_library()
+    check(lib.nvfp4_quantize(x_ptr, rows, cols, ld, dtype, global_scale, packed_ptr, packed_ld,
+                             sf_ptr, stream_ptr), lib)
 
 
 def sf_to_blocked_raw(plain_ptr: int, blocked_ptr: int, rows: int, sf_cols: int, ld: int,

@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdarg>
 #include <cstddef>
 #include <cstdio>
@@ -19,6 +20,7 @@
 #include "grouped_gemm_kernel.cuh"
 #include "grouped_gemm_pair_kernel.cuh"
 #include "grouped_gemm_swap_kernel.cuh"
+#include "quantize_kernel.cuh"
 #include "nvfp4_types.cuh"
 #include "sm100_ptx.cuh"
 
@@ -615,6 +617,56 @@ NVFP4_API int nvfp4_sf_to_blocked(const void* plain, void* blocked, int rows, in
       chunks);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "sf_to_blocked launch");
+  return NVFP4_OK;
+}
+
+NVFP4_API int nvfp4_quantize(const void* x, int rows, int cols, int64_t ld, int dtype,
+                             float global_scale, void* packed, int64_t packed_ld, void* sf_blocked,
+                             void* stream) {
+  g_last_error.clear();
+  if (dtype != NVFP4_DTYPE_BF16 && dtype != NVFP4_DTYPE_FP16)
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "dtype=%d (expected NVFP4_DTYPE_BF16 or _FP16)", dtype);
+  if (!(global_scale > 0.0f) || !std::isfinite(global_scale))
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "global_scale must be finite and > 0");
+  if (rows < 0 || cols <= 0 || cols % 64 != 0)
+    return fail(NVFP4_ERR_BAD_SHAPE, "rows=%d cols=%d (cols must be a positive multiple of 64)",
+                rows, cols);
+  if (rows == 0) return NVFP4_OK;
+  if (x == nullptr || packed == nullptr || sf_blocked == nullptr)
+    return fail(NVFP4_ERR_NULL_POINTER, "x, packed or sf_blocked is NULL");
+  if (ld < cols || packed_ld < cols / 2)
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "ld=%lld packed_ld=%lld too small for cols=%d",
+                static_cast<long long>(ld), static_cast<long long>(packed_ld), cols);
+  if (!aligned16(x) || !aligned16(packed) || !aligned16(sf_blocked) || ld % 8 != 0 ||
+      packed_ld % 16 != 0)
+    return fail(NVFP4_ERR_MISALIGNED,
+                "x, packed and sf_blocked must be 16-byte aligned, ld a multiple of 8 elements "
+                "and packed_ld a multiple of 16 bytes");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_INVALID_ARGUMENT, "device %d", dev);
+  DeviceState& ds = g_dev[dev];
+  std::call_once(ds.once, init_device, dev, std::ref(ds));
+  if (ds.status != NVFP4_OK) return fail(ds.status, "%s", ds.detail.c_str());
+  const int row_blocks = (rows + 127) / 128;
+  const int rest_k = cols / 64;
+  const int64_t warps = static_cast<int64_t>(row_blocks) * rest_k;
+  const int threads = 32 * kQuantWarps;
+  const int64_t blocks = std::min<int64_t>((warps + kQuantWarps - 1) / kQuantWarps,
+                                           static_cast<int64_t>(ds.num_sms) * 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == NVFP4_DTYPE_BF16)
+    nvfp4_quantize_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), rows, ld, global_scale,
+        static_cast<uint8_t*>(packed), packed_ld, static_cast<uint8_t*>(sf_blocked), row_blocks,
+        rest_k);
+  else
+    nvfp4_quantize_kernel<__half><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
+        static_cast<const __half*>(x), rows, ld, global_scale, static_cast<uint8_t*>(packed),
+        packed_ld, static_cast<uint8_t*>(sf_blocked), row_blocks, rest_k);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
   return NVFP4_OK;
 }
 

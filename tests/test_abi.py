@@ -124,3 +124,25 @@ def test_sf_converter_validation(pkg):
     assert lib.nvfp4_sf_to_blocked(0x1000, 0x2000, -1, 4, 4, None) == 2
     assert lib.nvfp4_sf_to_blocked(0x1000, 0x2008, 4, 4, 4, None) == 3
     assert lib.nvfp4_sf_to_blocked(0x1000, 0x2000, 4, 8, 4, None) == 1
+
+
+def test_quantize_validation_before_launch(pkg):
+    lib = pkg.load_library()
+    ok = dict(x=0x1000, rows=4, cols=64, ld=64, dtype=0, sg=1.0, packed=0x2000, pld=32, sf=0x3000)
+
+    def call(**kw):
+        a = dict(ok, **kw)
+        return lib.nvfp4_quantize(a["x"], a["rows"], a["cols"], a["ld"], a["dtype"], a["sg"],
+                                  a["packed"], a["pld"], a["sf"], None)
+
+    assert call(dtype=2) == 1                # unknown dtype
+    assert call(sg=0.0) == 1                 # scale must be > 0
+    assert call(sg=float("inf")) == 1
+    assert call(cols=96) == 2                # cols % 64
+    assert call(rows=-1) == 2
+    assert call(rows=0) == 0                 # nothing to do
+    assert call(x=0) == 4                    # NULL input
+    assert call(ld=32) == 1                  # ld < cols
+    assert call(x=0x1008) == 3               # misaligned input
+    assert call(pld=40) == 3                 # packed row stride not a multiple of 16
+    assert lib.nvfp4_last_error_detail()
