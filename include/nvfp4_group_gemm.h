@@ -147,6 +147,51 @@ NVFP4_API int nvfp4_quantize(const void* x, int rows, int cols, int64_t ld, int 
                              void* stream);
 
 /*
+ * nvfp4_quantize with a row map (`src_rows`, device int32 [rows]):
+ *   NVFP4_ROWS_GATHER: output row r quantises input row src_rows[r] (MoE dispatch: the row
+ *                      map from nvfp4_moe_route); src_rows[r] < 0 gives a zero row.
+ *   NVFP4_ROWS_MASK:   output row r quantises input row r where src_rows[r] >= 0, zeros
+ *                      elsewhere (a dispatched buffer whose padding rows hold no data).
+ * No counterpart in the reference (see nvfp4_quantize).
+ */
+#define NVFP4_ROWS_GATHER 1
+#define NVFP4_ROWS_MASK 2
+NVFP4_API int nvfp4_quantize_rows(const void* x, int rows, int cols, int64_t ld, int dtype,
+                                  float global_scale, const int32_t* src_rows, int mode,
+                                  void* packed, int64_t packed_ld, void* sf_blocked, void* stream);
+
+/*
+ * MoE token dispatch metadata (no counterpart in the reference, which receives its groups
+ * already formed; this is the routing step before the grouped GEMM). topk_ids: device int32
+ * [tokens, topk], expert of each (token, slot) pair (< 0 or >= num_experts: dropped).
+ * Outputs (device int32): counts [num_experts] rows per expert; offsets [num_experts + 1]
+ * first row of each expert in the dispatched buffers, every expert starting on a 128-row
+ * boundary (offsets[num_experts] = padded total), so one blocked scale buffer for all rows is
+ * the concatenation of the experts' blocked layouts; dest [tokens * topk] the dispatched row
+ * of each pair (-1 if dropped), rows of an expert in token order; src_rows [rows_capacity] the
+ * token of each dispatched row (-1 for padding rows; entries past offsets[num_experts] are
+ * not written). rows_capacity >= tokens * topk + 127 * num_experts; num_experts <= 1024.
+ * Deterministic. workspace: nvfp4_moe_route_workspace_size(tokens * topk, num_experts) bytes
+ * of device memory (no initialisation needed).
+ */
+NVFP4_API size_t nvfp4_moe_route_workspace_size(int64_t pairs, int num_experts);
+NVFP4_API int nvfp4_moe_route(const int32_t* topk_ids, int tokens, int topk, int num_experts,
+                              int32_t* counts, int32_t* offsets, int32_t* dest, int32_t* src_rows,
+                              int64_t rows_capacity, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/*
+ * MoE combine (no counterpart in the reference): out[t, :] = bf16( sum_j weights[t, j] *
+ * y[dest[t * topk + j], :] ), y fp16 [dispatched rows, cols] (row stride ldy elements),
+ * weights fp32 [tokens, topk], out bf16 [tokens, cols] (row stride ldo); fp32 products and
+ * sums in slot order; pairs with dest < 0 are skipped. cols, ldy, ldo multiples of 8;
+ * y and out 16-byte aligned.
+ */
+NVFP4_API int nvfp4_moe_combine(const void* y, int64_t ldy, const int32_t* dest,
+                                const float* weights, int tokens, int topk, int cols, void* out,
+                                int64_t ldo, void* stream);
+
+/*
  * Synchronise `stream`, then read and clear the device error word of `workspace`.
  * Returns NVFP4_ERR_DEVICE_TIMEOUT if a kernel using it gave up on a wait; the
  * reason bits are stored to *device_error_bits when non-NULL.

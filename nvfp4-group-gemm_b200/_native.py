@@ -56,7 +56,15 @@ EXPORTED_SYMBOLS = (
     "nvfp4_workspace_check",
     "nvfp4_grouped_gemm_noalloc",
     "nvfp4_quantize",
+    "nvfp4_quantize_rows",
+    "nvfp4_moe_route_workspace_size",
+    "nvfp4_moe_route",
+    "nvfp4_moe_combine",
 )
+
+# Row-map modes of nvfp4_quantize_rows (NVFP4_ROWS_*).
+ROWS_GATHER = 1
+ROWS_MASK = 2
 
 # Input dtypes of nvfp4_quantize (NVFP4_DTYPE_*).
 DTYPE_BF16 = 0
@@ -153,6 +161,15 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_grouped_gemm_noalloc.restype = i32
         lib.nvfp4_quantize.argtypes = [vp, i32, i32, i64, i32, ctypes.c_float, vp, i64, vp, vp]
         lib.nvfp4_quantize.restype = i32
+        lib.nvfp4_quantize_rows.argtypes = [vp, i32, i32, i64, i32, ctypes.c_float, vp, i32, vp,
+                                            i64, vp, vp]
+        lib.nvfp4_quantize_rows.restype = i32
+        lib.nvfp4_moe_route_workspace_size.argtypes = [i64, i32]
+        lib.nvfp4_moe_route_workspace_size.restype = sz
+        lib.nvfp4_moe_route.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, i64, vp, sz, vp]
+        lib.nvfp4_moe_route.restype = i32
+        lib.nvfp4_moe_combine.argtypes = [vp, i64, vp, vp, i32, i32, i32, vp, i64, vp]
+        lib.nvfp4_moe_combine.restype = i32
         if path is None:
             _lib = lib
         return lib

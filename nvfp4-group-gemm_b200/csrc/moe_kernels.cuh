@@ -1,0 +1,174 @@
+// MoE token dispatch and combine around the grouped GEMM.
+//
+// Routing (deterministic stable counting sort of the (token, slot) pairs by expert):
+//   1. nvfp4_route_histogram_kernel: per chunk of kRouteChunk pairs, a histogram per expert.
+//   2. nvfp4_route_scan_kernel: per expert, the running base of every chunk and the total;
+//      padded row offsets (every expert's rows start on a 128-row boundary, so the blocked
+//      scale layout of the whole dispatched buffer is the concatenation of the experts'
+//      blocked layouts); padding rows marked -1 in the row -> token map.
+//   3. nvfp4_route_scatter_kernel: the destination row of every pair, in token order within
+//      each expert: chunk base + rank within the chunk (warp match_any for the rank inside a
+//      warp's 32 pairs, per-warp expert counts for the rank across a chunk's warps).
+// Combine: out[t] = sum_j w[t, j] * Y[dest[t, j]] in fp32 (slot order, each product and sum
+// rounded to nearest), written as bf16.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace nvfp4 {
+
+constexpr int kRouteChunk = 2048;       // pairs per chunk
+constexpr int kRouteThreads = 256;      // 8 warps; a warp owns 256 consecutive pairs of a chunk
+constexpr int kRouteMaxExperts = 1024;
+
+__global__ void __launch_bounds__(kRouteThreads) nvfp4_route_histogram_kernel(
+    const int32_t* __restrict__ ids, int64_t pairs, int num_experts, int32_t* __restrict__ hist) {
+  __shared__ int32_t h[kRouteMaxExperts];
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) h[e] = 0;
+  __syncthreads();
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kRouteChunk;
+  for (int i = threadIdx.x; i < kRouteChunk; i += blockDim.x) {
+    const int64_t p = base + i;
+    if (p < pairs) {
+      const int e = ids[p];
+      if (e >= 0 && e < num_experts) atomicAdd(&h[e], 1);
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x)
+    hist[static_cast<int64_t>(blockIdx.x) * num_experts + e] = h[e];
+}
+
+// One block of 1024 threads. hist[c][e] becomes the exclusive running count of expert e
+// before chunk c; counts[e] the total; offsets[e] the padded first row of expert e
+// (offsets[num_experts] = padded total). src_rows of padding rows are set to -1.
+__global__ void __launch_bounds__(1024) nvfp4_route_scan_kernel(
+    int32_t* __restrict__ hist, int chunks, int num_experts, int32_t* __restrict__ counts,
+    int32_t* __restrict__ offsets, int32_t* __restrict__ src_rows) {
+  __shared__ int32_t padded[kRouteMaxExperts];
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
+    int32_t run = 0;
+    for (int c = 0; c < chunks; ++c) {
+      int32_t* slot = &hist[static_cast<int64_t>(c) * num_experts + e];
+      const int32_t v = *slot;
+      *slot = run;
+      run += v;
+    }
+    counts[e] = run;
+    padded[e] = (run + 127) / 128 * 128;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // exclusive scan over at most 1024 experts
+    int32_t acc = 0;
+    for (int e = 0; e < num_experts; ++e) {
+      offsets[e] = acc;
+      acc += padded[e];
+    }
+    offsets[num_experts] = acc;
+  }
+  __syncthreads();
+  for (int e = 0; e < num_experts; ++e) {
+    const int32_t first = offsets[e] + counts[e];
+    const int32_t end = offsets[e + 1];
+    for (int32_t r = first + static_cast<int32_t>(threadIdx.x); r < end; r += blockDim.x)
+      src_rows[r] = -1;
+  }
+}
+
+__global__ void __launch_bounds__(kRouteThreads) nvfp4_route_scatter_kernel(
+    const int32_t* __restrict__ ids, int64_t pairs, int topk, int num_experts,
+    const int32_t* __restrict__ hist, const int32_t* __restrict__ offsets,
+    int32_t* __restrict__ dest, int32_t* __restrict__ src_rows) {
+  constexpr int kWarps = kRouteThreads / 32;
+  constexpr int kPerWarp = kRouteChunk / kWarps;  // 256 consecutive pairs per warp
+  __shared__ int32_t wcount[kWarps][kRouteMaxExperts];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kWarps * num_experts; i += blockDim.x)
+    wcount[i / num_experts][i % num_experts] = 0;
+  __syncthreads();
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kRouteChunk + warp * kPerWarp;
+  // Pass 1: each warp counts its pairs per expert (lane 0 of each peer set adds the set).
+  for (int s = 0; s < kPerWarp; s += 32) {
+    const int64_t p = base + s + lane;
+    int e = p < pairs ? ids[p] : -1;
+    if (e >= num_experts) e = -1;
+    const uint32_t peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && lane == __ffs(peers) - 1) wcount[warp][e] += __popc(peers);
+  }
+  __syncthreads();
+  // Exclusive prefix over the chunk's warps, per expert.
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
+    int32_t run = 0;
+    for (int w = 0; w < kWarps; ++w) {
+      const int32_t v = wcount[w][e];
+      wcount[w][e] = run;
+      run += v;
+    }
+  }
+  __syncthreads();
+  // Pass 2: destination rows in pair order.
+  const int32_t* chunk_base = hist + static_cast<int64_t>(blockIdx.x) * num_experts;
+  for (int s = 0; s < kPerWarp; s += 32) {
+    const int64_t p = base + s + lane;
+    int e = p < pairs ? ids[p] : -1;
+    if (e >= num_experts) e = -1;
+    const uint32_t peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (e >= 0) {
+      const int32_t row = offsets[e] + chunk_base[e] + wcount[warp][e] + rank;
+      dest[p] = row;
+      src_rows[row] = static_cast<int32_t>(p / topk);
+    } else if (p < pairs) {
+      dest[p] = -1;
+    }
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(peers) - 1) wcount[warp][e] += __popc(peers);
+    __syncwarp();
+  }
+}
+
+// out[t, :] = bf16( sum_j w[t, j] * y[dest[t*topk + j], :] ), fp32 products and sums in slot
+// order; pairs with dest < 0 contribute nothing. One warp per (token, 256-column chunk):
+// lane l handles 8 consecutive columns (16-byte loads of fp16, 16-byte stores of bf16).
+__global__ void __launch_bounds__(256) nvfp4_moe_combine_kernel(
+    const __half* __restrict__ y, int64_t ldy, const int32_t* __restrict__ dest,
+    const float* __restrict__ weights, int tokens, int topk, int cols,
+    __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int lane = threadIdx.x & 31;
+  const int chunks = (cols + 255) / 256;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t task = warp0; task < static_cast<int64_t>(tokens) * chunks; task += nwarps) {
+    const int t = static_cast<int>(task / chunks);
+    const int col = static_cast<int>(task % chunks) * 256 + lane * 8;
+    if (col >= cols) continue;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    for (int j = 0; j < topk; ++j) {
+      const int32_t r = dest[static_cast<int64_t>(t) * topk + j];
+      if (r < 0) continue;
+      const float w = weights[static_cast<int64_t>(t) * topk + j];
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(r) * ldy + col));
+      const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&words[i]));
+        acc[2 * i] = __fadd_rn(acc[2 * i], __fmul_rn(w, f.x));
+        acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __fmul_rn(w, f.y));
+      }
+    }
+    uint32_t packed[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+      packed[i] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * ldo + col) =
+        make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  }
+}
+
+}  // namespace nvfp4

@@ -79,10 +79,16 @@ __device__ __forceinline__ void unpack16(const uint4& lo, const uint4& hi, float
 constexpr int kQuantWarps = 8;
 constexpr int kQuantUnroll = 8;  // rows in flight per lane
 
+// Row maps: output row r reads input row r (kQuantRowsPlain), input row src_rows[r]
+// (kQuantRowsGather: MoE dispatch; -1 = a padding row, quantised as zeros), or input row r
+// only where src_rows[r] >= 0 (kQuantRowsMask: rows of a dispatched buffer that hold data).
+enum : int { kQuantRowsPlain = 0, kQuantRowsGather = 1, kQuantRowsMask = 2 };
+
 template <typename T>
 __global__ void __launch_bounds__(32 * kQuantWarps, 4) nvfp4_quantize_kernel(
     const T* __restrict__ x, int rows, int64_t ld, float sg, uint8_t* __restrict__ packed,
-    int64_t packed_ld, uint8_t* __restrict__ sf, int row_blocks, int rest_k) {
+    int64_t packed_ld, uint8_t* __restrict__ sf, int row_blocks, int rest_k,
+    const int32_t* __restrict__ src_rows, int row_mode) {
   __shared__ __align__(16) uint8_t sf_stage[kQuantWarps][512];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
@@ -102,10 +108,15 @@ __global__ void __launch_bounds__(32 * kQuantWarps, 4) nvfp4_quantize_kernel(
 #pragma unroll
       for (int u = 0; u < kQuantUnroll; ++u) {
         const int row = mm * 128 + (it0 + u) * 4 + rgrp;
-        raw[u] = row < rows ? __ldg(reinterpret_cast<const uint4*>(
-                                  x + static_cast<int64_t>(row) * ld +
-                                  static_cast<int64_t>(kk) * 64) + sub)
-                            : make_uint4(0u, 0u, 0u, 0u);
+        int in_row = row < rows ? row : -1;
+        if (row_mode != kQuantRowsPlain && in_row >= 0) {
+          const int32_t m = __ldg(src_rows + row);
+          in_row = m < 0 ? -1 : (row_mode == kQuantRowsGather ? m : row);
+        }
+        raw[u] = in_row >= 0 ? __ldg(reinterpret_cast<const uint4*>(
+                                   x + static_cast<int64_t>(in_row) * ld +
+                                   static_cast<int64_t>(kk) * 64) + sub)
+                             : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
       for (int u = 0; u < kQuantUnroll; ++u) {

@@ -1,0 +1,192 @@
+"""An NVFP4 mixture-of-experts feed-forward block built around the grouped GEMM.
+
+    x (bf16 [tokens, H]) --route--> per-expert rows --quantize+gather--> A (NVFP4)
+      --gated grouped GEMM (gate/up, fused SiLU)--> h (fp16 [rows, I])
+      --quantize--> h (NVFP4) --grouped GEMM (down)--> y (fp16 [rows, H])
+      --weighted combine--> out (bf16 [tokens, H])
+
+Every step is a kernel of this library (nvfp4_moe_route, nvfp4_quantize_rows,
+nvfp4_grouped_gemm, nvfp4_moe_combine). Dispatched buffers give every expert's rows a
+128-row-aligned range, so one blocked scale buffer serves all experts and every per-expert
+operand is a view. The host reads the per-expert row counts once per call (one device ->
+host copy) to build the group tables.
+
+The reference has no counterpart: it runs a grouped GEMM whose groups arrive already formed
+and quantised. This is the surrounding layer (token dispatch, activation quantisation,
+down-projection and combine) that a model calls.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _native
+from .interface import grouped_gemm
+from .layout import blocked_sf_bytes
+from .quantize import _DTYPES, global_scale_for
+
+
+@dataclass
+class Routing:
+    """Dispatch metadata of one batch (see nvfp4_moe_route)."""
+
+    tokens: int
+    topk: int
+    num_experts: int
+    counts: list            # rows per expert (host)
+    offsets: list           # first dispatched row per expert, 128-aligned (host, E + 1 entries)
+    dest: torch.Tensor      # int32 [tokens * topk] dispatched row of each pair (-1: dropped)
+    src_rows: torch.Tensor  # int32 [capacity] token of each dispatched row (-1: padding)
+
+    @property
+    def rows(self) -> int:
+        """Dispatched rows including each expert's padding to a multiple of 128."""
+        return self.offsets[-1]
+
+
+def route(topk_ids: torch.Tensor, num_experts: int, stream: torch.cuda.Stream | None = None) -> Routing:
+    """Route (token, slot) pairs to experts: ``topk_ids`` int32 [tokens, topk] on the GPU."""
+    if topk_ids.dtype != torch.int32 or topk_ids.dim() != 2 or not topk_ids.is_cuda:
+        raise ValueError("topk_ids must be a CUDA int32 tensor [tokens, topk]")
+    ids = topk_ids.contiguous()
+    tokens, topk = int(ids.shape[0]), int(ids.shape[1])
+    dev = ids.device
+    pairs = tokens * topk
+    capacity = pairs + 127 * num_experts
+    meta = torch.empty(2 * num_experts + 1, dtype=torch.int32, device=dev)
+    counts, offsets = meta[:num_experts], meta[num_experts:]
+    dest = torch.empty(max(pairs, 1), dtype=torch.int32, device=dev)
+    src_rows = torch.empty(max(capacity, 1), dtype=torch.int32, device=dev)
+    lib = _native.load_library()
+    ws_bytes = int(lib.nvfp4_moe_route_workspace_size(pairs, num_experts))
+    ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
+    s = stream or torch.cuda.current_stream(dev)
+    with torch.cuda.device(dev):
+        _native.check(lib.nvfp4_moe_route(ids.data_ptr(), tokens, topk, num_experts,
+                                          counts.data_ptr(), offsets.data_ptr(), dest.data_ptr(),
+                                          src_rows.data_ptr(), capacity, ws.data_ptr(), ws_bytes,
+                                          s.cuda_stream), lib)
+    host = meta.cpu().tolist()  # the one host read of the call
+    return Routing(tokens, topk, num_experts, host[:num_experts], host[num_experts:],
+                   dest[:pairs], src_rows)
+
+
+def quantize_rows(x: torch.Tensor, rows: int, src_rows: torch.Tensor, mode: int,
+                  global_scale: float, stream: torch.cuda.Stream | None = None) -> tuple:
+    """nvfp4_quantize_rows: ``rows`` output rows through a row map (gather or mask)."""
+    if x.dtype not in _DTYPES or x.dim() != 2 or x.stride(1) != 1 or not x.is_cuda:
+        raise ValueError("x must be a CUDA bf16/fp16 2-D tensor with unit inner stride")
+    cols = int(x.shape[1])
+    packed = torch.empty((rows, cols // 2), dtype=torch.uint8, device=x.device)
+    sf = torch.empty(max(blocked_sf_bytes(rows, cols // 16), 16), dtype=torch.uint8, device=x.device)
+    s = stream or torch.cuda.current_stream(x.device)
+    lib = _native.load_library()
+    with torch.cuda.device(x.device):
+        _native.check(lib.nvfp4_quantize_rows(x.data_ptr(), rows, cols, x.stride(0), _DTYPES[x.dtype],
+                                              float(global_scale), src_rows.data_ptr(), mode,
+                                              packed.data_ptr(), packed.stride(0), sf.data_ptr(),
+                                              s.cuda_stream), lib)
+    return packed, sf
+
+
+def combine(y: torch.Tensor, routing: Routing, topk_weights: torch.Tensor,
+            stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """out[t] = sum_j w[t, j] * y[dest[t, j]] (fp32 accumulation, bf16 result)."""
+    if y.dtype != torch.float16 or y.dim() != 2 or y.stride(1) != 1:
+        raise ValueError("y must be fp16 [rows, cols] with unit inner stride")
+    w = topk_weights.to(torch.float32).contiguous()
+    if tuple(w.shape) != (routing.tokens, routing.topk):
+        raise ValueError("topk_weights must be [tokens, topk]")
+    cols = int(y.shape[1])
+    out = torch.empty((routing.tokens, cols), dtype=torch.bfloat16, device=y.device)
+    s = stream or torch.cuda.current_stream(y.device)
+    lib = _native.load_library()
+    with torch.cuda.device(y.device):
+        _native.check(lib.nvfp4_moe_combine(y.data_ptr(), y.stride(0), routing.dest.data_ptr(),
+                                            w.data_ptr(), routing.tokens, routing.topk, cols,
+                                            out.data_ptr(), out.stride(0), s.cuda_stream), lib)
+    return out
+
+
+def expert_views(routing: Routing, packed: torch.Tensor, sf: torch.Tensor, out: torch.Tensor,
+                 k: int) -> tuple:
+    """Per-expert A, scale and output views into dispatched buffers (no copies)."""
+    sf_block = (k // 64) * 512  # bytes of one 128-row block of scales
+    a, sfa, c, m = [], [], [], []
+    for e in range(routing.num_experts):
+        r0, n_e = routing.offsets[e], routing.counts[e]
+        a.append(packed[r0:r0 + n_e])
+        b0 = (r0 // 128) * sf_block
+        sfa.append(sf[b0:b0 + max(blocked_sf_bytes(n_e, k // 16), 0)])
+        c.append(out[r0:r0 + n_e])
+        m.append(n_e)
+    return a, sfa, c, m
+
+
+@dataclass
+class ExpertWeights:
+    """NVFP4 weights of the experts: gate/up [I, H] and down [H, I] per expert (packed codes,
+    blocked scales) with their per-expert global scales."""
+
+    w_gate: list
+    sf_gate: list
+    w_up: list
+    sf_up: list
+    w_down: list
+    sf_down: list
+    s_gate: list
+    s_up: list
+    s_down: list
+
+    @property
+    def num_experts(self) -> int:
+        return len(self.w_gate)
+
+
+def quantize_expert_weights(gate: list, up: list, down: list) -> ExpertWeights:
+    """Quantise bf16 expert weights (gate/up [I, H], down [H, I]) with this library's kernel."""
+    from .quantize import quantize
+
+    out = {k: [] for k in ("w_gate", "sf_gate", "w_up", "sf_up", "w_down", "sf_down",
+                           "s_gate", "s_up", "s_down")}
+    for g, u, d in zip(gate, up, down):
+        for name, w in (("gate", g), ("up", u), ("down", d)):
+            s = global_scale_for(w)
+            q, sf = quantize(w, s)
+            out[f"w_{name}"].append(q)
+            out[f"sf_{name}"].append(sf)
+            out[f"s_{name}"].append(s)
+    return ExpertWeights(**out)
+
+
+def moe_ffn(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+            weights: ExpertWeights, act_scale: float | None = None,
+            hidden_scale: float | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """One MoE feed-forward block: out[t] = sum_j w[t, j] * down_e(silu(gate_e(x_t)) * up_e(x_t))
+    with e = topk_ids[t, j], all products in NVFP4 with fp32 accumulation.
+
+    ``act_scale`` / ``hidden_scale`` are the per-tensor scales of x and of the SiLU output;
+    when None they are computed from the data (one device reduction and host read each).
+    """
+    tokens, hdim = int(x.shape[0]), int(x.shape[1])
+    E = weights.num_experts
+    idim = int(weights.w_gate[0].shape[0])
+    r = route(topk_ids, E, stream)
+    s_x = global_scale_for(x) if act_scale is None else act_scale
+    a, sfa = quantize_rows(x, r.rows, r.src_rows, _native.ROWS_GATHER, s_x, stream)
+    # Padding rows of h are never written by the GEMM; zero them when the SiLU output's
+    # scale is computed from the data, so that they cannot enter its amax.
+    alloc = torch.zeros if hidden_scale is None else torch.empty
+    h = alloc((max(r.rows, 1), idim), dtype=torch.float16, device=x.device)
+    av, sfav, hv, m = expert_views(r, a, sfa, h, hdim)
+    grouped_gemm(av, weights.w_gate, sfav, weights.sf_gate, hv, [(mi, idim, hdim) for mi in m],
+                 alpha=[s_x * s for s in weights.s_gate], b2=weights.w_up, sfb2=weights.sf_up,
+                 alpha2=[s_x * s for s in weights.s_up], stream=stream)
+    s_h = global_scale_for(h) if hidden_scale is None else hidden_scale
+    a2, sfa2 = quantize_rows(h, r.rows, r.src_rows, _native.ROWS_MASK, s_h, stream)
+    y = torch.empty((max(r.rows, 1), hdim), dtype=torch.float16, device=x.device)
+    av2, sfav2, yv, m2 = expert_views(r, a2, sfa2, y, idim)
+    grouped_gemm(av2, weights.w_down, sfav2, weights.sf_down, yv, [(mi, hdim, idim) for mi in m2],
+                 alpha=[s_h * s for s in weights.s_down], stream=stream)
+    return combine(y, r, topk_weights, stream)
