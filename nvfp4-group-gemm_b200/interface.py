@@ -284,6 +284,20 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
     return list(c)
 
 
+
+def grouped_gemm_table(table: np.ndarray, flags: int, device: torch.device,
+                       stream: torch.cuda.Stream | None = None) -> None:
+    """Launch a prebuilt ``GROUP_DTYPE`` table (device pointers, sizes, scales) through this
+    stream's workspace. For callers that assemble the table themselves from buffers they
+    have already validated (the MoE block builds it from dispatch offsets in a few vectorised
+    column operations); the library still checks every record before launching."""
+    s = stream or torch.cuda.current_stream(device)
+    ws = _workspace_for(device, s, _native.workspace_size(int(table.shape[0])))
+    with torch.cuda.device(device):
+        _native.grouped_gemm_raw(table, flags, ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
+    ws.last_table = None  # the next grouped_gemm call on this stream rebuilds its descriptors
+    ws.last_sig = None
+
 class GroupedGemmPlan:
     """A grouped launch validated once and then run many times on the same tensors.
 

@@ -19,10 +19,11 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import _native
-from .interface import grouped_gemm
+from .interface import grouped_gemm, grouped_gemm_table
 from .layout import blocked_sf_bytes
 from .quantize import _DTYPES, global_scale_for
 
@@ -143,6 +144,13 @@ class ExpertWeights:
     def num_experts(self) -> int:
         return len(self.w_gate)
 
+    def pointers(self) -> dict:
+        """Device addresses of every expert's weights and scales (computed once)."""
+        if getattr(self, "_ptrs", None) is None:
+            self._ptrs = {name: np.array([t.data_ptr() for t in getattr(self, name)], dtype=np.uint64)
+                          for name in ("w_gate", "sf_gate", "w_up", "sf_up", "w_down", "sf_down")}
+        return self._ptrs
+
 
 def quantize_expert_weights(gate: list, up: list, down: list) -> ExpertWeights:
     """Quantise bf16 expert weights (gate/up [I, H], down [H, I]) with this library's kernel."""
@@ -158,6 +166,30 @@ def quantize_expert_weights(gate: list, up: list, down: list) -> ExpertWeights:
             out[f"sf_{name}"].append(sf)
             out[f"s_{name}"].append(s)
     return ExpertWeights(**out)
+
+
+def dispatched_table(routing: Routing, a: torch.Tensor, sfa: torch.Tensor, c: torch.Tensor,
+                     b_ptrs: np.ndarray, sfb_ptrs: np.ndarray, n: int, k: int, alpha: np.ndarray,
+                     b2_ptrs: np.ndarray | None = None, sfb2_ptrs: np.ndarray | None = None,
+                     alpha2: np.ndarray | None = None) -> np.ndarray:
+    """Group table of a grouped GEMM over dispatched buffers: expert e's A rows, scale block
+    and output rows start at routing.offsets[e]; built with vectorised column operations."""
+    E = routing.num_experts
+    off = np.asarray(routing.offsets[:E], dtype=np.uint64)
+    t = np.zeros(E, dtype=_native.GROUP_DTYPE)
+    t["a"] = a.data_ptr() + off * np.uint64(k // 2)
+    t["sfa"] = sfa.data_ptr() + (off // np.uint64(128)) * np.uint64((k // 64) * 512)
+    t["c"] = c.data_ptr() + off * np.uint64(n * c.element_size())
+    t["b"], t["sfb"] = b_ptrs, sfb_ptrs
+    if b2_ptrs is not None:
+        t["b2"], t["sfb2"] = b2_ptrs, sfb2_ptrs
+        t["alpha2"] = alpha2
+    else:
+        t["alpha2"] = 1.0
+    t["m"] = np.asarray(routing.counts, dtype=np.int32)
+    t["n"], t["k"] = n, k
+    t["alpha"] = alpha
+    return t
 
 
 def moe_ffn(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
@@ -179,14 +211,15 @@ def moe_ffn(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
     # scale is computed from the data, so that they cannot enter its amax.
     alloc = torch.zeros if hidden_scale is None else torch.empty
     h = alloc((max(r.rows, 1), idim), dtype=torch.float16, device=x.device)
-    av, sfav, hv, m = expert_views(r, a, sfa, h, hdim)
-    grouped_gemm(av, weights.w_gate, sfav, weights.sf_gate, hv, [(mi, idim, hdim) for mi in m],
-                 alpha=[s_x * s for s in weights.s_gate], b2=weights.w_up, sfb2=weights.sf_up,
-                 alpha2=[s_x * s for s in weights.s_up], stream=stream)
+    P = weights.pointers()
+    t1 = dispatched_table(r, a, sfa, h, P["w_gate"], P["sf_gate"], idim, hdim,
+                          s_x * np.asarray(weights.s_gate, dtype=np.float32),
+                          P["w_up"], P["sf_up"], s_x * np.asarray(weights.s_up, dtype=np.float32))
+    grouped_gemm_table(t1, _native.FLAG_GATED, x.device, stream)
     s_h = global_scale_for(h) if hidden_scale is None else hidden_scale
     a2, sfa2 = quantize_rows(h, r.rows, r.src_rows, _native.ROWS_MASK, s_h, stream)
     y = torch.empty((max(r.rows, 1), hdim), dtype=torch.float16, device=x.device)
-    av2, sfav2, yv, m2 = expert_views(r, a2, sfa2, y, idim)
-    grouped_gemm(av2, weights.w_down, sfav2, weights.sf_down, yv, [(mi, hdim, idim) for mi in m2],
-                 alpha=[s_h * s for s in weights.s_down], stream=stream)
+    t2 = dispatched_table(r, a2, sfa2, y, P["w_down"], P["sf_down"], hdim, idim,
+                          s_h * np.asarray(weights.s_down, dtype=np.float32))
+    grouped_gemm_table(t2, 0, x.device, stream)
     return combine(y, r, topk_weights, stream)
