@@ -374,12 +374,14 @@ def run_moe(args):
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / steps
     # Per-stage split of one call (events between the stages of moe_ffn).
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
     ev[0].record()
     r = pkg.moe.route(ids, E)
     ev[1].record()
-    a, sfa = pkg.moe.quantize_rows(x, r.rows, r.src_rows, pkg._native.ROWS_GATHER, s_x)
+    qx, sfx = pkg.quantize(x, s_x)
     ev[2].record()
+    a, sfa = pkg.moe.gather_quantized(qx, sfx, r)
+    ev[3].record()
     h = torch.empty((r.rows, I), dtype=torch.float16, device=dev)
     P = weights.pointers()
     t1 = pkg.moe.dispatched_table(r, a, sfa, h, P["w_gate"], P["sf_gate"], I, H,
@@ -387,19 +389,19 @@ def run_moe(args):
                                   P["w_up"], P["sf_up"],
                                   s_x * np.asarray(weights.s_up, dtype=np.float32))
     pkg.interface.grouped_gemm_table(t1, pkg._native.FLAG_GATED, dev)
-    ev[3].record()
-    a2, sfa2 = pkg.moe.quantize_rows(h, r.rows, r.src_rows, pkg._native.ROWS_MASK, s_h)
     ev[4].record()
+    a2, sfa2 = pkg.moe.quantize_rows(h, r.rows, r.src_rows, pkg._native.ROWS_MASK, s_h)
+    ev[5].record()
     y = torch.empty((r.rows, H), dtype=torch.float16, device=dev)
     t2 = pkg.moe.dispatched_table(r, a2, sfa2, y, P["w_down"], P["sf_down"], H, I,
                                   s_h * np.asarray(weights.s_down, dtype=np.float32))
     pkg.interface.grouped_gemm_table(t2, 0, dev)
-    ev[5].record()
-    pkg.moe.combine(y, r, wts)
     ev[6].record()
+    pkg.moe.combine(y, r, wts)
+    ev[7].record()
     torch.cuda.synchronize(dev)
-    names = ["route (incl. host read)", "dispatch + quantise x", "gate/up GEMM + SiLU",
-             "quantise h", "down GEMM", "combine"]
+    names = ["route (incl. host read)", "quantise x (once per token)", "dispatch (gather codes + scales)",
+             "gate/up GEMM + SiLU", "quantise h", "down GEMM", "combine"]
     split = {n: ev[i].elapsed_time(ev[i + 1]) * 1e3 for i, n in enumerate(names)}
     rows = int(sum(r.counts))
     flops = 6.0 * rows * H * I
@@ -417,7 +419,7 @@ def run_moe(args):
         "config": {"workload": "moe:cfg5", "experts": E, "tokens": T, "topk": topk, "hidden": H,
                    "intermediate": I, "dispatched_rows": r.rows,
                    "l2": "inputs larger than L2 (126 MB); no flush"},
-        "gpu_launches_per_call": 3 + 1 + 1 + 1 + 1 + 1,
+        "gpu_launches_per_call": "route 3, quantise 1, gather 2, gate/up GEMM 1 (+ descriptor uploads), quantise 1, down GEMM 1 (+ uploads), combine 1",
         "stage_us": split,
         "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
                      "frac": tf / peak, "peak_source": f"{kind}: 4 x bf16 (sustained)",

@@ -181,6 +181,20 @@ NVFP4_API int nvfp4_moe_route(const int32_t* topk_ids, int tokens, int topk, int
                               void* stream);
 
 /*
+ * MoE dispatch of quantised rows (no counterpart in the reference): dispatched row r
+ * receives packed row src_rows[r] of packed_src ([*, cols/2] bytes, row stride ld_src) and its
+ * scales from sf_src (blocked layout of the source rows) into packed_dst (row stride ld_dst)
+ * and sf_dst (blocked layout of `rows` rows); rows with src_rows[r] < 0 become zeros.
+ * Quantising tokens once with nvfp4_quantize and gathering equals nvfp4_quantize_rows in
+ * gather mode bit for bit, with a quarter of the bytes read per dispatched row.
+ * cols a multiple of 64; buffers 16-byte aligned; strides multiples of 16 bytes.
+ */
+NVFP4_API int nvfp4_moe_gather_quantized(const void* packed_src, int64_t ld_src,
+                                         const void* sf_src, const int32_t* src_rows, int rows,
+                                         int cols, void* packed_dst, int64_t ld_dst, void* sf_dst,
+                                         void* stream);
+
+/*
  * MoE combine (no counterpart in the reference): out[t, :] = bf16( sum_j weights[t, j] *
  * y[dest[t * topk + j], :] ), y fp16 [dispatched rows, cols] (row stride ldy elements),
  * weights fp32 [tokens, topk], out bf16 [tokens, cols] (row stride ldo); fp32 products and

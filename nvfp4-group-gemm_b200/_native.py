@@ -60,6 +60,7 @@ EXPORTED_SYMBOLS = (
     "nvfp4_moe_route_workspace_size",
     "nvfp4_moe_route",
     "nvfp4_moe_combine",
+    "nvfp4_moe_gather_quantized",
 )
 
 # Row-map modes of nvfp4_quantize_rows (NVFP4_ROWS_*).
@@ -170,6 +171,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_moe_route.restype = i32
         lib.nvfp4_moe_combine.argtypes = [vp, i64, vp, vp, i32, i32, i32, vp, i64, vp]
         lib.nvfp4_moe_combine.restype = i32
+        lib.nvfp4_moe_gather_quantized.argtypes = [vp, i64, vp, vp, i32, i32, vp, i64, vp, vp]
+        lib.nvfp4_moe_gather_quantized.restype = i32
         if path is None:
             _lib = lib
         return lib

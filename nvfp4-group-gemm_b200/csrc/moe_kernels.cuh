@@ -171,4 +171,58 @@ __global__ void __launch_bounds__(256) nvfp4_moe_combine_kernel(
   }
 }
 
+// Dispatch of already-quantised rows: dispatched row r takes packed row src_rows[r] and its
+// scales (zeros where src_rows[r] < 0). Quantisation is row-local, so quantising each token
+// once and gathering is bit-identical to quantising the gathered bf16 rows, with a quarter of
+// the bytes moved per dispatched row (K/2 + K/16 instead of 2K read).
+// Packed rows: one warp per dispatched row, 16 bytes per lane.
+__global__ void __launch_bounds__(256) nvfp4_gather_packed_rows_kernel(
+    const uint8_t* __restrict__ src, int64_t ld_src, const int32_t* __restrict__ src_rows,
+    int rows, int row_bytes, uint8_t* __restrict__ dst, int64_t ld_dst) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int chunks = row_bytes / 16;
+  for (int64_t r = warp0; r < rows; r += nwarps) {
+    const int32_t s = __ldg(src_rows + r);
+    uint4* d = reinterpret_cast<uint4*>(dst + r * ld_dst);
+    if (s >= 0) {
+      const uint4* q = reinterpret_cast<const uint4*>(src + static_cast<int64_t>(s) * ld_src);
+      for (int c = lane; c < chunks; c += 32) d[c] = __ldg(q + c);
+    } else {
+      for (int c = lane; c < chunks; c += 32) d[c] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
+// Blocked scales: one warp per destination 512-byte block (128 rows mm, 4 scale columns kk);
+// lane i0 assembles the block's 16-byte row i0 from the four rows 32*i1 + i0 (their 4-byte
+// groups in the source blocked layout) and stores it in one piece.
+__global__ void __launch_bounds__(256) nvfp4_gather_blocked_scales_kernel(
+    const uint8_t* __restrict__ sf_src, const int32_t* __restrict__ src_rows, int rows,
+    int rest_k, uint8_t* __restrict__ sf_dst) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int row_blocks = (rows + 127) / 128;
+  const int64_t tasks = static_cast<int64_t>(row_blocks) * rest_k;
+  for (int64_t task = warp0; task < tasks; task += nwarps) {
+    const int mm = static_cast<int>(task / rest_k);
+    const int kk = static_cast<int>(task % rest_k);
+    uint32_t w[4];
+#pragma unroll
+    for (int i1 = 0; i1 < 4; ++i1) {
+      const int r = mm * 128 + i1 * 32 + lane;
+      const int32_t s = r < rows ? __ldg(src_rows + r) : -1;
+      w[i1] = 0u;
+      if (s >= 0) {
+        const int64_t off = ((static_cast<int64_t>(s >> 7) * rest_k + kk) * 32 + (s & 31)) * 16 +
+                            ((s & 127) >> 5) * 4;
+        w[i1] = __ldg(reinterpret_cast<const uint32_t*>(sf_src + off));
+      }
+    }
+    *reinterpret_cast<uint4*>(sf_dst + (task * 32 + lane) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 }  // namespace nvfp4

@@ -749,6 +749,37 @@ NVFP4_API int nvfp4_moe_route(const int32_t* topk_ids, int tokens, int topk, int
   return NVFP4_OK;
 }
 
+NVFP4_API int nvfp4_moe_gather_quantized(const void* packed_src, int64_t ld_src,
+                                         const void* sf_src, const int32_t* src_rows, int rows,
+                                         int cols, void* packed_dst, int64_t ld_dst, void* sf_dst,
+                                         void* stream) {
+  g_last_error.clear();
+  if (rows < 0 || cols <= 0 || cols % 64 != 0)
+    return fail(NVFP4_ERR_BAD_SHAPE, "rows=%d cols=%d (cols a positive multiple of 64)", rows, cols);
+  if (rows == 0) return NVFP4_OK;
+  if (packed_src == nullptr || sf_src == nullptr || src_rows == nullptr || packed_dst == nullptr ||
+      sf_dst == nullptr)
+    return fail(NVFP4_ERR_NULL_POINTER, "a gather buffer is NULL");
+  if (ld_src < cols / 2 || ld_dst < cols / 2)
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "row strides smaller than cols/2 bytes");
+  if (!aligned16(packed_src) || !aligned16(packed_dst) || !aligned16(sf_src) || !aligned16(sf_dst) ||
+      ld_src % 16 != 0 || ld_dst % 16 != 0)
+    return fail(NVFP4_ERR_MISALIGNED, "buffers must be 16-byte aligned, row strides multiples of 16");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t row_blocks = std::min<int64_t>((static_cast<int64_t>(rows) + 7) / 8, 148 * 16);
+  nvfp4_gather_packed_rows_kernel<<<static_cast<unsigned>(row_blocks), 256, 0, s>>>(
+      static_cast<const uint8_t*>(packed_src), ld_src, src_rows, rows, cols / 2,
+      static_cast<uint8_t*>(packed_dst), ld_dst);
+  const int rest_k = cols / 64;
+  const int64_t sf_tasks = static_cast<int64_t>((rows + 127) / 128) * rest_k;
+  const int64_t sf_blocks = std::min<int64_t>((sf_tasks + 7) / 8, 148 * 16);
+  nvfp4_gather_blocked_scales_kernel<<<static_cast<unsigned>(sf_blocks), 256, 0, s>>>(
+      static_cast<const uint8_t*>(sf_src), src_rows, rows, rest_k, static_cast<uint8_t*>(sf_dst));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gather launch");
+  return NVFP4_OK;
+}
+
 NVFP4_API int nvfp4_moe_combine(const void* y, int64_t ldy, const int32_t* dest,
                                 const float* weights, int tokens, int topk, int cols, void* out,
                                 int64_t ldo, void* stream) {

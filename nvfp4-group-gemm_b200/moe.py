@@ -25,7 +25,7 @@ import torch
 from . import _native
 from .interface import grouped_gemm, grouped_gemm_table
 from .layout import blocked_sf_bytes
-from .quantize import _DTYPES, global_scale_for
+from .quantize import _DTYPES, global_scale_for, quantize
 
 
 @dataclass
@@ -91,6 +91,25 @@ def quantize_rows(x: torch.Tensor, rows: int, src_rows: torch.Tensor, mode: int,
     return packed, sf
 
 
+def gather_quantized(packed: torch.Tensor, sf: torch.Tensor, routing: Routing,
+                     stream: torch.cuda.Stream | None = None) -> tuple:
+    """Dispatch already-quantised token rows (``quantize(x)``'s packed codes and blocked
+    scales) into the dispatched order: bit-identical to quantising the gathered rows, with a
+    quarter of the bytes moved per dispatched row."""
+    rows = routing.rows
+    cols = int(packed.shape[1]) * 2
+    out = torch.empty((rows, cols // 2), dtype=torch.uint8, device=packed.device)
+    out_sf = torch.empty(max(blocked_sf_bytes(rows, cols // 16), 16), dtype=torch.uint8,
+                         device=packed.device)
+    s = stream or torch.cuda.current_stream(packed.device)
+    lib = _native.load_library()
+    with torch.cuda.device(packed.device):
+        _native.check(lib.nvfp4_moe_gather_quantized(
+            packed.data_ptr(), packed.stride(0), sf.data_ptr(), routing.src_rows.data_ptr(), rows,
+            cols, out.data_ptr(), out.stride(0), out_sf.data_ptr(), s.cuda_stream), lib)
+    return out, out_sf
+
+
 def combine(y: torch.Tensor, routing: Routing, topk_weights: torch.Tensor,
             stream: torch.cuda.Stream | None = None) -> torch.Tensor:
     """out[t] = sum_j w[t, j] * y[dest[t, j]] (fp32 accumulation, bf16 result)."""
@@ -154,8 +173,6 @@ class ExpertWeights:
 
 def quantize_expert_weights(gate: list, up: list, down: list) -> ExpertWeights:
     """Quantise bf16 expert weights (gate/up [I, H], down [H, I]) with this library's kernel."""
-    from .quantize import quantize
-
     out = {k: [] for k in ("w_gate", "sf_gate", "w_up", "sf_up", "w_down", "sf_down",
                            "s_gate", "s_up", "s_down")}
     for g, u, d in zip(gate, up, down):
@@ -206,7 +223,9 @@ def moe_ffn(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
     idim = int(weights.w_gate[0].shape[0])
     r = route(topk_ids, E, stream)
     s_x = global_scale_for(x) if act_scale is None else act_scale
-    a, sfa = quantize_rows(x, r.rows, r.src_rows, _native.ROWS_GATHER, s_x, stream)
+    # Each token is quantised once and its codes and scales are gathered topk times.
+    qx, sfx = quantize(x, s_x, stream=stream)
+    a, sfa = gather_quantized(qx, sfx, r, stream)
     # Padding rows of h are never written by the GEMM; zero them when the SiLU output's
     # scale is computed from the data, so that they cannot enter its amax.
     alloc = torch.zeros if hidden_scale is None else torch.empty

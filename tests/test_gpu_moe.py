@@ -50,6 +50,12 @@ def test_gather_quantize_and_combine_bit_exact(pkg):
     exp_packed, exp_sf = Q.quantize_nvfp4_blocked(xg, sg)
     assert np.array_equal(a.cpu().numpy(), exp_packed)
     assert np.array_equal(sf.cpu().numpy()[:exp_sf.size], exp_sf)
+    # Quantise once, then gather: the same bytes.
+    qx, sfx = pkg.quantize(x.cuda(), sg)
+    a2, sf2 = pkg.moe.gather_quantized(qx, sfx, r)
+    torch.cuda.synchronize()
+    assert torch.equal(a2, a)
+    assert torch.equal(sf2[:exp_sf.size], sf[:exp_sf.size])
     # combine of an arbitrary fp16 dispatched buffer
     y = (torch.randn((r.rows, hdim), generator=torch.Generator().manual_seed(3))).to(torch.float16)
     w = torch.rand((tokens, topk), generator=torch.Generator().manual_seed(4))
