@@ -221,6 +221,9 @@ def moe_ffn(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
     tokens, hdim = int(x.shape[0]), int(x.shape[1])
     E = weights.num_experts
     idim = int(weights.w_gate[0].shape[0])
+    if hdim % 256 or idim % 256:
+        raise ValueError(f"hidden ({hdim}) and intermediate ({idim}) sizes must be multiples of 256 "
+                         "(the K of the two grouped GEMMs)")
     r = route(topk_ids, E, stream)
     s_x = global_scale_for(x) if act_scale is None else act_scale
     # Each token is quantised once and its codes and scales are gathered topk times.

@@ -113,3 +113,25 @@ def test_moe_ffn_stage_by_stage_and_end_to_end(pkg):
         exp = O.ref_gated(ae, bg, bu, sfa_e, sfg, sfu, s_x * W.s_gate[e], s_x * W.s_up[e])
         res = O.compare_fp16(hv[e].cpu().numpy(), exp, None, rtol=1e-2, atol=1e-2)
         assert res["ok"], (e, res)
+
+
+@pytest.mark.parametrize("tokens,topk,experts", [(1, 1, 4), (3, 2, 64), (0, 2, 4)])
+def test_moe_ffn_edge_cases(pkg, tokens, topk, experts):
+    """A single token, most experts unused, and an empty batch."""
+    hdim, idim = 256, 256
+    g = torch.Generator().manual_seed(tokens + experts)
+    x = torch.randn((tokens, hdim), generator=g).to(torch.bfloat16).cuda()
+    gate = [(torch.randn((idim, hdim), generator=g) * 0.05).to(torch.bfloat16).cuda() for _ in range(experts)]
+    up = [(torch.randn((idim, hdim), generator=g) * 0.05).to(torch.bfloat16).cuda() for _ in range(experts)]
+    down = [(torch.randn((hdim, idim), generator=g) * 0.05).to(torch.bfloat16).cuda() for _ in range(experts)]
+    W = pkg.moe.quantize_expert_weights(gate, up, down)
+    ids = torch.from_numpy(_ids(tokens, topk, experts, seed=3) if tokens else
+                           np.zeros((0, topk), dtype=np.int32)).cuda()
+    wts = torch.full((tokens, topk), 1.0 / topk, device="cuda")
+    out = pkg.moe.moe_ffn(x, ids, wts, W, act_scale=0.01, hidden_scale=0.001)
+    torch.cuda.synchronize()
+    assert out.shape == (tokens, hdim)
+    if tokens:
+        assert torch.isfinite(out.float()).all()
+        r = pkg.moe.route(ids, experts)
+        assert sum(r.counts) == tokens * topk and r.rows % 128 == 0
