@@ -596,6 +596,50 @@ def main():
     flops_rank = prob.flops()
     value = flops_rank * world / (ms_per_step * 1e-3) / 1e12
 
+    # ---------------------------------------------------------------- library baseline
+    # The reference's own GPU arithmetic (ref_kernel: torch._scaled_mm, i.e. cuBLASLt's
+    # block-scaled NVFP4 GEMM) once per group on the same device-resident inputs; gated
+    # configurations run it twice per group plus silu(g) * u, as the reference's path does.
+    lib_base = None
+    if rank == 0 and world == 1:
+        try:
+            f4 = torch.float4_e2m1fn_x2
+            e4 = torch.float8_e4m3fn
+            ops = []
+            for g in range(prob.num_groups):
+                if prob.m[g] == 0:
+                    continue
+                a4 = prob.a[g].view(f4)
+                ops.append((a4, prob.b[g].view(f4).t(), prob.sfa[g].view(e4), prob.sfb[g].view(e4),
+                            None if not prob.gated else prob.b2[g].view(f4).t(),
+                            None if not prob.gated else prob.sfb2[g].view(e4)))
+
+            def lib_step():
+                for a4, bt, sa, sb, b2t, sb2 in ops:
+                    t1 = torch._scaled_mm(a4, bt, sa, sb, out_dtype=torch.float16)
+                    if b2t is not None:
+                        t2 = torch._scaled_mm(a4, b2t, sa, sb2, out_dtype=torch.float16)
+                        (torch.nn.functional.silu(t1.float()) * t2.float()).half()
+
+            for _ in range(3):
+                lib_step()
+            torch.cuda.synchronize(dev)
+            l0 = torch.cuda.Event(enable_timing=True)
+            l1 = torch.cuda.Event(enable_timing=True)
+            l0.record(stream)
+            for _ in range(args.steps):
+                lib_step()
+            l1.record(stream)
+            torch.cuda.synchronize(dev)
+            lib_ms = l0.elapsed_time(l1) / args.steps
+            lib_base = {"us_per_call": lib_ms * 1e3,
+                        "value": prob.flops() / (lib_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                        "what": "torch._scaled_mm (cuBLASLt block-scaled NVFP4) once per group"
+                                + (" x2 + silu(g)*u" if prob.gated else "")
+                                + ", device-resident, timed like value (no sustain window)"}
+        except Exception as exc:  # the library path is a comparison, not part of the product
+            lib_base = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+
     # ---------------------------------------------------------------- end to end (host buffers)
     e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
     host_in = [t.cpu().pin_memory() for t in
@@ -706,6 +750,8 @@ def main():
     }
     if gather is not None:
         line["with_gather"] = gather
+    if lib_base is not None:
+        line["library_baseline"] = lib_base
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
