@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tile-n", type=int, default=None)
     ap.add_argument("--cta", default=None, choices=[None, "pair", "single", "weights"])
+    ap.add_argument("--split-k", action="store_true",
+                    help="let single-CTA launches split the K loop of their last partial wave")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
@@ -465,7 +467,7 @@ def main():
     # built once, so each step is one library call (no per-tensor Python work).
     plan = pkg.GroupedGemmPlan(prob.a, prob.b, prob.sfa, prob.sfb, prob.c, sizes,
                                alpha=prob.alpha, b2=prob.b2, sfb2=prob.sfb2, alpha2=prob.alpha2,
-                               tile_n=args.tile_n, cta=args.cta)
+                               tile_n=args.tile_n, cta=args.cta, split_k=args.split_k)
 
     def step():
         plan.run(stream)
@@ -653,7 +655,7 @@ def main():
         for h, d in zip(host_in, dev_in):
             d.copy_(h, non_blocking=True)
         pkg.custom_kernel(data, global_scales=scales, tile_n=args.tile_n, stream=stream,
-                          cta=args.cta)
+                          cta=args.cta, split_k=args.split_k)
         for h, c in zip(host_out, prob.c):
             h.copy_(c, non_blocking=True)
 
@@ -723,7 +725,8 @@ def main():
                    "l2": ("inputs smaller than L2 (126 MB): 256 MiB flush before every timed "
                           "call, outside its events" if flush_l2 else
                           "inputs larger than L2 (126 MB); no flush"),
-                   "parallelism": f"ep{world} (experts sharded, no data-path collective)"},
+                   "parallelism": f"ep{world} (experts sharded, no data-path collective)",
+                   **({"split_k": True} if args.split_k else {})},
         "gpu_launches": args.steps,  # one persistent GEMM kernel per timed call (descriptors reused)
         "api": "GroupedGemmPlan.run (value, burst); custom_kernel(data) (e2e)",
         "device_error_bits": errors,

@@ -62,6 +62,8 @@ typedef enum nvfp4_status {
                                        Default: CTA pairs when the non-empty groups average
                                        at least 192 rows, or at least 96 rows with
                                        K >= 4096; single CTAs otherwise */
+#define NVFP4_FLAG_SPLIT_K 0x100u /* allow split-K of a single-CTA launch's last partial wave
+                                     (needs the split scratch, see NVFP4_SPLIT_SCRATCH_BYTES) */
 #define NVFP4_FLAG_WEIGHT_STATIONARY 0x80u /* force the weight-stationary kernel (non-gated
                                               only): tiles of 128 weight rows x 64 token
                                               rows, computed as C^T so that small groups
@@ -114,6 +116,19 @@ NVFP4_API size_t nvfp4_workspace_size(int num_groups);
  */
 NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsigned int flags,
                                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Extra workspace for split-K: with NVFP4_FLAG_SPLIT_K and workspace_bytes at least
+ * nvfp4_workspace_size(num_groups) rounded up to 256, plus this, single-CTA launches split
+ * the K loop of the tiles that would otherwise run in a last, partly idle wave (all tiles,
+ * when the launch has fewer tiles than the GPU has SMs) into several units; each writes an
+ * fp32 partial tile to this space and the last part of a tile to finish sums the parts in a
+ * fixed order and writes C (results are bit-identical from run to run). Zero-filled before
+ * its first use, like the rest of the workspace. 4 KiB of counters + 148 x 128 KiB. Opt-in:
+ * the final sum of a tile runs on one SM, which on the shapes measured cost more than the
+ * balanced tail saved (cfg4-like 64 experts: 138 vs 52 us per call).
+ */
+#define NVFP4_SPLIT_SCRATCH_BYTES (4096u + 148u * 131072u)
 
 /*
  * Convert plain row-major E4M3 scales [rows, sf_cols] (row stride `ld` bytes)

@@ -36,6 +36,7 @@ FLAG_CTA_PAIR = 0x10
 FLAG_SINGLE_CTA = 0x20
 FLAG_DIAG_SKIP_MMA = 0x40
 FLAG_WEIGHT_STATIONARY = 0x80
+FLAG_SPLIT_K = 0x100
 
 # Device error bits (WorkspaceHeader::error_bits).
 DEV_ERR_PRODUCER_TIMEOUT = 1 << 0
@@ -73,6 +74,9 @@ DTYPE_FP16 = 1
 
 # Largest group count nvfp4_grouped_gemm_noalloc accepts (NVFP4_NOALLOC_MAX_GROUPS).
 NOALLOC_MAX_GROUPS = 512
+
+# Extra workspace that enables split-K of a launch's last partial wave (NVFP4_SPLIT_SCRATCH_BYTES).
+SPLIT_SCRATCH_BYTES = 4096 + 148 * 131072
 
 
 class Nvfp4Group(ctypes.Structure):
@@ -190,6 +194,12 @@ def check(status: int, lib: ctypes.CDLL | None = None) -> None:
 
 def workspace_size(num_groups: int) -> int:
     return int(load_library().nvfp4_workspace_size(num_groups))
+
+
+def workspace_size_with_split(num_groups: int) -> int:
+    """Workspace bytes that also enable split-K: the workspace rounded up to 256 bytes plus
+    SPLIT_SCRATCH_BYTES."""
+    return (workspace_size(num_groups) + 255) // 256 * 256 + SPLIT_SCRATCH_BYTES
 
 
 def sf_blocked_size(rows: int, sf_cols: int) -> int:

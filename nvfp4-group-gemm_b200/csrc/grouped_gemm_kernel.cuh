@@ -103,7 +103,7 @@ struct GemmConfig {
   // mbarriers (stage ring, accumulators, drain, tile-schedule ring), TMEM address and
   // abort flag, tile-schedule slots.
   static constexpr int kBarrierBytes =
-      8 * (2 * STAGES + 2 * kAccStages + 1 + 2 * kSchedSlots) + 16 + 16 * kSchedSlots;
+      8 * (2 * STAGES + 2 * kAccStages + 1 + 2 * kSchedSlots + 2) + 16 + 16 * kSchedSlots;
   static constexpr int kSmemBytes = 1024 /*alignment slack*/ + STAGES * kStageBytes + kEpiBytes +
                                     kBarrierBytes + kTileEndBytes;
   static_assert(kSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
@@ -178,6 +178,31 @@ __device__ __forceinline__ int advance_group(const int32_t* ends, const GroupDev
   return lo;
 }
 
+// Work units: tiles [0, split_first_tile) are one unit each; every later tile is split into
+// split_parts units along K (split s takes k-tiles [s*kt/S, (s+1)*kt/S)), which come last
+// in the unit order. split = -1 marks an unsplit tile.
+__device__ __forceinline__ void unit_tile(const GemmParams& p, int unit, int& tile, int& split) {
+  if (unit < p.split_first_tile) {
+    tile = unit;
+    split = -1;
+  } else {
+    const int r = unit - p.split_first_tile;
+    tile = p.split_first_tile + r / p.split_parts;
+    split = r % p.split_parts;
+  }
+}
+
+__device__ __forceinline__ void unit_krange(const GemmParams& p, int split, int ktiles, int& k0,
+                                            int& k1) {
+  if (split < 0) {
+    k0 = 0;
+    k1 = ktiles;
+  } else {
+    k0 = split * ktiles / p.split_parts;
+    k1 = (split + 1) * ktiles / p.split_parts;
+  }
+}
+
 // Dynamic schedule bookkeeping in the workspace header: counter[0] hands out tiles,
 // counter[1] counts CTAs that have finished. The last CTA to finish sets both back to
 // zero, so the next launch on the same workspace starts from zero without a memset.
@@ -207,9 +232,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint64_t* drain_bar = acce_bar + Cfg::kAccStages;
   uint64_t* sched_full = drain_bar + 1;
   uint64_t* sched_empty = sched_full + kSchedSlots;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sched_empty + kSchedSlots);
+  uint64_t* split_arrive = sched_empty + kSchedSlots;  // epilogue warps wrote their partials
+  uint64_t* split_result = split_arrive + 1;           // the leader published "last part"
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(split_result + 1);
   volatile uint32_t* abort_flag = tmem_holder + 1;
-  // Slot i: {tile, group, K, unused}; a tile >= total_tiles marks the end of the schedule.
+  volatile uint32_t* split_last = tmem_holder + 2;
+  // Slot i: {unit, group, first k-tile, end k-tile}; a unit >= total_units ends the schedule.
   volatile int32_t* sched_info = reinterpret_cast<volatile int32_t*>(tmem_holder + 4);
   int32_t* tile_ends = const_cast<int32_t*>(sched_info + 4 * kSchedSlots);
 
@@ -231,6 +259,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       ptx::mbar_init(&sched_full[i], 1);
       ptx::mbar_init(&sched_empty[i], kSchedConsumers);
     }
+    ptx::mbar_init(split_arrive, kEpilogueWarps);
+    ptx::mbar_init(split_result, 1);
     *abort_flag = 0u;
     ptx::fence_mbarrier_init();
   }
@@ -262,21 +292,27 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         ptx::tensormap_fence_acquire(&m[kMapB]);
         if (GATED) ptx::tensormap_fence_acquire(&m[kMapB2]);
       };
-      int tile = blockIdx.x;  // grid <= total_tiles: every CTA has a first tile
+      int unit = blockIdx.x;  // grid <= total_units: every CTA has a first unit
+      int tile, split;
+      unit_tile(p, unit, tile, split);
       int g = advance_group(tile_ends, groups, p.num_groups, 0, tile);
       GroupDev gd = groups[g];
       acquire_maps(g);
       for (uint32_t seq = 0;; ++seq) {
-        // Publish this CTA's seq-th tile (or the end marker) to the MMA issuer and epilogue.
+        // Publish this CTA's seq-th unit (or the end marker) to the MMA issuer and epilogue:
+        // {unit, group, first k-tile, end k-tile}.
         const int slot = static_cast<int>(seq % kSchedSlots);
         if (!wait_phase(&sched_empty[slot], ((seq / kSchedSlots) & 1u) ^ 1u, abort_flag,
                         p.error_bits, kDevErrProducerTimeout))
           break;
-        sched_info[4 * slot + 0] = tile;
+        int k0 = 0, k1 = 0;
+        if (unit < p.total_units) unit_krange(p, split, gd.k / kBlockK, k0, k1);
+        sched_info[4 * slot + 0] = unit;
         sched_info[4 * slot + 1] = g;
-        sched_info[4 * slot + 2] = gd.k;
+        sched_info[4 * slot + 2] = k0;
+        sched_info[4 * slot + 3] = k1;
         ptx::mbar_arrive(&sched_full[slot]);
-        if (tile >= p.total_tiles) break;
+        if (unit >= p.total_units) break;
         const TmaDesc* maps = p.maps + static_cast<size_t>(g) * kMapsPerGroup;
         const int local = tile - gd.tile_start;
         const int mt = local % gd.tiles_m;
@@ -331,25 +367,28 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (sfb_blk1 != nullptr) ptx::bulk_prefetch_l2(sfb_blk1 + psf, 4 * kSfBlockBytes);
           }
         };
-        const int claim_kt = ktiles > kClaimLeadKTiles ? ktiles - kClaimLeadKTiles : 0;
-        int next_tile = p.total_tiles;
+        const int claim_kt = k1 - k0 > kClaimLeadKTiles ? k1 - kClaimLeadKTiles : k0;
+        int next_unit = p.total_units;
+        int next_tile = p.total_tiles, next_split = -1;
         int g_next = g;
         GroupDev next_gd = gd;
         bool resolved = false;
         auto claim_next = [&]() -> int {
           if (p.dynamic_schedule)
             return static_cast<int>(gridDim.x + atomicAdd(p.tile_counter, 1u));
-          return tile + static_cast<int>(gridDim.x);
+          return unit + static_cast<int>(gridDim.x);
         };
         auto resolve_next = [&]() {
           resolved = true;
-          if (next_tile >= p.total_tiles) return;
+          if (next_unit >= p.total_units) return;
+          unit_tile(p, next_unit, next_tile, next_split);
           g_next = advance_group(tile_ends, groups, p.num_groups, g, next_tile);
           next_gd = groups[g_next];
           if (g_next != g) acquire_maps(g_next);
         };
-        for (int kt = 0; kt < ktiles; ++kt) {
-          if ((warm_a || warm_b) && kt > 0 && kt + kL2PrefetchKTiles < ktiles)
+        (void)ktiles;
+        for (int kt = k0; kt < k1; ++kt) {
+          if ((warm_a || warm_b) && kt > k0 && kt + kL2PrefetchKTiles < k1)
             prefetch_ktile(kt + kL2PrefetchKTiles);
           if (!wait_phase(&empty_bar[stage], phase ^ 1u, abort_flag, p.error_bits,
                           kDevErrProducerTimeout)) {
@@ -382,13 +421,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                            &full_bar[stage]);
           // The first warm-up prefetches go behind the tile's first loads, which would
           // otherwise wait for the TMA unit to work through them.
-          if (kt == 0 && (warm_a || warm_b))
-            for (int kp = 1; kp <= kL2PrefetchKTiles && kp < ktiles; ++kp) prefetch_ktile(kp);
+          if (kt == k0 && (warm_a || warm_b))
+            for (int kp = k0 + 1; kp <= k0 + kL2PrefetchKTiles && kp < k1; ++kp) prefetch_ktile(kp);
           // Claim the next tile a few k-tiles before the end of this one; one k-tile
           // later (the claim's atomic has returned by then) look up its group, load its
           // record and acquire its tensor maps (about a microsecond per group switch),
           // all behind loads already in flight.
-          if (kt == claim_kt) next_tile = claim_next();
+          if (kt == claim_kt) next_unit = claim_next();
           if (kt == claim_kt + 1) resolve_next();
           ++issued;
           if (++stage == STAGES) {
@@ -398,7 +437,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         if (!ok) break;
         if (!resolved) resolve_next();
+        unit = next_unit;
         tile = next_tile;
+        split = next_split;
         g = g_next;
         gd = next_gd;
       }
@@ -435,10 +476,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if (!wait_phase(&sched_full[slot], (local / kSchedSlots) & 1u, abort_flag, p.error_bits,
                         kDevErrMmaTimeout))
           break;
-        const int tile = sched_info[4 * slot + 0];
-        const int ktiles = sched_info[4 * slot + 2] / kBlockK;
+        const int unit = sched_info[4 * slot + 0];
+        const int ktiles = sched_info[4 * slot + 3] - sched_info[4 * slot + 2];  // this unit's
         ptx::mbar_arrive(&sched_empty[slot]);
-        if (tile >= p.total_tiles) break;
+        if (unit >= p.total_units) break;
         const int acc = static_cast<int>(local & 1u);
         if (!wait_phase(&acce_bar[acc], (acc_parity >> acc) & 1u, abort_flag, p.error_bits,
                         kDevErrAccTimeout)) {
@@ -509,6 +550,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const uint32_t my_bufs_s = ptx::smem_u32(my_bufs);
     uint32_t full_parity = 0;  // bit s: parity to wait for on accf_bar[s]
     uint32_t stores = 0;
+    uint32_t split_count = 0;  // split-tile parts this CTA has handled (rendezvous parity)
     int acquired_g = -1;
     constexpr int kBoxes = Cfg::kOutN / 64;
     for (uint32_t local = 0;; ++local) {
@@ -517,14 +559,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (!warp_wait_phase(&sched_full[slot], (local / kSchedSlots) & 1u, abort_flag,
                            p.error_bits, kDevErrEpilogueTimeout, lane))
         break;
-      const int tile = sched_info[4 * slot + 0];
+      const int unit = sched_info[4 * slot + 0];
       const int g = sched_info[4 * slot + 1];
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&sched_empty[slot]);
-      if (tile >= p.total_tiles) break;
+      if (unit >= p.total_units) break;
+      int tile, split;
+      unit_tile(p, unit, tile, split);
       const GroupDev gd = groups[g];
       const TmaDesc* map_c = p.maps + static_cast<size_t>(g) * kMapsPerGroup + kMapC;
-      if (!DIRECT && g != acquired_g) {
+      if (!DIRECT && split < 0 && g != acquired_g) {
         if (lane == 0) ptx::tensormap_fence_acquire(map_c);
         acquired_g = g;
       }
@@ -545,6 +589,90 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // stage 0 -> its last box (up-projection half of box 1 when gated), stage 1 -> box 0.
       const int first_box = (Cfg::kOverlapAcc && acc == 0) ? kBoxes - 1 : 0;
       const int row0 = mt * kBlockM + 32 * quarter;
+      const int row = row0 + lane;
+      // Split units write their fp32 partial rows here (slot = part of a split tile).
+      float* part_row = nullptr;
+      if (split >= 0)
+        part_row = p.split_partials +
+                   (static_cast<size_t>((tile - p.split_first_tile) * p.split_parts + split) *
+                        kBlockM + 32 * quarter + lane) * MMA_N;
+      // Convert one 64-column box (accumulator bits v0/v1, up-projection bits u0/u1 when
+      // gated) to fp16 and store it: straight from registers (DIRECT, and the final sum of
+      // split tiles) or through the swizzled staging box and a TMA store.
+      auto emit_box = [&](const uint32_t* v0, const uint32_t* v1, const uint32_t* u0,
+                          const uint32_t* u1, int box, bool direct) {
+        const uint32_t buf = my_bufs_s + (stores & 1u) * Cfg::kEpiBufBytes;
+        if (!direct) {
+          // The store that last read this staging buffer (two boxes ago) must be done with it.
+          if (lane == 0) ptx::bulk_wait_group_read<1>();
+          __syncwarp();
+        }
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const uint32_t* v = half ? v1 : v0;
+          uint32_t packed[16];
+          if (GATED) {
+            const uint32_t* u = half ? u1 : u0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float o[2];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                // Gate and up are rounded to fp16 first, as the reference's two-GEMM
+                // path does; SiLU and the product are fp32.
+                const float gte = __half2float(
+                    __float2half_rn(__uint_as_float(v[2 * i + h]) * gd.alpha));
+                const float up = __half2float(
+                    __float2half_rn(__uint_as_float(u[2 * i + h]) * gd.alpha2));
+                o[h] = __fdividef(gte, 1.0f + __expf(-gte)) * up;
+              }
+              __half2 hv = __floats2half2_rn(o[0], o[1]);
+              packed[i] = *reinterpret_cast<uint32_t*>(&hv);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              __half2 hv = __floats2half2_rn(__uint_as_float(v[2 * i]) * gd.alpha,
+                                             __uint_as_float(v[2 * i + 1]) * gd.alpha);
+              packed[i] = *reinterpret_cast<uint32_t*>(&hv);
+            }
+          }
+          if (direct) {
+            // Row row0 + lane, columns [col, col + 32): four 16-byte stores (N is a
+            // multiple of 8, so a chunk is either inside the row or past its end).
+            const int col = nt * Cfg::kOutN + box * 64 + half * 32;
+            if (row < gd.m) {
+              uint4* dst = reinterpret_cast<uint4*>(
+                  gd.c + (static_cast<size_t>(row) * gd.n + col) * sizeof(__half));
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                if (col + 8 * c < gd.n)
+                  dst[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
+                                      packed[4 * c + 3]);
+            }
+          } else {
+            // Row `lane` of the 32 x 128 B box, 16-byte chunks XOR-swizzled by (row & 7)
+            // to match the map's 128B swizzle (and to spread the stores over all banks).
+            const uint32_t row_addr = buf + lane * 128;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint32_t chunk = static_cast<uint32_t>(half * 4 + c) ^ (lane & 7);
+              ptx::st_shared_v4(row_addr + chunk * 16, packed[4 * c], packed[4 * c + 1],
+                                packed[4 * c + 2], packed[4 * c + 3]);
+            }
+          }
+        }
+        if (!direct) {
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            ptx::tma_store_2d(map_c, my_bufs + (stores & 1u) * Cfg::kEpiBufBytes,
+                              nt * Cfg::kOutN + box * 64, row0);
+            ptx::bulk_commit_group();
+          }
+          ++stores;
+        }
+      };
       bool released = false;
       if (row0 < gd.m) {
         const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(32 * quarter) << 16) +
@@ -552,7 +680,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll 1
         for (int bi = 0; bi < kBoxes; ++bi) {
           const int box = (first_box + bi) % kBoxes;
-          const uint32_t buf = my_bufs_s + (stores & 1u) * Cfg::kEpiBufBytes;
           // 64 output columns: issue every TMEM load of the box, then wait once.
           uint32_t v0[32], v1[32];
           ptx::tmem_ld_32x32b_x32(t_acc + box * 64, v0);
@@ -569,83 +696,109 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (lane == 0) ptx::mbar_arrive(release_bar);
             released = true;
           }
-          if (!DIRECT) {
-            // The store that last read this staging buffer (two boxes ago) must be done with it.
-            if (lane == 0) ptx::bulk_wait_group_read<1>();
-            __syncwarp();
-          }
+          if (split >= 0) {
+            // A part of a split tile: its fp32 sums go to the tile's partial slot.
+            float4* dv = reinterpret_cast<float4*>(part_row + box * 64);
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const uint32_t* v = half ? v1 : v0;
-            uint32_t packed[16];
+            for (int c = 0; c < 8; ++c) {
+              dv[c] = make_float4(__uint_as_float(v0[4 * c]), __uint_as_float(v0[4 * c + 1]),
+                                  __uint_as_float(v0[4 * c + 2]), __uint_as_float(v0[4 * c + 3]));
+              dv[8 + c] = make_float4(__uint_as_float(v1[4 * c]), __uint_as_float(v1[4 * c + 1]),
+                                      __uint_as_float(v1[4 * c + 2]), __uint_as_float(v1[4 * c + 3]));
+            }
             if (GATED) {
-              const uint32_t* u = half ? u1 : u0;
+              float4* du = reinterpret_cast<float4*>(part_row + 128 + box * 64);
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                float o[2];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  // Gate and up are rounded to fp16 first, as the reference's two-GEMM
-                  // path does; SiLU and the product are fp32.
-                  const float gte = __half2float(
-                      __float2half_rn(__uint_as_float(v[2 * i + h]) * gd.alpha));
-                  const float up = __half2float(
-                      __float2half_rn(__uint_as_float(u[2 * i + h]) * gd.alpha2));
-                  o[h] = __fdividef(gte, 1.0f + __expf(-gte)) * up;
-                }
-                __half2 hv = __floats2half2_rn(o[0], o[1]);
-                packed[i] = *reinterpret_cast<uint32_t*>(&hv);
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                __half2 hv = __floats2half2_rn(__uint_as_float(v[2 * i]) * gd.alpha,
-                                               __uint_as_float(v[2 * i + 1]) * gd.alpha);
-                packed[i] = *reinterpret_cast<uint32_t*>(&hv);
+              for (int c = 0; c < 8; ++c) {
+                du[c] = make_float4(__uint_as_float(u0[4 * c]), __uint_as_float(u0[4 * c + 1]),
+                                    __uint_as_float(u0[4 * c + 2]), __uint_as_float(u0[4 * c + 3]));
+                du[8 + c] = make_float4(__uint_as_float(u1[4 * c]), __uint_as_float(u1[4 * c + 1]),
+                                        __uint_as_float(u1[4 * c + 2]), __uint_as_float(u1[4 * c + 3]));
               }
             }
-            if (DIRECT) {
-              // Row row0 + lane, columns [col, col + 32): four 16-byte stores (N is a
-              // multiple of 8, so a chunk is either inside the row or past its end).
-              const int row = row0 + lane;
-              const int col = nt * Cfg::kOutN + box * 64 + half * 32;
-              if (row < gd.m) {
-                uint4* dst = reinterpret_cast<uint4*>(
-                    gd.c + (static_cast<size_t>(row) * gd.n + col) * sizeof(__half));
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-                  if (col + 8 * c < gd.n)
-                    dst[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
-                                        packed[4 * c + 3]);
-              }
-            } else {
-              // Row `lane` of the 32 x 128 B box, 16-byte chunks XOR-swizzled by (row & 7)
-              // to match the map's 128B swizzle (and to spread the stores over all banks).
-              const uint32_t row_addr = buf + lane * 128;
-#pragma unroll
-              for (int c = 0; c < 4; ++c) {
-                const uint32_t chunk = static_cast<uint32_t>(half * 4 + c) ^ (lane & 7);
-                ptx::st_shared_v4(row_addr + chunk * 16, packed[4 * c], packed[4 * c + 1],
-                                  packed[4 * c + 2], packed[4 * c + 3]);
-              }
-            }
+            continue;
           }
-          if (!DIRECT) {
-            ptx::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              ptx::tma_store_2d(map_c, my_bufs + (stores & 1u) * Cfg::kEpiBufBytes,
-                                nt * Cfg::kOutN + box * 64, row0);
-              ptx::bulk_commit_group();
-            }
-            ++stores;
-          }
+          emit_box(v0, v1, u0, u1, box, DIRECT);
         }
       }
       if (!released) {
         ptx::tcgen05_fence_before_sync();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(release_bar);
+      }
+      if (split >= 0) {
+        // Rendezvous of the four epilogue warps (bounded waits), then one thread counts this
+        // part in; the part that arrives last sums all parts in split order (so the result
+        // does not depend on arrival order), writes C and resets the counter. No CTA ever
+        // waits for another CTA.
+        const uint32_t par = split_count & 1u;
+        ++split_count;
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(split_arrive);
+        if (ew == 0 && lane == 0) {
+          uint32_t last = 0;
+          if (wait_phase(split_arrive, par, abort_flag, p.error_bits, kDevErrEpilogueTimeout)) {
+            __threadfence();
+            int32_t* counter = p.split_counters + (tile - p.split_first_tile);
+            last = atomicAdd(counter, 1) == p.split_parts - 1 ? 1u : 0u;
+            if (last) {
+              __threadfence();
+              *counter = 0;
+            }
+          }
+          *split_last = last;
+          ptx::mbar_arrive(split_result);
+        }
+        if (!warp_wait_phase(split_result, par, abort_flag, p.error_bits, kDevErrEpilogueTimeout,
+                             lane))
+          break;
+        if (*split_last && row0 < gd.m) {
+          __threadfence();
+          const float* base = p.split_partials +
+                              (static_cast<size_t>((tile - p.split_first_tile) * p.split_parts) *
+                                   kBlockM + 32 * quarter + lane) * MMA_N;
+          const size_t part_stride = static_cast<size_t>(kBlockM) * MMA_N;
+#pragma unroll 1
+          for (int box = 0; box < kBoxes; ++box) {
+            uint32_t v0[32], v1[32], u0[32], u1[32];
+            float sv[64], su[64];
+#pragma unroll
+            for (int i = 0; i < 64; ++i) sv[i] = su[i] = 0.0f;
+#pragma unroll 1
+            for (int sp = 0; sp < p.split_parts; ++sp) {
+              const float4* src = reinterpret_cast<const float4*>(base + sp * part_stride + box * 64);
+#pragma unroll
+              for (int c = 0; c < 16; ++c) {
+                const float4 f = __ldcg(src + c);  // written by other SMs: read through L2
+                sv[4 * c] += f.x;
+                sv[4 * c + 1] += f.y;
+                sv[4 * c + 2] += f.z;
+                sv[4 * c + 3] += f.w;
+              }
+              if (GATED) {
+                const float4* srcu =
+                    reinterpret_cast<const float4*>(base + sp * part_stride + 128 + box * 64);
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                  const float4 f = __ldcg(srcu + c);
+                  su[4 * c] += f.x;
+                  su[4 * c + 1] += f.y;
+                  su[4 * c + 2] += f.z;
+                  su[4 * c + 3] += f.w;
+                }
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              v0[i] = __float_as_uint(sv[i]);
+              v1[i] = __float_as_uint(sv[32 + i]);
+              u0[i] = __float_as_uint(su[i]);
+              u1[i] = __float_as_uint(su[32 + i]);
+            }
+            emit_box(v0, v1, u0, u1, box, true);
+          }
+        }
       }
     }
     if (lane == 0) ptx::bulk_wait_group<0>();

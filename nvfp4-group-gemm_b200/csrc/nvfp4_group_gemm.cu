@@ -38,6 +38,8 @@ __global__ void __launch_bounds__(32) nvfp4_upload_descriptors_kernel(
     const __grid_constant__ UploadParams p) {
   const int gi = blockIdx.x;
   const int lane = threadIdx.x;
+  if (gi == 0 && p.zero_counters != nullptr)
+    for (int i = lane; i < static_cast<int>(kSplitCounterBytes / 4); i += 32) p.zero_counters[i] = 0;
   if (gi >= p.count) return;
   const int g = p.first_group + gi;
   const uint4* src = reinterpret_cast<const uint4*>(&p.maps[gi][0]);
@@ -327,6 +329,15 @@ constexpr int kSwapMaxAvgRows = NVFP4_SWAP_MAX_AVG_ROWS;
 #endif
 constexpr int kStreamMaxAvgRows = NVFP4_STREAM_MAX_AVG_ROWS;
 
+// Split-K of a single-CTA launch's last partial wave (NVFP4_FLAG_SPLIT_K): at least
+// kSplitMinKTiles k-tiles per part. -DNVFP4_SPLIT_K=0 compiles it out.
+#ifndef NVFP4_SPLIT_K
+#define NVFP4_SPLIT_K 1
+#endif
+constexpr bool kSplitEnabled = NVFP4_SPLIT_K != 0;
+constexpr int kSplitMinKTiles = 2;
+static_assert(NVFP4_SPLIT_SCRATCH_BYTES == kSplitScratchBytes, "header and library disagree");
+
 // GEMM kernels are launched with programmatic stream serialization: a launch may be
 // scheduled while the previous kernel in the stream is still finishing, and waits
 // (griddepcontrol.wait) before reading anything that kernel may have written.
@@ -379,7 +390,7 @@ cudaError_t launch_pair(const GemmParams& gp, int clusters, cudaStream_t stream)
 // and upload descriptors into `ws`, launch. `rec` holds num_groups records of host
 // scratch; `use_cache` selects the cached tensor-map encoder.
 int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int flags, uint8_t* ws,
-                      cudaStream_t s, GroupDev* rec, bool use_cache) {
+                      size_t ws_bytes, cudaStream_t s, GroupDev* rec, bool use_cache) {
   const bool gated = (flags & NVFP4_FLAG_GATED) != 0;
   // Tile shape: CTA pairs (256-row tiles) when the groups are tall enough to fill
   // them, single CTAs (128-row tiles) otherwise; 256 MMA columns unless asked otherwise.
@@ -468,6 +479,12 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
     static thread_local UploadParams up;  // ~26 KB: kept off the caller's stack
     up.groups_out = groups_dev;
     up.maps_out = maps_dev;
+    // Split-K counters move with the group count: zero them with every new table (when the
+    // workspace has the split scratch at all).
+    const bool has_split_scratch = ws_bytes >= ws_split_offset(num_groups) + kSplitScratchBytes;
+    up.zero_counters = has_split_scratch
+                           ? reinterpret_cast<int32_t*>(ws + ws_split_offset(num_groups))
+                           : nullptr;
     for (int first = 0; first < num_groups; first += kGroupsPerUpload) {
       const int count = std::min(kGroupsPerUpload, num_groups - first);
       up.first_group = first;
@@ -495,6 +512,7 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
         if (!ok) return fail(NVFP4_ERR_DRIVER, "group %d: cuTensorMapEncodeTiled rejected a tensor", i);
       }
       nvfp4_upload_descriptors_kernel<<<count, 32, 0, s>>>(up);
+      up.zero_counters = nullptr;  // once per table
       e = cudaGetLastError();
       if (e != cudaSuccess) return cuda_fail(e, "descriptor upload launch");
     }
@@ -509,6 +527,29 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
   gp.diag_skip_mma = (flags & NVFP4_FLAG_DIAG_SKIP_MMA) ? 1 : 0;
   gp.dynamic_schedule = (!pair && kDynamicSchedule) ? 1 : 0;  // single-CTA kernels only
   gp.tile_counter = reinterpret_cast<WorkspaceHeader*>(ws)->tile_counter;
+  // Split-K of the last partial wave (single-CTA row tiles, when the workspace has room).
+  int split_parts = 1;
+  int64_t tail = 0;
+  if (!pair && !swap && kSplitEnabled && (flags & NVFP4_FLAG_SPLIT_K) &&
+      ws_bytes >= ws_split_offset(num_groups) + kSplitScratchBytes) {
+    const int64_t sms = ds.num_sms;
+    tail = total_tiles >= sms ? total_tiles % sms : total_tiles;
+    int min_ktiles = 1 << 30;
+    for (int i = 0; i < num_groups; ++i)
+      if (rec[i].tile_end > rec[i].tile_start) min_ktiles = std::min(min_ktiles, rec[i].k / kBlockK);
+    if (tail > 0) {
+      int64_t parts = sms / tail;
+      parts = std::min<int64_t>(parts, min_ktiles / kSplitMinKTiles);
+      parts = std::min<int64_t>(parts, kSplitMaxSlots / tail);
+      if (parts >= 2) split_parts = static_cast<int>(parts);
+    }
+  }
+  gp.split_parts = split_parts;
+  gp.split_first_tile = static_cast<int32_t>(split_parts > 1 ? total_tiles - tail : total_tiles);
+  gp.total_units = static_cast<int32_t>(gp.split_first_tile + (total_tiles - gp.split_first_tile) *
+                                                                  split_parts);
+  gp.split_counters = reinterpret_cast<int32_t*>(ws + ws_split_offset(num_groups));
+  gp.split_partials = reinterpret_cast<float*>(ws + ws_split_offset(num_groups) + kSplitCounterBytes);
   if (swap) {
     const int grid = static_cast<int>(std::min<int64_t>(total_tiles, ds.num_sms));
     e = launch_gemm(nvfp4_grouped_gemm_swap_kernel<kSwapStages>, gp, grid, Kswap::kSmemBytes, 1,
@@ -518,7 +559,7 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
     const int clusters = static_cast<int>(std::min<int64_t>(total_tiles, max_clusters));
     e = gated ? launch_pair<true>(gp, clusters, s) : launch_pair<false>(gp, clusters, s);
   } else {
-    const int grid = static_cast<int>(std::min<int64_t>(total_tiles, ds.num_sms));
+    const int grid = static_cast<int>(std::min<int64_t>(gp.total_units, ds.num_sms));
     if (gated)
       e = launch_single<256, true, 3>(gp, grid, s);
     else if (mma_n == 128)
@@ -536,7 +577,7 @@ int check_common_args(const nvfp4_group* groups, int num_groups, unsigned int fl
   const unsigned known = NVFP4_FLAG_GATED | NVFP4_FLAG_TILE_N128 | NVFP4_FLAG_TILE_N256 |
                          NVFP4_FLAG_REUSE_DESCRIPTORS | NVFP4_FLAG_CTA_PAIR |
                          NVFP4_FLAG_SINGLE_CTA | NVFP4_FLAG_DIAG_SKIP_MMA |
-                         NVFP4_FLAG_WEIGHT_STATIONARY;
+                         NVFP4_FLAG_WEIGHT_STATIONARY | NVFP4_FLAG_SPLIT_K;
   if (flags & ~known) return fail(NVFP4_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags & ~known);
   if (num_groups < 0) return fail(NVFP4_ERR_INVALID_ARGUMENT, "num_groups=%d", num_groups);
   if (num_groups > 0 && groups == nullptr)
@@ -837,7 +878,8 @@ NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsi
                 ws_total_bytes(num_groups));
   std::vector<GroupDev> rec(static_cast<size_t>(num_groups));
   return grouped_gemm_impl(groups, num_groups, flags, static_cast<uint8_t*>(workspace),
-                           static_cast<cudaStream_t>(stream), rec.data(), /*use_cache=*/true);
+                           workspace_bytes, static_cast<cudaStream_t>(stream), rec.data(),
+                           /*use_cache=*/true);
 }
 
 }  // extern "C"
@@ -905,5 +947,6 @@ extern "C" NVFP4_API int nvfp4_grouped_gemm_noalloc(const nvfp4_group* groups, i
   if (e != cudaSuccess) return cuda_fail(e, "clear scratch error word");
   // Fixed-size host staging and uncached encoding: no heap use on this path.
   static thread_local GroupDev rec[NVFP4_NOALLOC_MAX_GROUPS];
-  return grouped_gemm_impl(groups, num_groups, flags, ws, s, rec, /*use_cache=*/false);
+  return grouped_gemm_impl(groups, num_groups, flags, ws, kNoAllocScratchBytes, s, rec,
+                           /*use_cache=*/false);
 }

@@ -74,6 +74,16 @@ __host__ __device__ constexpr size_t ws_total_bytes(int num_groups) {
          static_cast<size_t>(num_groups) * kMapsPerGroup * sizeof(TmaDesc);
 }
 
+// Split-K scratch, after the workspace proper (256-byte aligned): split_counters (4 KiB),
+// then kSplitMaxSlots partial slots of 128 rows x 256 fp32 (128 KiB each).
+constexpr int kSplitMaxSlots = 148;
+constexpr size_t kSplitSlotBytes = 128 * 256 * 4;
+constexpr size_t kSplitCounterBytes = 4096;
+constexpr size_t kSplitScratchBytes = kSplitCounterBytes + kSplitMaxSlots * kSplitSlotBytes;
+__host__ __device__ constexpr size_t ws_split_offset(int num_groups) {
+  return (ws_total_bytes(num_groups) + 255) & ~static_cast<size_t>(255);
+}
+
 // Parameter block of the descriptor upload kernel: host-encoded records and
 // tensor maps of up to kGroupsPerUpload groups (about 26 KB of kernel parameters).
 struct UploadParams {
@@ -83,6 +93,9 @@ struct UploadParams {
   TmaDesc* maps_out;
   int32_t first_group;
   int32_t count;
+  // Split-K counters to zero (or nullptr): their place depends on the group count, so a
+  // new group table may put them over bytes an earlier launch used for something else.
+  int32_t* zero_counters;
 };
 static_assert(sizeof(UploadParams) <= 32000, "kernel parameter block too large");
 
@@ -95,6 +108,16 @@ struct GemmParams {
   int32_t diag_skip_mma;  // NVFP4_FLAG_DIAG_SKIP_MMA: the MMA issuer does no work
   int32_t dynamic_schedule;  // single-CTA kernel: claim tiles from tile_counter after the first
   uint32_t* tile_counter;    // WorkspaceHeader::tile_counter
+  // Split-K of the last tiles (single-CTA kernels): units [0, split_first_tile) are whole
+  // tiles; tiles split_first_tile.. are split into split_parts K ranges each. total_units =
+  // split_first_tile + (total_tiles - split_first_tile) * split_parts (= total_tiles when
+  // split_parts is 1). Partial tiles go to split_partials (one 128 x MMA_N fp32 slot per
+  // split unit), split_counters[tile - split_first_tile] counts the parts that arrived.
+  int32_t split_first_tile;
+  int32_t split_parts;
+  int32_t total_units;
+  float* split_partials;
+  int32_t* split_counters;
 };
 
 }  // namespace nvfp4

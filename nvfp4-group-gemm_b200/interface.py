@@ -123,7 +123,8 @@ def _check_sf(t: torch.Tensor, rows: int, k: int, name: str) -> None:
 # ----------------------------------------------------------------------------
 # Core grouped launch
 # ----------------------------------------------------------------------------
-def _prepare(a, b, sfa, sfb, c, problem_sizes, alpha, b2, sfb2, alpha2, tile_n, cta):
+def _prepare(a, b, sfa, sfb, c, problem_sizes, alpha, b2, sfb2, alpha2, tile_n, cta,
+             split_k=False):
     """Validate one grouped launch and build its group table.
 
     Returns ``(table, flags, device)``, or None when there is nothing to launch (no
@@ -212,6 +213,8 @@ def _prepare(a, b, sfa, sfb, c, problem_sizes, alpha, b2, sfb2, alpha2, tile_n, 
             flags |= _native.FLAG_TILE_N256
         else:
             raise ValueError(f"tile_n must be 128 or 256, got {tile_n}")
+    if split_k:
+        flags |= _native.FLAG_SPLIT_K
     return table, flags, device
 
 
@@ -225,7 +228,7 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
                  tile_n: int | None = None,
                  stream: torch.cuda.Stream | None = None,
                  reuse_descriptors: bool = True,
-                 cta: str | None = None) -> list:
+                 cta: str | None = None, split_k: bool = False) -> list:
     """One grouped NVFP4 launch. Scale tensors are in the blocked layout.
 
     ``problem_sizes`` holds (m, n, k[, l]) per group. When ``b2``/``sfb2`` are given
@@ -234,7 +237,10 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
     CTAs (``"single"``) or the weight-stationary kernel's 128-weight-row x 64-token
     tiles (``"weights"``, non-gated only); by default the library picks pairs when the
     groups average at least 192 rows (96 with K >= 4096) and single CTAs otherwise.
-    ``tile_n`` (128 or 256) applies to single-CTA tiles.
+    ``tile_n`` (128 or 256) applies to single-CTA tiles. ``split_k`` lets a single-CTA
+    launch split the K loop of the tiles of its last, partly idle wave (the stream's
+    workspace then also holds the split scratch, about 19 MB); results stay bit-identical
+    from run to run.
     """
     if cta not in (None, "pair", "single", "weights"):
         raise ValueError(f"cta must be None, 'pair', 'single' or 'weights', got {cta!r}")
@@ -253,7 +259,7 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
                    tuple(t.data_ptr() for lst in lists for t in lst),
                    tuple(tuple(ps) for ps in problem_sizes),
                    None if alpha is None else tuple(alpha),
-                   None if alpha2 is None else tuple(alpha2), tile_n, gated, cta)
+                   None if alpha2 is None else tuple(alpha2), tile_n, gated, cta, split_k)
         except (AttributeError, TypeError):
             sig = None
         if sig is not None:
@@ -266,12 +272,14 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
                                              ws.last_flags | _native.FLAG_REUSE_DESCRIPTORS,
                                              ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
                 return list(c)
-    prepared = _prepare(a, b, sfa, sfb, c, problem_sizes, alpha, b2, sfb2, alpha2, tile_n, cta)
+    prepared = _prepare(a, b, sfa, sfb, c, problem_sizes, alpha, b2, sfb2, alpha2, tile_n, cta,
+                        split_k)
     if prepared is None:
         return list(c)
     table, flags, device = prepared
     s = stream or torch.cuda.current_stream(device)
-    ws = _workspace_for(device, s, _native.workspace_size(G))
+    ws = _workspace_for(device, s, _native.workspace_size_with_split(G) if split_k
+                        else _native.workspace_size(G))
     call_flags = flags
     if (reuse_descriptors and ws.last_flags == flags and ws.last_table is not None
             and ws.last_table.shape == table.shape and np.array_equal(ws.last_table, table)):
@@ -292,7 +300,9 @@ def grouped_gemm_table(table: np.ndarray, flags: int, device: torch.device,
     have already validated (the MoE block builds it from dispatch offsets in a few vectorised
     column operations); the library still checks every record before launching."""
     s = stream or torch.cuda.current_stream(device)
-    ws = _workspace_for(device, s, _native.workspace_size(int(table.shape[0])))
+    G = int(table.shape[0])
+    ws = _workspace_for(device, s, _native.workspace_size_with_split(G)
+                        if flags & _native.FLAG_SPLIT_K else _native.workspace_size(G))
     with torch.cuda.device(device):
         _native.grouped_gemm_raw(table, flags, ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
     ws.last_table = None  # the next grouped_gemm call on this stream rebuilds its descriptors
@@ -313,16 +323,18 @@ class GroupedGemmPlan:
     """
 
     def __init__(self, a, b, sfa, sfb, c, problem_sizes, *, alpha=None, b2=None, sfb2=None,
-                 alpha2=None, tile_n=None, cta=None):
+                 alpha2=None, tile_n=None, cta=None, split_k=False):
         prepared = _prepare(a, b, sfa, sfb, c, problem_sizes, alpha, b2, sfb2, alpha2, tile_n,
-                            cta)
+                            cta, split_k)
         self.outputs = list(c)
         self._keep = (a, b, sfa, sfb, c, b2, sfb2)  # the table holds their addresses
         self._table = None
         if prepared is None:
             return
         self._table, self._flags, self.device = prepared
-        self._nbytes = _native.workspace_size(len(problem_sizes))
+        G = len(problem_sizes)
+        self._nbytes = (_native.workspace_size_with_split(G) if split_k
+                        else _native.workspace_size(G))
         # Zero-filled: the first 4 bytes are the device error word.
         self._ws = torch.zeros(self._nbytes, dtype=torch.uint8, device=self.device)
         self._lib = _native.load_library()
@@ -372,8 +384,10 @@ def _split_scales(global_scales, G: int, gated: bool):
 
 
 def custom_kernel(data: input_t, *, global_scales=None, tile_n: int | None = None,
-                  stream: torch.cuda.Stream | None = None, cta: str | None = None) -> output_t:
-    """Drop-in replacement of the reference's ``custom_kernel`` (submission.py:788)."""
+                  stream: torch.cuda.Stream | None = None, cta: str | None = None,
+                  split_k: bool = False) -> output_t:
+    """Drop-in replacement of the reference's ``custom_kernel`` (submission.py:788).
+    The keyword options are those of :func:`grouped_gemm`."""
     if not isinstance(data, (tuple, list)):
         raise ValueError(f"unsupported input: expected a tuple, got {type(data).__name__}")
     if len(data) == 10:
@@ -384,7 +398,8 @@ def custom_kernel(data: input_t, *, global_scales=None, tile_n: int | None = Non
         k = int(a.shape[1]) * 2
         alpha, alpha2 = _split_scales(global_scales, 1, True)
         grouped_gemm([a], [b1], [sfa_p], [sfb1_p], [c], [(m, n, k, 1)], alpha=alpha,
-                     b2=[b2], sfb2=[sfb2_p], alpha2=alpha2, stream=stream, cta=cta)
+                     b2=[b2], sfb2=[sfb2_p], alpha2=alpha2, stream=stream, cta=cta,
+                     split_k=split_k)
         return c
     if len(data) not in (4, 5):
         raise ValueError(f"unsupported input format with {len(data)} elements "
@@ -421,7 +436,7 @@ def custom_kernel(data: input_t, *, global_scales=None, tile_n: int | None = Non
         b2 = sfb2 = None
     alpha, alpha2 = _split_scales(global_scales, G, gated)
     grouped_gemm(a, b, sfa, sfb, c, problem_sizes, alpha=alpha, b2=b2, sfb2=sfb2,
-                 alpha2=alpha2, tile_n=tile_n, stream=stream, cta=cta)
+                 alpha2=alpha2, tile_n=tile_n, stream=stream, cta=cta, split_k=split_k)
     return list(c)
 
 

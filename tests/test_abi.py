@@ -77,7 +77,7 @@ def _table(N, **kw):
     (dict(a=0), 0, 4),              # NULL operand of a non-empty group
     (dict(c=0x50008), 0, 3),        # misaligned output
     (dict(b2=0), 1, 4),             # gated without up weights
-    (dict(), 0x100, 1),             # unknown flag bit
+    (dict(), 0x200, 1),             # unknown flag bit
     (dict(), 0x10 | 0x20, 1),       # exclusive CTA modes
     (dict(), 0x10 | 0x2, 1),        # pairs need 256-column tiles
     (dict(), 0x2 | 0x4, 1),         # exclusive tile flags
@@ -146,3 +146,12 @@ def test_quantize_validation_before_launch(pkg):
     assert call(x=0x1008) == 3               # misaligned input
     assert call(pld=40) == 3                 # packed row stride not a multiple of 16
     assert lib.nvfp4_last_error_detail()
+
+
+def test_split_scratch_constant_matches_header(pkg):
+    hdr = open(os.path.join(ROOT, "include", "nvfp4_group_gemm.h")).read()
+    m = re.search(r"#define NVFP4_SPLIT_SCRATCH_BYTES \((\d+)u \+ (\d+)u \* (\d+)u\)", hdr)
+    assert m, "NVFP4_SPLIT_SCRATCH_BYTES not found"
+    a, b, c = (int(x) for x in m.groups())
+    assert a + b * c == pkg._native.SPLIT_SCRATCH_BYTES
+    assert pkg._native.workspace_size_with_split(8) % 256 == 0

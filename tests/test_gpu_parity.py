@@ -59,12 +59,12 @@ VARIANTS = [(None, None), (128, "single"), (256, "single"), (None, "pair"), (Non
 VARIANT_IDS = ["auto", "single128", "single256", "pair", "weights"]
 
 
-def run_custom_kernel(pkg, prob, tile_n=None, cta=None):
+def run_custom_kernel(pkg, prob, tile_n=None, cta=None, split_k=False):
     data = prob.reference_data()
     scales = prob.global_scales()
     if all(s == 1.0 or s == (1.0, 1.0) for s in scales):
         scales = None
-    out = pkg.custom_kernel(data, global_scales=scales, tile_n=tile_n, cta=cta)
+    out = pkg.custom_kernel(data, global_scales=scales, tile_n=tile_n, cta=cta, split_k=split_k)
     assert len(out) == prob.num_groups
     for o, c in zip(out, prob.c):
         assert o.data_ptr() == c.data_ptr()
@@ -323,3 +323,41 @@ def test_cfg5_gated_checksum_subset(pkg):
     torch.cuda.synchronize()
     for i, g in enumerate(keep):
         assert torch.equal(sub.c[g], prob.c[g])
+
+
+# ----------------------------------------------------------------------------
+# Split-K of single-CTA launches that do not fill the GPU (the last partial wave, or all
+# tiles of a small launch; opt-in, NVFP4_FLAG_SPLIT_K): parts write fp32 partial tiles, the
+# last part sums them in a fixed order. Repeated launches check the counters reset; reruns
+# check determinism.
+# ----------------------------------------------------------------------------
+SPLIT_SHAPES = [
+    # (name, m_list, n, k, gated)
+    ("split_small", [100, 37, 250], 512, 2048, False),
+    ("split_one_row", [1], 256, 1024, False),
+    ("split_ragged", [129, 0, 7], 264, 4096, False),
+    ("split_gated", [64, 300], 256, 2048, True),
+]
+
+
+@pytest.mark.parametrize("tile_n", [None, 128])
+@pytest.mark.parametrize("shape", SPLIT_SHAPES, ids=[s[0] for s in SPLIT_SHAPES])
+def test_split_k_single_cta(pkg, shape, tile_n):
+    name, ms, n, k, gated = shape
+    if gated and tile_n is not None:
+        pytest.skip("gated launches use 128 gate + 128 up columns")
+    prob = pkg.workloads.make_problem(name, ms, n, k, gated=gated, seed=len(ms) + k,
+                                      device="cuda", alpha_range=(0.5, 2.0))
+    first = None
+    for rep in range(3):
+        for c in prob.c:
+            c.fill_(float("nan"))
+        run_custom_kernel(pkg, prob, tile_n=tile_n, cta="single", split_k=True)
+        check_problem(prob)
+        outs = [c.clone() for c in prob.c]
+        if first is None:
+            first = outs
+        else:
+            for a, b in zip(first, outs):
+                assert torch.equal(a.view(torch.int16), b.view(torch.int16)), "split-K not deterministic"
+    assert pkg.check_device_errors() == 0
