@@ -64,6 +64,9 @@ def parse_args():
                          "combine) at cfg5's shape")
     ap.add_argument("--experts", default=None,
                     help="START:STOP - run only this contiguous expert shard of the configuration")
+    ap.add_argument("--tokens", type=int, default=32768,
+                    help="--op moe: tokens per step (32768 = cfg5's 262144 routed rows; 64 = a "
+                         "decode step)")
     return ap.parse_args()
 
 
@@ -320,7 +323,7 @@ def run_moe(args):
     rank = int(os.environ.get("RANK", "0"))
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
-    E, T, topk, H, I = 256, 32768, 8, 7168, 2048
+    E, T, topk, H, I = 256, args.tokens, 8, 7168, 2048
     g = torch.Generator(device=dev).manual_seed(rank)
 
     def nvfp4_weights(rows, cols):
@@ -374,7 +377,24 @@ def run_moe(args):
         out = step()
     e1.record()
     torch.cuda.synchronize(dev)
+    ms_eager = e0.elapsed_time(e1) / steps
+    # The same block with no host read (MoEBlock: routing metadata stays on the GPU, both
+    # expert GEMMs are segment launches), captured once in a CUDA graph and replayed: the
+    # headline number. Its output is checked against moe_ffn's.
+    blk = pkg.moe.MoEBlock(weights, T, topk, act_scale=s_x, hidden_scale=s_h)
+    graph = blk.capture(x, ids, wts, warmup=max(args.warmup, 3))
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    same = bool(torch.equal(blk.out.view(torch.int16), out.view(torch.int16)))
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / steps
+    blk_errors = blk.check_device_errors()
+    del graph
     # Per-stage split of one call (events between the stages of moe_ffn).
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
     ev[0].record()
@@ -407,21 +427,28 @@ def run_moe(args):
     split = {n: ev[i].elapsed_time(ev[i + 1]) * 1e3 for i, n in enumerate(names)}
     rows = int(sum(r.counts))
     flops = 6.0 * rows * H * I
+    tf_eager = flops / (ms_eager * 1e-3) / 1e12
     peaks, kind = load_peaks()
     peak = FP4_PER_BF16 * float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
     tf = flops / (ms * 1e-3) / 1e12
     if rank != 0:
         return
     print(json.dumps({
-        "metric": "NVFP4 MoE block TFLOP/s (cfg5 shape: 256 experts, 32768 tokens x top-8, H 7168, I 2048)",
+        "metric": f"NVFP4 MoE block TFLOP/s (cfg5 shape: 256 experts, {T} tokens x top-8, H 7168, I 2048)",
         "value": tf, "unit": "TFLOP/s", "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 3),
         "ms_per_step": ms, "us_per_call": ms * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "e2m1xe4m3->f32->f16/bf16",
         "data": "synthetic (seeded; bf16 N(0,1) tokens, uniform top-8 routing, reference-set weights)",
-        "config": {"workload": "moe:cfg5", "experts": E, "tokens": T, "topk": topk, "hidden": H,
+        "config": {"workload": "moe:cfg5" if T == 32768 else f"moe:cfg5-experts:{T}-tokens",
+                   "experts": E, "tokens": T, "topk": topk, "hidden": H,
                    "intermediate": I, "dispatched_rows": r.rows,
                    "l2": "inputs larger than L2 (126 MB); no flush"},
-        "gpu_launches_per_call": "route 3, quantise 1, gather 2, gate/up GEMM 1 (+ descriptor uploads), quantise 1, down GEMM 1 (+ uploads), combine 1",
+        "api": "MoEBlock captured in a CUDA graph, graph.replay() (value); moe_ffn (eager)",
+        "gpu_launches_per_call": "route 3, quantise 1, gather 2, segment set-up 1 + gate/up GEMM 1, quantise 1, segment set-up 1 + down GEMM 1, combine 1",
+        "eager_moe_ffn": {"us_per_call": ms_eager * 1e3, "tflops": tf_eager,
+                          "note": "host-sized groups: one device->host read of the routing per call"},
+        "graph_output_equals_moe_ffn": same,
+        "device_error_bits": blk_errors,
         "stage_us": split,
         "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
                      "frac": tf / peak, "peak_source": f"{kind}: 4 x bf16 (sustained)",

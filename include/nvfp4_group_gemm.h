@@ -101,8 +101,8 @@ typedef struct nvfp4_group {
 
 /*
  * Device workspace bytes needed for `num_groups` groups (group records, tensor
- * maps and a device error word): 256 + 64 * num_groups rounded up to 128, plus
- * 1024 * num_groups. The workspace is owned by the caller, must be
+ * maps, segment row offsets and a device error word): 256 + 64 * num_groups rounded up
+ * to 128, plus 1024 * num_groups, plus 4 * num_groups rounded up to 128. The workspace is owned by the caller, must be
  * 256-byte aligned, must not be shared by calls that may run concurrently, and
  * may be reused by consecutive calls on one stream.
  */
@@ -116,6 +116,30 @@ NVFP4_API size_t nvfp4_workspace_size(int num_groups);
  */
 NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsigned int flags,
                                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Grouped GEMM whose groups' row counts are read on the GPU when the launch runs: group g
+ * multiplies rows [seg_offsets[g], seg_offsets[g] + seg_counts[g]) of a slab of
+ * groups[g].m rows (a, sfa and c of every group address such a slab; m must be the same
+ * for all groups) with its own weights. seg_offsets/seg_counts are device int32 arrays of
+ * num_groups entries, e.g. the offsets/counts nvfp4_moe_route writes, so a routed MoE
+ * step needs no device-to-host read between routing and the expert GEMMs and can be
+ * captured in a CUDA graph whole (no new graph per batch composition).
+ *
+ * Each offset must be a multiple of 128 and offset + count <= m; a group that breaks this
+ * is skipped and nvfp4_workspace_check reports NVFP4_ERR_BAD_SHAPE. Rows of C from
+ * offset + count up to the next multiple of 128 (inside the slab) may be overwritten:
+ * they are the segment's padding. `expected_rows` is a host estimate of the rows over all
+ * groups (tokens x top-k), used like the real rows of nvfp4_grouped_gemm to pick CTA
+ * pairs or single CTAs; <= 0 means m. The workspace is that of nvfp4_grouped_gemm and
+ * NVFP4_FLAG_REUSE_DESCRIPTORS has the same meaning (the slab addresses, not the
+ * segments, are the descriptors). NVFP4_FLAG_WEIGHT_STATIONARY and NVFP4_FLAG_SPLIT_K are
+ * rejected. No counterpart in the reference, whose groups are formed on the host.
+ */
+NVFP4_API int nvfp4_grouped_gemm_segments(const nvfp4_group* groups, int num_groups,
+                                          unsigned int flags, const int32_t* seg_offsets,
+                                          const int32_t* seg_counts, int64_t expected_rows,
+                                          void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Extra workspace for split-K: with NVFP4_FLAG_SPLIT_K and workspace_bytes at least
@@ -184,8 +208,9 @@ NVFP4_API int nvfp4_quantize_rows(const void* x, int rows, int cols, int64_t ld,
  * boundary (offsets[num_experts] = padded total), so one blocked scale buffer for all rows is
  * the concatenation of the experts' blocked layouts; dest [tokens * topk] the dispatched row
  * of each pair (-1 if dropped), rows of an expert in token order; src_rows [rows_capacity] the
- * token of each dispatched row (-1 for padding rows; entries past offsets[num_experts] are
- * not written). rows_capacity >= tokens * topk + 127 * num_experts; num_experts <= 1024.
+ * token of each dispatched row (-1 for padding rows and for every row past
+ * offsets[num_experts]). rows_capacity >= tokens * topk + 127 * num_experts;
+ * num_experts <= 1024.
  * Deterministic. workspace: nvfp4_moe_route_workspace_size(tokens * topk, num_experts) bytes
  * of device memory (no initialisation needed).
  */
@@ -222,7 +247,8 @@ NVFP4_API int nvfp4_moe_combine(const void* y, int64_t ldy, const int32_t* dest,
 
 /*
  * Synchronise `stream`, then read and clear the device error word of `workspace`.
- * Returns NVFP4_ERR_DEVICE_TIMEOUT if a kernel using it gave up on a wait; the
+ * Returns NVFP4_ERR_DEVICE_TIMEOUT if a kernel using it gave up on a wait, else
+ * NVFP4_ERR_BAD_SHAPE if a segment launch skipped an out-of-range segment (bit 0x20); the
  * reason bits are stored to *device_error_bits when non-NULL.
  */
 NVFP4_API int nvfp4_workspace_check(void* workspace, void* stream, unsigned int* device_error_bits);

@@ -13,7 +13,7 @@ Public API:
 from . import _native, expert_parallel, layout, moe, quantize as quantize_module, workloads
 from ._native import Nvfp4Error, load_library
 from .interface import (GroupedGemmPlan, check_device_errors, custom_kernel, grouped_gemm,
-                        input_t, output_t, solve)
+                        grouped_gemm_segments, input_t, output_t, solve)
 from .layout import (blocked_as_reordered, blocked_sf_bytes, blocked_to_plain, plain_to_blocked,
                      sf_to_blocked)
 from .quantize import global_scale_for, quantize
@@ -21,6 +21,7 @@ from .quantize import global_scale_for, quantize
 __all__ = [
     "GroupedGemmPlan", "Nvfp4Error", "blocked_as_reordered", "blocked_sf_bytes", "blocked_to_plain",
     "check_device_errors", "custom_kernel", "expert_parallel", "global_scale_for", "grouped_gemm",
+    "grouped_gemm_segments",
     "input_t", "moe", "quantize",
     "layout", "load_library", "output_t", "plain_to_blocked", "sf_to_blocked", "solve",
     "workloads",

@@ -44,6 +44,7 @@ DEV_ERR_MMA_TIMEOUT = 1 << 1
 DEV_ERR_ACC_TIMEOUT = 1 << 2
 DEV_ERR_EPILOGUE_TIMEOUT = 1 << 3
 DEV_ERR_DRAIN_TIMEOUT = 1 << 4
+DEV_ERR_BAD_SEGMENT = 1 << 5  # a segment launch skipped an out-of-range row segment
 
 # Every symbol the public header declares; the library must export all of them.
 EXPORTED_SYMBOLS = (
@@ -56,6 +57,7 @@ EXPORTED_SYMBOLS = (
     "nvfp4_sf_to_blocked",
     "nvfp4_workspace_check",
     "nvfp4_grouped_gemm_noalloc",
+    "nvfp4_grouped_gemm_segments",
     "nvfp4_quantize",
     "nvfp4_quantize_rows",
     "nvfp4_moe_route_workspace_size",
@@ -164,6 +166,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_workspace_check.restype = i32
         lib.nvfp4_grouped_gemm_noalloc.argtypes = [vp, i32, u32, vp]
         lib.nvfp4_grouped_gemm_noalloc.restype = i32
+        lib.nvfp4_grouped_gemm_segments.argtypes = [vp, i32, u32, vp, vp, i64, vp, sz, vp]
+        lib.nvfp4_grouped_gemm_segments.restype = i32
         lib.nvfp4_quantize.argtypes = [vp, i32, i32, i64, i32, ctypes.c_float, vp, i64, vp, vp]
         lib.nvfp4_quantize.restype = i32
         lib.nvfp4_quantize_rows.argtypes = [vp, i32, i32, i64, i32, ctypes.c_float, vp, i32, vp,
@@ -213,6 +217,19 @@ def grouped_gemm_raw(table: np.ndarray, flags: int, workspace_ptr: int, workspac
     lib = load_library()
     st = lib.nvfp4_grouped_gemm(table.ctypes.data, int(table.shape[0]), flags, workspace_ptr,
                                 workspace_bytes, stream_ptr)
+    check(st, lib)
+
+
+def grouped_gemm_segments_raw(table: np.ndarray, flags: int, offsets_ptr: int, counts_ptr: int,
+                              expected_rows: int, workspace_ptr: int, workspace_bytes: int,
+                              stream_ptr: int) -> None:
+    """Call nvfp4_grouped_gemm_segments on a GROUP_DTYPE table (host memory) whose rows are
+    given by device int32 arrays of per-group first rows and row counts."""
+    assert table.dtype == GROUP_DTYPE and table.flags["C_CONTIGUOUS"]
+    lib = load_library()
+    st = lib.nvfp4_grouped_gemm_segments(table.ctypes.data, int(table.shape[0]), flags,
+                                         offsets_ptr, counts_ptr, int(expected_rows),
+                                         workspace_ptr, workspace_bytes, stream_ptr)
     check(st, lib)
 
 

@@ -274,6 +274,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
   stage_tile_ends(tile_ends, groups, p.num_groups);
+  // Segment launches learn their tile count from the workspace (written by the segment
+  // set-up kernel); the grid may then have CTAs without a tile, which end at once.
+  const int total_tiles = p.seg_total_tiles != nullptr ? *p.seg_total_tiles : p.total_tiles;
+  const int total_units = p.seg_total_tiles != nullptr ? total_tiles : p.total_units;
   ptx::tcgen05_fence_before_sync();
   __syncthreads();
   ptx::tcgen05_fence_after_sync();
@@ -292,11 +296,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         ptx::tensormap_fence_acquire(&m[kMapB]);
         if (GATED) ptx::tensormap_fence_acquire(&m[kMapB2]);
       };
-      int unit = blockIdx.x;  // grid <= total_units: every CTA has a first unit
+      int unit = blockIdx.x;  // >= total_units only in segment launches: no tile
       int tile, split;
       unit_tile(p, unit, tile, split);
       int g = advance_group(tile_ends, groups, p.num_groups, 0, tile);
       GroupDev gd = groups[g];
+      int rb = seg_row(p, g);  // first row of the group's segment (0 outside segment launches)
       acquire_maps(g);
       for (uint32_t seq = 0;; ++seq) {
         // Publish this CTA's seq-th unit (or the end marker) to the MMA issuer and epilogue:
@@ -306,13 +311,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                         p.error_bits, kDevErrProducerTimeout))
           break;
         int k0 = 0, k1 = 0;
-        if (unit < p.total_units) unit_krange(p, split, gd.k / kBlockK, k0, k1);
+        if (unit < total_units) unit_krange(p, split, gd.k / kBlockK, k0, k1);
         sched_info[4 * slot + 0] = unit;
         sched_info[4 * slot + 1] = g;
         sched_info[4 * slot + 2] = k0;
         sched_info[4 * slot + 3] = k1;
         ptx::mbar_arrive(&sched_full[slot]);
-        if (unit >= p.total_units) break;
+        if (unit >= total_units) break;
         const TmaDesc* maps = p.maps + static_cast<size_t>(g) * kMapsPerGroup;
         const int local = tile - gd.tile_start;
         const int mt = local % gd.tiles_m;
@@ -333,7 +338,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         } else {
           sfb_blk0 = gd.sfb + static_cast<size_t>(nt) * rest_k * kSfBlockBytes;
         }
-        const uint8_t* sfa_blk = gd.sfa + static_cast<size_t>(mt) * rest_k * kSfBlockBytes;
+        const int row_a = rb + mt * kBlockM;
+        const uint8_t* sfa_blk =
+            gd.sfa + static_cast<size_t>(rb / kBlockM + mt) * rest_k * kSfBlockBytes;
         const uint32_t tx = Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes +
                             (sfb_blk1 != nullptr ? 2 : 1) * 4 * kSfBlockBytes;
         // L2 warm-up of k-tile `kp` of this tile (A, B halves, scale blocks). In mode 1 only
@@ -350,7 +357,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const int px = kp * kRowBytesPerStage;
           const size_t psf = static_cast<size_t>(kp) * 4 * kSfBlockBytes;
           if (warm_a) {
-            ptx::tma_prefetch_l2_2d(&maps[kMapA], px, mt * kBlockM);
+            ptx::tma_prefetch_l2_2d(&maps[kMapA], px, row_a);
             ptx::bulk_prefetch_l2(sfa_blk + psf, 4 * kSfBlockBytes);
           }
           if (warm_b) {
@@ -368,10 +375,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
         };
         const int claim_kt = k1 - k0 > kClaimLeadKTiles ? k1 - kClaimLeadKTiles : k0;
-        int next_unit = p.total_units;
-        int next_tile = p.total_tiles, next_split = -1;
+        int next_unit = total_units;
+        int next_tile = total_tiles, next_split = -1;
         int g_next = g;
         GroupDev next_gd = gd;
+        int next_rb = rb;
         bool resolved = false;
         auto claim_next = [&]() -> int {
           if (p.dynamic_schedule)
@@ -380,10 +388,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         };
         auto resolve_next = [&]() {
           resolved = true;
-          if (next_unit >= p.total_units) return;
+          if (next_unit >= total_units) return;
           unit_tile(p, next_unit, next_tile, next_split);
           g_next = advance_group(tile_ends, groups, p.num_groups, g, next_tile);
           next_gd = groups[g_next];
+          next_rb = seg_row(p, g_next);
           if (g_next != g) acquire_maps(g_next);
         };
         (void)ktiles;
@@ -401,7 +410,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint8_t* sSFB = sSFA + Cfg::kSfaBytes;
           ptx::mbar_arrive_expect_tx(&full_bar[stage], tx);
           const int kx = kt * kRowBytesPerStage;
-          ptx::tma_load_2d(sA, &maps[kMapA], &full_bar[stage], kx, mt * kBlockM);
+          ptx::tma_load_2d(sA, &maps[kMapA], &full_bar[stage], kx, row_a);
           if (GATED) {
             ptx::tma_load_2d(sB, &maps[kMapB], &full_bar[stage], kx, nt * 128);
             ptx::tma_load_2d(sB + 128 * kRowBytesPerStage, &maps[kMapB2], &full_bar[stage], kx,
@@ -442,6 +451,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         split = next_split;
         g = g_next;
         gd = next_gd;
+        rb = next_rb;
       }
       // Make sure no copy into this CTA's shared memory is still in flight at exit:
       // wait for the most recent fill of every stage (already complete on the normal path).
@@ -479,7 +489,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const int unit = sched_info[4 * slot + 0];
         const int ktiles = sched_info[4 * slot + 3] - sched_info[4 * slot + 2];  // this unit's
         ptx::mbar_arrive(&sched_empty[slot]);
-        if (unit >= p.total_units) break;
+        if (unit >= total_units) break;
         const int acc = static_cast<int>(local & 1u);
         if (!wait_phase(&acce_bar[acc], (acc_parity >> acc) & 1u, abort_flag, p.error_bits,
                         kDevErrAccTimeout)) {
@@ -563,10 +573,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const int g = sched_info[4 * slot + 1];
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&sched_empty[slot]);
-      if (unit >= p.total_units) break;
+      if (unit >= total_units) break;
       int tile, split;
       unit_tile(p, unit, tile, split);
       const GroupDev gd = groups[g];
+      const int rb = seg_row(p, g);  // C rows of the group start here
       const TmaDesc* map_c = p.maps + static_cast<size_t>(g) * kMapsPerGroup + kMapC;
       if (!DIRECT && split < 0 && g != acquired_g) {
         if (lane == 0) ptx::tensormap_fence_acquire(map_c);
@@ -643,7 +654,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             const int col = nt * Cfg::kOutN + box * 64 + half * 32;
             if (row < gd.m) {
               uint4* dst = reinterpret_cast<uint4*>(
-                  gd.c + (static_cast<size_t>(row) * gd.n + col) * sizeof(__half));
+                  gd.c + (static_cast<size_t>(rb + row) * gd.n + col) * sizeof(__half));
 #pragma unroll
               for (int c = 0; c < 4; ++c)
                 if (col + 8 * c < gd.n)
@@ -667,7 +678,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           __syncwarp();
           if (lane == 0) {
             ptx::tma_store_2d(map_c, my_bufs + (stores & 1u) * Cfg::kEpiBufBytes,
-                              nt * Cfg::kOutN + box * 64, row0);
+                              nt * Cfg::kOutN + box * 64, rb + row0);
             ptx::bulk_commit_group();
           }
           ++stores;

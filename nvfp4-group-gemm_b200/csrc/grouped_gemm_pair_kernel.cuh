@@ -105,6 +105,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
   stage_tile_ends(tile_ends, groups, p.num_groups);  // ordered by the cluster barrier below
+  // Segment launches learn their tile count from the workspace (written by the segment
+  // set-up kernel); clusters beyond it have no tile and end at once.
+  const int total_tiles = p.seg_total_tiles != nullptr ? *p.seg_total_tiles : p.total_tiles;
   // Barriers of both CTAs initialised and TMEM allocated in both before any
   // cross-CTA arrive, load completion or MMA.
   ptx::tcgen05_fence_before_sync();
@@ -123,7 +126,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // The record of the next tile's group is loaded while this tile's loads are issued.
       int g = advance_group(tile_ends, groups, p.num_groups, 0, cluster);
       GroupDev next_gd = groups[g];
-      for (int tile = cluster; ok && tile < p.total_tiles; tile += num_clusters) {
+      for (int tile = cluster; ok && tile < total_tiles; tile += num_clusters) {
         const GroupDev gd = next_gd;
         const int g_next = advance_group(tile_ends, groups, p.num_groups, g, tile + num_clusters);
         next_gd = groups[g_next];
@@ -149,13 +152,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const int nt = local / gd.tiles_m;
         const int ktiles = gd.k / kBlockK;
         const int rest_k = gd.k / 64;
-        const int row_a = mt * 256 + 128 * static_cast<int>(rank);
+        const int rb = seg_row(p, g);  // first row of the group's segment (0 normally)
+        const int row_a = rb + mt * 256 + 128 * static_cast<int>(rank);
         // This CTA's half of the MMA's B rows.
         const TmaDesc* map_b = (GATED && rank == 1) ? &maps[kMapB2] : &maps[kMapB];
         const int row_b = GATED ? nt * 128 : nt * 256 + 128 * static_cast<int>(rank);
         // Scale blocks, in 128-byte rows of the scale maps (16 rows = one k-tile of a
         // 128-row block; a block out of range reads as 0).
-        const int sfa_y0 = (2 * mt + static_cast<int>(rank)) * rest_k * 4;
+        const int sfa_y0 = (rb / 128 + 2 * mt + static_cast<int>(rank)) * rest_k * 4;
         const TmaDesc* map_sfb1 = GATED ? &maps[kMapSfb2] : &maps[kMapSfb];
         const int sfb0_y0 = (GATED ? nt : 2 * nt) * rest_k * 4;
         const int sfb1_y0 = (GATED ? nt : 2 * nt + 1) * rest_k * 4;
@@ -241,7 +245,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       bool ok = p.diag_skip_mma == 0;
       int g = advance_group(tile_ends, groups, p.num_groups, 0, cluster);
       int next_k = groups[g].k;
-      for (int tile = cluster; ok && tile < p.total_tiles; tile += num_clusters, ++local) {
+      for (int tile = cluster; ok && tile < total_tiles; tile += num_clusters, ++local) {
         const int ktiles = next_k / kBlockK;
         g = advance_group(tile_ends, groups, p.num_groups, g, tile + num_clusters);
         next_k = groups[g].k;
@@ -317,9 +321,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     constexpr int kBoxes = Cfg::kOutN / 64;
     int g_next = advance_group(tile_ends, groups, p.num_groups, 0, cluster);
     GroupDev next_gd = groups[g_next];
-    for (int tile = cluster; tile < p.total_tiles; tile += num_clusters, ++local) {
+    for (int tile = cluster; tile < total_tiles; tile += num_clusters, ++local) {
       const GroupDev gd = next_gd;
       const int g = g_next;
+      const int rb = seg_row(p, g);  // C rows of the group start here
       g_next = advance_group(tile_ends, groups, p.num_groups, g, tile + num_clusters);
       next_gd = groups[g_next];
       const TmaDesc* map_c = p.maps + static_cast<size_t>(g) * kMapsPerGroup + kMapC;
@@ -411,7 +416,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           __syncwarp();
           if (lane == 0) {
             ptx::tma_store_2d(map_c, my_bufs + (stores & 1u) * Cfg::kEpiBufBytes,
-                              nt * Cfg::kOutN + box * 64, row0);
+                              nt * Cfg::kOutN + box * 64, rb + row0);
             ptx::bulk_commit_group();
           }
           ++stores;

@@ -42,10 +42,11 @@ __global__ void __launch_bounds__(kRouteThreads) nvfp4_route_histogram_kernel(
 
 // One block of 1024 threads. hist[c][e] becomes the exclusive running count of expert e
 // before chunk c; counts[e] the total; offsets[e] the padded first row of expert e
-// (offsets[num_experts] = padded total). src_rows of padding rows are set to -1.
+// (offsets[num_experts] = padded total). src_rows of padding rows, and of the rows past the
+// padded total up to `capacity`, are set to -1.
 __global__ void __launch_bounds__(1024) nvfp4_route_scan_kernel(
     int32_t* __restrict__ hist, int chunks, int num_experts, int32_t* __restrict__ counts,
-    int32_t* __restrict__ offsets, int32_t* __restrict__ src_rows) {
+    int32_t* __restrict__ offsets, int32_t* __restrict__ src_rows, int64_t capacity) {
   __shared__ int32_t padded[kRouteMaxExperts];
   for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
     int32_t run = 0;
@@ -74,6 +75,9 @@ __global__ void __launch_bounds__(1024) nvfp4_route_scan_kernel(
     for (int32_t r = first + static_cast<int32_t>(threadIdx.x); r < end; r += blockDim.x)
       src_rows[r] = -1;
   }
+  for (int64_t r = offsets[num_experts] + static_cast<int64_t>(threadIdx.x); r < capacity;
+       r += blockDim.x)
+    src_rows[r] = -1;
 }
 
 __global__ void __launch_bounds__(kRouteThreads) nvfp4_route_scatter_kernel(

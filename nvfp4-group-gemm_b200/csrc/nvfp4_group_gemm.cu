@@ -51,6 +51,81 @@ __global__ void __launch_bounds__(32) nvfp4_upload_descriptors_kernel(
 }
 
 // ============================================================================
+// Segment launches: group sizes read on the device
+// ============================================================================
+// One block. Group g multiplies rows [seg_offsets[g], seg_offsets[g] + seg_counts[g]) of
+// a slab of `capacity` rows, as the routing step left them in device memory. The kernel
+// checks each segment (offset a multiple of 128, inside the slab; a group that fails is
+// skipped and kDevErrBadSegment is set), writes the group's m, tiles_m and tile range
+// into its record and its first row into seg_rows, and the launch's tile count into the
+// workspace header. Tile ranges follow group order: a block-wide exclusive scan of each
+// group's tile count, 1024 groups per pass.
+constexpr int kSegSetupThreads = 1024;
+
+__global__ void __launch_bounds__(kSegSetupThreads) nvfp4_segments_setup_kernel(
+    GroupDev* __restrict__ groups, int num_groups, const int32_t* __restrict__ seg_offsets,
+    const int32_t* __restrict__ seg_counts, int capacity, int tile_m, int out_n,
+    int32_t* __restrict__ seg_rows, int32_t* __restrict__ total_tiles, uint32_t* error_bits) {
+  __shared__ int32_t warp_sums[kSegSetupThreads / 32];
+  __shared__ int32_t carry;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < num_groups; base += kSegSetupThreads) {
+    const int g = base + static_cast<int>(threadIdx.x);
+    int32_t m = 0, off = 0, tiles_m = 1, tiles = 0;
+    if (g < num_groups) {
+      const int32_t n = groups[g].n;
+      const int32_t cnt = seg_counts[g];
+      off = seg_offsets[g];
+      const bool ok = cnt >= 0 && off >= 0 && off % kBlockM == 0 &&
+                      static_cast<int64_t>(off) + cnt <= capacity;
+      if (!ok) {
+        atomicOr(error_bits, kDevErrBadSegment);
+        off = 0;
+      } else if (cnt > 0 && n > 0) {
+        m = cnt;
+        tiles_m = (cnt + tile_m - 1) / tile_m;
+        tiles = tiles_m * ((n + out_n - 1) / out_n);
+      }
+    }
+    // Inclusive scan of `tiles` over the block: within each warp, then over warp totals.
+    int32_t v = tiles;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int32_t t = __shfl_up_sync(0xffffffffu, v, d);
+      if (lane >= d) v += t;
+    }
+    if (lane == 31) warp_sums[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      int32_t w = warp_sums[lane];
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int32_t t = __shfl_up_sync(0xffffffffu, w, d);
+        if (lane >= d) w += t;
+      }
+      warp_sums[lane] = w;
+    }
+    __syncthreads();
+    const int32_t incl = carry + v + (warp > 0 ? warp_sums[warp - 1] : 0);
+    if (g < num_groups) {
+      GroupDev& d = groups[g];
+      d.m = m;
+      d.tiles_m = tiles_m;
+      d.tile_start = incl - tiles;
+      d.tile_end = incl;
+      seg_rows[g] = off;
+    }
+    __syncthreads();  // every thread has read carry and warp_sums
+    if (threadIdx.x == kSegSetupThreads - 1) carry = incl;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *total_tiles = carry;
+}
+
+// ============================================================================
 // Scale-factor layout: plain [rows, cols] -> 128x4 blocks
 // ============================================================================
 // Output byte ((mm * rest_k + kk) * 32 + i0) * 16 + i1 * 4 + j holds
@@ -386,11 +461,21 @@ cudaError_t launch_pair(const GemmParams& gp, int clusters, cudaStream_t stream)
                      Cfg::kSmemBytes, 2, stream);
 }
 
-// Shared implementation of both grouped entry points: validate, schedule, encode
+// Row segments of a segment launch (nvfp4_grouped_gemm_segments): device arrays of
+// per-group first rows and row counts, and the host's estimate of their total.
+struct SegmentArgs {
+  const int32_t* offsets;
+  const int32_t* counts;
+  int64_t expected_rows;
+};
+
+// Shared implementation of the grouped entry points: validate, schedule, encode
 // and upload descriptors into `ws`, launch. `rec` holds num_groups records of host
-// scratch; `use_cache` selects the cached tensor-map encoder.
+// scratch; `use_cache` selects the cached tensor-map encoder. With `seg`, each group's
+// m is the slab's row count and the rows it multiplies are read on the device.
 int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int flags, uint8_t* ws,
-                      size_t ws_bytes, cudaStream_t s, GroupDev* rec, bool use_cache) {
+                      size_t ws_bytes, cudaStream_t s, GroupDev* rec, bool use_cache,
+                      const SegmentArgs* seg = nullptr) {
   const bool gated = (flags & NVFP4_FLAG_GATED) != 0;
   // Tile shape: CTA pairs (256-row tiles) when the groups are tall enough to fill
   // them, single CTAs (128-row tiles) otherwise; 256 MMA columns unless asked otherwise.
@@ -402,8 +487,14 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
       ++active;
       max_k = std::max(max_k, groups[i].k);
     }
+  if (seg != nullptr) {
+    // The rows are on the device: choose the kernel from the caller's estimate (or the
+    // slab), and never the weight-stationary or split-K variants.
+    rows = seg->expected_rows > 0 ? seg->expected_rows : (num_groups > 0 ? groups[0].m : 0);
+    flags &= ~NVFP4_FLAG_SPLIT_K;
+  }
   bool pair = false;
-  bool swap = (flags & NVFP4_FLAG_WEIGHT_STATIONARY) != 0;
+  bool swap = (flags & NVFP4_FLAG_WEIGHT_STATIONARY) != 0 && seg == nullptr;
   if (!swap && (flags & NVFP4_FLAG_TILE_N128) == 0 && (flags & NVFP4_FLAG_SINGLE_CTA) == 0) {
     if (flags & NVFP4_FLAG_CTA_PAIR) {
       pair = true;
@@ -414,8 +505,8 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
       pair = active > 0 && (rows >= 192 * active || (rows >= 96 * active && max_k >= 4096));
       // Small groups: weight-stationary tiles carry no padding rows (non-gated launches
       // without a forced tile width).
-      swap = !pair && !gated && (flags & NVFP4_FLAG_TILE_N256) == 0 && active > 0 &&
-             rows <= static_cast<int64_t>(kSwapMaxAvgRows) * active;
+      swap = !pair && !gated && seg == nullptr && (flags & NVFP4_FLAG_TILE_N256) == 0 &&
+             active > 0 && rows <= static_cast<int64_t>(kSwapMaxAvgRows) * active;
     }
   }
   const int mma_n = gated ? 256 : ((flags & NVFP4_FLAG_TILE_N128) ? 128 : 256);
@@ -519,6 +610,19 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
   }
 
   GemmParams gp;
+  gp.seg_rows = nullptr;
+  gp.seg_total_tiles = nullptr;
+  if (seg != nullptr) {
+    int32_t* seg_rows = reinterpret_cast<int32_t*>(ws + ws_seg_rows_offset(num_groups));
+    int32_t* seg_total = &reinterpret_cast<WorkspaceHeader*>(ws)->seg_total_tiles;
+    nvfp4_segments_setup_kernel<<<1, kSegSetupThreads, 0, s>>>(
+        groups_dev, num_groups, seg->offsets, seg->counts, groups[0].m, tile_m, out_n, seg_rows,
+        seg_total, reinterpret_cast<uint32_t*>(ws));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "segment set-up launch");
+    gp.seg_rows = seg_rows;
+    gp.seg_total_tiles = seg_total;
+  }
   gp.groups = groups_dev;
   gp.maps = maps_dev;
   gp.error_bits = reinterpret_cast<uint32_t*>(ws);
@@ -780,7 +884,7 @@ NVFP4_API int nvfp4_moe_route(const int32_t* topk_ids, int tokens, int topk, int
         topk_ids, pairs, num_experts, hist);
   }
   nvfp4_route_scan_kernel<<<1, 1024, 0, s>>>(hist, static_cast<int>(chunks), num_experts, counts,
-                                             offsets, src_rows);
+                                             offsets, src_rows, rows_capacity);
   if (chunks > 0) {
     nvfp4_route_scatter_kernel<<<static_cast<unsigned>(chunks), kRouteThreads, 0, s>>>(
         topk_ids, pairs, topk, num_experts, hist, offsets, dest, src_rows);
@@ -860,7 +964,11 @@ NVFP4_API int nvfp4_workspace_check(void* workspace, void* stream, unsigned int*
     e = cudaMemcpy(workspace, &zero, sizeof(zero), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return cuda_fail(e, "clear workspace error word");
     if (device_error_bits) *device_error_bits = bits;
-    return fail(NVFP4_ERR_DEVICE_TIMEOUT, "device error bits 0x%x", bits);
+    if (bits & kDevErrTimeouts)
+      return fail(NVFP4_ERR_DEVICE_TIMEOUT, "device error bits 0x%x", bits);
+    return fail(NVFP4_ERR_BAD_SHAPE,
+                "device error bits 0x%x: a device-side row segment was out of range (skipped)",
+                bits);
   }
   return NVFP4_OK;
 }
@@ -880,6 +988,38 @@ NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsi
   return grouped_gemm_impl(groups, num_groups, flags, static_cast<uint8_t*>(workspace),
                            workspace_bytes, static_cast<cudaStream_t>(stream), rec.data(),
                            /*use_cache=*/true);
+}
+
+NVFP4_API int nvfp4_grouped_gemm_segments(const nvfp4_group* groups, int num_groups,
+                                          unsigned int flags, const int32_t* seg_offsets,
+                                          const int32_t* seg_counts, int64_t expected_rows,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  int st = check_common_args(groups, num_groups, flags);
+  if (st != NVFP4_OK || num_groups == 0) return st;
+  if (flags & (NVFP4_FLAG_WEIGHT_STATIONARY | NVFP4_FLAG_SPLIT_K))
+    return fail(NVFP4_ERR_INVALID_ARGUMENT,
+                "segment launches use row tiles without split-K");
+  if (seg_offsets == nullptr || seg_counts == nullptr)
+    return fail(NVFP4_ERR_NULL_POINTER, "seg_offsets or seg_counts is NULL");
+  if ((reinterpret_cast<uintptr_t>(seg_offsets) & 3u) || (reinterpret_cast<uintptr_t>(seg_counts) & 3u))
+    return fail(NVFP4_ERR_MISALIGNED, "seg_offsets and seg_counts must be 4-byte aligned");
+  for (int i = 1; i < num_groups; ++i)
+    if (groups[i].m != groups[0].m)
+      return fail(NVFP4_ERR_BAD_SHAPE,
+                  "group %d: m=%d differs from group 0's %d (m is the slab's row count, the same "
+                  "for every group of a segment launch)", i, groups[i].m, groups[0].m);
+  if (workspace == nullptr) return fail(NVFP4_ERR_WORKSPACE, "workspace is NULL");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(NVFP4_ERR_WORKSPACE, "workspace not 256-byte aligned");
+  if (workspace_bytes < ws_total_bytes(num_groups))
+    return fail(NVFP4_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes,
+                ws_total_bytes(num_groups));
+  std::vector<GroupDev> rec(static_cast<size_t>(num_groups));
+  const SegmentArgs seg{seg_offsets, seg_counts, expected_rows};
+  return grouped_gemm_impl(groups, num_groups, flags, static_cast<uint8_t*>(workspace),
+                           workspace_bytes, static_cast<cudaStream_t>(stream), rec.data(),
+                           /*use_cache=*/true, &seg);
 }
 
 }  // extern "C"

@@ -50,7 +50,8 @@ static_assert(sizeof(GroupDev) == 64, "group record must fill its 64-byte worksp
 struct WorkspaceHeader {
   uint32_t error_bits;        // OR of device-side failure reasons (see kDevErr*)
   uint32_t tile_counter[2];   // dynamic tile schedule: next tile, finished CTAs (0 between launches)
-  uint32_t reserved[61];
+  int32_t seg_total_tiles;    // segment launches: tiles of the launch, written on the device
+  uint32_t reserved[60];
 };
 static_assert(sizeof(WorkspaceHeader) == 256, "header is 256 bytes");
 
@@ -61,17 +62,26 @@ enum : uint32_t {
   kDevErrAccTimeout = 1u << 2,       // MMA issuer gave up waiting for a drained accumulator
   kDevErrEpilogueTimeout = 1u << 3,  // epilogue gave up waiting for a finished accumulator
   kDevErrDrainTimeout = 1u << 4,     // in-flight copies or MMAs did not finish at exit
+  kDevErrBadSegment = 1u << 5,       // a device-side row segment was out of range (skipped)
 };
+constexpr uint32_t kDevErrTimeouts = kDevErrProducerTimeout | kDevErrMmaTimeout |
+                                     kDevErrAccTimeout | kDevErrEpilogueTimeout |
+                                     kDevErrDrainTimeout;
 
-// Workspace layout: header | GroupDev[G] (64 B each) | TmaDesc[G][8] (128 B aligned).
+// Workspace layout: header | GroupDev[G] (64 B each) | TmaDesc[G][8] (128 B aligned) |
+// int32 segment row offsets[G] (segment launches; 128 B aligned).
 __host__ __device__ constexpr size_t ws_groups_offset() { return sizeof(WorkspaceHeader); }
 __host__ __device__ constexpr size_t ws_maps_offset(int num_groups) {
   return (ws_groups_offset() + static_cast<size_t>(num_groups) * 64 + 127) &
          ~static_cast<size_t>(127);
 }
-__host__ __device__ constexpr size_t ws_total_bytes(int num_groups) {
+__host__ __device__ constexpr size_t ws_seg_rows_offset(int num_groups) {
   return ws_maps_offset(num_groups) +
          static_cast<size_t>(num_groups) * kMapsPerGroup * sizeof(TmaDesc);
+}
+__host__ __device__ constexpr size_t ws_total_bytes(int num_groups) {
+  return ws_seg_rows_offset(num_groups) +
+         ((static_cast<size_t>(num_groups) * 4 + 127) & ~static_cast<size_t>(127));
 }
 
 // Split-K scratch, after the workspace proper (256-byte aligned): split_counters (4 KiB),
@@ -118,6 +128,17 @@ struct GemmParams {
   int32_t total_units;
   float* split_partials;
   int32_t* split_counters;
+  // Segment launches (group rows given on the device): group g's A rows, scale blocks and C
+  // rows start at row seg_rows[g] (a multiple of 128) of its operands, and the launch's
+  // tile count is *seg_total_tiles (total_tiles and total_units above are then only upper
+  // bounds). Both nullptr otherwise.
+  const int32_t* seg_rows;
+  const int32_t* seg_total_tiles;
 };
+
+// First row of group g's segment (0 outside segment launches).
+__device__ __forceinline__ int seg_row(const GemmParams& p, int g) {
+  return p.seg_rows != nullptr ? p.seg_rows[g] : 0;
+}
 
 }  // namespace nvfp4

@@ -308,6 +308,89 @@ def grouped_gemm_table(table: np.ndarray, flags: int, device: torch.device,
     ws.last_table = None  # the next grouped_gemm call on this stream rebuilds its descriptors
     ws.last_sig = None
 
+def grouped_gemm_segments(a: torch.Tensor, sfa: torch.Tensor, c: torch.Tensor,
+                          b: Sequence[torch.Tensor], sfb: Sequence[torch.Tensor],
+                          seg_offsets: torch.Tensor, seg_counts: torch.Tensor,
+                          alpha: Sequence[float] | None = None,
+                          b2: Sequence[torch.Tensor] | None = None,
+                          sfb2: Sequence[torch.Tensor] | None = None,
+                          alpha2: Sequence[float] | None = None, expected_rows: int = 0,
+                          cta: str | None = None,
+                          stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """Grouped GEMM over row segments of one slab, with the segments read on the GPU.
+
+    ``a`` (packed e2m1 [R, K/2]), ``sfa`` (blocked scales of R rows) and ``c`` (fp16
+    [R, N]) are slabs shared by all groups; group g multiplies rows
+    ``[seg_offsets[g], seg_offsets[g] + seg_counts[g])`` of ``a`` by its weights ``b[g]``
+    (with ``b2[g]`` for the gated form) into the same rows of ``c``. ``seg_offsets`` and
+    ``seg_counts`` are int32 CUDA tensors, e.g. a routing step's output: nothing is read back
+    to the host, so the call can be captured in a CUDA graph. Offsets must be multiples of
+    128 inside the slab (a group that breaks this is skipped and :func:`check_device_errors`
+    raises); the rows from a segment's end up to the next multiple of 128 may be
+    overwritten. ``expected_rows`` (the host's estimate of the rows, e.g. tokens x top-k)
+    picks the tile shape like the rows of :func:`grouped_gemm`; ``cta`` forces it.
+    """
+    if cta not in (None, "pair", "single"):
+        raise ValueError(f"cta must be None, 'pair' or 'single', got {cta!r}")
+    G = len(b)
+    if len(sfb) != G:
+        raise ValueError("b and sfb must have one entry per group")
+    gated = b2 is not None
+    if gated and (sfb2 is None or len(b2) != G or len(sfb2) != G):
+        raise ValueError("b2 and sfb2 must both be given, one per group")
+    for name, t in (("seg_offsets", seg_offsets), ("seg_counts", seg_counts)):
+        if t.dtype != torch.int32 or not t.is_cuda or not t.is_contiguous() or t.numel() < G:
+            raise ValueError(f"{name} must be a contiguous CUDA int32 tensor of >= {G} entries")
+    if c.dtype != torch.float16 or c.dim() != 2 or not c.is_cuda:
+        raise ValueError("c must be a CUDA fp16 [rows, N] tensor")
+    rows, n = int(c.shape[0]), int(c.shape[1])
+    k = int(a.shape[1]) * 2 if a.dim() >= 2 else 0
+    _check_fp4(a, "a")
+    a = _as_2d_kmajor(a, rows, k // 2, "a")
+    _as_2d_kmajor(c, rows, n, "c")  # dense fp16 rows
+    _check_sf(sfa, rows, k, "sfa")
+    for g in range(G):
+        _check_fp4(b[g], f"b[{g}]")
+        _as_2d_kmajor(b[g], n, k // 2, f"b[{g}]")
+        _check_sf(sfb[g], n, k, f"sfb[{g}]")
+        if gated:
+            _check_fp4(b2[g], f"b2[{g}]")
+            _as_2d_kmajor(b2[g], n, k // 2, f"b2[{g}]")
+            _check_sf(sfb2[g], n, k, f"sfb2[{g}]")
+    device = c.device
+    table = np.zeros(G, dtype=_native.GROUP_DTYPE)
+    table["a"], table["sfa"], table["c"] = a.data_ptr(), sfa.data_ptr(), c.data_ptr()
+    table["b"] = [t.data_ptr() for t in b]
+    table["sfb"] = [t.data_ptr() for t in sfb]
+    if gated:
+        table["b2"] = [t.data_ptr() for t in b2]
+        table["sfb2"] = [t.data_ptr() for t in sfb2]
+    table["m"], table["n"], table["k"] = rows, n, k
+    table["alpha"] = 1.0 if alpha is None else np.asarray(alpha, dtype=np.float32)
+    table["alpha2"] = 1.0 if alpha2 is None else np.asarray(alpha2, dtype=np.float32)
+    flags = _native.FLAG_GATED if gated else 0
+    if cta == "pair":
+        flags |= _native.FLAG_CTA_PAIR
+    elif cta == "single":
+        flags |= _native.FLAG_SINGLE_CTA
+    if G == 0 or rows == 0:
+        return c
+    s = stream or torch.cuda.current_stream(device)
+    ws = _workspace_for(device, s, _native.workspace_size(G))
+    call_flags = flags
+    if (ws.last_flags == flags and ws.last_table is not None
+            and ws.last_table.shape == table.shape and np.array_equal(ws.last_table, table)):
+        call_flags |= _native.FLAG_REUSE_DESCRIPTORS
+    with torch.cuda.device(device):
+        _native.grouped_gemm_segments_raw(table, call_flags, seg_offsets.data_ptr(),
+                                          seg_counts.data_ptr(), int(expected_rows),
+                                          ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
+    ws.last_table = table
+    ws.last_flags = flags
+    ws.last_sig = None
+    return c
+
+
 class GroupedGemmPlan:
     """A grouped launch validated once and then run many times on the same tensors.
 

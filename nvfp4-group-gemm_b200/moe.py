@@ -8,8 +8,13 @@
 Every step is a kernel of this library (nvfp4_moe_route, nvfp4_quantize_rows,
 nvfp4_grouped_gemm, nvfp4_moe_combine). Dispatched buffers give every expert's rows a
 128-row-aligned range, so one blocked scale buffer serves all experts and every per-expert
-operand is a view. The host reads the per-expert row counts once per call (one device ->
-host copy) to build the group tables.
+operand is a view.
+
+Two forms: ``moe_ffn`` reads the per-expert row counts once per call (one device -> host
+copy) and sizes its buffers and group tables to them; ``MoEBlock`` sizes every buffer once
+for a token count, keeps the routing metadata on the GPU and runs both expert GEMMs through
+nvfp4_grouped_gemm_segments, so a call is a fixed sequence of launches with no host read,
+which ``MoEBlock.capture`` records in a CUDA graph.
 
 The reference has no counterpart: it runs a grouped GEMM whose groups arrive already formed
 and quantised. This is the surrounding layer (token dispatch, activation quantisation,
@@ -245,3 +250,169 @@ def moe_ffn(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
                           s_h * np.asarray(weights.s_down, dtype=np.float32))
     grouped_gemm_table(t2, 0, x.device, stream)
     return combine(y, r, topk_weights, stream)
+
+
+class MoEBlock:
+    """The MoE feed-forward block over buffers sized once for ``tokens`` x ``topk``, with no
+    device -> host read in :meth:`run`.
+
+    Routing metadata (per-expert counts and 128-aligned offsets, each pair's dispatched row,
+    each dispatched row's token) stays on the GPU; the gate/up and down GEMMs run over the
+    whole dispatched slabs and take every expert's rows from the device
+    (nvfp4_grouped_gemm_segments). The per-tensor scales of x and of the SiLU output are
+    fixed at construction (calibrated scales). Dispatched slabs hold ``tokens * topk +
+    127 * experts`` rows, the most any routing can need.
+
+    :meth:`run` returns ``self.out`` (bf16 [tokens, H]), overwritten by the next run.
+    :meth:`capture` records one run into a CUDA graph over the given input tensors; each
+    replay recomputes the block from whatever those tensors hold at that time.
+    """
+
+    def __init__(self, weights: ExpertWeights, tokens: int, topk: int, act_scale: float,
+                 hidden_scale: float, device: torch.device | None = None):
+        if not (act_scale > 0 and hidden_scale > 0):
+            raise ValueError("act_scale and hidden_scale must be positive")
+        dev = torch.device(device) if device is not None else weights.w_gate[0].device
+        E = weights.num_experts
+        idim = int(weights.w_gate[0].shape[0])
+        hdim = int(weights.w_gate[0].shape[1]) * 2
+        if hdim % 256 or idim % 256:
+            raise ValueError(f"hidden ({hdim}) and intermediate ({idim}) sizes must be multiples "
+                             "of 256 (the K of the two grouped GEMMs)")
+        if tokens <= 0 or topk <= 0:
+            raise ValueError("tokens and topk must be positive")
+        self.tokens, self.topk, self.num_experts = tokens, topk, E
+        self.hidden, self.intermediate = hdim, idim
+        self.act_scale, self.hidden_scale = float(act_scale), float(hidden_scale)
+        self.device = dev
+        pairs = tokens * topk
+        cap = pairs + 127 * E
+        self.capacity = cap
+        i32 = dict(dtype=torch.int32, device=dev)
+        u8 = dict(dtype=torch.uint8, device=dev)
+        self._meta = torch.zeros(2 * E + 1, **i32)
+        self.counts, self.offsets = self._meta[:E], self._meta[E:]
+        self.dest = torch.empty(pairs, **i32)
+        self.src_rows = torch.empty(cap, **i32)
+        lib = _native.load_library()
+        self._lib = lib
+        self._route_ws_bytes = int(lib.nvfp4_moe_route_workspace_size(pairs, E))
+        self._route_ws = torch.empty(max(self._route_ws_bytes, 16), **u8)
+        self._qx = torch.empty((tokens, hdim // 2), **u8)
+        self._sfx = torch.empty(blocked_sf_bytes(tokens, hdim // 16), **u8)
+        self._a = torch.empty((cap, hdim // 2), **u8)
+        self._sfa = torch.empty(blocked_sf_bytes(cap, hdim // 16), **u8)
+        self._h = torch.zeros((cap, idim), dtype=torch.float16, device=dev)
+        self._a2 = torch.empty((cap, idim // 2), **u8)
+        self._sfa2 = torch.empty(blocked_sf_bytes(cap, idim // 16), **u8)
+        self._y = torch.empty((cap, hdim), dtype=torch.float16, device=dev)
+        self._w = torch.empty((tokens, topk), dtype=torch.float32, device=dev)
+        self.out = torch.empty((tokens, hdim), dtype=torch.bfloat16, device=dev)
+        P = weights.pointers()
+        self._weights = weights  # the tables hold its addresses
+
+        def slab_table(a, sfa, c, b, sfb, n, k, alpha, b2=None, sfb2=None, alpha2=None):
+            t = np.zeros(E, dtype=_native.GROUP_DTYPE)
+            t["a"], t["sfa"], t["c"] = a.data_ptr(), sfa.data_ptr(), c.data_ptr()
+            t["b"], t["sfb"] = b, sfb
+            if b2 is not None:
+                t["b2"], t["sfb2"], t["alpha2"] = b2, sfb2, alpha2
+            else:
+                t["alpha2"] = 1.0
+            t["m"], t["n"], t["k"], t["alpha"] = cap, n, k, alpha
+            return t
+
+        s_x, s_h = self.act_scale, self.hidden_scale
+        self._t1 = slab_table(self._a, self._sfa, self._h, P["w_gate"], P["sf_gate"], idim, hdim,
+                              s_x * np.asarray(weights.s_gate, dtype=np.float32),
+                              P["w_up"], P["sf_up"],
+                              s_x * np.asarray(weights.s_up, dtype=np.float32))
+        self._t2 = slab_table(self._a2, self._sfa2, self._y, P["w_down"], P["sf_down"], hdim,
+                              idim, s_h * np.asarray(weights.s_down, dtype=np.float32))
+        ws_bytes = _native.workspace_size(E)
+        # Zero-filled: the first 4 bytes are the device error word.
+        self._ws1 = torch.zeros(ws_bytes, **u8)
+        self._ws2 = torch.zeros(ws_bytes, **u8)
+        self._ws_bytes = ws_bytes
+        self._uploaded = False
+
+    def _check_inputs(self, x, topk_ids, topk_weights):
+        if x.dtype not in _DTYPES or tuple(x.shape) != (self.tokens, self.hidden) or \
+                x.stride(1) != 1 or x.device != self.device:
+            raise ValueError(f"x must be bf16/fp16 [{self.tokens}, {self.hidden}] on {self.device}")
+        if topk_ids.dtype != torch.int32 or tuple(topk_ids.shape) != (self.tokens, self.topk) or \
+                not topk_ids.is_contiguous() or topk_ids.device != self.device:
+            raise ValueError(f"topk_ids must be contiguous int32 [{self.tokens}, {self.topk}]")
+        if tuple(topk_weights.shape) != (self.tokens, self.topk) or \
+                topk_weights.device != self.device:
+            raise ValueError(f"topk_weights must be [{self.tokens}, {self.topk}]")
+
+    def run(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+            stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """One block on ``stream``: route, quantise x once per token, dispatch codes and
+        scales, gated GEMM (segments), quantise h, down GEMM (segments), combine."""
+        self._check_inputs(x, topk_ids, topk_weights)
+        lib = self._lib
+        st = stream or torch.cuda.current_stream(self.device)
+        s = st.cuda_stream
+        E, T, K, H, I, cap = (self.num_experts, self.tokens, self.topk, self.hidden,
+                              self.intermediate, self.capacity)
+        chk = _native.check
+        with torch.cuda.device(self.device):
+            chk(lib.nvfp4_moe_route(topk_ids.data_ptr(), T, K, E, self.counts.data_ptr(),
+                                    self.offsets.data_ptr(), self.dest.data_ptr(),
+                                    self.src_rows.data_ptr(), cap, self._route_ws.data_ptr(),
+                                    self._route_ws_bytes, s), lib)
+            chk(lib.nvfp4_quantize(x.data_ptr(), T, H, x.stride(0), _DTYPES[x.dtype],
+                                   self.act_scale, self._qx.data_ptr(), self._qx.stride(0),
+                                   self._sfx.data_ptr(), s), lib)
+            chk(lib.nvfp4_moe_gather_quantized(self._qx.data_ptr(), self._qx.stride(0),
+                                               self._sfx.data_ptr(), self.src_rows.data_ptr(), cap,
+                                               H, self._a.data_ptr(), self._a.stride(0),
+                                               self._sfa.data_ptr(), s), lib)
+            reuse = _native.FLAG_REUSE_DESCRIPTORS if self._uploaded else 0
+            _native.grouped_gemm_segments_raw(self._t1, _native.FLAG_GATED | reuse,
+                                              self.offsets.data_ptr(), self.counts.data_ptr(),
+                                              T * K, self._ws1.data_ptr(), self._ws_bytes, s)
+            chk(lib.nvfp4_quantize_rows(self._h.data_ptr(), cap, I, self._h.stride(0),
+                                        _native.DTYPE_FP16, self.hidden_scale,
+                                        self.src_rows.data_ptr(), _native.ROWS_MASK,
+                                        self._a2.data_ptr(), self._a2.stride(0),
+                                        self._sfa2.data_ptr(), s), lib)
+            _native.grouped_gemm_segments_raw(self._t2, reuse, self.offsets.data_ptr(),
+                                              self.counts.data_ptr(), T * K,
+                                              self._ws2.data_ptr(), self._ws_bytes, s)
+            self._uploaded = True
+            w = topk_weights
+            if w.dtype != torch.float32 or not w.is_contiguous():
+                with torch.cuda.stream(st):
+                    self._w.copy_(w)
+                w = self._w
+            chk(lib.nvfp4_moe_combine(self._y.data_ptr(), self._y.stride(0), self.dest.data_ptr(),
+                                      w.data_ptr(), T, K, H, self.out.data_ptr(),
+                                      self.out.stride(0), s), lib)
+        return self.out
+
+    def check_device_errors(self) -> int:
+        """Synchronise and return the device error bits of both GEMM workspaces (raises
+        Nvfp4Error when a segment was out of range or a wait timed out)."""
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        with torch.cuda.device(self.device):
+            return (_native.workspace_check(self._ws1.data_ptr(), s) |
+                    _native.workspace_check(self._ws2.data_ptr(), s))
+
+    def capture(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+                warmup: int = 1) -> torch.cuda.CUDAGraph:
+        """Record one run over these input tensors into a CUDA graph (after ``warmup`` eager
+        runs, which upload the GEMMs' descriptors so the graph holds only their launches).
+        ``graph.replay()`` then recomputes ``self.out`` from the tensors' current contents."""
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(max(warmup, 1)):
+                self.run(x, topk_ids, topk_weights, side)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            self.run(x, topk_ids, topk_weights, side)
+        return graph

@@ -52,8 +52,10 @@ def test_version_and_strings(pkg):
 def test_size_queries(pkg):
     N = pkg._native
     assert N.workspace_size(0) == 256
-    assert N.workspace_size(8) == 256 + 8 * 64 + 8 * 8 * 128
-    assert N.workspace_size(3) == 512 + 3 * 8 * 128  # records padded to 128 bytes
+    # header + records + maps + segment row offsets (records and offsets padded to 128 B)
+    assert N.workspace_size(8) == 256 + 8 * 64 + 8 * 8 * 128 + 128
+    assert N.workspace_size(3) == 512 + 3 * 8 * 128 + 128
+    assert N.workspace_size(40) == 256 + 40 * 64 + 40 * 8 * 128 + 256
     assert N.sf_blocked_size(80, 32) == 1 * 8 * 512
     assert N.sf_blocked_size(129, 5) == 2 * 2 * 512
     assert N.sf_blocked_size(0, 4) == 0
@@ -93,6 +95,34 @@ def test_validation_errors_before_launch(pkg, kw, flags, status):
     ws = ctypes.create_string_buffer(N.workspace_size(1) + 256)
     ws_ptr = (ctypes.addressof(ws) + 255) & ~255
     st = lib.nvfp4_grouped_gemm(t.ctypes.data, 1, flags, ws_ptr, N.workspace_size(1), None)
+    assert st == status, lib.nvfp4_last_error_detail()
+    assert lib.nvfp4_last_error_detail()
+
+
+@pytest.mark.parametrize("case,flags,status", [
+    ("null_offsets", 0, 4),
+    ("misaligned_counts", 0, 3),
+    ("m_differs", 0, 2),            # every group addresses the same slab
+    ("weight_stationary", 0x80, 1),
+    ("split_k", 0x100, 1),
+    ("bad_k", 0, 2),                # the usual shape checks still apply
+    ("no_workspace", 0, 5),
+])
+def test_segment_validation_errors_before_launch(pkg, case, flags, status):
+    N = pkg._native
+    lib = pkg.load_library()
+    t = np.zeros(2, dtype=N.GROUP_DTYPE)  # (np.concatenate would drop the record padding)
+    t[0] = _table(N)[0]
+    t[1] = _table(N, m=128 if case != "m_differs" else 64)[0]
+    if case == "bad_k":
+        t["k"] = 100
+    ws = ctypes.create_string_buffer(N.workspace_size(2) + 256)
+    ws_ptr = (ctypes.addressof(ws) + 255) & ~255
+    offs = 0 if case == "null_offsets" else 0x70000
+    counts = 0x70102 if case == "misaligned_counts" else 0x70100
+    st = lib.nvfp4_grouped_gemm_segments(t.ctypes.data, 2, flags, offs, counts, 0,
+                                         None if case == "no_workspace" else ws_ptr,
+                                         N.workspace_size(2), None)
     assert st == status, lib.nvfp4_last_error_detail()
     assert lib.nvfp4_last_error_detail()
 
