@@ -135,11 +135,18 @@ NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsi
  * NVFP4_FLAG_REUSE_DESCRIPTORS has the same meaning (the slab addresses, not the
  * segments, are the descriptors). NVFP4_FLAG_WEIGHT_STATIONARY and NVFP4_FLAG_SPLIT_K are
  * rejected. No counterpart in the reference, whose groups are formed on the host.
+ *
+ * NVFP4 output (gated launches, out_sf != NULL): instead of fp16, c receives packed e2m1
+ * codes [m, n/2] and out_sf the 128x4-blocked E4M3 scales of the [m, n] output slab, as
+ * nvfp4_quantize(fp16 output, global_scale = out_scale) would write them (bit-identical);
+ * n must be a multiple of 64. The fp16 output is never written, which saves its write and
+ * the quantiser's read of it (the MoE block's down projection consumes this directly).
  */
 NVFP4_API int nvfp4_grouped_gemm_segments(const nvfp4_group* groups, int num_groups,
                                           unsigned int flags, const int32_t* seg_offsets,
                                           const int32_t* seg_counts, int64_t expected_rows,
-                                          void* workspace, size_t workspace_bytes, void* stream);
+                                          void* out_sf, float out_scale, void* workspace,
+                                          size_t workspace_bytes, void* stream);
 
 /*
  * Extra workspace for split-K: with NVFP4_FLAG_SPLIT_K and workspace_bytes at least

@@ -166,7 +166,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_workspace_check.restype = i32
         lib.nvfp4_grouped_gemm_noalloc.argtypes = [vp, i32, u32, vp]
         lib.nvfp4_grouped_gemm_noalloc.restype = i32
-        lib.nvfp4_grouped_gemm_segments.argtypes = [vp, i32, u32, vp, vp, i64, vp, sz, vp]
+        lib.nvfp4_grouped_gemm_segments.argtypes = [vp, i32, u32, vp, vp, i64, vp,
+                                                    ctypes.c_float, vp, sz, vp]
         lib.nvfp4_grouped_gemm_segments.restype = i32
         lib.nvfp4_quantize.argtypes = [vp, i32, i32, i64, i32, ctypes.c_float, vp, i64, vp, vp]
         lib.nvfp4_quantize.restype = i32
@@ -222,14 +223,16 @@ def grouped_gemm_raw(table: np.ndarray, flags: int, workspace_ptr: int, workspac
 
 def grouped_gemm_segments_raw(table: np.ndarray, flags: int, offsets_ptr: int, counts_ptr: int,
                               expected_rows: int, workspace_ptr: int, workspace_bytes: int,
-                              stream_ptr: int) -> None:
+                              stream_ptr: int, out_sf_ptr: int = 0, out_scale: float = 0.0) -> None:
     """Call nvfp4_grouped_gemm_segments on a GROUP_DTYPE table (host memory) whose rows are
-    given by device int32 arrays of per-group first rows and row counts."""
+    given by device int32 arrays of per-group first rows and row counts (NVFP4 output when
+    out_sf_ptr is non-zero)."""
     assert table.dtype == GROUP_DTYPE and table.flags["C_CONTIGUOUS"]
     lib = load_library()
     st = lib.nvfp4_grouped_gemm_segments(table.ctypes.data, int(table.shape[0]), flags,
                                          offsets_ptr, counts_ptr, int(expected_rows),
-                                         workspace_ptr, workspace_bytes, stream_ptr)
+                                         out_sf_ptr or None, float(out_scale), workspace_ptr,
+                                         workspace_bytes, stream_ptr)
     check(st, lib)
 
 

@@ -26,6 +26,7 @@
 
 #include <cuda_fp16.h>
 
+#include "nvfp4_quant_math.cuh"
 #include "nvfp4_types.cuh"
 #include "sm100_ptx.cuh"
 
@@ -147,6 +148,42 @@ __device__ __forceinline__ bool warp_wait_phase(uint64_t* bar, uint32_t parity,
     }
   }
   return ok != 0;
+}
+
+// Gated epilogue value of one output element: fp16(silu(fp16(alpha * gate)) * fp16(alpha2 *
+// up)). Gate and up are rounded to fp16 first, as the reference's two-GEMM path does; SiLU
+// and the product are fp32.
+__device__ __forceinline__ float gated_value(uint32_t gate_bits, uint32_t up_bits, float alpha,
+                                             float alpha2) {
+  const float gte = __half2float(__float2half_rn(__uint_as_float(gate_bits) * alpha));
+  const float up = __half2float(__float2half_rn(__uint_as_float(up_bits) * alpha2));
+  return __fdividef(gte, 1.0f + __expf(-gte)) * up;
+}
+
+// NVFP4 output of one row's 64-column box of a gated tile: the fp16 values the fp16 output
+// would hold, quantised in blocks of 16 exactly as nvfp4_quantize quantises that output.
+// Writes 32 bytes of codes at `codes` (16-byte aligned) and the four scale codes as one
+// 4-byte store at `sf`.
+__device__ __forceinline__ void store_gated_box_nvfp4(const uint32_t* v0, const uint32_t* v1,
+                                                      const uint32_t* u0, const uint32_t* u1,
+                                                      float alpha, float alpha2, float sg,
+                                                      float d6, uint8_t* codes, uint8_t* sf) {
+  uint32_t sf4 = 0;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const uint32_t* v = half ? v1 : v0;
+    const uint32_t* u = half ? u1 : u0;
+    float hv[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      hv[i] = __half2float(__float2half_rn(gated_value(v[i], u[i], alpha, alpha2)));
+    uint32_t c0, c1;
+    const uint2 q0 = quantize16(hv, sg, d6, c0);
+    const uint2 q1 = quantize16(hv + 16, sg, d6, c1);
+    sf4 |= (c0 | (c1 << 8)) << (16 * half);
+    *reinterpret_cast<uint4*>(codes + 16 * half) = make_uint4(q0.x, q0.y, q1.x, q1.y);
+  }
+  *reinterpret_cast<uint32_t*>(sf) = sf4;
 }
 
 // Tile -> group lookup. Tiles are numbered group by group and every CTA meets its
@@ -612,6 +649,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // split tiles) or through the swizzled staging box and a TMA store.
       auto emit_box = [&](const uint32_t* v0, const uint32_t* v1, const uint32_t* u0,
                           const uint32_t* u1, int box, bool direct) {
+        if (GATED && p.out_sf != nullptr) {
+          // NVFP4 output (codes and blocked scales; no fp16 staging).
+          if (row < gd.m) {
+            const int col0 = nt * Cfg::kOutN + box * 64;
+            const int64_t r = static_cast<int64_t>(rb) + row;
+            store_gated_box_nvfp4(v0, v1, u0, u1, gd.alpha, gd.alpha2, p.out_scale, p.out_d6,
+                                  gd.c + r * (gd.n / 2) + col0 / 2,
+                                  p.out_sf + blocked_sf_offset(r, col0 / 16, (gd.n + 63) / 64));
+          }
+          return;
+        }
         const uint32_t buf = my_bufs_s + (stores & 1u) * Cfg::kEpiBufBytes;
         if (!direct) {
           // The store that last read this staging buffer (two boxes ago) must be done with it.
@@ -626,18 +674,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             const uint32_t* u = half ? u1 : u0;
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              float o[2];
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                // Gate and up are rounded to fp16 first, as the reference's two-GEMM
-                // path does; SiLU and the product are fp32.
-                const float gte = __half2float(
-                    __float2half_rn(__uint_as_float(v[2 * i + h]) * gd.alpha));
-                const float up = __half2float(
-                    __float2half_rn(__uint_as_float(u[2 * i + h]) * gd.alpha2));
-                o[h] = __fdividef(gte, 1.0f + __expf(-gte)) * up;
-              }
-              __half2 hv = __floats2half2_rn(o[0], o[1]);
+              __half2 hv = __floats2half2_rn(gated_value(v[2 * i], u[2 * i], gd.alpha, gd.alpha2),
+                                             gated_value(v[2 * i + 1], u[2 * i + 1], gd.alpha,
+                                                         gd.alpha2));
               packed[i] = *reinterpret_cast<uint32_t*>(&hv);
             }
           } else {

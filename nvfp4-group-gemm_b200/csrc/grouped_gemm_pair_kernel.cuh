@@ -374,6 +374,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (lane == 0) ptx::mbar_arrive_cluster(release_bar);
             released = true;
           }
+          if (GATED && p.out_sf != nullptr) {
+            // NVFP4 output (codes and blocked scales; no fp16 staging).
+            const int row = row0 + lane;
+            if (row < gd.m) {
+              const int col0 = nt * Cfg::kOutN + box * 64;
+              const int64_t r = static_cast<int64_t>(rb) + row;
+              store_gated_box_nvfp4(v0, v1, u0, u1, gd.alpha, gd.alpha2, p.out_scale,
+                                    p.out_d6, gd.c + r * (gd.n / 2) + col0 / 2,
+                                    p.out_sf + blocked_sf_offset(r, col0 / 16, (gd.n + 63) / 64));
+            }
+            continue;
+          }
           if (lane == 0) ptx::bulk_wait_group_read<1>();
           __syncwarp();
 #pragma unroll
@@ -384,16 +396,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               const uint32_t* u = half ? u1 : u0;
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
-                float o[2];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const float gte = __half2float(
-                      __float2half_rn(__uint_as_float(v[2 * i + h]) * gd.alpha));
-                  const float up = __half2float(
-                      __float2half_rn(__uint_as_float(u[2 * i + h]) * gd.alpha2));
-                  o[h] = __fdividef(gte, 1.0f + __expf(-gte)) * up;
-                }
-                __half2 hv = __floats2half2_rn(o[0], o[1]);
+                __half2 hv = __floats2half2_rn(
+                    gated_value(v[2 * i], u[2 * i], gd.alpha, gd.alpha2),
+                    gated_value(v[2 * i + 1], u[2 * i + 1], gd.alpha, gd.alpha2));
                 packed[i] = *reinterpret_cast<uint32_t*>(&hv);
               }
             } else {

@@ -467,6 +467,8 @@ struct SegmentArgs {
   const int32_t* offsets;
   const int32_t* counts;
   int64_t expected_rows;
+  uint8_t* out_sf;   // NVFP4 output of a gated launch: blocked scales of the output slab
+  float out_scale;   // ... and its per-tensor scale
 };
 
 // Shared implementation of the grouped entry points: validate, schedule, encode
@@ -612,6 +614,9 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
   GemmParams gp;
   gp.seg_rows = nullptr;
   gp.seg_total_tiles = nullptr;
+  gp.out_sf = seg != nullptr ? seg->out_sf : nullptr;
+  gp.out_scale = seg != nullptr ? seg->out_scale : 0.0f;
+  gp.out_d6 = 6.0f * gp.out_scale;
   if (seg != nullptr) {
     int32_t* seg_rows = reinterpret_cast<int32_t*>(ws + ws_seg_rows_offset(num_groups));
     int32_t* seg_total = &reinterpret_cast<WorkspaceHeader*>(ws)->seg_total_tiles;
@@ -993,7 +998,8 @@ NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsi
 NVFP4_API int nvfp4_grouped_gemm_segments(const nvfp4_group* groups, int num_groups,
                                           unsigned int flags, const int32_t* seg_offsets,
                                           const int32_t* seg_counts, int64_t expected_rows,
-                                          void* workspace, size_t workspace_bytes, void* stream) {
+                                          void* out_sf, float out_scale, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
   g_last_error.clear();
   int st = check_common_args(groups, num_groups, flags);
   if (st != NVFP4_OK || num_groups == 0) return st;
@@ -1004,6 +1010,17 @@ NVFP4_API int nvfp4_grouped_gemm_segments(const nvfp4_group* groups, int num_gro
     return fail(NVFP4_ERR_NULL_POINTER, "seg_offsets or seg_counts is NULL");
   if ((reinterpret_cast<uintptr_t>(seg_offsets) & 3u) || (reinterpret_cast<uintptr_t>(seg_counts) & 3u))
     return fail(NVFP4_ERR_MISALIGNED, "seg_offsets and seg_counts must be 4-byte aligned");
+  if (out_sf != nullptr) {
+    if ((flags & NVFP4_FLAG_GATED) == 0)
+      return fail(NVFP4_ERR_INVALID_ARGUMENT, "NVFP4 output needs NVFP4_FLAG_GATED");
+    if (!(out_scale > 0.0f) || !std::isfinite(out_scale))
+      return fail(NVFP4_ERR_INVALID_ARGUMENT, "out_scale must be finite and > 0");
+    if (!aligned16(out_sf)) return fail(NVFP4_ERR_MISALIGNED, "out_sf not 16-byte aligned");
+    for (int i = 0; i < num_groups; ++i)
+      if (groups[i].n % 64 != 0)
+        return fail(NVFP4_ERR_BAD_SHAPE,
+                    "group %d: n=%d must be a multiple of 64 for NVFP4 output", i, groups[i].n);
+  }
   for (int i = 1; i < num_groups; ++i)
     if (groups[i].m != groups[0].m)
       return fail(NVFP4_ERR_BAD_SHAPE,
@@ -1016,7 +1033,8 @@ NVFP4_API int nvfp4_grouped_gemm_segments(const nvfp4_group* groups, int num_gro
     return fail(NVFP4_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes,
                 ws_total_bytes(num_groups));
   std::vector<GroupDev> rec(static_cast<size_t>(num_groups));
-  const SegmentArgs seg{seg_offsets, seg_counts, expected_rows};
+  const SegmentArgs seg{seg_offsets, seg_counts, expected_rows, static_cast<uint8_t*>(out_sf),
+                        out_scale};
   return grouped_gemm_impl(groups, num_groups, flags, static_cast<uint8_t*>(workspace),
                            workspace_bytes, static_cast<cudaStream_t>(stream), rec.data(),
                            /*use_cache=*/true, &seg);

@@ -134,6 +134,12 @@ struct GemmParams {
   // bounds). Both nullptr otherwise.
   const int32_t* seg_rows;
   const int32_t* seg_total_tiles;
+  // NVFP4 output of gated launches (out_sf != nullptr): each group's c holds packed e2m1
+  // codes [rows, n/2] and out_sf the blocked E4M3 scales of the output slab; out_scale is
+  // the output's per-tensor scale and out_d6 = 6 * out_scale (fp32).
+  uint8_t* out_sf;
+  float out_scale;
+  float out_d6;
 };
 
 // First row of group g's segment (0 outside segment launches).

@@ -1,11 +1,8 @@
 // NVFP4 activation quantiser: bf16/fp16 [rows, cols] -> packed e2m1 [rows, cols/2] and
 // E4M3 block scales written straight into the 128x4-blocked layout the GEMM consumes.
 //
-// Two-level scaling, with every fp32 operation rounded to nearest (no contraction):
-//   d6 = 6 * s_g; sf = E4M3_rn_sat(amax16 / d6); enc = 1 / (value(sf) * s_g) (0 if sf is 0);
-//   q  = E2M1_rn_sat(x * enc)
-// so that x ~= value(q) * value(sf) * s_g; s_g = amax_tensor / (6 * 448) keeps every block
-// scale in E4M3's range.
+// Two-level scaling (nvfp4_quant_math.cuh); s_g = amax_tensor / (6 * 448) keeps every
+// block scale in E4M3's range.
 //
 // Memory-bound: 2 bytes in, 0.5 + 1/16 bytes out per element. A first version gave each
 // lane whole rows (so each warp load touched 32 rows): L1 ran at 94 % of its peak and the
@@ -17,40 +14,10 @@
 
 #include <type_traits>
 
+#include "nvfp4_quant_math.cuh"
 #include "sm100_ptx.cuh"
 
 namespace nvfp4 {
-
-// Eight fp32 values -> four bytes of packed e2m1 (element 2i in the low nibble of byte i).
-__device__ __forceinline__ uint32_t cvt_e2m1x8(const float* v) {
-  uint32_t out;
-  asm("{\n"
-      ".reg .b8 b0, b1, b2, b3;\n"
-      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n"
-      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n"
-      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n"
-      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n"
-      "mov.b32 %0, {b0, b1, b2, b3};\n"
-      "}"
-      : "=r"(out)
-      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
-  return out;
-}
-
-// fp32 -> float8_e4m3fn code (round to nearest even, saturate to +-448).
-__device__ __forceinline__ uint32_t cvt_e4m3(float v) {
-  uint16_t out;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(out) : "f"(0.0f), "f"(v));
-  return out & 0xFFu;
-}
-
-// Value of a non-negative, non-NaN E4M3 code (exact in fp32).
-__device__ __forceinline__ float e4m3_value(uint32_t code) {
-  const uint32_t e = (code >> 3) & 0xFu;
-  const uint32_t m = code & 0x7u;
-  if (e == 0) return static_cast<float>(m) * 0.001953125f;  // m/8 * 2^-6
-  return __uint_as_float(((e + 120u) << 23) | (m << 20));   // (1 + m/8) * 2^(e-7)
-}
 
 // Sixteen elements held as eight 32-bit words (two 16-byte loads) -> fp32 (exact).
 template <typename T>
@@ -132,9 +99,8 @@ __global__ void __launch_bounds__(32 * kQuantWarps, 4) nvfp4_quantize_kernel(
 #pragma unroll
         for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-        const uint32_t code = cvt_e4m3(__fdiv_rn(amax, d6));
-        const float sval = e4m3_value(code);
-        const float enc = sval > 0.0f ? __fdiv_rn(1.0f, __fmul_rn(sval, sg)) : 0.0f;
+        float enc;
+        const uint32_t code = block_scale(amax, sg, d6, enc);
         float q[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(v[i], enc);

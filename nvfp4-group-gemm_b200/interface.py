@@ -315,7 +315,8 @@ def grouped_gemm_segments(a: torch.Tensor, sfa: torch.Tensor, c: torch.Tensor,
                           b2: Sequence[torch.Tensor] | None = None,
                           sfb2: Sequence[torch.Tensor] | None = None,
                           alpha2: Sequence[float] | None = None, expected_rows: int = 0,
-                          cta: str | None = None,
+                          cta: str | None = None, out_sf: torch.Tensor | None = None,
+                          out_scale: float | None = None,
                           stream: torch.cuda.Stream | None = None) -> torch.Tensor:
     """Grouped GEMM over row segments of one slab, with the segments read on the GPU.
 
@@ -329,6 +330,10 @@ def grouped_gemm_segments(a: torch.Tensor, sfa: torch.Tensor, c: torch.Tensor,
     raises); the rows from a segment's end up to the next multiple of 128 may be
     overwritten. ``expected_rows`` (the host's estimate of the rows, e.g. tokens x top-k)
     picks the tile shape like the rows of :func:`grouped_gemm`; ``cta`` forces it.
+
+    NVFP4 output (gated only): with ``out_sf`` (blocked scales of R rows x N) and
+    ``out_scale``, ``c`` is a uint8 [R, N/2] slab that receives the e2m1 codes of the
+    output, bit-identical to ``quantize(fp16 output, out_scale)``; N % 64 == 0.
     """
     if cta not in (None, "pair", "single"):
         raise ValueError(f"cta must be None, 'pair' or 'single', got {cta!r}")
@@ -341,13 +346,27 @@ def grouped_gemm_segments(a: torch.Tensor, sfa: torch.Tensor, c: torch.Tensor,
     for name, t in (("seg_offsets", seg_offsets), ("seg_counts", seg_counts)):
         if t.dtype != torch.int32 or not t.is_cuda or not t.is_contiguous() or t.numel() < G:
             raise ValueError(f"{name} must be a contiguous CUDA int32 tensor of >= {G} entries")
-    if c.dtype != torch.float16 or c.dim() != 2 or not c.is_cuda:
-        raise ValueError("c must be a CUDA fp16 [rows, N] tensor")
-    rows, n = int(c.shape[0]), int(c.shape[1])
+    quant_out = out_sf is not None
+    if quant_out:
+        if not gated:
+            raise ValueError("NVFP4 output (out_sf) is for gated launches")
+        if out_scale is None or not (out_scale > 0) or not np.isfinite(out_scale):
+            raise ValueError("out_scale must be finite and > 0 with out_sf")
+        if c.dtype != torch.uint8 or c.dim() != 2 or not c.is_cuda:
+            raise ValueError("with out_sf, c must be a CUDA uint8 [rows, N/2] tensor of codes")
+        rows, n = int(c.shape[0]), int(c.shape[1]) * 2
+        if n % 64:
+            raise ValueError(f"N={n} must be a multiple of 64 for NVFP4 output")
+        _as_2d_kmajor(c, rows, n // 2, "c")
+        _check_sf(out_sf, rows, n, "out_sf")
+    else:
+        if c.dtype != torch.float16 or c.dim() != 2 or not c.is_cuda:
+            raise ValueError("c must be a CUDA fp16 [rows, N] tensor")
+        rows, n = int(c.shape[0]), int(c.shape[1])
+        _as_2d_kmajor(c, rows, n, "c")  # dense fp16 rows
     k = int(a.shape[1]) * 2 if a.dim() >= 2 else 0
     _check_fp4(a, "a")
     a = _as_2d_kmajor(a, rows, k // 2, "a")
-    _as_2d_kmajor(c, rows, n, "c")  # dense fp16 rows
     _check_sf(sfa, rows, k, "sfa")
     for g in range(G):
         _check_fp4(b[g], f"b[{g}]")
@@ -384,7 +403,9 @@ def grouped_gemm_segments(a: torch.Tensor, sfa: torch.Tensor, c: torch.Tensor,
     with torch.cuda.device(device):
         _native.grouped_gemm_segments_raw(table, call_flags, seg_offsets.data_ptr(),
                                           seg_counts.data_ptr(), int(expected_rows),
-                                          ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
+                                          ws.buf.data_ptr(), ws.nbytes, s.cuda_stream,
+                                          out_sf.data_ptr() if quant_out else 0,
+                                          float(out_scale) if quant_out else 0.0)
     ws.last_table = table
     ws.last_flags = flags
     ws.last_sig = None

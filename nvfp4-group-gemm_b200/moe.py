@@ -14,7 +14,8 @@ Two forms: ``moe_ffn`` reads the per-expert row counts once per call (one device
 copy) and sizes its buffers and group tables to them; ``MoEBlock`` sizes every buffer once
 for a token count, keeps the routing metadata on the GPU and runs both expert GEMMs through
 nvfp4_grouped_gemm_segments, so a call is a fixed sequence of launches with no host read,
-which ``MoEBlock.capture`` records in a CUDA graph.
+which ``MoEBlock.capture`` records in a CUDA graph. Its gate/up GEMM writes the SiLU output
+directly as NVFP4 codes and scales (the separate quantise-h pass and the fp16 h are gone).
 
 The reference has no counterpart: it runs a grouped GEMM whose groups arrive already formed
 and quantised. This is the surrounding layer (token dispatch, activation quantisation,
@@ -259,7 +260,9 @@ class MoEBlock:
     Routing metadata (per-expert counts and 128-aligned offsets, each pair's dispatched row,
     each dispatched row's token) stays on the GPU; the gate/up and down GEMMs run over the
     whole dispatched slabs and take every expert's rows from the device
-    (nvfp4_grouped_gemm_segments). The per-tensor scales of x and of the SiLU output are
+    (nvfp4_grouped_gemm_segments), the gate/up GEMM writing NVFP4 codes and scales of the
+    SiLU output for the down GEMM (bit-identical to quantising its fp16 output). The
+    per-tensor scales of x and of the SiLU output are
     fixed at construction (calibrated scales). Dispatched slabs hold ``tokens * topk +
     127 * experts`` rows, the most any routing can need.
 
@@ -302,9 +305,9 @@ class MoEBlock:
         self._sfx = torch.empty(blocked_sf_bytes(tokens, hdim // 16), **u8)
         self._a = torch.empty((cap, hdim // 2), **u8)
         self._sfa = torch.empty(blocked_sf_bytes(cap, hdim // 16), **u8)
-        self._h = torch.zeros((cap, idim), dtype=torch.float16, device=dev)
-        self._a2 = torch.empty((cap, idim // 2), **u8)
-        self._sfa2 = torch.empty(blocked_sf_bytes(cap, idim // 16), **u8)
+        # Codes and scales of the SiLU output (padding rows keep these zeros or earlier data).
+        self._a2 = torch.zeros((cap, idim // 2), **u8)
+        self._sfa2 = torch.zeros(blocked_sf_bytes(cap, idim // 16), **u8)
         self._y = torch.empty((cap, hdim), dtype=torch.float16, device=dev)
         self._w = torch.empty((tokens, topk), dtype=torch.float32, device=dev)
         self.out = torch.empty((tokens, hdim), dtype=torch.bfloat16, device=dev)
@@ -323,7 +326,7 @@ class MoEBlock:
             return t
 
         s_x, s_h = self.act_scale, self.hidden_scale
-        self._t1 = slab_table(self._a, self._sfa, self._h, P["w_gate"], P["sf_gate"], idim, hdim,
+        self._t1 = slab_table(self._a, self._sfa, self._a2, P["w_gate"], P["sf_gate"], idim, hdim,
                               s_x * np.asarray(weights.s_gate, dtype=np.float32),
                               P["w_up"], P["sf_up"],
                               s_x * np.asarray(weights.s_up, dtype=np.float32))
@@ -350,13 +353,12 @@ class MoEBlock:
     def run(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
             stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """One block on ``stream``: route, quantise x once per token, dispatch codes and
-        scales, gated GEMM (segments), quantise h, down GEMM (segments), combine."""
+        scales, gated GEMM (segments, NVFP4 output), down GEMM (segments), combine."""
         self._check_inputs(x, topk_ids, topk_weights)
         lib = self._lib
         st = stream or torch.cuda.current_stream(self.device)
         s = st.cuda_stream
-        E, T, K, H, I, cap = (self.num_experts, self.tokens, self.topk, self.hidden,
-                              self.intermediate, self.capacity)
+        E, T, K, H, cap = self.num_experts, self.tokens, self.topk, self.hidden, self.capacity
         chk = _native.check
         with torch.cuda.device(self.device):
             chk(lib.nvfp4_moe_route(topk_ids.data_ptr(), T, K, E, self.counts.data_ptr(),
@@ -373,12 +375,8 @@ class MoEBlock:
             reuse = _native.FLAG_REUSE_DESCRIPTORS if self._uploaded else 0
             _native.grouped_gemm_segments_raw(self._t1, _native.FLAG_GATED | reuse,
                                               self.offsets.data_ptr(), self.counts.data_ptr(),
-                                              T * K, self._ws1.data_ptr(), self._ws_bytes, s)
-            chk(lib.nvfp4_quantize_rows(self._h.data_ptr(), cap, I, self._h.stride(0),
-                                        _native.DTYPE_FP16, self.hidden_scale,
-                                        self.src_rows.data_ptr(), _native.ROWS_MASK,
-                                        self._a2.data_ptr(), self._a2.stride(0),
-                                        self._sfa2.data_ptr(), s), lib)
+                                              T * K, self._ws1.data_ptr(), self._ws_bytes, s,
+                                              self._sfa2.data_ptr(), self.hidden_scale)
             _native.grouped_gemm_segments_raw(self._t2, reuse, self.offsets.data_ptr(),
                                               self.counts.data_ptr(), T * K,
                                               self._ws2.data_ptr(), self._ws_bytes, s)

@@ -107,6 +107,10 @@ def test_validation_errors_before_launch(pkg, kw, flags, status):
     ("split_k", 0x100, 1),
     ("bad_k", 0, 2),                # the usual shape checks still apply
     ("no_workspace", 0, 5),
+    ("nvfp4_out_not_gated", 0, 1),  # NVFP4 output is for gated launches
+    ("nvfp4_out_bad_scale", 1, 1),
+    ("nvfp4_out_misaligned", 1, 3),
+    ("nvfp4_out_n", 1, 2),          # n must be a multiple of 64
 ])
 def test_segment_validation_errors_before_launch(pkg, case, flags, status):
     N = pkg._native
@@ -116,12 +120,20 @@ def test_segment_validation_errors_before_launch(pkg, case, flags, status):
     t[1] = _table(N, m=128 if case != "m_differs" else 64)[0]
     if case == "bad_k":
         t["k"] = 100
+    if case == "nvfp4_out_n":
+        t["n"] = 200
+    t["b2"], t["sfb2"] = 0x60000, 0x68000
     ws = ctypes.create_string_buffer(N.workspace_size(2) + 256)
     ws_ptr = (ctypes.addressof(ws) + 255) & ~255
     offs = 0 if case == "null_offsets" else 0x70000
     counts = 0x70102 if case == "misaligned_counts" else 0x70100
-    st = lib.nvfp4_grouped_gemm_segments(t.ctypes.data, 2, flags, offs, counts, 0,
-                                         None if case == "no_workspace" else ws_ptr,
+    out_sf = None
+    out_scale = 0.0
+    if case.startswith("nvfp4_out"):
+        out_sf = 0x78008 if case == "nvfp4_out_misaligned" else 0x78000
+        out_scale = 0.0 if case == "nvfp4_out_bad_scale" else 0.5
+    st = lib.nvfp4_grouped_gemm_segments(t.ctypes.data, 2, flags, offs, counts, 0, out_sf,
+                                         out_scale, None if case == "no_workspace" else ws_ptr,
                                          N.workspace_size(2), None)
     assert st == status, lib.nvfp4_last_error_detail()
     assert lib.nvfp4_last_error_detail()

@@ -240,3 +240,33 @@ def test_moe_block_graph_replay(pkg):
         assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), rep
     assert blk.check_device_errors() == 0
     del graph
+
+
+@pytest.mark.parametrize("cta", [None, "single", "pair"])
+def test_gated_nvfp4_output_equals_quantised_fp16_output(pkg, cta):
+    """The gated segment launch writing NVFP4 codes and blocked scales is bit-identical to
+    the fp16 launch followed by the activation quantiser (over the real rows)."""
+    counts, n, k = [0, 1, 127, 300, 129, 64], 256, 1024
+    P = _slab_problem(pkg, counts, n, k, True, seed=31, tail=0)
+    cap = P["cap"]
+    so = torch.tensor(P["offs"], dtype=torch.int32, device="cuda")
+    sc = torch.tensor(counts, dtype=torch.int32, device="cuda")
+    h = torch.zeros((cap, n), dtype=torch.float16, device="cuda")
+    kw = dict(alpha=P["alpha"], b2=P["b2"], sfb2=P["sfb2"], alpha2=P["alpha2"], cta=cta)
+    pkg.grouped_gemm_segments(P["a"], P["sfa"], h, P["b"], P["sfb"], so, sc, **kw)
+    s_h = pkg.global_scale_for(h)
+    ref_codes, ref_sf = pkg.quantize(h, s_h)
+    codes = torch.full((cap, n // 2), 0x5A, dtype=torch.uint8, device="cuda")
+    sf = torch.full((pkg.blocked_sf_bytes(cap, n // 16),), 0x5A, dtype=torch.uint8, device="cuda")
+    pkg.grouped_gemm_segments(P["a"], P["sfa"], codes, P["b"], P["sfb"], so, sc, out_sf=sf,
+                              out_scale=s_h, **kw)
+    torch.cuda.synchronize()
+    assert pkg.check_device_errors() == 0
+    plain = pkg.blocked_to_plain(sf, cap, n // 16)
+    ref_plain = pkg.blocked_to_plain(ref_sf, cap, n // 16)
+    for e, (off, cnt) in enumerate(zip(P["offs"], counts)):
+        assert torch.equal(codes[off:off + cnt], ref_codes[off:off + cnt]), f"codes of segment {e}"
+        assert torch.equal(plain[off:off + cnt], ref_plain[off:off + cnt]), f"scales of segment {e}"
+    with pytest.raises(ValueError):  # non-gated launches have no NVFP4 output
+        pkg.grouped_gemm_segments(P["a"], P["sfa"], codes, P["b"], P["sfb"], so, sc, out_sf=sf,
+                                  out_scale=s_h)
