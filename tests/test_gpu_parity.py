@@ -236,6 +236,51 @@ def test_prepared_plan_runs_repeatedly(pkg, cta):
     assert plan.check_device_errors() == 0
 
 
+@pytest.mark.parametrize("cta", [None, "single", "pair"])
+def test_cuda_graph_capture_of_plan_and_custom_kernel(pkg, cta):
+    """The host path records into a CUDA graph: a prepared plan's runs and custom_kernel
+    (after one eager call on the capturing stream, which allocates its workspace and uploads
+    the descriptors). Replays after new input contents give the oracle's results."""
+    shapes = ([5, 0, 130, 64], 384, 512)
+    prob = pkg.workloads.make_problem("graph", shapes[0], shapes[1], shapes[2], seed=41,
+                                      device="cuda", alpha_range=(0.5, 2.0))
+    sizes = prob.problem_sizes()
+    plan = pkg.GroupedGemmPlan(prob.a, prob.b, prob.sfa, prob.sfb, prob.c, sizes,
+                               alpha=prob.alpha, cta=cta)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    data = prob.reference_data()
+    scales = prob.global_scales()
+    with torch.cuda.stream(side):
+        plan.run(side)
+        pkg.custom_kernel(data, global_scales=scales, cta=cta, stream=side)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graphs = {}
+    for name, fn in (("plan", lambda: plan.run(side)),
+                     ("custom_kernel", lambda: pkg.custom_kernel(data, global_scales=scales,
+                                                                 cta=cta, stream=side))):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            fn()
+            fn()  # two launches back to back in one graph
+        graphs[name] = g
+    for seed, name in ((42, "plan"), (43, "custom_kernel")):
+        other = pkg.workloads.make_problem("graph2", shapes[0], shapes[1], shapes[2], seed=seed,
+                                           device="cuda", alpha_range=(0.5, 2.0))
+        for dst, src in zip(prob.a + prob.b + prob.sfa + prob.sfb,
+                            other.a + other.b + other.sfa + other.sfb):
+            dst.copy_(src)
+        prob.sfa_plain, prob.sfb_plain = other.sfa_plain, other.sfb_plain
+        for c in prob.c:
+            c.fill_(float("nan"))
+        graphs[name].replay()
+        torch.cuda.synchronize()
+        check_problem(prob)
+    assert plan.check_device_errors() == 0
+    graphs.clear()
+
+
 def test_descriptor_reuse_and_rebuild(pkg):
     p1 = pkg.workloads.make_problem("r1", [128, 200], 256, 512, seed=21, device="cuda")
     run_custom_kernel(pkg, p1)
