@@ -253,6 +253,52 @@ NVFP4_API int nvfp4_moe_combine(const void* y, int64_t ldy, const int32_t* dest,
                                 int64_t ldo, void* stream);
 
 /*
+ * Expert-parallel MoE exchange over NVLink peer memory: one process per GPU, `world` ranks
+ * (<= NVFP4_EP_MAX_RANKS), rank p owning experts [p * E / world, (p + 1) * E / world).
+ * A nvfp4_ep_peers table holds, for every rank i < world, this process's device address of
+ * rank i's copy of one symmetric buffer (the same allocation size on every rank, mapped
+ * peer-to-peer, e.g. torch symmetric memory or CUDA IPC). The kernels only load and store;
+ * the caller orders the steps across ranks with a barrier on the same stream (a one-element
+ * NCCL all-reduce) where marked (|). Per MoE layer:
+ *
+ *   nvfp4_moe_route over all E experts (local pairs), nvfp4_quantize of the local tokens
+ *   nvfp4_ep_publish_counts: route counts -> row `rank` of every rank's [world, E] matrix  |
+ *   nvfp4_ep_layout: from this rank's copy of the matrix, this rank's expert segments in its
+ *     receive slab (rows of rank 0 first, then rank 1, ...; each expert 128-row aligned) and,
+ *     per expert, the first row of this rank's pairs in the owner's slab (send_base)
+ *   nvfp4_ep_dispatch: each routed token row (codes, and its scales as a plain row of cols/16
+ *     bytes) into the owner's receive slabs; remote_rows[pair] = its row there               |
+ *   owner: nvfp4_sf_to_blocked on the received scales, the expert GEMMs over its segments
+ *     (nvfp4_grouped_gemm_segments) into its y slab [recv_capacity, cols] fp16                |
+ *   nvfp4_ep_combine: out[t] = bf16(sum_j w[t, j] * y_owner[remote_rows[t, j]]) (fp32, slot
+ *     order: bit-identical to nvfp4_moe_combine over the same rows)
+ *
+ * A segment that does not fit the owner's receive slab is dropped on every rank (its pairs
+ * get remote_rows -1) and bit 0x1 is set in the layout's error word. No counterpart in the
+ * reference (single GPU).
+ */
+#define NVFP4_EP_MAX_RANKS 8
+typedef struct nvfp4_ep_peers {
+  void* ptr[NVFP4_EP_MAX_RANKS];
+} nvfp4_ep_peers;
+
+NVFP4_API int nvfp4_ep_publish_counts(const int32_t* counts, int num_experts, int rank, int world,
+                                      nvfp4_ep_peers count_mats, void* stream);
+NVFP4_API int nvfp4_ep_layout(const int32_t* count_mat, int num_experts, int rank, int world,
+                              int64_t recv_capacity, int32_t* seg_offsets, int32_t* seg_counts,
+                              int32_t* send_base, unsigned int* error_word, void* stream);
+NVFP4_API int nvfp4_ep_dispatch(const int32_t* topk_ids, int tokens, int topk, int num_experts,
+                                int rank, int world, const int32_t* dest, const int32_t* offsets,
+                                const int32_t* send_base, const void* codes, int64_t ld_codes,
+                                const void* sf_blocked, int cols, nvfp4_ep_peers recv_codes,
+                                nvfp4_ep_peers recv_sf, int64_t recv_capacity,
+                                int32_t* remote_rows, void* stream);
+NVFP4_API int nvfp4_ep_combine(const int32_t* topk_ids, const int32_t* remote_rows,
+                               const float* weights, int tokens, int topk, int num_experts,
+                               int world, nvfp4_ep_peers ys, int cols, void* out, int64_t ldo,
+                               void* stream);
+
+/*
  * Synchronise `stream`, then read and clear the device error word of `workspace`.
  * Returns NVFP4_ERR_DEVICE_TIMEOUT if a kernel using it gave up on a wait, else
  * NVFP4_ERR_BAD_SHAPE if a segment launch skipped an out-of-range segment (bit 0x20); the

@@ -64,7 +64,29 @@ EXPORTED_SYMBOLS = (
     "nvfp4_moe_route",
     "nvfp4_moe_combine",
     "nvfp4_moe_gather_quantized",
+    "nvfp4_ep_publish_counts",
+    "nvfp4_ep_layout",
+    "nvfp4_ep_dispatch",
+    "nvfp4_ep_combine",
 )
+
+EP_MAX_RANKS = 8  # NVFP4_EP_MAX_RANKS
+EP_ERR_CAPACITY = 1 << 0  # an expert segment did not fit the owner's receive slab
+
+
+class EpPeers(ctypes.Structure):
+    """nvfp4_ep_peers: one device address per rank (passed by value)."""
+
+    _fields_ = [("ptr", ctypes.c_void_p * EP_MAX_RANKS)]
+
+    @classmethod
+    def of(cls, addresses) -> "EpPeers":
+        if len(addresses) > EP_MAX_RANKS:
+            raise ValueError(f"at most {EP_MAX_RANKS} ranks")
+        p = cls()
+        for i, a in enumerate(addresses):
+            p.ptr[i] = int(a)
+        return p
 
 # Row-map modes of nvfp4_quantize_rows (NVFP4_ROWS_*).
 ROWS_GATHER = 1
@@ -182,6 +204,16 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_moe_combine.restype = i32
         lib.nvfp4_moe_gather_quantized.argtypes = [vp, i64, vp, vp, i32, i32, vp, i64, vp, vp]
         lib.nvfp4_moe_gather_quantized.restype = i32
+        lib.nvfp4_ep_publish_counts.argtypes = [vp, i32, i32, i32, EpPeers, vp]
+        lib.nvfp4_ep_publish_counts.restype = i32
+        lib.nvfp4_ep_layout.argtypes = [vp, i32, i32, i32, i64, vp, vp, vp, vp, vp]
+        lib.nvfp4_ep_layout.restype = i32
+        lib.nvfp4_ep_dispatch.argtypes = [vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, i64, vp,
+                                          i32, EpPeers, EpPeers, i64, vp, vp]
+        lib.nvfp4_ep_dispatch.restype = i32
+        lib.nvfp4_ep_combine.argtypes = [vp, vp, vp, i32, i32, i32, i32, EpPeers, i32, vp, i64,
+                                         vp]
+        lib.nvfp4_ep_combine.restype = i32
         if path is None:
             _lib = lib
         return lib

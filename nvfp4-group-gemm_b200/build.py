@@ -16,7 +16,7 @@ LIB_NAME = "libnvfp4_group_gemm.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
 SOURCES = ["nvfp4_group_gemm.cu"]
 HEADERS = ["grouped_gemm_kernel.cuh", "grouped_gemm_pair_kernel.cuh", "grouped_gemm_swap_kernel.cuh",
-           "quantize_kernel.cuh", "moe_kernels.cuh", "nvfp4_quant_math.cuh",
+           "quantize_kernel.cuh", "moe_kernels.cuh", "nvfp4_quant_math.cuh", "ep_kernels.cuh",
            "nvfp4_types.cuh", "sm100_ptx.cuh"]
 PUBLIC_HEADER = os.path.join(os.path.dirname(HERE), "include", "nvfp4_group_gemm.h")
 

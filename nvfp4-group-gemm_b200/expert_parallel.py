@@ -110,3 +110,204 @@ class ExpertParallelGroupedGemm:
         if not gather or self.world == 1:
             return outs
         return all_gather_expert_outputs(outs, rows_per_expert, local_problem.n, self.group)
+
+
+class EPMoEBlock:
+    """Expert-parallel MoE feed-forward block: one process per GPU, every rank holding
+    ``tokens`` tokens and the weights of its own experts (rank p: experts [p*E/P,
+    (p+1)*E/P)), exchanging NVFP4 token rows and fp16 expert outputs over NVLink peer
+    memory (nvfp4_ep_* kernels) with no device-to-host read.
+
+    Per call (one stream; barriers are one-element NCCL all-reduces):
+    route + quantise the local tokens; publish per-expert counts into every rank's count
+    matrix | layout (all ranks derive the same placement); dispatch codes + scale rows into
+    the owners' receive slabs | owner: scales to the blocked layout, gated GEMM over its
+    expert segments with NVFP4 output, down GEMM into its y slab | combine: pull each pair's
+    row from its owner's y slab, weighted fp32 sum in slot order, bf16.
+
+    The receive slabs hold ``world * tokens * topk + 127 * E/P`` rows (every pair of every
+    rank routed here, plus segment padding), so the exchange never drops a pair. Receive
+    slabs, count matrix and y slab live in one torch symmetric-memory allocation.
+    """
+
+    def __init__(self, local_weights, num_experts: int, tokens: int, topk: int,
+                 act_scale: float, hidden_scale: float, group=None, cta: str | None = None):
+        import numpy as np
+        from torch.distributed import _symmetric_memory as symm
+
+        from . import _native
+        from .layout import blocked_sf_bytes
+
+        if cta not in (None, "pair", "single"):
+            raise ValueError(f"cta must be None, 'pair' or 'single', got {cta!r}")
+        self.group = group if group is not None else dist.group.WORLD
+        world = dist.get_world_size(self.group)
+        rank = dist.get_rank(self.group)
+        if world > _native.EP_MAX_RANKS:
+            raise ValueError(f"at most {_native.EP_MAX_RANKS} ranks")
+        if num_experts % world:
+            raise ValueError(f"{num_experts} experts do not split evenly over {world} ranks")
+        epr = num_experts // world
+        if local_weights.num_experts != epr:
+            raise ValueError(f"rank {rank} must hold {epr} experts, got {local_weights.num_experts}")
+        if not (act_scale > 0 and hidden_scale > 0):
+            raise ValueError("act_scale and hidden_scale must be positive")
+        dev = local_weights.w_gate[0].device
+        idim = int(local_weights.w_gate[0].shape[0])
+        hdim = int(local_weights.w_gate[0].shape[1]) * 2
+        if hdim % 256 or idim % 256:
+            raise ValueError("hidden and intermediate sizes must be multiples of 256")
+        self.world, self.rank, self.num_experts, self.experts_per_rank = world, rank, num_experts, epr
+        self.tokens, self.topk, self.hidden, self.intermediate = tokens, topk, hdim, idim
+        self.act_scale, self.hidden_scale = float(act_scale), float(hidden_scale)
+        self.device = dev
+        self._cta_flags = {None: 0, "pair": _native.FLAG_CTA_PAIR,
+                           "single": _native.FLAG_SINGLE_CTA}[cta]
+        self._lib = lib = _native.load_library()
+        pairs = tokens * topk
+        cap = world * pairs + 127 * epr
+        self.capacity = cap
+
+        # One symmetric allocation: count matrix | received codes | received plain scales | y.
+        def up(n):
+            return (n + 255) // 256 * 256
+        sizes = [world * num_experts * 4, cap * hdim // 2, cap * hdim // 16, cap * hdim * 2]
+        offs = [0]
+        for n in sizes[:-1]:
+            offs.append(offs[-1] + up(n))
+        total = offs[-1] + up(sizes[-1])
+        self._symm = symm.empty(total, dtype=torch.uint8, device=dev)
+        self._symm.zero_()
+        try:
+            self._handle = symm.rendezvous(self._symm, self.group)
+        except RuntimeError:  # older releases want the group registered first
+            symm.enable_symm_mem_for_group(self.group.group_name)
+            self._handle = symm.rendezvous(self._symm, self.group)
+        bases = [int(b) for b in self._handle.buffer_ptrs]
+        # The tensor sits at the same offset inside every rank's copy of the allocation.
+        delta = self._symm.data_ptr() - bases[rank]
+        self._peers = [_native.EpPeers.of([b + delta + o for b in bases]) for o in offs]
+        sl = [self._symm[o:o + n] for o, n in zip(offs, sizes)]
+        self._mat = sl[0].view(torch.int32).view(world, num_experts)
+        self._recv_codes = sl[1].view(cap, hdim // 2)
+        self._recv_sf = sl[2].view(cap, hdim // 16)
+        self._y = sl[3].view(torch.float16).view(cap, hdim)
+
+        i32 = dict(dtype=torch.int32, device=dev)
+        u8 = dict(dtype=torch.uint8, device=dev)
+        self._meta = torch.zeros(2 * num_experts + 1, **i32)
+        self._counts, self._offsets = self._meta[:num_experts], self._meta[num_experts:]
+        self._dest = torch.empty(pairs, **i32)
+        self._src_rows = torch.empty(pairs + 127 * num_experts, **i32)
+        self._route_ws_bytes = int(lib.nvfp4_moe_route_workspace_size(pairs, num_experts))
+        self._route_ws = torch.empty(max(self._route_ws_bytes, 16), **u8)
+        self._qx = torch.empty((tokens, hdim // 2), **u8)
+        self._sfx = torch.empty(blocked_sf_bytes(tokens, hdim // 16), **u8)
+        self.seg_offsets = torch.zeros(epr, **i32)
+        self.seg_counts = torch.zeros(epr, **i32)
+        self.send_base = torch.zeros(num_experts, **i32)
+        self.remote_rows = torch.empty(pairs, **i32)
+        self._err = torch.zeros(1, **i32)
+        self._recv_sfa = torch.zeros(blocked_sf_bytes(cap, hdim // 16), **u8)
+        self._a2 = torch.zeros((cap, idim // 2), **u8)
+        self._sfa2 = torch.zeros(blocked_sf_bytes(cap, idim // 16), **u8)
+        self._w = torch.empty((tokens, topk), dtype=torch.float32, device=dev)
+        self.out = torch.empty((tokens, hdim), dtype=torch.bfloat16, device=dev)
+        self._bar = torch.zeros(1, dtype=torch.int32, device=dev)
+
+        W = local_weights
+        P = W.pointers()
+        s_x, s_h = self.act_scale, self.hidden_scale
+
+        def slab_table(a, sfa, c, b, sfb, n, k, alpha, b2=None, sfb2=None, alpha2=None):
+            t = np.zeros(epr, dtype=_native.GROUP_DTYPE)
+            t["a"], t["sfa"], t["c"] = a.data_ptr(), sfa.data_ptr(), c.data_ptr()
+            t["b"], t["sfb"] = b, sfb
+            if b2 is not None:
+                t["b2"], t["sfb2"], t["alpha2"] = b2, sfb2, alpha2
+            else:
+                t["alpha2"] = 1.0
+            t["m"], t["n"], t["k"], t["alpha"] = cap, n, k, alpha
+            return t
+
+        self._weights = W  # the tables hold its addresses
+        self._t1 = slab_table(self._recv_codes, self._recv_sfa, self._a2, P["w_gate"], P["sf_gate"],
+                              idim, hdim, s_x * np.asarray(W.s_gate, dtype=np.float32),
+                              P["w_up"], P["sf_up"], s_x * np.asarray(W.s_up, dtype=np.float32))
+        self._t2 = slab_table(self._a2, self._sfa2, self._y, P["w_down"], P["sf_down"], hdim, idim,
+                              s_h * np.asarray(W.s_down, dtype=np.float32))
+        ws_bytes = _native.workspace_size(epr)
+        self._ws1 = torch.zeros(ws_bytes, **u8)
+        self._ws2 = torch.zeros(ws_bytes, **u8)
+        self._ws_bytes = ws_bytes
+        self._uploaded = False
+        dist.barrier(group=self.group)
+
+    def _barrier(self):
+        dist.all_reduce(self._bar, group=self.group)
+
+    def run(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor) -> torch.Tensor:
+        """One expert-parallel block on the current stream; returns ``self.out`` (bf16
+        [tokens, H]) for this rank's tokens. Every rank of the group must call it."""
+        from . import _native
+        from .quantize import _DTYPES
+
+        T, K, H, E, world, rank = (self.tokens, self.topk, self.hidden, self.num_experts,
+                                   self.world, self.rank)
+        if x.dtype not in _DTYPES or tuple(x.shape) != (T, H) or x.stride(1) != 1:
+            raise ValueError(f"x must be bf16/fp16 [{T}, {H}]")
+        if topk_ids.dtype != torch.int32 or tuple(topk_ids.shape) != (T, K) or \
+                not topk_ids.is_contiguous():
+            raise ValueError(f"topk_ids must be contiguous int32 [{T}, {K}]")
+        lib, chk = self._lib, _native.check
+        st = torch.cuda.current_stream(self.device)
+        s = st.cuda_stream
+        cap = self.capacity
+        chk(lib.nvfp4_moe_route(topk_ids.data_ptr(), T, K, E, self._counts.data_ptr(),
+                                self._offsets.data_ptr(), self._dest.data_ptr(),
+                                self._src_rows.data_ptr(), self._src_rows.numel(),
+                                self._route_ws.data_ptr(), self._route_ws_bytes, s), lib)
+        chk(lib.nvfp4_quantize(x.data_ptr(), T, H, x.stride(0), _DTYPES[x.dtype], self.act_scale,
+                               self._qx.data_ptr(), self._qx.stride(0), self._sfx.data_ptr(), s), lib)
+        chk(lib.nvfp4_ep_publish_counts(self._counts.data_ptr(), E, rank, world, self._peers[0], s),
+            lib)
+        self._barrier()
+        chk(lib.nvfp4_ep_layout(self._mat.data_ptr(), E, rank, world, cap,
+                                self.seg_offsets.data_ptr(), self.seg_counts.data_ptr(),
+                                self.send_base.data_ptr(), self._err.data_ptr(), s), lib)
+        chk(lib.nvfp4_ep_dispatch(topk_ids.data_ptr(), T, K, E, rank, world, self._dest.data_ptr(),
+                                  self._offsets.data_ptr(), self.send_base.data_ptr(),
+                                  self._qx.data_ptr(), self._qx.stride(0), self._sfx.data_ptr(), H,
+                                  self._peers[1], self._peers[2], cap,
+                                  self.remote_rows.data_ptr(), s), lib)
+        self._barrier()
+        _native.sf_to_blocked_raw(self._recv_sf.data_ptr(), self._recv_sfa.data_ptr(), cap,
+                                  H // 16, H // 16, s)
+        flags = (_native.FLAG_REUSE_DESCRIPTORS if self._uploaded else 0) | self._cta_flags
+        _native.grouped_gemm_segments_raw(self._t1, _native.FLAG_GATED | flags,
+                                          self.seg_offsets.data_ptr(), self.seg_counts.data_ptr(),
+                                          T * K, self._ws1.data_ptr(), self._ws_bytes, s,
+                                          self._sfa2.data_ptr(), self.hidden_scale)
+        _native.grouped_gemm_segments_raw(self._t2, flags, self.seg_offsets.data_ptr(),
+                                          self.seg_counts.data_ptr(), T * K,
+                                          self._ws2.data_ptr(), self._ws_bytes, s)
+        self._uploaded = True
+        self._barrier()
+        w = topk_weights
+        if w.dtype != torch.float32 or not w.is_contiguous():
+            self._w.copy_(w)
+            w = self._w
+        chk(lib.nvfp4_ep_combine(topk_ids.data_ptr(), self.remote_rows.data_ptr(), w.data_ptr(), T,
+                                 K, E, world, self._peers[3], H, self.out.data_ptr(),
+                                 self.out.stride(0), s), lib)
+        return self.out
+
+    def check_errors(self) -> int:
+        """Synchronise; returns the exchange's error bits (EP_ERR_CAPACITY) and raises if a
+        GEMM reported a device error."""
+        from . import _native
+
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        _native.workspace_check(self._ws1.data_ptr(), s)
+        _native.workspace_check(self._ws2.data_ptr(), s)
+        return int(self._err.item())

@@ -272,7 +272,12 @@ class MoEBlock:
     """
 
     def __init__(self, weights: ExpertWeights, tokens: int, topk: int, act_scale: float,
-                 hidden_scale: float, device: torch.device | None = None):
+                 hidden_scale: float, device: torch.device | None = None,
+                 cta: str | None = None):
+        if cta not in (None, "pair", "single"):
+            raise ValueError(f"cta must be None, 'pair' or 'single', got {cta!r}")
+        self._cta_flags = {None: 0, "pair": _native.FLAG_CTA_PAIR,
+                           "single": _native.FLAG_SINGLE_CTA}[cta]
         if not (act_scale > 0 and hidden_scale > 0):
             raise ValueError("act_scale and hidden_scale must be positive")
         dev = torch.device(device) if device is not None else weights.w_gate[0].device
@@ -372,12 +377,12 @@ class MoEBlock:
                                                self._sfx.data_ptr(), self.src_rows.data_ptr(), cap,
                                                H, self._a.data_ptr(), self._a.stride(0),
                                                self._sfa.data_ptr(), s), lib)
-            reuse = _native.FLAG_REUSE_DESCRIPTORS if self._uploaded else 0
-            _native.grouped_gemm_segments_raw(self._t1, _native.FLAG_GATED | reuse,
+            flags = (_native.FLAG_REUSE_DESCRIPTORS if self._uploaded else 0) | self._cta_flags
+            _native.grouped_gemm_segments_raw(self._t1, _native.FLAG_GATED | flags,
                                               self.offsets.data_ptr(), self.counts.data_ptr(),
                                               T * K, self._ws1.data_ptr(), self._ws_bytes, s,
                                               self._sfa2.data_ptr(), self.hidden_scale)
-            _native.grouped_gemm_segments_raw(self._t2, reuse, self.offsets.data_ptr(),
+            _native.grouped_gemm_segments_raw(self._t2, flags, self.offsets.data_ptr(),
                                               self.counts.data_ptr(), T * K,
                                               self._ws2.data_ptr(), self._ws_bytes, s)
             self._uploaded = True

@@ -106,3 +106,114 @@ def test_shard_bookkeeping(pkg):
     assert lay == [(0, 2, 32), (2, 2, 64)]
     with pytest.raises(ValueError):
         EP.expert_shard(4, 2, 2)
+
+
+# ----------------------------------------------------------------------------
+# The expert-parallel MoE exchange: placement rule of nvfp4_ep_layout / nvfp4_ep_dispatch
+# ----------------------------------------------------------------------------
+def _ids(tokens, topk, experts, seed):
+    rng = np.random.default_rng(seed)
+    p = 1.0 / np.arange(1, experts + 1) ** 1.2
+    p /= p.sum()
+    ids = np.stack([rng.choice(experts, size=topk, replace=False, p=p) for _ in range(tokens)])
+    ids[rng.random(ids.shape) < 0.03] = -1
+    return ids.astype(np.int32)
+
+
+@pytest.mark.parametrize("world,experts,tokens,topk", [(2, 16, 300, 4), (4, 64, 129, 8),
+                                                       (8, 256, 64, 8), (3, 12, 1, 2)])
+def test_ep_layout_matches_pairwise_placement(world, experts, tokens, topk):
+    """The closed-form layout (segment starts + earlier ranks' counts) puts every pair where a
+    pair-by-pair walk puts it; segments are 128-aligned, disjoint and exactly filled."""
+    from oracle import nvfp4_ep_oracle as EPO
+
+    ids = [_ids(tokens, topk, experts, seed=world * 100 + q) for q in range(world)]
+    cap = world * tokens * topk + 127 * (experts // world)
+    counts, remote, received = EPO.place_pairs(ids, experts, world, cap)
+    from oracle import nvfp4_moe_oracle as M
+
+    for q in range(world):
+        seg_off, seg_cnt, send_base, dropped = EPO.ep_layout(counts, world, q, cap)
+        assert not dropped
+        assert np.all(seg_off % 128 == 0)
+        _, offsets, dest, _ = M.route(ids[q], experts)
+        flat = ids[q].reshape(-1)
+        for i, e in enumerate(flat):
+            if dest[i] < 0:
+                assert remote[q][i] == -1
+                continue
+            assert remote[q][i] == send_base[e] + dest[i] - offsets[e]
+        # As owner: the received rows are exactly the segments' first seg_cnt rows.
+        rows = sorted(received[q])
+        want = sorted(r for o, c in zip(seg_off, seg_cnt) for r in range(o, o + c))
+        assert rows == want
+
+
+def test_ep_layout_drops_segments_that_do_not_fit():
+    from oracle import nvfp4_ep_oracle as EPO
+
+    world, experts = 2, 8
+    mat = np.array([[100, 0, 50, 200, 0, 1, 3, 7], [30, 5, 0, 100, 9, 0, 0, 1]])
+    seg_off, seg_cnt, send_base, dropped = EPO.ep_layout(mat, world, 0, capacity=400)
+    # owner 0: experts 0..3 with totals 130, 5, 50, 300 -> starts 0, 256, 384, 512
+    assert dropped
+    assert list(seg_off[:3]) == [0, 256, 0] and list(seg_cnt) == [130, 5, 0, 0]
+    assert send_base[0] == 0 and send_base[1] == 256 and send_base[2] == -1 and send_base[3] == -1
+
+
+def _ep_gloo_worker(rank, world, port, experts, tokens, topk, q):
+    try:
+        import sys
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, root)
+        from oracle import nvfp4_ep_oracle as EPO
+        from oracle import nvfp4_moe_oracle as M
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=__import__("datetime").timedelta(seconds=60))
+        ids = _ids(tokens, topk, experts, seed=rank + 7)
+        counts = torch.from_numpy(M.route(ids, experts)[0].astype(np.int32))
+        # The count matrix every rank assembles (the device path writes it with peer stores).
+        mat = [torch.zeros_like(counts) for _ in range(world)]
+        dist.all_gather(mat, counts)
+        mat = torch.stack(mat).numpy()
+        cap = world * tokens * topk + 127 * (experts // world)
+        seg_off, seg_cnt, send_base, _ = EPO.ep_layout(mat, world, rank, cap)
+        _, offsets, dest, _ = M.route(ids, experts)
+        flat = ids.reshape(-1)
+        rows = [(int(e) // (experts // world), int(send_base[e] + dest[i] - offsets[e]))
+                for i, e in enumerate(flat) if dest[i] >= 0]
+        everything = [None] * world
+        dist.all_gather_object(everything, (rows, seg_off.tolist(), seg_cnt.tolist()))
+        q.put((rank, everything))
+        dist.destroy_process_group()
+    except BaseException as e:
+        q.put((rank, repr(e)))
+
+
+def test_ep_placement_over_gloo_ranks():
+    """Two CPU ranks exchange their routing counts over gloo and place their pairs: the
+    rows written into each owner's slab are distinct and fill its segments exactly."""
+    world, experts, tokens, topk = 2, 16, 200, 4
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_gloo_worker, args=(r, world, port, experts, tokens, topk, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    everything = res[0]
+    assert isinstance(everything, list), everything
+    for owner in range(world):
+        written = [r for rows, _, _ in everything for (o, r) in rows if o == owner]
+        assert len(written) == len(set(written))
+        _, seg_off, seg_cnt = everything[owner]
+        want = sorted(r for o, c in zip(seg_off, seg_cnt) for r in range(o, o + c))
+        assert sorted(written) == want

@@ -1,0 +1,135 @@
+"""Expert-parallel MoE block on 2 GPUs (EPMoEBlock: routed NVFP4 rows pushed into the owners'
+receive slabs over NVLink, expert GEMMs over device-side segments, results pulled back and
+combined). Skipped with fewer than 2 GPUs.
+
+Each rank checks, for its own tokens: the placement (count matrix, segments, every pair's
+row in its owner's slab) against the CPU oracle of the exchange, and the block's output
+bit for bit against the single-GPU MoEBlock run over the same tokens with all experts (the
+same rows meet the same weights in both; tiles forced to single CTAs so both pick the same
+kernels). Two calls with different tokens and routings check the buffers' reuse.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+E, H, I, T, TOPK = 16, 512, 256, 300, 4
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs(seed, dev):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn((T, H), generator=g).to(torch.bfloat16)
+    scores = torch.rand((T, E), generator=g) ** 3
+    top = torch.topk(scores, TOPK, dim=1)
+    ids = top.indices.to(torch.int32)
+    ids[::37, 1] = -1  # a few dropped pairs
+    wts = torch.softmax(top.values, dim=1)
+    return x.to(dev), ids.to(dev), wts.to(dev)
+
+
+def _worker(rank, world, port, cta, q):
+    try:
+        import sys
+
+        import torch.distributed as dist
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, root)
+        import submission
+        from oracle import nvfp4_ep_oracle as EPO
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+        pkg = submission.load_package()
+        g = torch.Generator().manual_seed(5)
+        gate = [(torch.randn((I, H), generator=g) * 0.05).to(torch.bfloat16).to(dev) for _ in range(E)]
+        up = [(torch.randn((I, H), generator=g) * 0.05).to(torch.bfloat16).to(dev) for _ in range(E)]
+        down = [(torch.randn((H, I), generator=g) * 0.05).to(torch.bfloat16).to(dev) for _ in range(E)]
+        W = pkg.moe.quantize_expert_weights(gate, up, down)
+        epr = E // world
+        sl = slice(rank * epr, (rank + 1) * epr)
+        local = pkg.moe.ExpertWeights(**{f: getattr(W, f)[sl] for f in (
+            "w_gate", "sf_gate", "w_up", "sf_up", "w_down", "sf_down", "s_gate", "s_up", "s_down")})
+        s_x, s_h = 0.004, 0.002
+        ep = pkg.expert_parallel.EPMoEBlock(local, E, T, TOPK, s_x, s_h, cta=cta)
+        ref_blk = pkg.moe.MoEBlock(W, T, TOPK, s_x, s_h, cta=cta)
+        checks = []
+        for call in range(2):
+            x, ids, wts = _inputs(1000 * call + rank, dev)
+            out = ep.run(x, ids, wts).clone()
+            torch.cuda.synchronize()
+            err = ep.check_errors()
+            ref = ref_blk.run(x, ids, wts)
+            torch.cuda.synchronize()
+            # Placement against the oracle (every rank's routing is rebuilt here from seeds).
+            all_ids = [_inputs(1000 * call + r, "cpu")[1].numpy() for r in range(world)]
+            counts, remote, _ = EPO.place_pairs(all_ids, E, world, ep.capacity)
+            seg_off, seg_cnt, send_base, dropped = EPO.ep_layout(counts, world, rank, ep.capacity)
+            checks.append(dict(
+                err=err, dropped=dropped,
+                mat=np.array_equal(ep._mat.cpu().numpy(), counts),
+                seg=np.array_equal(ep.seg_offsets.cpu().numpy(), seg_off) and
+                np.array_equal(ep.seg_counts.cpu().numpy(), seg_cnt),
+                send=np.array_equal(ep.send_base.cpu().numpy(), send_base),
+                rows=np.array_equal(ep.remote_rows.cpu().numpy(), remote[rank]),
+                out_equal=bool(torch.equal(out.view(torch.int16), ref.view(torch.int16))),
+                rel=float((out.float() - ref.float()).norm() / ref.float().norm()),
+                finite=bool(torch.isfinite(out.float()).all())))
+        q.put((rank, checks))
+        dist.barrier(device_ids=[rank])
+        del ep
+        dist.destroy_process_group()
+    except BaseException as e:  # report instead of hanging the parent
+        import traceback
+
+        q.put((rank, traceback.format_exc()[-2000:] + repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("cta", ["single", None])
+def test_ep_moe_block_two_gpus(cta):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cta, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        rank, res = q.get(timeout=600)
+        results[rank] = res
+    for p in procs:
+        p.join(timeout=60)
+    for rank in range(world):
+        res = results[rank]
+        assert isinstance(res, list), res
+        for call, c in enumerate(res):
+            assert c["err"] == 0 and not c["dropped"], (rank, call, c)
+            assert c["mat"] and c["seg"] and c["send"] and c["rows"], (rank, call, c)
+            assert c["finite"], (rank, call, c)
+            if cta == "single":
+                assert c["out_equal"], (rank, call, c)
+            else:
+                assert c["rel"] < 1e-2, (rank, call, c)
+    for p in procs:
+        assert p.exitcode == 0
