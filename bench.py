@@ -311,13 +311,121 @@ def run_quantize(args):
     print(json.dumps(line), flush=True)
 
 
+def run_moe_ep(args, world):
+    """The expert-parallel MoE block (EPMoEBlock) at cfg5's shape over `world` GPUs: the
+    32768 tokens split evenly over the ranks, the 256 experts too (strong scaling of one
+    batch); routed rows cross NVLink in NVFP4 and results come back to their tokens' rank."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import submission
+
+    pkg = submission.load_package()
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    E, topk, H, I = 256, 8, 7168, 2048
+    T = args.tokens // world
+    epr = E // world
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+
+    def nvfp4_weights(rows, cols):
+        codes = torch.randint(0, 256, (rows, cols // 2), generator=g, device=dev,
+                              dtype=torch.int32).to(torch.uint8) & 0xBB
+        sf_plain = torch.where(torch.rand((rows, cols // 16), generator=g, device=dev) < 0.5,
+                               torch.tensor(0x38, dtype=torch.uint8, device=dev),
+                               torch.tensor(0x40, dtype=torch.uint8, device=dev))
+        return codes, pkg.plain_to_blocked(sf_plain)
+
+    W = {k: [] for k in ("w_gate", "sf_gate", "w_up", "sf_up", "w_down", "sf_down")}
+    for _ in range(epr):
+        for name, (r, c) in (("gate", (I, H)), ("up", (I, H)), ("down", (H, I))):
+            q, sf = nvfp4_weights(r, c)
+            W[f"w_{name}"].append(q)
+            W[f"sf_{name}"].append(sf)
+    weights = pkg.moe.ExpertWeights(**W, s_gate=[2.0 ** -6] * epr, s_up=[2.0 ** -6] * epr,
+                                    s_down=[2.0 ** -6] * epr)
+    x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
+    scores = torch.rand((T, E), generator=g, device=dev)
+    top = torch.topk(scores, topk, dim=1)
+    ids = top.indices.to(torch.int32)
+    wts = torch.softmax(top.values, dim=1)
+    s_x = pkg.global_scale_for(x)
+    s_h = 0.01  # fixed SiLU-output scale (values do not change the timing)
+    blk = pkg.expert_parallel.EPMoEBlock(weights, E, T, topk, s_x, s_h)
+    for _ in range(max(args.warmup, 3)):
+        blk.run(x, ids, wts)
+    torch.cuda.synchronize(dev)
+    dist.barrier(device_ids=[local_rank])
+    steps = max(1, min(args.steps, 10))
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        blk.run(x, ids, wts)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms_rank = e0.elapsed_time(e1) / steps
+    t = torch.tensor([ms_rank], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # One instrumented call: device time between the stages (this rank).
+    evs = []
+    blk.run(x, ids, wts, stage_events=evs)
+    torch.cuda.synchronize(dev)
+    stage_us = {n: a.elapsed_time(b) * 1e3 for (_, a), (n, b) in zip(evs[:-1], evs[1:])}
+    err = blk.check_errors()
+    pairs = torch.tensor([int((ids >= 0).sum().item())], dtype=torch.float64, device=dev)
+    dist.all_reduce(pairs)
+    flops = 6.0 * float(pairs.item()) * H * I
+    tf = flops / (ms * 1e-3) / 1e12
+    peaks, kind = load_peaks()
+    peak = world * FP4_PER_BF16 * float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+    dist.barrier(device_ids=[local_rank])
+    del blk
+    dist.destroy_process_group()
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": f"NVFP4 expert-parallel MoE block TFLOP/s (cfg5 shape: 256 experts, {args.tokens} "
+                  "tokens x top-8, H 7168, I 2048)",
+        "value": tf, "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "us_per_call": ms * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "e2m1xe4m3->f32->f16/bf16",
+        "data": "synthetic (seeded; bf16 N(0,1) tokens, uniform top-8 routing, reference-set weights)",
+        "config": {"workload": "moe-ep:cfg5", "experts": E, "tokens": args.tokens,
+                   "tokens_per_rank": T, "experts_per_rank": epr, "topk": topk, "hidden": H,
+                   "intermediate": I, "parallelism": f"ep{world} (NVFP4 rows over NVLink peer "
+                   "stores; expert output rows stored back to their tokens' ranks by the down "
+                   "GEMM's epilogue; 3 NCCL one-element barriers per call)"},
+        "api": "expert_parallel.EPMoEBlock.run",
+        "gpu_launches_per_call": "route 3, quantise 1, publish 1, layout 1, dispatch 1, "
+                                 "scale layout 1, segment set-up + GEMM x2, combine 1 (+3 NCCL)",
+        "exchange_error_bits": err,
+        "stage_us_rank0": stage_us,
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                     "frac": tf / peak, "peak_source": f"{kind}: {world} x 4 x bf16 (sustained)",
+                     "traffic": None},
+    }), flush=True)
+
+
 def run_moe(args):
     """The MoE feed-forward block at cfg5's shape (256 experts, 32768 tokens x top-8,
-    H = 7168, I = 2048), one JSON line (rank 0 of N independent replicas)."""
+    H = 7168, I = 2048), one JSON line (rank 0). With more than one rank: the
+    expert-parallel block (run_moe_ep)."""
     import numpy as np
     import torch
 
     import submission
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        return run_moe_ep(args, world)
 
     pkg = submission.load_package()
     rank = int(os.environ.get("RANK", "0"))

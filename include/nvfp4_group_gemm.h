@@ -136,16 +136,31 @@ NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsi
  * segments, are the descriptors). NVFP4_FLAG_WEIGHT_STATIONARY and NVFP4_FLAG_SPLIT_K are
  * rejected. No counterpart in the reference, whose groups are formed on the host.
  *
- * NVFP4 output (gated launches, out_sf != NULL): instead of fp16, c receives packed e2m1
- * codes [m, n/2] and out_sf the 128x4-blocked E4M3 scales of the [m, n] output slab, as
- * nvfp4_quantize(fp16 output, global_scale = out_scale) would write them (bit-identical);
- * n must be a multiple of 64. The fp16 output is never written, which saves its write and
- * the quantiser's read of it (the MoE block's down projection consumes this directly).
+ * `output` (may be NULL: fp16 rows into c) selects another output form, see below.
  */
+#define NVFP4_EP_MAX_RANKS 8
+typedef struct nvfp4_segment_output {
+  /* NVFP4 output (gated launches, sf != NULL): instead of fp16, c receives packed e2m1
+   * codes [m, n/2] and sf the 128x4-blocked E4M3 scales of the [m, n] output slab, as
+   * nvfp4_quantize(fp16 output, global_scale = scale) would write them (bit-identical); n a
+   * multiple of 64. Saves the fp16 write and the quantiser's read of it. */
+  void* sf;
+  float scale;
+  /* Scattered rows (non-gated launches, row_dest != NULL): the fp16 row of slab row r goes
+   * to dest_base[row_dest[r] >> 40] + (row_dest[r] & 0xFFFFFFFFFF) * dest_ld bytes instead
+   * of c (row_dest[r] < 0: not stored). The bases may be peer GPUs' memory (P2P stores):
+   * the expert-parallel block returns each expert output row to its token's rank this way,
+   * from the GEMM's epilogue, overlapping the transfer with the GEMM. dest_ld and the
+   * bases 16-byte aligned. */
+  const int64_t* row_dest;
+  void* dest_base[NVFP4_EP_MAX_RANKS];
+  int64_t dest_ld;
+} nvfp4_segment_output;
+
 NVFP4_API int nvfp4_grouped_gemm_segments(const nvfp4_group* groups, int num_groups,
                                           unsigned int flags, const int32_t* seg_offsets,
                                           const int32_t* seg_counts, int64_t expected_rows,
-                                          void* out_sf, float out_scale, void* workspace,
+                                          const nvfp4_segment_output* output, void* workspace,
                                           size_t workspace_bytes, void* stream);
 
 /*
@@ -267,17 +282,19 @@ NVFP4_API int nvfp4_moe_combine(const void* y, int64_t ldy, const int32_t* dest,
  *     receive slab (rows of rank 0 first, then rank 1, ...; each expert 128-row aligned) and,
  *     per expert, the first row of this rank's pairs in the owner's slab (send_base)
  *   nvfp4_ep_dispatch: each routed token row (codes, and its scales as a plain row of cols/16
- *     bytes) into the owner's receive slabs; remote_rows[pair] = its row there               |
- *   owner: nvfp4_sf_to_blocked on the received scales, the expert GEMMs over its segments
- *     (nvfp4_grouped_gemm_segments) into its y slab [recv_capacity, cols] fp16                |
- *   nvfp4_ep_combine: out[t] = bf16(sum_j w[t, j] * y_owner[remote_rows[t, j]]) (fp32, slot
- *     order: bit-identical to nvfp4_moe_combine over the same rows)
+ *     bytes) into the owner's receive slabs, with the row's return address (rank << 40 |
+ *     pair index) in the owner's recv_meta; remote_rows[pair] = its row there (-1: dropped)  |
+ *   owner: nvfp4_sf_to_blocked on the received scales, the gate/up GEMM over its segments
+ *     (nvfp4_grouped_gemm_segments, NVFP4 output), the down GEMM with scattered output
+ *     (row_dest = recv_meta, dest_base = every rank's return buffer): each output row is
+ *     stored by the GEMM's epilogue into its token's rank, [tokens * topk, cols] fp16 there  |
+ *   nvfp4_ep_combine: out[t] = bf16(sum_j w[t, j] * ret[t * topk + j]) over kept pairs
+ *     (fp32, slot order: bit-identical to nvfp4_moe_combine over the same rows)
  *
  * A segment that does not fit the owner's receive slab is dropped on every rank (its pairs
  * get remote_rows -1) and bit 0x1 is set in the layout's error word. No counterpart in the
  * reference (single GPU).
  */
-#define NVFP4_EP_MAX_RANKS 8
 typedef struct nvfp4_ep_peers {
   void* ptr[NVFP4_EP_MAX_RANKS];
 } nvfp4_ep_peers;
@@ -291,11 +308,10 @@ NVFP4_API int nvfp4_ep_dispatch(const int32_t* topk_ids, int tokens, int topk, i
                                 int rank, int world, const int32_t* dest, const int32_t* offsets,
                                 const int32_t* send_base, const void* codes, int64_t ld_codes,
                                 const void* sf_blocked, int cols, nvfp4_ep_peers recv_codes,
-                                nvfp4_ep_peers recv_sf, int64_t recv_capacity,
-                                int32_t* remote_rows, void* stream);
-NVFP4_API int nvfp4_ep_combine(const int32_t* topk_ids, const int32_t* remote_rows,
-                               const float* weights, int tokens, int topk, int num_experts,
-                               int world, nvfp4_ep_peers ys, int cols, void* out, int64_t ldo,
+                                nvfp4_ep_peers recv_sf, nvfp4_ep_peers recv_meta,
+                                int64_t recv_capacity, int32_t* remote_rows, void* stream);
+NVFP4_API int nvfp4_ep_combine(const int32_t* remote_rows, const float* weights, int tokens,
+                               int topk, const void* ret, int cols, void* out, int64_t ldo,
                                void* stream);
 
 /*

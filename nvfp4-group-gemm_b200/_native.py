@@ -74,6 +74,29 @@ EP_MAX_RANKS = 8  # NVFP4_EP_MAX_RANKS
 EP_ERR_CAPACITY = 1 << 0  # an expert segment did not fit the owner's receive slab
 
 
+class SegmentOutput(ctypes.Structure):
+    """nvfp4_segment_output: NVFP4 output (sf, scale) or scattered rows (row_dest,
+    dest_base, dest_ld) of a segment launch."""
+
+    _fields_ = [("sf", ctypes.c_void_p), ("scale", ctypes.c_float),
+                ("row_dest", ctypes.c_void_p), ("dest_base", ctypes.c_void_p * EP_MAX_RANKS),
+                ("dest_ld", ctypes.c_int64)]
+
+    @classmethod
+    def nvfp4(cls, sf_ptr: int, scale: float) -> "SegmentOutput":
+        o = cls()
+        o.sf, o.scale = int(sf_ptr), float(scale)
+        return o
+
+    @classmethod
+    def scattered(cls, row_dest_ptr: int, bases, ld: int) -> "SegmentOutput":
+        o = cls()
+        o.row_dest, o.dest_ld = int(row_dest_ptr), int(ld)
+        for i, b in enumerate(bases):
+            o.dest_base[i] = int(b)
+        return o
+
+
 class EpPeers(ctypes.Structure):
     """nvfp4_ep_peers: one device address per rank (passed by value)."""
 
@@ -188,8 +211,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_workspace_check.restype = i32
         lib.nvfp4_grouped_gemm_noalloc.argtypes = [vp, i32, u32, vp]
         lib.nvfp4_grouped_gemm_noalloc.restype = i32
-        lib.nvfp4_grouped_gemm_segments.argtypes = [vp, i32, u32, vp, vp, i64, vp,
-                                                    ctypes.c_float, vp, sz, vp]
+        lib.nvfp4_grouped_gemm_segments.argtypes = [vp, i32, u32, vp, vp, i64,
+                                                    ctypes.POINTER(SegmentOutput), vp, sz, vp]
         lib.nvfp4_grouped_gemm_segments.restype = i32
         lib.nvfp4_quantize.argtypes = [vp, i32, i32, i64, i32, ctypes.c_float, vp, i64, vp, vp]
         lib.nvfp4_quantize.restype = i32
@@ -209,10 +232,9 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_ep_layout.argtypes = [vp, i32, i32, i32, i64, vp, vp, vp, vp, vp]
         lib.nvfp4_ep_layout.restype = i32
         lib.nvfp4_ep_dispatch.argtypes = [vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, i64, vp,
-                                          i32, EpPeers, EpPeers, i64, vp, vp]
+                                          i32, EpPeers, EpPeers, EpPeers, i64, vp, vp]
         lib.nvfp4_ep_dispatch.restype = i32
-        lib.nvfp4_ep_combine.argtypes = [vp, vp, vp, i32, i32, i32, i32, EpPeers, i32, vp, i64,
-                                         vp]
+        lib.nvfp4_ep_combine.argtypes = [vp, vp, i32, i32, vp, i32, vp, i64, vp]
         lib.nvfp4_ep_combine.restype = i32
         if path is None:
             _lib = lib
@@ -255,16 +277,16 @@ def grouped_gemm_raw(table: np.ndarray, flags: int, workspace_ptr: int, workspac
 
 def grouped_gemm_segments_raw(table: np.ndarray, flags: int, offsets_ptr: int, counts_ptr: int,
                               expected_rows: int, workspace_ptr: int, workspace_bytes: int,
-                              stream_ptr: int, out_sf_ptr: int = 0, out_scale: float = 0.0) -> None:
+                              stream_ptr: int, output: "SegmentOutput | None" = None) -> None:
     """Call nvfp4_grouped_gemm_segments on a GROUP_DTYPE table (host memory) whose rows are
-    given by device int32 arrays of per-group first rows and row counts (NVFP4 output when
-    out_sf_ptr is non-zero)."""
+    given by device int32 arrays of per-group first rows and row counts; ``output`` selects
+    NVFP4 or scattered output (None: fp16 rows into c)."""
     assert table.dtype == GROUP_DTYPE and table.flags["C_CONTIGUOUS"]
     lib = load_library()
     st = lib.nvfp4_grouped_gemm_segments(table.ctypes.data, int(table.shape[0]), flags,
                                          offsets_ptr, counts_ptr, int(expected_rows),
-                                         out_sf_ptr or None, float(out_scale), workspace_ptr,
-                                         workspace_bytes, stream_ptr)
+                                         ctypes.byref(output) if output is not None else None,
+                                         workspace_ptr, workspace_bytes, stream_ptr)
     check(st, lib)
 
 

@@ -11,9 +11,11 @@
 //                    expert segments (rows from rank 0 first, then rank 1, ...) and where
 //                    its own rows for each expert start in the owner's receive slab
 //   dispatch:        rank q writes each routed token row (NVFP4 codes + plain scale row)
-//                    straight into the owner's receive slab                          |
-//   (owner: scales plain -> blocked, expert GEMMs over its segments into its y slab) |
-//   combine:         rank q reads its pairs' rows from the owners' y slabs and sums them
+//                    straight into the owner's receive slab, and the row's return address
+//                    (q << 40 | pair index) into the owner's recv_meta                |
+//   (owner: scales plain -> blocked, expert GEMMs over its segments; the down GEMM's
+//    epilogue stores every output row into its token's rank's return buffer)        |
+//   combine:         rank q sums its pairs' returned rows (local reads)
 //
 // The kernels only load and store: no kernel waits on another rank, so the barriers (a
 // one-element NCCL all-reduce on the same stream) carry all cross-rank ordering.
@@ -92,17 +94,22 @@ __global__ void __launch_bounds__(1024) nvfp4_ep_layout_kernel(
   }
 }
 
+// Return address of a received row: the source rank and the pair's index there.
+constexpr int kEpRankShift = 40;
+constexpr int64_t kEpPairMask = (int64_t{1} << kEpRankShift) - 1;
+
 // One warp per (token, slot) pair. The pair's row in the local dispatched order is dest[i]
 // (its rank within expert e is dest[i] - offsets[e]); its row in the owner's slab is
 // send_base[e] + that rank. Copies the token's codes (cols/2 bytes) and its scales as a plain
-// row (cols/16 bytes, gathered from the blocked layout) into the owner's slabs, and records
-// the row in remote_rows[i] (-1 for dropped pairs).
+// row (cols/16 bytes, gathered from the blocked layout) into the owner's slabs, writes the
+// row's return address (rank << 40 | i) into the owner's recv_meta, and records the row in
+// remote_rows[i] (-1 for dropped pairs).
 __global__ void __launch_bounds__(256) nvfp4_ep_dispatch_kernel(
-    const int32_t* __restrict__ ids, int64_t pairs, int topk, int num_experts, int world,
-    const int32_t* __restrict__ dest, const int32_t* __restrict__ offsets,
+    const int32_t* __restrict__ ids, int64_t pairs, int topk, int num_experts, int rank,
+    int world, const int32_t* __restrict__ dest, const int32_t* __restrict__ offsets,
     const int32_t* __restrict__ send_base, const uint8_t* __restrict__ codes, int64_t ld_codes,
     const uint8_t* __restrict__ sf_blocked, int cols, EpPeers recv_codes, EpPeers recv_sf,
-    int64_t capacity, int32_t* __restrict__ remote_rows) {
+    EpPeers recv_meta, int64_t capacity, int32_t* __restrict__ remote_rows) {
   const int lane = threadIdx.x & 31;
   const int epr = num_experts / world;
   const int code_chunks = cols / 32;   // 16-byte chunks of a codes row
@@ -121,6 +128,8 @@ __global__ void __launch_bounds__(256) nvfp4_ep_dispatch_kernel(
     if (lane == 0) remote_rows[i] = static_cast<int32_t>(row);
     if (row < 0) continue;
     const int p = e / epr;
+    if (lane == 0)
+      static_cast<int64_t*>(recv_meta.ptr[p])[row] = (static_cast<int64_t>(rank) << kEpRankShift) | i;
     const int64_t t = i / topk;
     const uint4* src = reinterpret_cast<const uint4*>(codes + t * ld_codes);
     uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(recv_codes.ptr[p]) +
@@ -140,15 +149,15 @@ __global__ void __launch_bounds__(256) nvfp4_ep_dispatch_kernel(
   __threadfence_system();
 }
 
-// out[t, :] = bf16( sum_j w[t, j] * y_owner(e)[remote_rows[t*topk + j], :] ), fp32 products
-// and sums in slot order (the single-GPU combine's arithmetic); dropped pairs add nothing.
-// One warp per (token, 256-column chunk), 16-byte loads from the owners' y slabs.
+// out[t, :] = bf16( sum_j w[t, j] * ret[t*topk + j, :] ) over the pairs that were kept
+// (remote_rows >= 0), fp32 products and sums in slot order (the single-GPU combine's
+// arithmetic). ret holds each pair's expert output row, returned by its owner's down GEMM.
+// One warp per (token, 256-column chunk), 16-byte loads.
 __global__ void __launch_bounds__(256) nvfp4_ep_combine_kernel(
-    const int32_t* __restrict__ ids, const int32_t* __restrict__ remote_rows,
-    const float* __restrict__ weights, int tokens, int topk, int num_experts, int world,
-    EpPeers ys, int cols, __nv_bfloat16* __restrict__ out, int64_t ldo) {
+    const int32_t* __restrict__ remote_rows, const float* __restrict__ weights, int tokens,
+    int topk, const __half* __restrict__ ret, int cols, __nv_bfloat16* __restrict__ out,
+    int64_t ldo) {
   const int lane = threadIdx.x & 31;
-  const int epr = num_experts / world;
   const int chunks = (cols + 255) / 256;
   const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -161,12 +170,9 @@ __global__ void __launch_bounds__(256) nvfp4_ep_combine_kernel(
     for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
     for (int j = 0; j < topk; ++j) {
       const int64_t i = static_cast<int64_t>(t) * topk + j;
-      const int32_t r = remote_rows[i];
-      if (r < 0) continue;
-      const int e = ids[i];
-      const __half* y = static_cast<const __half*>(ys.ptr[e / epr]);
+      if (remote_rows[i] < 0) continue;
       const float w = weights[i];
-      const uint4 raw = *reinterpret_cast<const uint4*>(y + static_cast<int64_t>(r) * cols + col);
+      const uint4 raw = *reinterpret_cast<const uint4*>(ret + i * cols + col);
       const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {

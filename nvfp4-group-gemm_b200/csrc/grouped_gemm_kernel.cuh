@@ -186,6 +186,26 @@ __device__ __forceinline__ void store_gated_box_nvfp4(const uint32_t* v0, const 
   *reinterpret_cast<uint32_t*>(sf) = sf4;
 }
 
+// Scattered output of one staged box: the warp's 32 rows x 64 fp16 columns sit in shared
+// memory (row i at box + 128 * i, 16-byte chunks XOR-swizzled by (i & 7)); `dst` is this
+// lane's row destination (nullptr: not stored). Each store instruction writes four whole
+// 128-byte row pieces (eight lanes per row), so remote (NVLink) writes go out as full lines
+// instead of 32 separate 16-byte pieces.
+__device__ __forceinline__ void store_box_rows(const uint8_t* box, uint8_t* dst, int col0, int n,
+                                               int lane) {
+  const unsigned long long mine = reinterpret_cast<unsigned long long>(dst);
+  const int c = lane & 7;  // 16-byte chunk = 8 columns
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int r = 4 * k + (lane >> 3);
+    uint8_t* row = reinterpret_cast<uint8_t*>(__shfl_sync(0xffffffffu, mine, r));
+    const uint4 v = *reinterpret_cast<const uint4*>(box + r * 128 + ((c ^ (r & 7)) * 16));
+    const int col = col0 + 8 * c;
+    if (row != nullptr && col < n)
+      *reinterpret_cast<uint4*>(row + static_cast<size_t>(col) * sizeof(__half)) = v;
+  }
+}
+
 // Tile -> group lookup. Tiles are numbered group by group and every CTA meets its
 // tiles in increasing order, so the lookup starts from the previous answer `g`.
 // Launches of up to kSmemGroups groups first copy each group's tile_end into shared
@@ -647,6 +667,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // Convert one 64-column box (accumulator bits v0/v1, up-projection bits u0/u1 when
       // gated) to fp16 and store it: straight from registers (DIRECT, and the final sum of
       // split tiles) or through the swizzled staging box and a TMA store.
+      // Where this thread's row goes when stored from registers (or, for a scattered output,
+      // from the staged box): its C row, or the row it maps to (nullptr: not stored).
+      const bool scatter = !GATED && p.row_dest != nullptr;
+      uint8_t* out_row = nullptr;
+      if (row < gd.m)
+        out_row = scatter ? scatter_row(p, static_cast<int64_t>(rb) + row)
+                          : gd.c + static_cast<size_t>(rb + row) * gd.n * sizeof(__half);
       auto emit_box = [&](const uint32_t* v0, const uint32_t* v1, const uint32_t* u0,
                           const uint32_t* u1, int box, bool direct) {
         if (GATED && p.out_sf != nullptr) {
@@ -691,9 +718,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             // Row row0 + lane, columns [col, col + 32): four 16-byte stores (N is a
             // multiple of 8, so a chunk is either inside the row or past its end).
             const int col = nt * Cfg::kOutN + box * 64 + half * 32;
-            if (row < gd.m) {
-              uint4* dst = reinterpret_cast<uint4*>(
-                  gd.c + (static_cast<size_t>(rb + row) * gd.n + col) * sizeof(__half));
+            if (out_row != nullptr) {
+              uint4* dst = reinterpret_cast<uint4*>(out_row + static_cast<size_t>(col) * sizeof(__half));
 #pragma unroll
               for (int c = 0; c < 4; ++c)
                 if (col + 8 * c < gd.n)
@@ -712,7 +738,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
           }
         }
-        if (!direct) {
+        if (!direct && scatter) {
+          __syncwarp();
+          store_box_rows(my_bufs + (stores & 1u) * Cfg::kEpiBufBytes, out_row,
+                         nt * Cfg::kOutN + box * 64, gd.n, lane);
+          __syncwarp();  // the box is read before it is written again
+          ++stores;
+        } else if (!direct) {
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {

@@ -353,6 +353,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (row0 < gd.m) {
         const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(32 * quarter) << 16) +
                                acc * Cfg::kAccStride;
+        // Scattered output: where this thread's row goes (nullptr: not stored).
+        const bool scatter = !GATED && p.row_dest != nullptr;
+        uint8_t* out_row = nullptr;
+        if (scatter && row0 + lane < gd.m)
+          out_row = scatter_row(p, static_cast<int64_t>(rb) + row0 + lane);
 #pragma unroll 1
         for (int bi = 0; bi < kBoxes; ++bi) {
           const int box = (first_box + bi) % kBoxes;
@@ -416,6 +421,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               ptx::st_shared_v4(row_addr + chunk * 16, packed[4 * c], packed[4 * c + 1],
                                 packed[4 * c + 2], packed[4 * c + 3]);
             }
+          }
+          if (scatter) {
+            __syncwarp();
+            store_box_rows(my_bufs + (stores & 1u) * Cfg::kEpiBufBytes, out_row,
+                           nt * Cfg::kOutN + box * 64, gd.n, lane);
+            __syncwarp();  // the box is read before it is written again
+            ++stores;
+            continue;
           }
           ptx::fence_proxy_async_smem();
           __syncwarp();

@@ -468,8 +468,7 @@ struct SegmentArgs {
   const int32_t* offsets;
   const int32_t* counts;
   int64_t expected_rows;
-  uint8_t* out_sf;   // NVFP4 output of a gated launch: blocked scales of the output slab
-  float out_scale;   // ... and its per-tensor scale
+  const nvfp4_segment_output* output;  // nullptr: fp16 rows into c
 };
 
 // Shared implementation of the grouped entry points: validate, schedule, encode
@@ -615,9 +614,14 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
   GemmParams gp;
   gp.seg_rows = nullptr;
   gp.seg_total_tiles = nullptr;
-  gp.out_sf = seg != nullptr ? seg->out_sf : nullptr;
-  gp.out_scale = seg != nullptr ? seg->out_scale : 0.0f;
+  const nvfp4_segment_output* out = seg != nullptr ? seg->output : nullptr;
+  gp.out_sf = out != nullptr ? static_cast<uint8_t*>(out->sf) : nullptr;
+  gp.out_scale = out != nullptr ? out->scale : 0.0f;
   gp.out_d6 = 6.0f * gp.out_scale;
+  gp.row_dest = out != nullptr ? out->row_dest : nullptr;
+  for (int i = 0; i < 8; ++i)
+    gp.dest_base[i] = out != nullptr ? static_cast<uint8_t*>(out->dest_base[i]) : nullptr;
+  gp.dest_ld = out != nullptr ? out->dest_ld : 0;
   if (seg != nullptr) {
     int32_t* seg_rows = reinterpret_cast<int32_t*>(ws + ws_seg_rows_offset(num_groups));
     int32_t* seg_total = &reinterpret_cast<WorkspaceHeader*>(ws)->seg_total_tiles;
@@ -674,7 +678,7 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
       e = launch_single<256, true, 3>(gp, grid, s);
     else if (mma_n == 128)
       e = launch_single<128, false, 5>(gp, grid, s);
-    else if (rows <= static_cast<int64_t>(kStreamMaxAvgRows) * active)
+    else if (rows <= static_cast<int64_t>(kStreamMaxAvgRows) * active && gp.row_dest == nullptr)
       e = launch_single<256, false, 4, true>(gp, grid, s);  // weight-streaming shapes
     else
       e = launch_single<256, false, 3>(gp, grid, s);
@@ -1026,8 +1030,8 @@ NVFP4_API int nvfp4_ep_dispatch(const int32_t* topk_ids, int tokens, int topk, i
                                 int rank, int world, const int32_t* dest, const int32_t* offsets,
                                 const int32_t* send_base, const void* codes, int64_t ld_codes,
                                 const void* sf_blocked, int cols, nvfp4_ep_peers recv_codes,
-                                nvfp4_ep_peers recv_sf, int64_t recv_capacity,
-                                int32_t* remote_rows, void* stream) {
+                                nvfp4_ep_peers recv_sf, nvfp4_ep_peers recv_meta,
+                                int64_t recv_capacity, int32_t* remote_rows, void* stream) {
   g_last_error.clear();
   int st = check_ep_world(num_experts, rank, world);
   if (st != NVFP4_OK) return st;
@@ -1044,40 +1048,37 @@ NVFP4_API int nvfp4_ep_dispatch(const int32_t* topk_ids, int tokens, int topk, i
                 "scales 4-byte aligned");
   if ((st = check_peers(recv_codes, world, "recv_codes", true)) != NVFP4_OK) return st;
   if ((st = check_peers(recv_sf, world, "recv_sf", true)) != NVFP4_OK) return st;
+  if ((st = check_peers(recv_meta, world, "recv_meta", true)) != NVFP4_OK) return st;
   const int64_t pairs = static_cast<int64_t>(tokens) * topk;
   const int64_t blocks = std::min<int64_t>((pairs + 7) / 8, 148 * 16);
   nvfp4_ep_dispatch_kernel<<<static_cast<unsigned>(blocks), 256, 0,
                              static_cast<cudaStream_t>(stream)>>>(
-      topk_ids, pairs, topk, num_experts, world, dest, offsets, send_base,
+      topk_ids, pairs, topk, num_experts, rank, world, dest, offsets, send_base,
       static_cast<const uint8_t*>(codes), ld_codes, static_cast<const uint8_t*>(sf_blocked), cols,
-      to_peers(recv_codes), to_peers(recv_sf), recv_capacity, remote_rows);
+      to_peers(recv_codes), to_peers(recv_sf), to_peers(recv_meta), recv_capacity, remote_rows);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "dispatch launch");
   return NVFP4_OK;
 }
 
-NVFP4_API int nvfp4_ep_combine(const int32_t* topk_ids, const int32_t* remote_rows,
-                               const float* weights, int tokens, int topk, int num_experts,
-                               int world, nvfp4_ep_peers ys, int cols, void* out, int64_t ldo,
+NVFP4_API int nvfp4_ep_combine(const int32_t* remote_rows, const float* weights, int tokens,
+                               int topk, const void* ret, int cols, void* out, int64_t ldo,
                                void* stream) {
   g_last_error.clear();
-  int st = check_ep_world(num_experts, 0, world);
-  if (st != NVFP4_OK) return st;
   if (tokens < 0 || topk <= 0 || cols <= 0 || cols % 8 != 0)
     return fail(NVFP4_ERR_BAD_SHAPE, "tokens=%d topk=%d cols=%d (cols a multiple of 8)", tokens,
                 topk, cols);
   if (tokens == 0) return NVFP4_OK;
-  if (topk_ids == nullptr || remote_rows == nullptr || weights == nullptr || out == nullptr)
+  if (remote_rows == nullptr || weights == nullptr || ret == nullptr || out == nullptr)
     return fail(NVFP4_ERR_NULL_POINTER, "a combine buffer is NULL");
-  if (!aligned16(out) || ldo % 8 != 0 || ldo < cols)
-    return fail(NVFP4_ERR_MISALIGNED, "out 16-byte aligned, ldo a multiple of 8 >= cols");
-  if ((st = check_peers(ys, world, "ys", true)) != NVFP4_OK) return st;
+  if (!aligned16(out) || !aligned16(ret) || ldo % 8 != 0 || ldo < cols)
+    return fail(NVFP4_ERR_MISALIGNED, "ret and out 16-byte aligned, ldo a multiple of 8 >= cols");
   const int chunks = (cols + 255) / 256;
   const int64_t warps = static_cast<int64_t>(tokens) * chunks;
   const int64_t blocks = std::min<int64_t>((warps + 7) / 8, 148 * 16);
   nvfp4_ep_combine_kernel<<<static_cast<unsigned>(blocks), 256, 0,
                             static_cast<cudaStream_t>(stream)>>>(
-      topk_ids, remote_rows, weights, tokens, topk, num_experts, world, to_peers(ys), cols,
+      remote_rows, weights, tokens, topk, static_cast<const __half*>(ret), cols,
       static_cast<__nv_bfloat16*>(out), ldo);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "combine launch");
@@ -1128,7 +1129,7 @@ NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsi
 NVFP4_API int nvfp4_grouped_gemm_segments(const nvfp4_group* groups, int num_groups,
                                           unsigned int flags, const int32_t* seg_offsets,
                                           const int32_t* seg_counts, int64_t expected_rows,
-                                          void* out_sf, float out_scale, void* workspace,
+                                          const nvfp4_segment_output* output, void* workspace,
                                           size_t workspace_bytes, void* stream) {
   g_last_error.clear();
   int st = check_common_args(groups, num_groups, flags);
@@ -1140,16 +1141,30 @@ NVFP4_API int nvfp4_grouped_gemm_segments(const nvfp4_group* groups, int num_gro
     return fail(NVFP4_ERR_NULL_POINTER, "seg_offsets or seg_counts is NULL");
   if ((reinterpret_cast<uintptr_t>(seg_offsets) & 3u) || (reinterpret_cast<uintptr_t>(seg_counts) & 3u))
     return fail(NVFP4_ERR_MISALIGNED, "seg_offsets and seg_counts must be 4-byte aligned");
-  if (out_sf != nullptr) {
+  if (output != nullptr && output->sf != nullptr) {
     if ((flags & NVFP4_FLAG_GATED) == 0)
       return fail(NVFP4_ERR_INVALID_ARGUMENT, "NVFP4 output needs NVFP4_FLAG_GATED");
-    if (!(out_scale > 0.0f) || !std::isfinite(out_scale))
-      return fail(NVFP4_ERR_INVALID_ARGUMENT, "out_scale must be finite and > 0");
-    if (!aligned16(out_sf)) return fail(NVFP4_ERR_MISALIGNED, "out_sf not 16-byte aligned");
+    if (!(output->scale > 0.0f) || !std::isfinite(output->scale))
+      return fail(NVFP4_ERR_INVALID_ARGUMENT, "output scale must be finite and > 0");
+    if (!aligned16(output->sf)) return fail(NVFP4_ERR_MISALIGNED, "output sf not 16-byte aligned");
     for (int i = 0; i < num_groups; ++i)
       if (groups[i].n % 64 != 0)
         return fail(NVFP4_ERR_BAD_SHAPE,
                     "group %d: n=%d must be a multiple of 64 for NVFP4 output", i, groups[i].n);
+  }
+  if (output != nullptr && output->row_dest != nullptr) {
+    if (flags & NVFP4_FLAG_GATED)
+      return fail(NVFP4_ERR_INVALID_ARGUMENT, "scattered output is for non-gated launches");
+    if ((reinterpret_cast<uintptr_t>(output->row_dest) & 7u) != 0 || output->dest_ld % 16 != 0)
+      return fail(NVFP4_ERR_MISALIGNED, "row_dest 8-byte aligned and dest_ld a multiple of 16");
+    int nmax = 0;
+    for (int i = 0; i < num_groups; ++i) nmax = std::max(nmax, groups[i].n);
+    if (output->dest_ld < static_cast<int64_t>(nmax) * 2)
+      return fail(NVFP4_ERR_INVALID_ARGUMENT, "dest_ld=%lld < 2 * n",
+                  static_cast<long long>(output->dest_ld));
+    for (int i = 0; i < NVFP4_EP_MAX_RANKS; ++i)
+      if (output->dest_base[i] != nullptr && !aligned16(output->dest_base[i]))
+        return fail(NVFP4_ERR_MISALIGNED, "dest_base[%d] not 16-byte aligned", i);
   }
   for (int i = 1; i < num_groups; ++i)
     if (groups[i].m != groups[0].m)
@@ -1163,8 +1178,7 @@ NVFP4_API int nvfp4_grouped_gemm_segments(const nvfp4_group* groups, int num_gro
     return fail(NVFP4_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes,
                 ws_total_bytes(num_groups));
   std::vector<GroupDev> rec(static_cast<size_t>(num_groups));
-  const SegmentArgs seg{seg_offsets, seg_counts, expected_rows, static_cast<uint8_t*>(out_sf),
-                        out_scale};
+  const SegmentArgs seg{seg_offsets, seg_counts, expected_rows, output};
   return grouped_gemm_impl(groups, num_groups, flags, static_cast<uint8_t*>(workspace),
                            workspace_bytes, static_cast<cudaStream_t>(stream), rec.data(),
                            /*use_cache=*/true, &seg);

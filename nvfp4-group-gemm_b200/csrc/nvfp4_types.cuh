@@ -140,7 +140,22 @@ struct GemmParams {
   uint8_t* out_sf;
   float out_scale;
   float out_d6;
+  // Scattered fp16 output of non-gated segment launches (row_dest != nullptr): slab row r
+  // goes to dest_base[row_dest[r] >> 40] + (row_dest[r] & (2^40 - 1)) * dest_ld bytes
+  // (row_dest[r] < 0: not stored); c is not written.
+  const int64_t* row_dest;
+  uint8_t* dest_base[8];
+  int64_t dest_ld;
 };
+
+// Destination of slab row r of a scattered output (nullptr: not stored).
+__device__ __forceinline__ uint8_t* scatter_row(const GemmParams& p, int64_t r) {
+  const int64_t code = p.row_dest[r];
+  if (code < 0) return nullptr;
+  uint8_t* base = p.dest_base[(code >> 40) & 7];
+  if (base == nullptr) return nullptr;
+  return base + (code & ((int64_t{1} << 40) - 1)) * p.dest_ld;
+}
 
 // First row of group g's segment (0 outside segment launches).
 __device__ __forceinline__ int seg_row(const GemmParams& p, int g) {

@@ -120,14 +120,16 @@ class EPMoEBlock:
 
     Per call (one stream; barriers are one-element NCCL all-reduces):
     route + quantise the local tokens; publish per-expert counts into every rank's count
-    matrix | layout (all ranks derive the same placement); dispatch codes + scale rows into
-    the owners' receive slabs | owner: scales to the blocked layout, gated GEMM over its
-    expert segments with NVFP4 output, down GEMM into its y slab | combine: pull each pair's
-    row from its owner's y slab, weighted fp32 sum in slot order, bf16.
+    matrix | layout (all ranks derive the same placement); dispatch codes + scale rows (and
+    each row's return address) into the owners' receive slabs | owner: scales to the blocked
+    layout, gated GEMM over its expert segments with NVFP4 output, down GEMM whose epilogue
+    stores every output row into its token's rank (NVLink stores overlapping the GEMM) |
+    combine: weighted fp32 sum of each token's returned rows in slot order, bf16.
 
     The receive slabs hold ``world * tokens * topk + 127 * E/P`` rows (every pair of every
-    rank routed here, plus segment padding), so the exchange never drops a pair. Receive
-    slabs, count matrix and y slab live in one torch symmetric-memory allocation.
+    rank routed here, plus segment padding), so the exchange never drops a pair. Count
+    matrix, receive slabs, return addresses and the return buffer ([tokens * topk, H] fp16)
+    live in one torch symmetric-memory allocation.
     """
 
     def __init__(self, local_weights, num_experts: int, tokens: int, topk: int,
@@ -168,10 +170,12 @@ class EPMoEBlock:
         cap = world * pairs + 127 * epr
         self.capacity = cap
 
-        # One symmetric allocation: count matrix | received codes | received plain scales | y.
+        # One symmetric allocation: count matrix | received codes | received plain scales |
+        # return address of each received row | returned expert rows of this rank's pairs.
         def up(n):
             return (n + 255) // 256 * 256
-        sizes = [world * num_experts * 4, cap * hdim // 2, cap * hdim // 16, cap * hdim * 2]
+        sizes = [world * num_experts * 4, cap * hdim // 2, cap * hdim // 16, cap * 8,
+                 pairs * hdim * 2]
         offs = [0]
         for n in sizes[:-1]:
             offs.append(offs[-1] + up(n))
@@ -191,7 +195,12 @@ class EPMoEBlock:
         self._mat = sl[0].view(torch.int32).view(world, num_experts)
         self._recv_codes = sl[1].view(cap, hdim // 2)
         self._recv_sf = sl[2].view(cap, hdim // 16)
-        self._y = sl[3].view(torch.float16).view(cap, hdim)
+        self._recv_meta = sl[3].view(torch.int64)
+        self._ret = sl[4].view(torch.float16).view(pairs, hdim)
+        # The down GEMM's output rows go to the token's rank: row r of this rank's slab to
+        # return buffer (recv_meta[r] >> 40) at pair (recv_meta[r] & (2^40 - 1)).
+        self._scatter = _native.SegmentOutput.scattered(
+            self._recv_meta.data_ptr(), [b + delta + offs[4] for b in bases], hdim * 2)
 
         i32 = dict(dtype=torch.int32, device=dev)
         u8 = dict(dtype=torch.uint8, device=dev)
@@ -234,8 +243,10 @@ class EPMoEBlock:
         self._t1 = slab_table(self._recv_codes, self._recv_sfa, self._a2, P["w_gate"], P["sf_gate"],
                               idim, hdim, s_x * np.asarray(W.s_gate, dtype=np.float32),
                               P["w_up"], P["sf_up"], s_x * np.asarray(W.s_up, dtype=np.float32))
-        self._t2 = slab_table(self._a2, self._sfa2, self._y, P["w_down"], P["sf_down"], hdim, idim,
-                              s_h * np.asarray(W.s_down, dtype=np.float32))
+        # c of the down GEMM is never written (scattered output); any valid aligned address.
+        self._t2 = slab_table(self._a2, self._sfa2, self._ret, P["w_down"], P["sf_down"], hdim,
+                              idim, s_h * np.asarray(W.s_down, dtype=np.float32))
+        self._nvfp4_out = _native.SegmentOutput.nvfp4(self._sfa2.data_ptr(), self.hidden_scale)
         ws_bytes = _native.workspace_size(epr)
         self._ws1 = torch.zeros(ws_bytes, **u8)
         self._ws2 = torch.zeros(ws_bytes, **u8)
@@ -246,9 +257,12 @@ class EPMoEBlock:
     def _barrier(self):
         dist.all_reduce(self._bar, group=self.group)
 
-    def run(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor) -> torch.Tensor:
+    def run(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+            stage_events: list | None = None) -> torch.Tensor:
         """One expert-parallel block on the current stream; returns ``self.out`` (bf16
-        [tokens, H]) for this rank's tokens. Every rank of the group must call it."""
+        [tokens, H]) for this rank's tokens. Every rank of the group must call it. With
+        ``stage_events`` (a list), (stage name, CUDA event recorded after it) pairs are
+        appended for timing."""
         from . import _native
         from .quantize import _DTYPES
 
@@ -263,43 +277,59 @@ class EPMoEBlock:
         st = torch.cuda.current_stream(self.device)
         s = st.cuda_stream
         cap = self.capacity
+
+        def mark(name):
+            if stage_events is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(st)
+                stage_events.append((name, ev))
+
+        mark("start")
         chk(lib.nvfp4_moe_route(topk_ids.data_ptr(), T, K, E, self._counts.data_ptr(),
                                 self._offsets.data_ptr(), self._dest.data_ptr(),
                                 self._src_rows.data_ptr(), self._src_rows.numel(),
                                 self._route_ws.data_ptr(), self._route_ws_bytes, s), lib)
         chk(lib.nvfp4_quantize(x.data_ptr(), T, H, x.stride(0), _DTYPES[x.dtype], self.act_scale,
                                self._qx.data_ptr(), self._qx.stride(0), self._sfx.data_ptr(), s), lib)
+        mark("route + quantise")
         chk(lib.nvfp4_ep_publish_counts(self._counts.data_ptr(), E, rank, world, self._peers[0], s),
             lib)
         self._barrier()
+        mark("publish counts + barrier")
         chk(lib.nvfp4_ep_layout(self._mat.data_ptr(), E, rank, world, cap,
                                 self.seg_offsets.data_ptr(), self.seg_counts.data_ptr(),
                                 self.send_base.data_ptr(), self._err.data_ptr(), s), lib)
         chk(lib.nvfp4_ep_dispatch(topk_ids.data_ptr(), T, K, E, rank, world, self._dest.data_ptr(),
                                   self._offsets.data_ptr(), self.send_base.data_ptr(),
                                   self._qx.data_ptr(), self._qx.stride(0), self._sfx.data_ptr(), H,
-                                  self._peers[1], self._peers[2], cap,
+                                  self._peers[1], self._peers[2], self._peers[3], cap,
                                   self.remote_rows.data_ptr(), s), lib)
+        mark("layout + dispatch")
         self._barrier()
+        mark("barrier")
         _native.sf_to_blocked_raw(self._recv_sf.data_ptr(), self._recv_sfa.data_ptr(), cap,
                                   H // 16, H // 16, s)
         flags = (_native.FLAG_REUSE_DESCRIPTORS if self._uploaded else 0) | self._cta_flags
         _native.grouped_gemm_segments_raw(self._t1, _native.FLAG_GATED | flags,
                                           self.seg_offsets.data_ptr(), self.seg_counts.data_ptr(),
                                           T * K, self._ws1.data_ptr(), self._ws_bytes, s,
-                                          self._sfa2.data_ptr(), self.hidden_scale)
+                                          self._nvfp4_out)
+        mark("scale layout + gate/up GEMM")
         _native.grouped_gemm_segments_raw(self._t2, flags, self.seg_offsets.data_ptr(),
                                           self.seg_counts.data_ptr(), T * K,
-                                          self._ws2.data_ptr(), self._ws_bytes, s)
+                                          self._ws2.data_ptr(), self._ws_bytes, s, self._scatter)
         self._uploaded = True
+        mark("down GEMM + return rows")
         self._barrier()
+        mark("barrier 2")
         w = topk_weights
         if w.dtype != torch.float32 or not w.is_contiguous():
             self._w.copy_(w)
             w = self._w
-        chk(lib.nvfp4_ep_combine(topk_ids.data_ptr(), self.remote_rows.data_ptr(), w.data_ptr(), T,
-                                 K, E, world, self._peers[3], H, self.out.data_ptr(),
-                                 self.out.stride(0), s), lib)
+        chk(lib.nvfp4_ep_combine(self.remote_rows.data_ptr(), w.data_ptr(), T, K,
+                                 self._ret.data_ptr(), H, self.out.data_ptr(), self.out.stride(0),
+                                 s), lib)
+        mark("combine")
         return self.out
 
     def check_errors(self) -> int:

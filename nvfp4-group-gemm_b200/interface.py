@@ -316,7 +316,8 @@ def grouped_gemm_segments(a: torch.Tensor, sfa: torch.Tensor, c: torch.Tensor,
                           sfb2: Sequence[torch.Tensor] | None = None,
                           alpha2: Sequence[float] | None = None, expected_rows: int = 0,
                           cta: str | None = None, out_sf: torch.Tensor | None = None,
-                          out_scale: float | None = None,
+                          out_scale: float | None = None, row_dest: torch.Tensor | None = None,
+                          dest: Sequence[torch.Tensor] | None = None,
                           stream: torch.cuda.Stream | None = None) -> torch.Tensor:
     """Grouped GEMM over row segments of one slab, with the segments read on the GPU.
 
@@ -334,6 +335,11 @@ def grouped_gemm_segments(a: torch.Tensor, sfa: torch.Tensor, c: torch.Tensor,
     NVFP4 output (gated only): with ``out_sf`` (blocked scales of R rows x N) and
     ``out_scale``, ``c`` is a uint8 [R, N/2] slab that receives the e2m1 codes of the
     output, bit-identical to ``quantize(fp16 output, out_scale)``; N % 64 == 0.
+
+    Scattered output (non-gated only): with ``row_dest`` (int64 CUDA tensor, one entry per
+    slab row) and ``dest`` (up to 8 fp16 [*, N] tensors with the same row stride, which may
+    live on peer GPUs), slab row r is stored to row ``row_dest[r] & (2**40 - 1)`` of
+    ``dest[row_dest[r] >> 40]`` instead of ``c`` (negative entries: not stored).
     """
     if cta not in (None, "pair", "single"):
         raise ValueError(f"cta must be None, 'pair' or 'single', got {cta!r}")
@@ -364,6 +370,22 @@ def grouped_gemm_segments(a: torch.Tensor, sfa: torch.Tensor, c: torch.Tensor,
             raise ValueError("c must be a CUDA fp16 [rows, N] tensor")
         rows, n = int(c.shape[0]), int(c.shape[1])
         _as_2d_kmajor(c, rows, n, "c")  # dense fp16 rows
+    scatter = None
+    if row_dest is not None:
+        if gated:
+            raise ValueError("scattered output (row_dest) is for non-gated launches")
+        if row_dest.dtype != torch.int64 or not row_dest.is_cuda or not row_dest.is_contiguous() \
+                or row_dest.numel() < rows:
+            raise ValueError(f"row_dest must be a contiguous CUDA int64 tensor of >= {rows} entries")
+        if not dest or len(dest) > _native.EP_MAX_RANKS:
+            raise ValueError(f"dest must hold 1..{_native.EP_MAX_RANKS} tensors")
+        ld = int(dest[0].stride(0)) * 2
+        for i, t in enumerate(dest):
+            if t.dtype != torch.float16 or t.dim() != 2 or int(t.shape[1]) < n or \
+                    t.stride(1) != 1 or int(t.stride(0)) * 2 != ld:
+                raise ValueError(f"dest[{i}] must be fp16 [*, >= {n}] with the row stride of dest[0]")
+        scatter = _native.SegmentOutput.scattered(row_dest.data_ptr(),
+                                                  [t.data_ptr() for t in dest], ld)
     k = int(a.shape[1]) * 2 if a.dim() >= 2 else 0
     _check_fp4(a, "a")
     a = _as_2d_kmajor(a, rows, k // 2, "a")
@@ -404,8 +426,8 @@ def grouped_gemm_segments(a: torch.Tensor, sfa: torch.Tensor, c: torch.Tensor,
         _native.grouped_gemm_segments_raw(table, call_flags, seg_offsets.data_ptr(),
                                           seg_counts.data_ptr(), int(expected_rows),
                                           ws.buf.data_ptr(), ws.nbytes, s.cuda_stream,
-                                          out_sf.data_ptr() if quant_out else 0,
-                                          float(out_scale) if quant_out else 0.0)
+                                          _native.SegmentOutput.nvfp4(out_sf.data_ptr(), out_scale)
+                                          if quant_out else scatter)
     ws.last_table = table
     ws.last_flags = flags
     ws.last_sig = None

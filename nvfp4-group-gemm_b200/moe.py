@@ -337,6 +337,7 @@ class MoEBlock:
                               s_x * np.asarray(weights.s_up, dtype=np.float32))
         self._t2 = slab_table(self._a2, self._sfa2, self._y, P["w_down"], P["sf_down"], hdim,
                               idim, s_h * np.asarray(weights.s_down, dtype=np.float32))
+        self._nvfp4_out = _native.SegmentOutput.nvfp4(self._sfa2.data_ptr(), self.hidden_scale)
         ws_bytes = _native.workspace_size(E)
         # Zero-filled: the first 4 bytes are the device error word.
         self._ws1 = torch.zeros(ws_bytes, **u8)
@@ -381,7 +382,7 @@ class MoEBlock:
             _native.grouped_gemm_segments_raw(self._t1, _native.FLAG_GATED | flags,
                                               self.offsets.data_ptr(), self.counts.data_ptr(),
                                               T * K, self._ws1.data_ptr(), self._ws_bytes, s,
-                                              self._sfa2.data_ptr(), self.hidden_scale)
+                                              self._nvfp4_out)
             _native.grouped_gemm_segments_raw(self._t2, flags, self.offsets.data_ptr(),
                                               self.counts.data_ptr(), T * K,
                                               self._ws2.data_ptr(), self._ws_bytes, s)

@@ -111,6 +111,10 @@ def test_validation_errors_before_launch(pkg, kw, flags, status):
     ("nvfp4_out_bad_scale", 1, 1),
     ("nvfp4_out_misaligned", 1, 3),
     ("nvfp4_out_n", 1, 2),          # n must be a multiple of 64
+    ("scatter_gated", 1, 1),        # scattered rows are for non-gated launches
+    ("scatter_ld", 0, 3),           # dest_ld a multiple of 16
+    ("scatter_short_ld", 0, 1),     # dest_ld >= 2 n
+    ("scatter_base", 0, 3),         # bases 16-byte aligned
 ])
 def test_segment_validation_errors_before_launch(pkg, case, flags, status):
     N = pkg._native
@@ -127,13 +131,17 @@ def test_segment_validation_errors_before_launch(pkg, case, flags, status):
     ws_ptr = (ctypes.addressof(ws) + 255) & ~255
     offs = 0 if case == "null_offsets" else 0x70000
     counts = 0x70102 if case == "misaligned_counts" else 0x70100
-    out_sf = None
-    out_scale = 0.0
+    out = None
     if case.startswith("nvfp4_out"):
-        out_sf = 0x78008 if case == "nvfp4_out_misaligned" else 0x78000
-        out_scale = 0.0 if case == "nvfp4_out_bad_scale" else 0.5
-    st = lib.nvfp4_grouped_gemm_segments(t.ctypes.data, 2, flags, offs, counts, 0, out_sf,
-                                         out_scale, None if case == "no_workspace" else ws_ptr,
+        out = N.SegmentOutput.nvfp4(0x78008 if case == "nvfp4_out_misaligned" else 0x78000,
+                                    0.0 if case == "nvfp4_out_bad_scale" else 0.5)
+    elif case.startswith("scatter"):
+        ld = {"scatter_ld": 520, "scatter_short_ld": 256}.get(case, 512)
+        bases = [0x90008 if case == "scatter_base" else 0x90000, 0xA0000]
+        out = N.SegmentOutput.scattered(0x88000, bases, ld)
+    st = lib.nvfp4_grouped_gemm_segments(t.ctypes.data, 2, flags, offs, counts, 0,
+                                         ctypes.byref(out) if out is not None else None,
+                                         None if case == "no_workspace" else ws_ptr,
                                          N.workspace_size(2), None)
     assert st == status, lib.nvfp4_last_error_detail()
     assert lib.nvfp4_last_error_detail()

@@ -270,3 +270,38 @@ def test_gated_nvfp4_output_equals_quantised_fp16_output(pkg, cta):
     with pytest.raises(ValueError):  # non-gated launches have no NVFP4 output
         pkg.grouped_gemm_segments(P["a"], P["sfa"], codes, P["b"], P["sfb"], so, sc, out_sf=sf,
                                   out_scale=s_h)
+
+
+@pytest.mark.parametrize("cta", [None, "single", "pair"])
+def test_scattered_output_rows(pkg, cta):
+    """Non-gated segment launch with scattered output: every slab row lands, bit for bit as
+    the fp16 launch computes it, at the (buffer, row) its row_dest entry names; rows marked
+    -1 and rows outside the segments are stored nowhere."""
+    counts, n, k = [0, 1, 127, 300, 129, 64], 256, 1024
+    P = _slab_problem(pkg, counts, n, k, False, seed=47, tail=0)
+    cap = P["cap"]
+    ref = _segment_launch(pkg, P, P["offs"], counts, cta)
+    rng = np.random.default_rng(3)
+    rows = [r for off, cnt in zip(P["offs"], counts) for r in range(off, off + cnt)]
+    perm = rng.permutation(2 * cap)[:len(rows)]  # target slots over two buffers of cap rows
+    code = np.full(cap, -1, dtype=np.int64)
+    for r, slot in zip(rows, perm):
+        if rng.random() < 0.1:
+            continue  # not stored
+        code[r] = (int(slot // cap) << 40) | int(slot % cap)
+    dest = [torch.full((cap, n + 8), SENTINEL, dtype=torch.float16, device="cuda") for _ in range(2)]
+    c = torch.full((cap, n), SENTINEL, dtype=torch.float16, device="cuda")
+    so = torch.tensor(P["offs"], dtype=torch.int32, device="cuda")
+    sc = torch.tensor(counts, dtype=torch.int32, device="cuda")
+    pkg.grouped_gemm_segments(P["a"], P["sfa"], c, P["b"], P["sfb"], so, sc, alpha=P["alpha"],
+                              cta=cta, row_dest=torch.from_numpy(code).cuda(), dest=dest)
+    torch.cuda.synchronize()
+    assert pkg.check_device_errors() == 0
+    assert bool((c == SENTINEL).all()), "c must not be written"
+    want = [torch.full((cap, n + 8), SENTINEL, dtype=torch.float16) for _ in range(2)]
+    ref_cpu = ref.cpu()
+    for r in range(cap):
+        if code[r] >= 0:
+            want[code[r] >> 40][code[r] & ((1 << 40) - 1), :n] = ref_cpu[r]
+    for b in range(2):
+        assert torch.equal(dest[b].cpu().view(torch.int16), want[b].view(torch.int16)), b
