@@ -501,6 +501,11 @@ def run_moe(args):
     e1.record()
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / steps
+    # Device time between the stages of one eager MoEBlock call.
+    evs = []
+    blk.run(x, ids, wts, stage_events=evs)
+    torch.cuda.synchronize(dev)
+    block_stage_us = {n: a.elapsed_time(b) * 1e3 for (_, a), (n, b) in zip(evs[:-1], evs[1:])}
     blk_errors = blk.check_device_errors()
     del graph
     # Per-stage split of one call (events between the stages of moe_ffn).
@@ -557,7 +562,8 @@ def run_moe(args):
                           "note": "host-sized groups: one device->host read of the routing per call"},
         "graph_output_equals_moe_ffn": same,
         "device_error_bits": blk_errors,
-        "stage_us": split,
+        "stage_us": block_stage_us,
+        "stage_us_moe_ffn": split,
         "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
                      "frac": tf / peak, "peak_source": f"{kind}: 4 x bf16 (sustained)",
                      "traffic": None},

@@ -26,6 +26,7 @@
 
 #include <cstdint>
 
+#include "moe_kernels.cuh"
 #include "nvfp4_quant_math.cuh"
 
 namespace nvfp4 {
@@ -134,7 +135,7 @@ __global__ void __launch_bounds__(256) nvfp4_ep_dispatch_kernel(
     const uint4* src = reinterpret_cast<const uint4*>(codes + t * ld_codes);
     uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(recv_codes.ptr[p]) +
                                           row * (cols / 2));
-    for (int c = lane; c < code_chunks; c += 32) dst[c] = __ldg(src + c);
+    copy_row_chunks(src, dst, code_chunks, lane);
     uint4* sdst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(recv_sf.ptr[p]) +
                                            row * (cols / 16));
     for (int c = lane; c < sf_chunks; c += 32) {
@@ -151,8 +152,8 @@ __global__ void __launch_bounds__(256) nvfp4_ep_dispatch_kernel(
 
 // out[t, :] = bf16( sum_j w[t, j] * ret[t*topk + j, :] ) over the pairs that were kept
 // (remote_rows >= 0), fp32 products and sums in slot order (the single-GPU combine's
-// arithmetic). ret holds each pair's expert output row, returned by its owner's down GEMM.
-// One warp per (token, 256-column chunk), 16-byte loads.
+// arithmetic, combine_slots). ret holds each pair's expert output row, returned by its
+// owner's down GEMM. One warp per (token, 256-column chunk), 16-byte loads.
 __global__ void __launch_bounds__(256) nvfp4_ep_combine_kernel(
     const int32_t* __restrict__ remote_rows, const float* __restrict__ weights, int tokens,
     int topk, const __half* __restrict__ ret, int cols, __nv_bfloat16* __restrict__ out,
@@ -162,33 +163,15 @@ __global__ void __launch_bounds__(256) nvfp4_ep_combine_kernel(
   const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   for (int64_t task = warp0; task < static_cast<int64_t>(tokens) * chunks; task += nwarps) {
-    const int t = static_cast<int>(task / chunks);
+    const int64_t t = task / chunks;
     const int col = static_cast<int>(task % chunks) * 256 + lane * 8;
-    if (col >= cols) continue;
+    const bool active = col < cols;
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-    for (int j = 0; j < topk; ++j) {
-      const int64_t i = static_cast<int64_t>(t) * topk + j;
-      if (remote_rows[i] < 0) continue;
-      const float w = weights[i];
-      const uint4 raw = *reinterpret_cast<const uint4*>(ret + i * cols + col);
-      const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&words[k]));
-        acc[2 * k] = __fadd_rn(acc[2 * k], __fmul_rn(w, f.x));
-        acc[2 * k + 1] = __fadd_rn(acc[2 * k + 1], __fmul_rn(w, f.y));
-      }
-    }
-    uint32_t packed[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
-      packed[k] = *reinterpret_cast<const uint32_t*>(&b);
-    }
-    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * ldo + col) =
-        make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    combine_slots(t, topk, col, active, ret, cols, weights,
+                  [&](int64_t i) -> int64_t { return __ldg(remote_rows + i) < 0 ? -1 : i; }, acc);
+    if (active) store_bf16x8(out + t * ldo + col, acc);
   }
 }
 

@@ -5,7 +5,7 @@
 //   2. nvfp4_route_scan_kernel: per expert, the running base of every chunk and the total;
 //      padded row offsets (every expert's rows start on a 128-row boundary, so the blocked
 //      scale layout of the whole dispatched buffer is the concatenation of the experts'
-//      blocked layouts); padding rows marked -1 in the row -> token map.
+//      blocked layouts). The row -> token map is set to -1 (a memset) before the scatter.
 //   3. nvfp4_route_scatter_kernel: the destination row of every pair, in token order within
 //      each expert: chunk base + rank within the chunk (warp match_any for the rank inside a
 //      warp's 32 pairs, per-warp expert counts for the rank across a chunk's warps).
@@ -40,44 +40,62 @@ __global__ void __launch_bounds__(kRouteThreads) nvfp4_route_histogram_kernel(
     hist[static_cast<int64_t>(blockIdx.x) * num_experts + e] = h[e];
 }
 
-// One block of 1024 threads. hist[c][e] becomes the exclusive running count of expert e
-// before chunk c; counts[e] the total; offsets[e] the padded first row of expert e
-// (offsets[num_experts] = padded total). src_rows of padding rows, and of the rows past the
-// padded total up to `capacity`, are set to -1.
-__global__ void __launch_bounds__(1024) nvfp4_route_scan_kernel(
+// One block of kRouteMaxExperts threads, thread e for expert e. hist[c][e] becomes the
+// exclusive running count of expert e before chunk c; counts[e] the total; offsets[e] the
+// padded first row of expert e (offsets[num_experts] = padded total), from a block-wide
+// exclusive scan of the padded counts. (Padding rows are marked -1 in the row -> token map
+// by a memset before the scatter writes the real rows.)
+__global__ void __launch_bounds__(kRouteMaxExperts) nvfp4_route_scan_kernel(
     int32_t* __restrict__ hist, int chunks, int num_experts, int32_t* __restrict__ counts,
-    int32_t* __restrict__ offsets, int32_t* __restrict__ src_rows, int64_t capacity) {
-  __shared__ int32_t padded[kRouteMaxExperts];
-  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
-    int32_t run = 0;
-    for (int c = 0; c < chunks; ++c) {
-      int32_t* slot = &hist[static_cast<int64_t>(c) * num_experts + e];
+    int32_t* __restrict__ offsets) {
+  __shared__ int32_t warp_sums[kRouteMaxExperts / 32];
+  const int e = threadIdx.x;
+  const int lane = e & 31;
+  const int warp = e >> 5;
+  int32_t run = 0;
+  if (e < num_experts) {
+    int c = 0;
+    for (; c + 4 <= chunks; c += 4) {  // four independent loads in flight
+      int32_t* slot = hist + static_cast<int64_t>(c) * num_experts + e;
+      int32_t v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = slot[static_cast<int64_t>(u) * num_experts];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        slot[static_cast<int64_t>(u) * num_experts] = run;
+        run += v[u];
+      }
+    }
+    for (; c < chunks; ++c) {
+      int32_t* slot = hist + static_cast<int64_t>(c) * num_experts + e;
       const int32_t v = *slot;
       *slot = run;
       run += v;
     }
     counts[e] = run;
-    padded[e] = (run + 127) / 128 * 128;
   }
+  const int32_t padded = e < num_experts ? (run + 127) / 128 * 128 : 0;
+  int32_t incl = padded;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int32_t t = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += t;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
   __syncthreads();
-  if (threadIdx.x == 0) {  // exclusive scan over at most 1024 experts
-    int32_t acc = 0;
-    for (int e = 0; e < num_experts; ++e) {
-      offsets[e] = acc;
-      acc += padded[e];
+  if (warp == 0) {
+    int32_t w = lane < static_cast<int>(blockDim.x >> 5) ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int32_t t = __shfl_up_sync(0xffffffffu, w, d);
+      if (lane >= d) w += t;
     }
-    offsets[num_experts] = acc;
+    warp_sums[lane] = w;
   }
   __syncthreads();
-  for (int e = 0; e < num_experts; ++e) {
-    const int32_t first = offsets[e] + counts[e];
-    const int32_t end = offsets[e + 1];
-    for (int32_t r = first + static_cast<int32_t>(threadIdx.x); r < end; r += blockDim.x)
-      src_rows[r] = -1;
-  }
-  for (int64_t r = offsets[num_experts] + static_cast<int64_t>(threadIdx.x); r < capacity;
-       r += blockDim.x)
-    src_rows[r] = -1;
+  incl += warp > 0 ? warp_sums[warp - 1] : 0;
+  if (e < num_experts) offsets[e] = incl - padded;
+  if (e == num_experts - 1) offsets[num_experts] = incl;
 }
 
 __global__ void __launch_bounds__(kRouteThreads) nvfp4_route_scatter_kernel(
@@ -133,6 +151,53 @@ __global__ void __launch_bounds__(kRouteThreads) nvfp4_route_scatter_kernel(
   }
 }
 
+// Weighted fp32 sum, in slot order, of a token's expert output rows at 8 columns per lane:
+// acc[c] += w_j * y[row_j * ld + col + c] for the token's slots j with row_of(pair) >= 0
+// (each product and each sum rounded to fp32). Per 8 slots, the row indices and weights
+// (the same addresses for every lane: one transaction each) and then all 8 row loads are
+// issued before the first add, so a lane keeps 8 x 16 bytes in flight.
+template <typename RowOf>
+__device__ __forceinline__ void combine_slots(int64_t t, int topk, int col, bool active,
+                                              const __half* __restrict__ y, int64_t ld,
+                                              const float* __restrict__ weights, RowOf row_of,
+                                              float* acc) {
+  for (int j0 = 0; j0 < topk; j0 += 8) {
+    const int jn = topk - j0 < 8 ? topk - j0 : 8;
+    int64_t r[8];
+    float w[8];
+    uint4 raw[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = j < jn ? row_of(t * topk + j0 + j) : -1;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      raw[j] = (active && r[j] >= 0) ? __ldg(reinterpret_cast<const uint4*>(y + r[j] * ld + col))
+                                     : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w[j] = j < jn ? __ldg(weights + t * topk + j0 + j) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (r[j] < 0) continue;
+      const uint32_t words[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&words[k]));
+        acc[2 * k] = __fadd_rn(acc[2 * k], __fmul_rn(w[j], f.x));
+        acc[2 * k + 1] = __fadd_rn(acc[2 * k + 1], __fmul_rn(w[j], f.y));
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void store_bf16x8(__nv_bfloat16* dst, const float* acc) {
+  uint32_t packed[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
+    packed[k] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+}
+
 // out[t, :] = bf16( sum_j w[t, j] * y[dest[t*topk + j], :] ), fp32 products and sums in slot
 // order; pairs with dest < 0 contribute nothing. One warp per (token, 256-column chunk):
 // lane l handles 8 consecutive columns (16-byte loads of fp16, 16-byte stores of bf16).
@@ -145,33 +210,32 @@ __global__ void __launch_bounds__(256) nvfp4_moe_combine_kernel(
   const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   for (int64_t task = warp0; task < static_cast<int64_t>(tokens) * chunks; task += nwarps) {
-    const int t = static_cast<int>(task / chunks);
+    const int64_t t = task / chunks;
     const int col = static_cast<int>(task % chunks) * 256 + lane * 8;
-    if (col >= cols) continue;
+    const bool active = col < cols;
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-    for (int j = 0; j < topk; ++j) {
-      const int32_t r = dest[static_cast<int64_t>(t) * topk + j];
-      if (r < 0) continue;
-      const float w = weights[static_cast<int64_t>(t) * topk + j];
-      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(r) * ldy + col));
-      const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+    combine_slots(t, topk, col, active, y, ldy, weights,
+                  [&](int64_t i) -> int64_t { return __ldg(dest + i); }, acc);
+    if (active) store_bf16x8(out + t * ldo + col, acc);
+  }
+}
+
+// Row copy by one warp, 16 bytes per lane per chunk: four chunks' loads are issued before
+// their stores, so a lane has 64 bytes in flight.
+__device__ __forceinline__ void copy_row_chunks(const uint4* __restrict__ src, uint4* dst,
+                                                int chunks, int lane) {
+  for (int c0 = lane; c0 < chunks; c0 += 128) {
+    uint4 v[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&words[i]));
-        acc[2 * i] = __fadd_rn(acc[2 * i], __fmul_rn(w, f.x));
-        acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __fmul_rn(w, f.y));
-      }
+    for (int u = 0; u < 4; ++u) {
+      const int c = c0 + 32 * u;
+      v[u] = c < chunks ? __ldg(src + c) : make_uint4(0u, 0u, 0u, 0u);
     }
-    uint32_t packed[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-      packed[i] = *reinterpret_cast<const uint32_t*>(&b);
-    }
-    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * ldo + col) =
-        make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    for (int u = 0; u < 4; ++u)
+      if (c0 + 32 * u < chunks) dst[c0 + 32 * u] = v[u];
   }
 }
 
@@ -192,7 +256,7 @@ __global__ void __launch_bounds__(256) nvfp4_gather_packed_rows_kernel(
     uint4* d = reinterpret_cast<uint4*>(dst + r * ld_dst);
     if (s >= 0) {
       const uint4* q = reinterpret_cast<const uint4*>(src + static_cast<int64_t>(s) * ld_src);
-      for (int c = lane; c < chunks; c += 32) d[c] = __ldg(q + c);
+      copy_row_chunks(q, d, chunks, lane);
     } else {
       for (int c = lane; c < chunks; c += 32) d[c] = make_uint4(0u, 0u, 0u, 0u);
     }

@@ -893,8 +893,13 @@ NVFP4_API int nvfp4_moe_route(const int32_t* topk_ids, int tokens, int topk, int
     nvfp4_route_histogram_kernel<<<static_cast<unsigned>(chunks), kRouteThreads, 0, s>>>(
         topk_ids, pairs, num_experts, hist);
   }
-  nvfp4_route_scan_kernel<<<1, 1024, 0, s>>>(hist, static_cast<int>(chunks), num_experts, counts,
-                                             offsets, src_rows, rows_capacity);
+  // Every row of the map starts as padding (-1); the scatter writes the real rows.
+  if (src_rows != nullptr) {
+    cudaError_t me = cudaMemsetAsync(src_rows, 0xFF, static_cast<size_t>(rows_capacity) * 4, s);
+    if (me != cudaSuccess) return cuda_fail(me, "routing map reset");
+  }
+  nvfp4_route_scan_kernel<<<1, kRouteMaxExperts, 0, s>>>(hist, static_cast<int>(chunks),
+                                                         num_experts, counts, offsets);
   if (chunks > 0) {
     nvfp4_route_scatter_kernel<<<static_cast<unsigned>(chunks), kRouteThreads, 0, s>>>(
         topk_ids, pairs, topk, num_experts, hist, offsets, dest, src_rows);

@@ -357,13 +357,23 @@ class MoEBlock:
             raise ValueError(f"topk_weights must be [{self.tokens}, {self.topk}]")
 
     def run(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
-            stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+            stream: torch.cuda.Stream | None = None, stage_events: list | None = None) -> torch.Tensor:
         """One block on ``stream``: route, quantise x once per token, dispatch codes and
-        scales, gated GEMM (segments, NVFP4 output), down GEMM (segments), combine."""
+        scales, gated GEMM (segments, NVFP4 output), down GEMM (segments), combine. With
+        ``stage_events`` (a list, eager runs only), (stage name, CUDA event recorded after
+        it) pairs are appended for timing."""
         self._check_inputs(x, topk_ids, topk_weights)
         lib = self._lib
         st = stream or torch.cuda.current_stream(self.device)
         s = st.cuda_stream
+
+        def mark(name):
+            if stage_events is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(st)
+                stage_events.append((name, ev))
+
+        mark("start")
         E, T, K, H, cap = self.num_experts, self.tokens, self.topk, self.hidden, self.capacity
         chk = _native.check
         with torch.cuda.device(self.device):
@@ -371,21 +381,26 @@ class MoEBlock:
                                     self.offsets.data_ptr(), self.dest.data_ptr(),
                                     self.src_rows.data_ptr(), cap, self._route_ws.data_ptr(),
                                     self._route_ws_bytes, s), lib)
+            mark("route")
             chk(lib.nvfp4_quantize(x.data_ptr(), T, H, x.stride(0), _DTYPES[x.dtype],
                                    self.act_scale, self._qx.data_ptr(), self._qx.stride(0),
                                    self._sfx.data_ptr(), s), lib)
+            mark("quantise x")
             chk(lib.nvfp4_moe_gather_quantized(self._qx.data_ptr(), self._qx.stride(0),
                                                self._sfx.data_ptr(), self.src_rows.data_ptr(), cap,
                                                H, self._a.data_ptr(), self._a.stride(0),
                                                self._sfa.data_ptr(), s), lib)
+            mark("dispatch (gather codes + scales)")
             flags = (_native.FLAG_REUSE_DESCRIPTORS if self._uploaded else 0) | self._cta_flags
             _native.grouped_gemm_segments_raw(self._t1, _native.FLAG_GATED | flags,
                                               self.offsets.data_ptr(), self.counts.data_ptr(),
                                               T * K, self._ws1.data_ptr(), self._ws_bytes, s,
                                               self._nvfp4_out)
+            mark("gate/up GEMM + SiLU (NVFP4 output)")
             _native.grouped_gemm_segments_raw(self._t2, flags, self.offsets.data_ptr(),
                                               self.counts.data_ptr(), T * K,
                                               self._ws2.data_ptr(), self._ws_bytes, s)
+            mark("down GEMM")
             self._uploaded = True
             w = topk_weights
             if w.dtype != torch.float32 or not w.is_contiguous():
@@ -395,6 +410,7 @@ class MoEBlock:
             chk(lib.nvfp4_moe_combine(self._y.data_ptr(), self._y.stride(0), self.dest.data_ptr(),
                                       w.data_ptr(), T, K, H, self.out.data_ptr(),
                                       self.out.stride(0), s), lib)
+            mark("combine")
         return self.out
 
     def check_device_errors(self) -> int:
