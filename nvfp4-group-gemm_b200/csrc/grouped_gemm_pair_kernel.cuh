@@ -10,13 +10,15 @@
 //   CTA's TMEM. Per SM this halves the B bytes per MMA compared with a 128 x 256 tile
 //   on one SM, which is what lets the mainloop keep the tensor pipe fed.
 //
-// Synchronisation between the two CTAs (no multicast anywhere):
+// Synchronisation between the two CTAs (no TMA multicast anywhere):
 //   full[s]   even CTA; one arrive.expect_tx (both CTAs' bytes) by its producer, and
 //             every load of both CTAs completes its bytes there (cta_group::2 TMA)
-//   empty[s]  each CTA; the even CTA's MMA commit frees its own, and its producer
-//             forwards each release to the odd CTA with a remote arrive
-//   accf[a]   each CTA; MMA commit on the even CTA, forwarded to the odd CTA by the
-//             even CTA's epilogue
+//   empty[s]  each CTA; the even CTA's MMA commit arrives on both CTAs' barriers
+//             (tcgen05.commit .multicast::cluster, mask 0x3). Forwarding the release
+//             to the odd CTA from the even CTA's producer instead left the odd CTA's
+//             refill behind that producer's wake-up: cfg2's MMA issuer waited for data
+//             46 % of each k-tile.
+//   accf[a]   each CTA; the same two-CTA commit
 //   acce[a]   even CTA; the 8 epilogue warps of both CTAs release accumulators there
 // All waits are bounded (same timeout/abort scheme as the single-CTA kernel); a
 // final cluster barrier keeps both CTAs alive until every cross-CTA access is done.
@@ -187,13 +189,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             break;
           }
           const uint32_t full_leader = ptx::mapa_shared(ptx::smem_u32(&full_bar[stage]), 0);
-          if (leader) {
-            // The MMAs that read this stage have finished: let the odd CTA refill its
-            // half too (from the second use of the stage on; the first use is free).
-            if (issued >= static_cast<uint32_t>(STAGES))
-              ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&empty_bar[stage]), 1));
-            ptx::mbar_arrive_expect_tx(&full_bar[stage], Cfg::kPairTxBytes);
-          }
+          // Both CTAs' empty barriers are arrived by the MMAs' commit, so the odd CTA may
+          // load its half before the leader has armed the full barrier with both halves'
+          // byte count: its completed bytes then wait in the barrier's transaction count,
+          // and the phase cannot complete before the leader's arrival.
+          if (leader) ptx::mbar_arrive_expect_tx(&full_bar[stage], Cfg::kPairTxBytes);
           uint8_t* sA = stage_base + stage * Cfg::kStageBytes;
           uint8_t* sB = sA + Cfg::kABytes;
           uint8_t* sSFA = sB + Cfg::kBBytes;
@@ -290,14 +290,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                                    sfa_t + 4 * kb, sfb_t + Cfg::kSfbColsPerMma * kb,
                                    (kt | kb) != 0 ? 1u : 0u);
           }
-          ptx::tcgen05_commit_pair(&empty_bar[stage]);
+          ptx::tcgen05_commit_pair_both(&empty_bar[stage]);  // frees the stage in both CTAs
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        ptx::tcgen05_commit_pair(&accf_bar[acc]);
+        ptx::tcgen05_commit_pair_both(&accf_bar[acc]);  // both CTAs' epilogues may start
       }
       ptx::tcgen05_commit_pair(drain_bar);
       const uint64_t t0 = ptx::globaltimer_ns();
@@ -341,10 +341,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         break;
       }
       full_parity ^= 1u << acc;
-      if (leader && warp == kEpilogueWarp0 && lane == 0) {
-        // Accumulators of both CTAs are complete: tell the odd CTA's epilogue.
-        ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&accf_bar[acc]), 1));
-      }
       ptx::tcgen05_fence_after_sync();
       const uint32_t release_bar = ptx::mapa_shared(ptx::smem_u32(&acce_bar[acc ^ 1]), 0);
       const int first_box = (acc == 0) ? kBoxes - 1 : 0;

@@ -399,6 +399,15 @@ __device__ __forceinline__ void tcgen05_commit_pair(uint64_t* bar) {
                    smem_u32(bar))
                : "memory");
 }
+// The same commit arriving on the barrier at this shared-memory offset in every CTA of
+// `cta_mask` (both CTAs of a pair: 0x3), so each CTA learns of the MMAs' completion directly.
+__device__ __forceinline__ void tcgen05_commit_pair_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(static_cast<uint16_t>(0x3))
+      : "memory");
+}
 
 }  // namespace ptx
 }  // namespace nvfp4
