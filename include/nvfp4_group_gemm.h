@@ -30,7 +30,10 @@ extern "C" {
 #define NVFP4_API
 #endif
 
-#define NVFP4_ABI_VERSION 1
+/* 2: segment launches (nvfp4_grouped_gemm_segments, nvfp4_segment_output), the
+ * expert-parallel exchange (nvfp4_ep_*), NVFP4_FLAG_SPLIT_K, a segment-row table in the
+ * workspace (nvfp4_workspace_size grew by 4 bytes per group, rounded up to 128). */
+#define NVFP4_ABI_VERSION 2
 
 typedef enum nvfp4_status {
   NVFP4_OK = 0,

@@ -70,6 +70,7 @@ EXPORTED_SYMBOLS = (
     "nvfp4_ep_combine",
 )
 
+ABI_VERSION = 2   # NVFP4_ABI_VERSION
 EP_MAX_RANKS = 8  # NVFP4_EP_MAX_RANKS
 EP_ERR_CAPACITY = 1 << 0  # an expert segment did not fit the owner's receive slab
 
@@ -195,6 +196,10 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
                                  ctypes.c_int64, ctypes.c_uint)
         lib.nvfp4_abi_version.argtypes = []
         lib.nvfp4_abi_version.restype = i32
+        found = int(lib.nvfp4_abi_version())
+        if found != ABI_VERSION:
+            raise ImportError(f"native library {p} has ABI version {found}, this package needs "
+                              f"{ABI_VERSION}; rebuild it with `python __graft_entry__.py build`")
         lib.nvfp4_strerror.argtypes = [i32]
         lib.nvfp4_strerror.restype = ctypes.c_char_p
         lib.nvfp4_last_error_detail.argtypes = []

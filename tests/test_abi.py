@@ -43,7 +43,9 @@ def test_struct_layout_matches_header(pkg):
 
 def test_version_and_strings(pkg):
     lib = pkg.load_library()
-    assert lib.nvfp4_abi_version() == 1
+    assert lib.nvfp4_abi_version() == pkg._native.ABI_VERSION
+    hdr = open(os.path.join(ROOT, "include", "nvfp4_group_gemm.h")).read()
+    assert f"#define NVFP4_ABI_VERSION {pkg._native.ABI_VERSION}" in hdr
     assert lib.nvfp4_strerror(0) == b"success"
     assert b"timed out" in lib.nvfp4_strerror(7)
     assert lib.nvfp4_strerror(999) == b"unknown status"
