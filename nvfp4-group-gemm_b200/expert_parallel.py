@@ -332,6 +332,24 @@ class EPMoEBlock:
         mark("combine")
         return self.out
 
+    def capture(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+                warmup: int = 1) -> torch.cuda.CUDAGraph:
+        """Record one call over these input tensors into a CUDA graph, NCCL barriers
+        included (after ``warmup`` eager calls, which upload the GEMMs' descriptors). Every
+        rank of the group must capture, and replay in the same order; ``graph.replay()``
+        recomputes ``self.out`` from the tensors' current contents."""
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(max(warmup, 1)):
+                self.run(x, topk_ids, topk_weights)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            self.run(x, topk_ids, topk_weights)
+        return graph
+
     def check_errors(self) -> int:
         """Synchronise; returns the exchange's error bits (EP_ERR_CAPACITY) and raises if a
         GEMM reported a device error."""

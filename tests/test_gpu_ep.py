@@ -1,12 +1,15 @@
 """Expert-parallel MoE block on 2 GPUs (EPMoEBlock: routed NVFP4 rows pushed into the owners'
-receive slabs over NVLink, expert GEMMs over device-side segments, results pulled back and
-combined). Skipped with fewer than 2 GPUs.
+receive slabs over NVLink, expert GEMMs over device-side segments, each result row stored
+back into its token's rank by the down GEMM's epilogue, then combined). Skipped with fewer
+than 2 GPUs.
 
 Each rank checks, for its own tokens: the placement (count matrix, segments, every pair's
 row in its owner's slab) against the CPU oracle of the exchange, and the block's output
 bit for bit against the single-GPU MoEBlock run over the same tokens with all experts (the
 same rows meet the same weights in both; tiles forced to single CTAs so both pick the same
-kernels). Two calls with different tokens and routings check the buffers' reuse.
+kernels). Two calls with different tokens and routings check the buffers' reuse; a CUDA
+graph of a whole call (NCCL barriers included), replayed on new inputs, must equal an
+eager call.
 """
 from __future__ import annotations
 
@@ -94,6 +97,23 @@ def _worker(rank, world, port, cta, q):
                 out_equal=bool(torch.equal(out.view(torch.int16), ref.view(torch.int16))),
                 rel=float((out.float() - ref.float()).norm() / ref.float().norm()),
                 finite=bool(torch.isfinite(out.float()).all())))
+        # CUDA graph of the whole exchange (NCCL barriers included), replayed on new inputs
+        # written into the captured tensors: identical to an eager call.
+        x, ids, wts = _inputs(77 + rank, dev)
+        graph = ep.capture(x, ids, wts)
+        x2, ids2, wts2 = _inputs(5000 + rank, dev)
+        x.copy_(x2)
+        ids.copy_(ids2)
+        wts.copy_(wts2)
+        graph.replay()
+        torch.cuda.synchronize()
+        replayed = ep.out.clone()
+        eager = ep.run(x, ids, wts)
+        torch.cuda.synchronize()
+        checks.append(dict(graph_equal=bool(torch.equal(replayed.view(torch.int16),
+                                                        eager.view(torch.int16))),
+                           err=ep.check_errors()))
+        del graph
         q.put((rank, checks))
         dist.barrier(device_ids=[rank])
         del ep
@@ -123,7 +143,9 @@ def test_ep_moe_block_two_gpus(cta):
     for rank in range(world):
         res = results[rank]
         assert isinstance(res, list), res
-        for call, c in enumerate(res):
+        *calls, graph = res
+        assert graph["graph_equal"] and graph["err"] == 0, (rank, graph)
+        for call, c in enumerate(calls):
             assert c["err"] == 0 and not c["dropped"], (rank, call, c)
             assert c["mat"] and c["seg"] and c["send"] and c["rows"], (rank, call, c)
             assert c["finite"], (rank, call, c)
