@@ -378,6 +378,20 @@ def run_moe_ep(args, world):
     blk.run(x, ids, wts, stage_events=evs)
     torch.cuda.synchronize(dev)
     stage_us = {n: a.elapsed_time(b) * 1e3 for (_, a), (n, b) in zip(evs[:-1], evs[1:])}
+    # The same call captured in a CUDA graph (NCCL barriers included) and replayed.
+    graph = blk.capture(x, ids, wts)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    dist.barrier(device_ids=[local_rank])
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    graph_ms = float(t.item())
+    del graph
     err = blk.check_errors()
     pairs = torch.tensor([int((ids >= 0).sum().item())], dtype=torch.float64, device=dev)
     dist.all_reduce(pairs)
@@ -408,6 +422,9 @@ def run_moe_ep(args, world):
                                  "scale layout 1, segment set-up + GEMM x2, combine 1 (+3 NCCL)",
         "exchange_error_bits": err,
         "stage_us_rank0": stage_us,
+        "cuda_graph": {"ms_per_step": graph_ms, "value": flops / (graph_ms * 1e-3) / 1e12,
+                       "unit": "TFLOP/s", "what": "EPMoEBlock.capture, one call per replay, max "
+                                                  "over ranks"},
         "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
                      "frac": tf / peak, "peak_source": f"{kind}: {world} x 4 x bf16 (sustained)",
                      "traffic": None},
