@@ -64,6 +64,10 @@ def parse_args():
                          "combine) at cfg5's shape")
     ap.add_argument("--experts", default=None,
                     help="START:STOP - run only this contiguous expert shard of the configuration")
+    ap.add_argument("--shard-experts", action="store_true",
+                    help="N > 1: rank r runs expert_shard(G, N, r) of ONE configuration (strong "
+                         "scaling; cfg5 = 256/N experts per GPU); default: every rank its own "
+                         "full configuration (weak scaling)")
     ap.add_argument("--tokens", type=int, default=32768,
                     help="--op moe: tokens per step (32768 = cfg5's 262144 routed rows; 64 = a "
                          "decode step)")
@@ -204,6 +208,66 @@ def run_reference(args):
         "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def run_all_configs(args):
+    """BASELINE's headline form: microseconds per call of configs 1-5 through the prepared
+    launch (one GPU, device-resident inputs, a 256 MiB L2 flush before each call of a
+    configuration whose inputs fit in L2), their geometric mean, and each configuration's
+    fraction of its roofline. One JSON line."""
+    import math
+
+    import torch
+
+    import submission
+
+    pkg = submission.load_package()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks, kind = load_peaks()
+    tensor_peak = FP4_PER_BF16 * float(peaks["bf16_tflops"])
+    hbm_peak = float(peaks["hbm_gbs"])
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    per = {}
+    for cfg in ("cfg1", "cfg2", "cfg3", "cfg4", "cfg5"):
+        prob = pkg.workloads.make_config(cfg, seed=0, device=dev)
+        plan = pkg.GroupedGemmPlan(prob.a, prob.b, prob.sfa, prob.sfb, prob.c,
+                                   prob.problem_sizes(), alpha=prob.alpha, b2=prob.b2,
+                                   sfb2=prob.sfb2, alpha2=prob.alpha2)
+        for _ in range(max(args.warmup, 3)):
+            plan.run()
+        torch.cuda.synchronize(dev)
+        small = prob.input_bytes() < L2_BYTES
+        times = []
+        for _ in range(args.steps):
+            if small:
+                flush.fill_(1)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            plan.run()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            times.append(e0.elapsed_time(e1) * 1e3)
+        us = sorted(times)[len(times) // 2]
+        flops, nbytes = prob.flops(), prob.algorithmic_bytes()
+        bound = "tensor" if flops / nbytes >= tensor_peak * 1e12 / (hbm_peak * 1e9) else "hbm"
+        frac = (flops / (us * 1e-6) / 1e12 / tensor_peak if bound == "tensor"
+                else nbytes / (us * 1e-6) / 1e9 / hbm_peak)
+        per[cfg] = {"us_per_call": us, "tflops": flops / (us * 1e-6) / 1e12, "bound": bound,
+                    "frac_of_roofline": frac, "errors": plan.check_device_errors()}
+        del plan, prob
+        torch.cuda.empty_cache()
+    geo = math.exp(sum(math.log(v["us_per_call"]) for v in per.values()) / len(per))
+    print(json.dumps({
+        "metric": "us/call (geomean of configs 1-5)", "value": geo, "unit": "us",
+        "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e2m1xe4m3->f32->f16", "data": "synthetic (seeded)",
+        "config": {"workload": "cfg1..cfg5", "timing": "median of per-call events; L2 flushed "
+                   "before each call when a configuration's inputs fit in L2"},
+        "per_config": per, "peak_source": f"{kind}: burst bf16 x 4 / HBM copy",
+    }), flush=True)
 
 
 def run_quantize(args):
@@ -593,6 +657,8 @@ def main():
         return run_quantize(args)
     if args.op == "moe":
         return run_moe(args)
+    if args.config == "all" and args.impl != "reference":
+        return run_all_configs(args)
     if args.impl == "reference":
         return run_reference(args)
 
@@ -613,11 +679,19 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
 
     # Each rank owns its own experts (seed = rank): weak scaling, no data-path collective.
+    # With --shard-experts the ranks split one configuration's experts (strong scaling).
     shard = None
+    seed = rank
+    strong = args.shard_experts and world > 1 and not args.experts
     if args.experts:
         start, stop = (int(x) for x in args.experts.split(":"))
         shard = slice(start, stop)
-    prob = pkg.workloads.make_config(args.config, seed=rank, device=dev, experts=shard)
+    elif strong:
+        G = len(pkg.workloads.config_rows(args.config)[0])
+        sh = pkg.expert_parallel.expert_shard(G, world, rank)
+        shard = slice(sh.start, sh.stop)
+        seed = 0  # every rank takes its slice of the same configuration
+    prob = pkg.workloads.make_config(args.config, seed=seed, device=dev, experts=shard)
     stream = torch.cuda.current_stream(dev)
     sizes = prob.problem_sizes()
 
@@ -754,7 +828,12 @@ def main():
                                                         - sum(prob.m) * prob.n * 2),
                   "what": "GEMM + NCCL all-gather of every expert's fp16 output to every rank"}
     flops_rank = prob.flops()
-    value = flops_rank * world / (ms_per_step * 1e-3) / 1e12
+    flops_job = flops_rank * world  # weak scaling: every rank the same amount of work
+    if strong:
+        t = torch.tensor([flops_rank], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        flops_job = float(t.item())
+    value = flops_job / (ms_per_step * 1e-3) / 1e12
 
     # ---------------------------------------------------------------- CUDA graph
     # The same calls recorded back to back in one CUDA graph and replayed: no per-call host
@@ -906,7 +985,7 @@ def main():
         "us_per_call": ms_per_step * 1e3,
         "host_us_per_call": host_us,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if strong else "weak",
         "vs_baseline": None,
         "dtype": "e2m1xe4m3->f32->f16",
         "data": "synthetic (seeded; e2m1 codes uniform over 16, E4M3 scales 2^U{-4..3})",
@@ -918,12 +997,14 @@ def main():
                    "l2": ("inputs smaller than L2 (126 MB): 256 MiB flush before every timed "
                           "call, outside its events" if flush_l2 else
                           "inputs larger than L2 (126 MB); no flush"),
-                   "parallelism": f"ep{world} (experts sharded, no data-path collective)",
+                   "parallelism": f"ep{world} (" + ("experts of one configuration split over "
+                                                     "the ranks" if strong else "every rank its own "
+                                                     "experts") + ", no data-path collective)",
                    **({"split_k": True} if args.split_k else {})},
         "gpu_launches": args.steps,  # one persistent GEMM kernel per timed call (descriptors reused)
         "api": "GroupedGemmPlan.run (value, burst); custom_kernel(data) (e2e)",
         "device_error_bits": errors,
-        "e2e": {"value": flops_rank * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+        "e2e": {"value": flops_job / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "custom_kernel(data) with pinned-host copies of inputs and outputs"},
         "cuda_graph": graph_info,
