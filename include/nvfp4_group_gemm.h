@@ -167,6 +167,22 @@ NVFP4_API int nvfp4_grouped_gemm_segments(const nvfp4_group* groups, int num_gro
                                           size_t workspace_bytes, void* stream);
 
 /*
+ * Prepared launches: nvfp4_plan_create validates a group table, uploads its descriptors into
+ * `workspace` on `stream` and keeps the launch (kernel, grid, parameters); each
+ * nvfp4_plan_launch then only launches the kernel (host work of a plain launch with
+ * NVFP4_FLAG_REUSE_DESCRIPTORS, minus the per-group pass over the table). The tensors,
+ * the workspace and the device must stay as they were when the plan was made; launches of
+ * one plan share its workspace and must be ordered on the GPU. Neither REUSE_DESCRIPTORS nor
+ * SPLIT_K may be passed to nvfp4_plan_create. nvfp4_plan_launch is CUDA-graph capturable.
+ */
+typedef struct nvfp4_plan nvfp4_plan;
+NVFP4_API int nvfp4_plan_create(const nvfp4_group* groups, int num_groups, unsigned int flags,
+                                void* workspace, size_t workspace_bytes, void* stream,
+                                nvfp4_plan** plan);
+NVFP4_API int nvfp4_plan_launch(const nvfp4_plan* plan, void* stream);
+NVFP4_API void nvfp4_plan_destroy(nvfp4_plan* plan);
+
+/*
  * Extra workspace for split-K: with NVFP4_FLAG_SPLIT_K and workspace_bytes at least
  * nvfp4_workspace_size(num_groups) rounded up to 256, plus this, single-CTA launches split
  * the K loop of the tiles that would otherwise run in a last, partly idle wave (all tiles,

@@ -58,6 +58,9 @@ EXPORTED_SYMBOLS = (
     "nvfp4_workspace_check",
     "nvfp4_grouped_gemm_noalloc",
     "nvfp4_grouped_gemm_segments",
+    "nvfp4_plan_create",
+    "nvfp4_plan_launch",
+    "nvfp4_plan_destroy",
     "nvfp4_quantize",
     "nvfp4_quantize_rows",
     "nvfp4_moe_route_workspace_size",
@@ -219,6 +222,12 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_grouped_gemm_segments.argtypes = [vp, i32, u32, vp, vp, i64,
                                                     ctypes.POINTER(SegmentOutput), vp, sz, vp]
         lib.nvfp4_grouped_gemm_segments.restype = i32
+        lib.nvfp4_plan_create.argtypes = [vp, i32, u32, vp, sz, vp, ctypes.POINTER(vp)]
+        lib.nvfp4_plan_create.restype = i32
+        lib.nvfp4_plan_launch.argtypes = [vp, vp]
+        lib.nvfp4_plan_launch.restype = i32
+        lib.nvfp4_plan_destroy.argtypes = [vp]
+        lib.nvfp4_plan_destroy.restype = None
         lib.nvfp4_quantize.argtypes = [vp, i32, i32, i64, i32, ctypes.c_float, vp, i64, vp, vp]
         lib.nvfp4_quantize.restype = i32
         lib.nvfp4_quantize_rows.argtypes = [vp, i32, i32, i64, i32, ctypes.c_float, vp, i32, vp,

@@ -462,6 +462,33 @@ cudaError_t launch_pair(const GemmParams& gp, int clusters, cudaStream_t stream)
                      Cfg::kSmemBytes, 2, stream);
 }
 
+// Everything a launch needs once descriptors are in the workspace: the kernel variant, its
+// grid and its parameters. grouped_gemm_impl builds one per call; a prepared plan
+// (nvfp4_plan_create) keeps it and replays only the launch.
+enum class KernelKind : int {
+  kSwap, kPair, kPairGated, kSingleGated, kSingle128, kStream, kSingle256
+};
+struct LaunchSpec {
+  GemmParams gp;
+  KernelKind kind;
+  int grid;  // CTAs (single-CTA and swap kernels) or clusters (pair kernels)
+};
+
+cudaError_t run_spec(const LaunchSpec& sp, cudaStream_t s) {
+  switch (sp.kind) {
+    case KernelKind::kSwap:
+      return launch_gemm(nvfp4_grouped_gemm_swap_kernel<kSwapStages>, sp.gp, sp.grid,
+                         Kswap::kSmemBytes, 1, s);
+    case KernelKind::kPair: return launch_pair<false>(sp.gp, sp.grid, s);
+    case KernelKind::kPairGated: return launch_pair<true>(sp.gp, sp.grid, s);
+    case KernelKind::kSingleGated: return launch_single<256, true, 3>(sp.gp, sp.grid, s);
+    case KernelKind::kSingle128: return launch_single<128, false, 5>(sp.gp, sp.grid, s);
+    case KernelKind::kStream: return launch_single<256, false, 4, true>(sp.gp, sp.grid, s);
+    case KernelKind::kSingle256: return launch_single<256, false, 3>(sp.gp, sp.grid, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
 // Row segments of a segment launch (nvfp4_grouped_gemm_segments): device arrays of
 // per-group first rows and row counts, and the host's estimate of their total.
 struct SegmentArgs {
@@ -477,7 +504,7 @@ struct SegmentArgs {
 // m is the slab's row count and the rows it multiplies are read on the device.
 int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int flags, uint8_t* ws,
                       size_t ws_bytes, cudaStream_t s, GroupDev* rec, bool use_cache,
-                      const SegmentArgs* seg = nullptr) {
+                      const SegmentArgs* seg = nullptr, LaunchSpec* prepared = nullptr) {
   const bool gated = (flags & NVFP4_FLAG_GATED) != 0;
   // Tile shape: CTA pairs (256-row tiles) when the groups are tall enough to fill
   // them, single CTAs (128-row tiles) otherwise; 256 MMA columns unless asked otherwise.
@@ -664,25 +691,31 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
                                                                   split_parts);
   gp.split_counters = reinterpret_cast<int32_t*>(ws + ws_split_offset(num_groups));
   gp.split_partials = reinterpret_cast<float*>(ws + ws_split_offset(num_groups) + kSplitCounterBytes);
+  LaunchSpec sp;
+  sp.gp = gp;
   if (swap) {
-    const int grid = static_cast<int>(std::min<int64_t>(total_tiles, ds.num_sms));
-    e = launch_gemm(nvfp4_grouped_gemm_swap_kernel<kSwapStages>, gp, grid, Kswap::kSmemBytes, 1,
-                    s);
+    sp.kind = KernelKind::kSwap;
+    sp.grid = static_cast<int>(std::min<int64_t>(total_tiles, ds.num_sms));
   } else if (pair) {
     const int max_clusters = gated ? ds.pair_clusters_gated : ds.pair_clusters;
-    const int clusters = static_cast<int>(std::min<int64_t>(total_tiles, max_clusters));
-    e = gated ? launch_pair<true>(gp, clusters, s) : launch_pair<false>(gp, clusters, s);
+    sp.kind = gated ? KernelKind::kPairGated : KernelKind::kPair;
+    sp.grid = static_cast<int>(std::min<int64_t>(total_tiles, max_clusters));
   } else {
-    const int grid = static_cast<int>(std::min<int64_t>(gp.total_units, ds.num_sms));
+    sp.grid = static_cast<int>(std::min<int64_t>(gp.total_units, ds.num_sms));
     if (gated)
-      e = launch_single<256, true, 3>(gp, grid, s);
+      sp.kind = KernelKind::kSingleGated;
     else if (mma_n == 128)
-      e = launch_single<128, false, 5>(gp, grid, s);
+      sp.kind = KernelKind::kSingle128;
     else if (rows <= static_cast<int64_t>(kStreamMaxAvgRows) * active && gp.row_dest == nullptr)
-      e = launch_single<256, false, 4, true>(gp, grid, s);  // weight-streaming shapes
+      sp.kind = KernelKind::kStream;  // weight-streaming shapes
     else
-      e = launch_single<256, false, 3>(gp, grid, s);
+      sp.kind = KernelKind::kSingle256;
   }
+  if (prepared != nullptr) {  // a plan: descriptors uploaded, the launch is replayed later
+    *prepared = sp;
+    return NVFP4_OK;
+  }
+  e = run_spec(sp, s);
   if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
   return NVFP4_OK;
 }
@@ -1130,6 +1163,64 @@ NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsi
                            workspace_bytes, static_cast<cudaStream_t>(stream), rec.data(),
                            /*use_cache=*/true);
 }
+
+}  // extern "C"
+
+struct nvfp4_plan {
+  LaunchSpec spec;
+  int device;
+};
+
+extern "C" {
+
+NVFP4_API int nvfp4_plan_create(const nvfp4_group* groups, int num_groups, unsigned int flags,
+                                void* workspace, size_t workspace_bytes, void* stream,
+                                nvfp4_plan** plan) {
+  g_last_error.clear();
+  if (plan == nullptr) return fail(NVFP4_ERR_INVALID_ARGUMENT, "plan is NULL");
+  *plan = nullptr;
+  if (flags & (NVFP4_FLAG_REUSE_DESCRIPTORS | NVFP4_FLAG_SPLIT_K))
+    return fail(NVFP4_ERR_INVALID_ARGUMENT,
+                "a plan uploads its own descriptors and does not split K");
+  int st = check_common_args(groups, num_groups, flags);
+  if (st != NVFP4_OK) return st;
+  if (num_groups == 0) return fail(NVFP4_ERR_BAD_SHAPE, "a plan needs at least one group");
+  if (workspace == nullptr) return fail(NVFP4_ERR_WORKSPACE, "workspace is NULL");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(NVFP4_ERR_WORKSPACE, "workspace not 256-byte aligned");
+  if (workspace_bytes < ws_total_bytes(num_groups))
+    return fail(NVFP4_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes,
+                ws_total_bytes(num_groups));
+  std::vector<GroupDev> rec(static_cast<size_t>(num_groups));
+  nvfp4_plan* p = new nvfp4_plan();
+  p->spec.grid = 0;  // no tiles at all: launching does nothing
+  st = grouped_gemm_impl(groups, num_groups, flags, static_cast<uint8_t*>(workspace),
+                         workspace_bytes, static_cast<cudaStream_t>(stream), rec.data(),
+                         /*use_cache=*/true, nullptr, &p->spec);
+  cudaError_t e = cudaSuccess;
+  if (st == NVFP4_OK && (e = cudaGetDevice(&p->device)) != cudaSuccess)
+    st = cuda_fail(e, "cudaGetDevice");
+  if (st != NVFP4_OK) {
+    delete p;
+    return st;
+  }
+  *plan = p;
+  return NVFP4_OK;
+}
+
+NVFP4_API int nvfp4_plan_launch(const nvfp4_plan* plan, void* stream) {
+  if (plan == nullptr) return fail(NVFP4_ERR_INVALID_ARGUMENT, "plan is NULL");
+  if (plan->spec.grid == 0) return NVFP4_OK;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->device)
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "plan made on device %d, current device %d",
+                plan->device, dev);
+  const cudaError_t e = run_spec(plan->spec, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
+  return NVFP4_OK;
+}
+
+NVFP4_API void nvfp4_plan_destroy(nvfp4_plan* plan) { delete plan; }
 
 NVFP4_API int nvfp4_grouped_gemm_segments(const nvfp4_group* groups, int num_groups,
                                           unsigned int flags, const int32_t* seg_offsets,

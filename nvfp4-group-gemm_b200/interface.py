@@ -25,6 +25,7 @@ There is no CPU or library fallback.
 """
 from __future__ import annotations
 
+import ctypes
 import threading
 from typing import Sequence
 
@@ -40,6 +41,15 @@ output_t = list
 _FP4_DTYPES = tuple(
     d for d in (getattr(torch, "float4_e2m1fn_x2", None), torch.uint8, torch.int8) if d is not None
 )
+
+
+def _current_raw_stream(device_index: int) -> int:
+    """Handle of the current stream of a device (torch's C accessor when it exists: it
+    skips building a Stream object, which costs a few microseconds per call)."""
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return raw(device_index)
+    return torch.cuda.current_stream(device_index).cuda_stream
 
 
 # ----------------------------------------------------------------------------
@@ -465,12 +475,45 @@ class GroupedGemmPlan:
         self._ws = torch.zeros(self._nbytes, dtype=torch.uint8, device=self.device)
         self._lib = _native.load_library()
         self._uploaded = False
+        # The first run makes a native plan (validates, uploads the descriptors, keeps the
+        # launch); later runs replay only the kernel launch. Split-K launches keep the plain
+        # entry point.
+        self._native_plan = None
+        self._use_native_plan = not split_k
+        self._launch = self._lib.nvfp4_plan_launch
+
+    def __del__(self):
+        plan = getattr(self, "_native_plan", None)
+        if plan is not None:
+            self._lib.nvfp4_plan_destroy(plan)
+            self._native_plan = None
 
     def run(self, stream: torch.cuda.Stream | None = None) -> list:
         """Launch on ``stream`` (default: the current stream); returns the outputs."""
         if self._table is None:
             return self.outputs
+        idx = self.device.index
+        plan = self._native_plan
+        if plan is not None and torch.cuda.current_device() == idx:
+            # Fast path: one native call that only launches the kernel.
+            s = stream.cuda_stream if stream is not None else _current_raw_stream(idx)
+            st = self._launch(plan, s)
+            if st:
+                _native.check(st, self._lib)
+            return self.outputs
         s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        if self._use_native_plan:
+            if plan is None:
+                out = ctypes.c_void_p()
+                with torch.cuda.device(self.device):
+                    _native.check(self._lib.nvfp4_plan_create(
+                        self._table.ctypes.data, int(self._table.shape[0]), self._flags,
+                        self._ws.data_ptr(), self._nbytes, s, ctypes.byref(out)), self._lib)
+                self._native_plan = plan = out.value
+            with torch.cuda.device(self.device):
+                _native.check(self._launch(plan, s), self._lib)
+            self._uploaded = True
+            return self.outputs
         flags = self._flags | (_native.FLAG_REUSE_DESCRIPTORS if self._uploaded else 0)
         args = (self._table.ctypes.data, int(self._table.shape[0]), flags, self._ws.data_ptr(),
                 self._nbytes, s)

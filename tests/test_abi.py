@@ -207,3 +207,29 @@ def test_split_scratch_constant_matches_header(pkg):
     a, b, c = (int(x) for x in m.groups())
     assert a + b * c == pkg._native.SPLIT_SCRATCH_BYTES
     assert pkg._native.workspace_size_with_split(8) % 256 == 0
+
+
+@pytest.mark.parametrize("case,flags,status", [
+    ("reuse_flag", 0x8, 1),      # a plan uploads its own descriptors
+    ("split_flag", 0x100, 1),
+    ("no_groups", 0, 2),
+    ("bad_k", 0, 2),
+    ("misaligned_ws", 0, 5),
+    ("null_out", 0, 1),
+])
+def test_plan_create_validation(pkg, case, flags, status):
+    N = pkg._native
+    lib = pkg.load_library()
+    t = _table(N, k=100 if case == "bad_k" else 512)
+    ws = ctypes.create_string_buffer(N.workspace_size(1) + 512)
+    ws_ptr = (ctypes.addressof(ws) + 255) & ~255
+    if case == "misaligned_ws":
+        ws_ptr += 16
+    out = ctypes.c_void_p()
+    st = lib.nvfp4_plan_create(t.ctypes.data, 0 if case == "no_groups" else 1, flags, ws_ptr,
+                               N.workspace_size(1), None,
+                               None if case == "null_out" else ctypes.byref(out))
+    assert st == status, lib.nvfp4_last_error_detail()
+    assert out.value is None
+    assert lib.nvfp4_plan_launch(None, None) == 1
+    lib.nvfp4_plan_destroy(None)  # destroying nothing is allowed
