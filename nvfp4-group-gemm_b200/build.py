@@ -14,9 +14,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB_NAME = "libnvfp4_group_gemm.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
-SOURCES = ["nvfp4_group_gemm.cu"]
+SOURCES = ["nvfp4_group_gemm.cu", "moe_host.cu", "ep_host.cu"]
 HEADERS = ["grouped_gemm_kernel.cuh", "grouped_gemm_pair_kernel.cuh", "grouped_gemm_swap_kernel.cuh",
            "quantize_kernel.cuh", "moe_kernels.cuh", "nvfp4_quant_math.cuh", "ep_kernels.cuh",
+           "row_ops.cuh", "host_common.cuh",
            "nvfp4_types.cuh", "sm100_ptx.cuh"]
 PUBLIC_HEADER = os.path.join(os.path.dirname(HERE), "include", "nvfp4_group_gemm.h")
 

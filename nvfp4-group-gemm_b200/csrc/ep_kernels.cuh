@@ -26,7 +26,7 @@
 
 #include <cstdint>
 
-#include "moe_kernels.cuh"
+#include "row_ops.cuh"
 #include "nvfp4_quant_math.cuh"
 
 namespace nvfp4 {

@@ -18,11 +18,9 @@
 
 #include "../../include/nvfp4_group_gemm.h"
 #include "grouped_gemm_kernel.cuh"
+#include "host_common.cuh"
 #include "grouped_gemm_pair_kernel.cuh"
 #include "grouped_gemm_swap_kernel.cuh"
-#include "ep_kernels.cuh"
-#include "moe_kernels.cuh"
-#include "quantize_kernel.cuh"
 #include "nvfp4_types.cuh"
 #include "sm100_ptx.cuh"
 
@@ -165,8 +163,6 @@ __global__ void __launch_bounds__(256) nvfp4_sf_to_blocked_kernel(const uint8_t*
 // ============================================================================
 // Host side
 // ============================================================================
-namespace {
-
 thread_local std::string g_last_error;
 
 int fail(int code, const char* fmt, ...) {
@@ -183,6 +179,8 @@ int cuda_fail(cudaError_t e, const char* what) {
   return fail(NVFP4_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
+namespace {
+
 // Kernel variants. Single CTA: <MMA N, gated, stages>; CTA pair: <gated, stages>.
 using Kn128 = GemmConfig<128, false, 5>;
 using Kn256 = GemmConfig<256, false, 3>;
@@ -194,16 +192,6 @@ using KpairGated = PairConfig<true, kPairStages>;
 constexpr int kSwapStages = 7;
 using Kswap = SwapConfig<kSwapStages>;
 
-constexpr int kMaxDevices = 64;
-
-struct DeviceState {
-  std::once_flag once;
-  int status = NVFP4_OK;
-  int num_sms = 0;
-  int pair_clusters = 0;        // CTA pairs that can be resident at once (plain pair kernel)
-  int pair_clusters_gated = 0;  // same for the gated pair kernel
-  std::string detail;
-};
 DeviceState g_dev[kMaxDevices];
 
 int max_pair_clusters(const void* fn, int smem, int num_sms) {
@@ -274,6 +262,22 @@ void init_device(int dev, DeviceState& st) {
       reinterpret_cast<const void*>(&nvfp4_grouped_gemm_pair_kernel<true, kPairStages>),
       KpairGated::kSmemBytes, st.num_sms);
 }
+
+}  // namespace
+
+int current_device_state(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_INVALID_ARGUMENT, "device %d", dev);
+  DeviceState& ds = g_dev[dev];
+  std::call_once(ds.once, init_device, dev, std::ref(ds));
+  if (ds.status != NVFP4_OK) return fail(ds.status, "%s", ds.detail.c_str());
+  *out = &ds;
+  return NVFP4_OK;
+}
+
+namespace {
 
 // cuTensorMapEncodeTiled, resolved once through the runtime (no libcuda link).
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -374,7 +378,6 @@ bool encode_map(uint32_t kind, const void* addr, uint32_t rows, uint32_t row_ele
   return true;
 }
 
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Single-CTA launches hand out tiles dynamically (see kClaimLeadKTiles); building with
 // -DNVFP4_DYNAMIC_SCHEDULE=0 restores the static round-robin order.
@@ -811,317 +814,7 @@ NVFP4_API int nvfp4_sf_to_blocked(const void* plain, void* blocked, int rows, in
 
 }  // extern "C"
 
-namespace nvfp4 {
-namespace {
-
-int quantize_impl(const void* x, int rows, int cols, int64_t ld, int dtype, float global_scale,
-                  const int32_t* src_rows, int row_mode, void* packed, int64_t packed_ld,
-                  void* sf_blocked, void* stream) {
-  if (dtype != NVFP4_DTYPE_BF16 && dtype != NVFP4_DTYPE_FP16)
-    return fail(NVFP4_ERR_INVALID_ARGUMENT, "dtype=%d (expected NVFP4_DTYPE_BF16 or _FP16)", dtype);
-  if (!(global_scale > 0.0f) || !std::isfinite(global_scale))
-    return fail(NVFP4_ERR_INVALID_ARGUMENT, "global_scale must be finite and > 0");
-  if (rows < 0 || cols <= 0 || cols % 64 != 0)
-    return fail(NVFP4_ERR_BAD_SHAPE, "rows=%d cols=%d (cols must be a positive multiple of 64)",
-                rows, cols);
-  if (rows == 0) return NVFP4_OK;
-  if (x == nullptr || packed == nullptr || sf_blocked == nullptr ||
-      (row_mode != kQuantRowsPlain && src_rows == nullptr))
-    return fail(NVFP4_ERR_NULL_POINTER, "x, packed, sf_blocked or src_rows is NULL");
-  if (ld < cols || packed_ld < cols / 2)
-    return fail(NVFP4_ERR_INVALID_ARGUMENT, "ld=%lld packed_ld=%lld too small for cols=%d",
-                static_cast<long long>(ld), static_cast<long long>(packed_ld), cols);
-  if (!aligned16(x) || !aligned16(packed) || !aligned16(sf_blocked) || ld % 8 != 0 ||
-      packed_ld % 16 != 0)
-    return fail(NVFP4_ERR_MISALIGNED,
-                "x, packed and sf_blocked must be 16-byte aligned, ld a multiple of 8 elements "
-                "and packed_ld a multiple of 16 bytes");
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_INVALID_ARGUMENT, "device %d", dev);
-  DeviceState& ds = g_dev[dev];
-  std::call_once(ds.once, init_device, dev, std::ref(ds));
-  if (ds.status != NVFP4_OK) return fail(ds.status, "%s", ds.detail.c_str());
-  const int row_blocks = (rows + 127) / 128;
-  const int rest_k = cols / 64;
-  const int64_t warps = static_cast<int64_t>(row_blocks) * rest_k;
-  const int threads = 32 * kQuantWarps;
-  const int64_t blocks = std::min<int64_t>((warps + kQuantWarps - 1) / kQuantWarps,
-                                           static_cast<int64_t>(ds.num_sms) * 8);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == NVFP4_DTYPE_BF16)
-    nvfp4_quantize_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(x), rows, ld, global_scale,
-        static_cast<uint8_t*>(packed), packed_ld, static_cast<uint8_t*>(sf_blocked), row_blocks,
-        rest_k, src_rows, row_mode);
-  else
-    nvfp4_quantize_kernel<__half><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
-        static_cast<const __half*>(x), rows, ld, global_scale, static_cast<uint8_t*>(packed),
-        packed_ld, static_cast<uint8_t*>(sf_blocked), row_blocks, rest_k, src_rows, row_mode);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
-  return NVFP4_OK;
-}
-
-int64_t route_chunks(int64_t pairs) { return (pairs + kRouteChunk - 1) / kRouteChunk; }
-
-}  // namespace
-}  // namespace nvfp4
-
 extern "C" {
-
-NVFP4_API int nvfp4_quantize(const void* x, int rows, int cols, int64_t ld, int dtype,
-                             float global_scale, void* packed, int64_t packed_ld, void* sf_blocked,
-                             void* stream) {
-  g_last_error.clear();
-  return quantize_impl(x, rows, cols, ld, dtype, global_scale, nullptr, kQuantRowsPlain, packed,
-                       packed_ld, sf_blocked, stream);
-}
-
-NVFP4_API int nvfp4_quantize_rows(const void* x, int rows, int cols, int64_t ld, int dtype,
-                                  float global_scale, const int32_t* src_rows, int mode,
-                                  void* packed, int64_t packed_ld, void* sf_blocked,
-                                  void* stream) {
-  g_last_error.clear();
-  if (mode != NVFP4_ROWS_GATHER && mode != NVFP4_ROWS_MASK)
-    return fail(NVFP4_ERR_INVALID_ARGUMENT, "mode=%d (expected NVFP4_ROWS_GATHER or _MASK)", mode);
-  return quantize_impl(x, rows, cols, ld, dtype, global_scale, src_rows,
-                       mode == NVFP4_ROWS_GATHER ? kQuantRowsGather : kQuantRowsMask, packed,
-                       packed_ld, sf_blocked, stream);
-}
-
-NVFP4_API size_t nvfp4_moe_route_workspace_size(int64_t pairs, int num_experts) {
-  if (pairs <= 0 || num_experts <= 0) return 0;
-  return static_cast<size_t>(route_chunks(pairs)) * static_cast<size_t>(num_experts) * 4u;
-}
-
-NVFP4_API int nvfp4_moe_route(const int32_t* topk_ids, int tokens, int topk, int num_experts,
-                              int32_t* counts, int32_t* offsets, int32_t* dest, int32_t* src_rows,
-                              int64_t rows_capacity, void* workspace, size_t workspace_bytes,
-                              void* stream) {
-  g_last_error.clear();
-  if (num_experts <= 0 || num_experts > kRouteMaxExperts)
-    return fail(NVFP4_ERR_INVALID_ARGUMENT, "num_experts=%d must be in [1, %d]", num_experts,
-                kRouteMaxExperts);
-  if (tokens < 0 || topk <= 0) return fail(NVFP4_ERR_BAD_SHAPE, "tokens=%d topk=%d", tokens, topk);
-  const int64_t pairs = static_cast<int64_t>(tokens) * topk;
-  if (pairs > (int64_t{1} << 30)) return fail(NVFP4_ERR_BAD_SHAPE, "too many pairs");
-  if (counts == nullptr || offsets == nullptr ||
-      (pairs > 0 && (topk_ids == nullptr || dest == nullptr || src_rows == nullptr)))
-    return fail(NVFP4_ERR_NULL_POINTER, "a routing buffer is NULL");
-  const int64_t need_rows = pairs + static_cast<int64_t>(num_experts) * 127;
-  if (rows_capacity < need_rows)
-    return fail(NVFP4_ERR_INVALID_ARGUMENT,
-                "rows_capacity=%lld < tokens*topk + 127*num_experts = %lld",
-                static_cast<long long>(rows_capacity), static_cast<long long>(need_rows));
-  const size_t ws_need = nvfp4_moe_route_workspace_size(pairs, num_experts);
-  if (ws_need > 0 && (workspace == nullptr || workspace_bytes < ws_need))
-    return fail(NVFP4_ERR_WORKSPACE, "routing workspace has %zu bytes, needs %zu", workspace_bytes,
-                ws_need);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t chunks = route_chunks(pairs);
-  int32_t* hist = static_cast<int32_t*>(workspace);
-  if (chunks > 0) {
-    nvfp4_route_histogram_kernel<<<static_cast<unsigned>(chunks), kRouteThreads, 0, s>>>(
-        topk_ids, pairs, num_experts, hist);
-  }
-  // Every row of the map starts as padding (-1); the scatter writes the real rows.
-  if (src_rows != nullptr) {
-    cudaError_t me = cudaMemsetAsync(src_rows, 0xFF, static_cast<size_t>(rows_capacity) * 4, s);
-    if (me != cudaSuccess) return cuda_fail(me, "routing map reset");
-  }
-  nvfp4_route_scan_kernel<<<1, kRouteMaxExperts, 0, s>>>(hist, static_cast<int>(chunks),
-                                                         num_experts, counts, offsets);
-  if (chunks > 0) {
-    nvfp4_route_scatter_kernel<<<static_cast<unsigned>(chunks), kRouteThreads, 0, s>>>(
-        topk_ids, pairs, topk, num_experts, hist, offsets, dest, src_rows);
-  }
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "routing launch");
-  return NVFP4_OK;
-}
-
-NVFP4_API int nvfp4_moe_gather_quantized(const void* packed_src, int64_t ld_src,
-                                         const void* sf_src, const int32_t* src_rows, int rows,
-                                         int cols, void* packed_dst, int64_t ld_dst, void* sf_dst,
-                                         void* stream) {
-  g_last_error.clear();
-  if (rows < 0 || cols <= 0 || cols % 64 != 0)
-    return fail(NVFP4_ERR_BAD_SHAPE, "rows=%d cols=%d (cols a positive multiple of 64)", rows, cols);
-  if (rows == 0) return NVFP4_OK;
-  if (packed_src == nullptr || sf_src == nullptr || src_rows == nullptr || packed_dst == nullptr ||
-      sf_dst == nullptr)
-    return fail(NVFP4_ERR_NULL_POINTER, "a gather buffer is NULL");
-  if (ld_src < cols / 2 || ld_dst < cols / 2)
-    return fail(NVFP4_ERR_INVALID_ARGUMENT, "row strides smaller than cols/2 bytes");
-  if (!aligned16(packed_src) || !aligned16(packed_dst) || !aligned16(sf_src) || !aligned16(sf_dst) ||
-      ld_src % 16 != 0 || ld_dst % 16 != 0)
-    return fail(NVFP4_ERR_MISALIGNED, "buffers must be 16-byte aligned, row strides multiples of 16");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t row_blocks = std::min<int64_t>((static_cast<int64_t>(rows) + 7) / 8, 148 * 16);
-  nvfp4_gather_packed_rows_kernel<<<static_cast<unsigned>(row_blocks), 256, 0, s>>>(
-      static_cast<const uint8_t*>(packed_src), ld_src, src_rows, rows, cols / 2,
-      static_cast<uint8_t*>(packed_dst), ld_dst);
-  const int rest_k = cols / 64;
-  const int64_t sf_tasks = static_cast<int64_t>((rows + 127) / 128) * rest_k;
-  const int64_t sf_blocks = std::min<int64_t>((sf_tasks + 7) / 8, 148 * 16);
-  nvfp4_gather_blocked_scales_kernel<<<static_cast<unsigned>(sf_blocks), 256, 0, s>>>(
-      static_cast<const uint8_t*>(sf_src), src_rows, rows, rest_k, static_cast<uint8_t*>(sf_dst));
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "gather launch");
-  return NVFP4_OK;
-}
-
-NVFP4_API int nvfp4_moe_combine(const void* y, int64_t ldy, const int32_t* dest,
-                                const float* weights, int tokens, int topk, int cols, void* out,
-                                int64_t ldo, void* stream) {
-  g_last_error.clear();
-  if (tokens < 0 || topk <= 0 || cols <= 0 || cols % 8 != 0)
-    return fail(NVFP4_ERR_BAD_SHAPE, "tokens=%d topk=%d cols=%d (cols a multiple of 8)", tokens,
-                topk, cols);
-  if (tokens == 0) return NVFP4_OK;
-  if (y == nullptr || dest == nullptr || weights == nullptr || out == nullptr)
-    return fail(NVFP4_ERR_NULL_POINTER, "a combine buffer is NULL");
-  if (ldy < cols || ldo < cols) return fail(NVFP4_ERR_INVALID_ARGUMENT, "ldy/ldo < cols");
-  if (!aligned16(y) || !aligned16(out) || ldy % 8 != 0 || ldo % 8 != 0)
-    return fail(NVFP4_ERR_MISALIGNED, "y and out must be 16-byte aligned, ldy and ldo multiples of 8");
-  const int chunks = (cols + 255) / 256;
-  const int64_t warps = static_cast<int64_t>(tokens) * chunks;
-  const int64_t blocks = std::min<int64_t>((warps + 7) / 8, 148 * 16);
-  nvfp4_moe_combine_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(y), ldy, dest, weights, tokens, topk, cols,
-      static_cast<__nv_bfloat16*>(out), ldo);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "combine launch");
-  return NVFP4_OK;
-}
-
-// ---------------------------------------------------------------------------- expert parallel
-static_assert(sizeof(nvfp4_ep_peers) == sizeof(EpPeers), "peer table layouts differ");
-static_assert(NVFP4_EP_MAX_RANKS == kEpMaxRanks, "header and library disagree");
-
-namespace {
-EpPeers to_peers(const nvfp4_ep_peers& p) {
-  EpPeers out;
-  for (int i = 0; i < kEpMaxRanks; ++i) out.ptr[i] = p.ptr[i];
-  return out;
-}
-
-int check_ep_world(int num_experts, int rank, int world) {
-  if (world < 1 || world > kEpMaxRanks || rank < 0 || rank >= world)
-    return fail(NVFP4_ERR_INVALID_ARGUMENT, "rank %d of world %d (1..%d ranks)", rank, world,
-                kEpMaxRanks);
-  if (num_experts <= 0 || num_experts > kEpMaxExperts || num_experts % world != 0)
-    return fail(NVFP4_ERR_INVALID_ARGUMENT,
-                "num_experts=%d must be in 1..%d and a multiple of the world size %d",
-                num_experts, kEpMaxExperts, world);
-  return NVFP4_OK;
-}
-
-int check_peers(const nvfp4_ep_peers& p, int world, const char* name, bool align16) {
-  for (int i = 0; i < world; ++i) {
-    if (p.ptr[i] == nullptr) return fail(NVFP4_ERR_NULL_POINTER, "%s[%d] is NULL", name, i);
-    if (align16 ? !aligned16(p.ptr[i]) : (reinterpret_cast<uintptr_t>(p.ptr[i]) & 3u) != 0)
-      return fail(NVFP4_ERR_MISALIGNED, "%s[%d] misaligned", name, i);
-  }
-  return NVFP4_OK;
-}
-}  // namespace
-
-NVFP4_API int nvfp4_ep_publish_counts(const int32_t* counts, int num_experts, int rank, int world,
-                                      nvfp4_ep_peers count_mats, void* stream) {
-  g_last_error.clear();
-  int st = check_ep_world(num_experts, rank, world);
-  if (st != NVFP4_OK) return st;
-  if (counts == nullptr) return fail(NVFP4_ERR_NULL_POINTER, "counts is NULL");
-  if ((st = check_peers(count_mats, world, "count_mats", false)) != NVFP4_OK) return st;
-  const int n = world * num_experts;
-  nvfp4_ep_publish_counts_kernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      counts, num_experts, rank, world, to_peers(count_mats));
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "publish counts launch");
-  return NVFP4_OK;
-}
-
-NVFP4_API int nvfp4_ep_layout(const int32_t* count_mat, int num_experts, int rank, int world,
-                              int64_t recv_capacity, int32_t* seg_offsets, int32_t* seg_counts,
-                              int32_t* send_base, unsigned int* error_word, void* stream) {
-  g_last_error.clear();
-  int st = check_ep_world(num_experts, rank, world);
-  if (st != NVFP4_OK) return st;
-  if (count_mat == nullptr || seg_offsets == nullptr || seg_counts == nullptr ||
-      send_base == nullptr || error_word == nullptr)
-    return fail(NVFP4_ERR_NULL_POINTER, "a layout buffer is NULL");
-  if (recv_capacity < 0 || recv_capacity > INT32_MAX)
-    return fail(NVFP4_ERR_INVALID_ARGUMENT, "recv_capacity=%lld",
-                static_cast<long long>(recv_capacity));
-  nvfp4_ep_layout_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
-      count_mat, num_experts, rank, world, recv_capacity, seg_offsets, seg_counts, send_base,
-      error_word);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "layout launch");
-  return NVFP4_OK;
-}
-
-NVFP4_API int nvfp4_ep_dispatch(const int32_t* topk_ids, int tokens, int topk, int num_experts,
-                                int rank, int world, const int32_t* dest, const int32_t* offsets,
-                                const int32_t* send_base, const void* codes, int64_t ld_codes,
-                                const void* sf_blocked, int cols, nvfp4_ep_peers recv_codes,
-                                nvfp4_ep_peers recv_sf, nvfp4_ep_peers recv_meta,
-                                int64_t recv_capacity, int32_t* remote_rows, void* stream) {
-  g_last_error.clear();
-  int st = check_ep_world(num_experts, rank, world);
-  if (st != NVFP4_OK) return st;
-  if (tokens < 0 || topk <= 0 || cols <= 0 || cols % 256 != 0)
-    return fail(NVFP4_ERR_BAD_SHAPE, "tokens=%d topk=%d cols=%d (cols a multiple of 256)",
-                tokens, topk, cols);
-  if (tokens == 0) return NVFP4_OK;
-  if (topk_ids == nullptr || dest == nullptr || offsets == nullptr || send_base == nullptr ||
-      codes == nullptr || sf_blocked == nullptr || remote_rows == nullptr)
-    return fail(NVFP4_ERR_NULL_POINTER, "a dispatch buffer is NULL");
-  if (!aligned16(codes) || ld_codes % 16 != 0 || ld_codes < cols / 2 ||
-      (reinterpret_cast<uintptr_t>(sf_blocked) & 3u) != 0)
-    return fail(NVFP4_ERR_MISALIGNED, "codes 16-byte aligned with ld a multiple of 16 >= cols/2, "
-                "scales 4-byte aligned");
-  if ((st = check_peers(recv_codes, world, "recv_codes", true)) != NVFP4_OK) return st;
-  if ((st = check_peers(recv_sf, world, "recv_sf", true)) != NVFP4_OK) return st;
-  if ((st = check_peers(recv_meta, world, "recv_meta", true)) != NVFP4_OK) return st;
-  const int64_t pairs = static_cast<int64_t>(tokens) * topk;
-  const int64_t blocks = std::min<int64_t>((pairs + 7) / 8, 148 * 16);
-  nvfp4_ep_dispatch_kernel<<<static_cast<unsigned>(blocks), 256, 0,
-                             static_cast<cudaStream_t>(stream)>>>(
-      topk_ids, pairs, topk, num_experts, rank, world, dest, offsets, send_base,
-      static_cast<const uint8_t*>(codes), ld_codes, static_cast<const uint8_t*>(sf_blocked), cols,
-      to_peers(recv_codes), to_peers(recv_sf), to_peers(recv_meta), recv_capacity, remote_rows);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "dispatch launch");
-  return NVFP4_OK;
-}
-
-NVFP4_API int nvfp4_ep_combine(const int32_t* remote_rows, const float* weights, int tokens,
-                               int topk, const void* ret, int cols, void* out, int64_t ldo,
-                               void* stream) {
-  g_last_error.clear();
-  if (tokens < 0 || topk <= 0 || cols <= 0 || cols % 8 != 0)
-    return fail(NVFP4_ERR_BAD_SHAPE, "tokens=%d topk=%d cols=%d (cols a multiple of 8)", tokens,
-                topk, cols);
-  if (tokens == 0) return NVFP4_OK;
-  if (remote_rows == nullptr || weights == nullptr || ret == nullptr || out == nullptr)
-    return fail(NVFP4_ERR_NULL_POINTER, "a combine buffer is NULL");
-  if (!aligned16(out) || !aligned16(ret) || ldo % 8 != 0 || ldo < cols)
-    return fail(NVFP4_ERR_MISALIGNED, "ret and out 16-byte aligned, ldo a multiple of 8 >= cols");
-  const int chunks = (cols + 255) / 256;
-  const int64_t warps = static_cast<int64_t>(tokens) * chunks;
-  const int64_t blocks = std::min<int64_t>((warps + 7) / 8, 148 * 16);
-  nvfp4_ep_combine_kernel<<<static_cast<unsigned>(blocks), 256, 0,
-                            static_cast<cudaStream_t>(stream)>>>(
-      remote_rows, weights, tokens, topk, static_cast<const __half*>(ret), cols,
-      static_cast<__nv_bfloat16*>(out), ldo);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "combine launch");
-  return NVFP4_OK;
-}
 
 NVFP4_API int nvfp4_workspace_check(void* workspace, void* stream, unsigned int* device_error_bits) {
   g_last_error.clear();
