@@ -225,6 +225,9 @@ def config_rows(name: str, seed: int = 0) -> tuple:
         return zipf_topk_rows(64, 512, 8, 1.2, seed), 1536, 4096, False, None
     if name == "cfg5":
         return uniform_topk_rows(256, 32768, 8, seed), 2048, 7168, True, None
+    if name == "moe_down":
+        # cfg5's down projection: the same routed rows, N = hidden 7168, K = intermediate 2048
+        return uniform_topk_rows(256, 32768, 8, seed), 7168, 2048, False, None
     if name == "decode":
         # cfg4's experts at a decode step of 64 tokens x top-8: 512 rows over 64 experts
         return zipf_topk_rows(64, 64, 8, 1.2, seed), 1536, 4096, False, None
