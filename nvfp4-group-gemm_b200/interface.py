@@ -56,7 +56,7 @@ def _current_raw_stream(device_index: int) -> int:
 # Workspace and descriptor-table cache (one per device and stream)
 # ----------------------------------------------------------------------------
 class _Workspace:
-    __slots__ = ("buf", "nbytes", "last_table", "last_flags", "last_sig")
+    __slots__ = ("buf", "nbytes", "last_table", "last_flags", "last_sig", "plan")
 
     def __init__(self):
         self.buf = None
@@ -64,6 +64,13 @@ class _Workspace:
         self.last_table = None
         self.last_flags = None
         self.last_sig = None
+        self.plan = None  # native prepared launch of last_table (nvfp4_plan_create)
+
+    def drop_plan(self):
+        """Forget the prepared launch (the workspace is about to hold other descriptors)."""
+        if self.plan is not None:
+            _native.load_library().nvfp4_plan_destroy(self.plan)
+            self.plan = None
 
 
 _ws_lock = threading.Lock()
@@ -79,6 +86,7 @@ def _workspace_for(device: torch.device, stream: torch.cuda.Stream, nbytes: int)
     if ws.nbytes < nbytes:
         size = max(nbytes, 2 * ws.nbytes, 1 << 16)
         # Zero-filled: the first 4 bytes are the device error word.
+        ws.drop_plan()
         ws.buf = torch.zeros(size, dtype=torch.uint8, device=device)
         ws.nbytes = size
         ws.last_table = None
@@ -278,9 +286,13 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
             ws = _workspaces.get((device.index, s.cuda_stream))
             if ws is not None and ws.last_sig == sig and ws.last_table is not None:
                 with torch.cuda.device(device):
-                    _native.grouped_gemm_raw(ws.last_table,
-                                             ws.last_flags | _native.FLAG_REUSE_DESCRIPTORS,
-                                             ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
+                    if ws.plan is not None:  # the launch itself only
+                        _native.check(_native.load_library().nvfp4_plan_launch(ws.plan,
+                                                                               s.cuda_stream))
+                    else:
+                        _native.grouped_gemm_raw(ws.last_table,
+                                                 ws.last_flags | _native.FLAG_REUSE_DESCRIPTORS,
+                                                 ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
                 return list(c)
     prepared = _prepare(a, b, sfa, sfb, c, problem_sizes, alpha, b2, sfb2, alpha2, tile_n, cta,
                         split_k)
@@ -290,12 +302,27 @@ def grouped_gemm(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor],
     s = stream or torch.cuda.current_stream(device)
     ws = _workspace_for(device, s, _native.workspace_size_with_split(G) if split_k
                         else _native.workspace_size(G))
-    call_flags = flags
-    if (reuse_descriptors and ws.last_flags == flags and ws.last_table is not None
-            and ws.last_table.shape == table.shape and np.array_equal(ws.last_table, table)):
-        call_flags |= _native.FLAG_REUSE_DESCRIPTORS
+    same = (reuse_descriptors and ws.last_flags == flags and ws.last_table is not None
+            and ws.last_table.shape == table.shape and np.array_equal(ws.last_table, table))
+    lib = _native.load_library()
     with torch.cuda.device(device):
-        _native.grouped_gemm_raw(table, call_flags, ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
+        if same and ws.plan is not None:
+            _native.check(lib.nvfp4_plan_launch(ws.plan, s.cuda_stream), lib)
+        elif reuse_descriptors and not split_k:
+            # Upload once into a native prepared launch; repeated calls on the same tensors
+            # then replay only the kernel launch.
+            ws.drop_plan()
+            out = ctypes.c_void_p()
+            _native.check(lib.nvfp4_plan_create(table.ctypes.data, int(table.shape[0]), flags,
+                                                ws.buf.data_ptr(), ws.nbytes, s.cuda_stream,
+                                                ctypes.byref(out)), lib)
+            ws.plan = out.value
+            _native.check(lib.nvfp4_plan_launch(ws.plan, s.cuda_stream), lib)
+        else:
+            ws.drop_plan()
+            call_flags = flags | (_native.FLAG_REUSE_DESCRIPTORS if same else 0)
+            _native.grouped_gemm_raw(table, call_flags, ws.buf.data_ptr(), ws.nbytes,
+                                     s.cuda_stream)
     ws.last_table = table
     ws.last_flags = flags
     ws.last_sig = sig
@@ -315,6 +342,7 @@ def grouped_gemm_table(table: np.ndarray, flags: int, device: torch.device,
                         if flags & _native.FLAG_SPLIT_K else _native.workspace_size(G))
     with torch.cuda.device(device):
         _native.grouped_gemm_raw(table, flags, ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
+    ws.drop_plan()
     ws.last_table = None  # the next grouped_gemm call on this stream rebuilds its descriptors
     ws.last_sig = None
 
@@ -438,6 +466,7 @@ def grouped_gemm_segments(a: torch.Tensor, sfa: torch.Tensor, c: torch.Tensor,
                                           ws.buf.data_ptr(), ws.nbytes, s.cuda_stream,
                                           _native.SegmentOutput.nvfp4(out_sf.data_ptr(), out_scale)
                                           if quant_out else scatter)
+    ws.drop_plan()
     ws.last_table = table
     ws.last_flags = flags
     ws.last_sig = None
