@@ -946,6 +946,27 @@ def main():
     h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = sum(t.numel() * t.element_size() for t in host_out)
 
+    # The drop-in call itself on device-resident inputs: custom_kernel(data) back to back
+    # (device time per call, and the host time to issue one call).
+    ck_host = []
+    for _ in range(3):
+        pkg.custom_kernel(data, global_scales=scales, tile_n=args.tile_n, stream=stream,
+                          cta=args.cta, split_k=args.split_k)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ck0 = torch.cuda.Event(enable_timing=True)
+    ck1 = torch.cuda.Event(enable_timing=True)
+    ck0.record(stream)
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        pkg.custom_kernel(data, global_scales=scales, tile_n=args.tile_n, stream=stream,
+                          cta=args.cta, split_k=args.split_k)
+        ck_host.append(time.perf_counter() - t0)
+    ck1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ck_ms = max_over_ranks(ck0.elapsed_time(ck1)) / args.steps
+
     # ---------------------------------------------------------------- CPU baseline (rank 0, N=1)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1008,6 +1029,11 @@ def main():
                 "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "custom_kernel(data) with pinned-host copies of inputs and outputs"},
         "cuda_graph": graph_info,
+        "custom_kernel_device_resident": {
+            "us_per_call": ck_ms * 1e3, "host_us_per_call": sorted(ck_host)[len(ck_host) // 2] * 1e6,
+            "what": "custom_kernel(data) back to back on device-resident inputs (the harness's "
+                    "call; descriptors prepared by the first call)" +
+                    ("; L2 not flushed between calls" if flush_l2 else "")},
         "burst": {"us_per_call": burst_ms * 1e3, "tflops_per_gpu": burst_tflops,
                   "frac_of_burst_peak": burst_tflops / burst_peak,
                   "hbm_frac": alg_bytes / (burst_ms * 1e-3) / 1e9 / hbm_peak,
