@@ -581,11 +581,52 @@ def _split_scales(global_scales, G: int, gated: bool):
     return [float(x) for x in gs], None
 
 
+class _CallCache:
+    """The last grouped custom_kernel call that left a prepared launch in its stream's
+    workspace: the same input object with the same tensors (identities and addresses), sizes
+    and options may replay that launch without rebuilding anything."""
+
+    __slots__ = ("data", "scales", "scales_val", "opts", "ids", "ptrs", "sizes", "ws", "sig",
+                 "out", "ws_stream")
+
+
+def _scales_value(global_scales):
+    """A comparable copy of the global scales argument (lists may be changed in place)."""
+    if global_scales is None:
+        return None
+    return tuple(tuple(x) if isinstance(x, (tuple, list)) else float(x) for x in global_scales)
+
+
+_last_call: _CallCache | None = None
+
+
+def _grouped_tensors(data) -> list:
+    return [t for grp in data[0] for t in grp] + [t for grp in data[2] for t in grp]
+
+
 def custom_kernel(data: input_t, *, global_scales=None, tile_n: int | None = None,
                   stream: torch.cuda.Stream | None = None, cta: str | None = None,
                   split_k: bool = False) -> output_t:
     """Drop-in replacement of the reference's ``custom_kernel`` (submission.py:788).
     The keyword options are those of :func:`grouped_gemm`."""
+    global _last_call
+    last = _last_call
+    if (last is not None and data is last.data and global_scales is last.scales
+            and (global_scales is None or _scales_value(global_scales) == last.scales_val)
+            and last.opts == (tile_n, cta, split_k,
+                              stream.cuda_stream if stream is not None else None)
+            and last.ws.plan is not None and last.ws.last_sig is last.sig):
+        ts = _grouped_tensors(data)
+        if ([id(t) for t in ts] == last.ids and [t.data_ptr() for t in ts] == last.ptrs
+                and [tuple(ps) for ps in data[3]] == last.sizes):
+            dev = last.out[0].device
+            if torch.cuda.current_device() == dev.index:
+                s = stream.cuda_stream if stream is not None else _current_raw_stream(dev.index)
+                if s == last.ws_stream:
+                    st = _native.load_library().nvfp4_plan_launch(last.ws.plan, s)
+                    if st:
+                        _native.check(st)
+                    return list(last.out)
     if not isinstance(data, (tuple, list)):
         raise ValueError(f"unsupported input: expected a tuple, got {type(data).__name__}")
     if len(data) == 10:
@@ -635,6 +676,24 @@ def custom_kernel(data: input_t, *, global_scales=None, tile_n: int | None = Non
     alpha, alpha2 = _split_scales(global_scales, G, gated)
     grouped_gemm(a, b, sfa, sfb, c, problem_sizes, alpha=alpha, b2=b2, sfb2=sfb2,
                  alpha2=alpha2, tile_n=tile_n, stream=stream, cta=cta, split_k=split_k)
+    # Remember the call if it left a prepared launch (see _CallCache).
+    _last_call = None
+    if len(data) == 4 and G > 0 and isinstance(c[0], torch.Tensor) and c[0].is_cuda:
+        dev = c[0].device
+        s = (stream or torch.cuda.current_stream(dev)).cuda_stream
+        ws = _workspaces.get((dev.index, s))
+        if ws is not None and ws.plan is not None and ws.last_sig is not None:
+            entry = _CallCache()
+            ts = _grouped_tensors(data)
+            entry.data, entry.scales = data, global_scales
+            entry.scales_val = _scales_value(global_scales)
+            entry.opts = (tile_n, cta, split_k, stream.cuda_stream if stream is not None else None)
+            entry.ids = [id(t) for t in ts]
+            entry.ptrs = [t.data_ptr() for t in ts]
+            entry.sizes = [tuple(ps) for ps in problem_sizes]
+            entry.ws, entry.sig, entry.out = ws, ws.last_sig, list(c)
+            entry.ws_stream = s
+            _last_call = entry
     return list(c)
 
 

@@ -406,3 +406,42 @@ def test_split_k_single_cta(pkg, shape, tile_n):
             for a, b in zip(first, outs):
                 assert torch.equal(a.view(torch.int16), b.view(torch.int16)), "split-K not deterministic"
     assert pkg.check_device_errors() == 0
+
+
+def test_custom_kernel_repeat_fast_path_and_invalidation(pkg):
+    """Repeated custom_kernel calls on the same input replay a prepared launch; every change
+    that matters (a tensor swapped in the input lists, global scales changed in place,
+    another input run in between, new contents) still gives the oracle's result."""
+    p1 = pkg.workloads.make_problem("fp1", [128, 40, 300], 256, 512, seed=61, device="cuda",
+                                    alpha_range=(0.5, 2.0))
+    p2 = pkg.workloads.make_problem("fp2", [64, 200], 384, 1024, seed=62, device="cuda",
+                                    alpha_range=(0.5, 2.0))
+    d1, d2 = p1.reference_data(), p2.reference_data()
+    s1 = list(p1.global_scales())
+    for _ in range(3):  # first call prepares, later calls replay
+        for c in p1.c:
+            c.fill_(float("nan"))
+        pkg.custom_kernel(d1, global_scales=s1)
+        check_problem(p1)
+    # Another input in between replaces the stream's descriptors; then back to the first.
+    pkg.custom_kernel(d2, global_scales=list(p2.global_scales()))
+    check_problem(p2)
+    for c in p1.c:
+        c.fill_(float("nan"))
+    pkg.custom_kernel(d1, global_scales=s1)
+    check_problem(p1)
+    # Global scales changed in place: the new values must be used.
+    s1[1] = s1[1] * 0.5
+    p1.alpha[1] = p1.alpha[1] * 0.5
+    pkg.custom_kernel(d1, global_scales=s1)
+    check_problem(p1)
+    # A group's output tensor swapped inside the input's list.
+    new_c = torch.full_like(p1.c[0], float("nan"))
+    grp = list(d1[0][0])
+    grp[2] = new_c.unsqueeze(-1) if d1[0][0][2].dim() == 3 else new_c
+    d1[0][0] = tuple(grp)
+    pkg.custom_kernel(d1, global_scales=s1)
+    torch.cuda.synchronize()
+    p1.c[0] = new_c
+    check_problem(p1)
+    assert pkg.check_device_errors() == 0
