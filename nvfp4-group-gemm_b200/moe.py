@@ -29,7 +29,7 @@ import numpy as np
 import torch
 
 from . import _native
-from .interface import grouped_gemm, grouped_gemm_table
+from .interface import grouped_gemm_table
 from .layout import blocked_sf_bytes
 from .quantize import _DTYPES, global_scale_for, quantize
 

@@ -8,7 +8,6 @@ process and after the rest of the suite.
 """
 from __future__ import annotations
 
-import ctypes
 
 import numpy as np
 import pytest
