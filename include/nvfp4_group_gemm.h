@@ -362,21 +362,31 @@ NVFP4_API const char* nvfp4_last_error_detail(void);
  *   NVFP4_ERR_INVALID_ARGUMENT (use nvfp4_grouped_gemm with a workspace instead).
  * - The first call on a device looks up the device address of the scratch array
  *   (cudaGetSymbolAddress) with that device current; make that first call before
- *   any stream capture.
+ *   any stream capture. Only a successful lookup is kept: if it fails, the call
+ *   returns NVFP4_ERR_CUDA and the next call on that device tries again.
  * - Every call on a device shares the one scratch array, which keeps the last
- *   call's contents (the device error word is cleared at the start of each call).
- *   Calls that can overlap on the GPU - on different streams, or from different
- *   threads without ordering - race on it and must not be issued.
+ *   call's contents. A call that passes its checks first zeroes the array's header
+ *   (device error word, tile counters) on its stream; a rejected call writes
+ *   nothing to it. Calls that can overlap on the GPU - on different streams, or
+ *   from different threads without ordering - race on it and must not be issued.
  * - NVFP4_FLAG_REUSE_DESCRIPTORS means the scratch array holds this exact group
  *   table from the previous call on the device.
- * - Device-side wait timeouts are recorded in the scratch array's error word and
- *   are not reported back; use nvfp4_grouped_gemm + nvfp4_workspace_check when
- *   they are needed.
+ * - Device-side wait timeouts set bits in the scratch array's error word; read
+ *   them with nvfp4_noalloc_check after the call (before the next call clears them).
  * Arguments, flags, outputs and other status codes are as in nvfp4_grouped_gemm.
  */
 #define NVFP4_NOALLOC_MAX_GROUPS 512
 NVFP4_API int nvfp4_grouped_gemm_noalloc(const nvfp4_group* groups, int num_groups,
                                          unsigned int flags, void* stream);
+
+/*
+ * nvfp4_workspace_check for the built-in scratch array of nvfp4_grouped_gemm_noalloc
+ * on the current device: synchronise `stream`, then read and clear the array's
+ * device error word. NVFP4_ERR_DEVICE_TIMEOUT if the last call's kernel gave up on a
+ * wait; the reason bits go to *device_error_bits when non-NULL. Allocates nothing.
+ * No counterpart in the reference.
+ */
+NVFP4_API int nvfp4_noalloc_check(void* stream, unsigned int* device_error_bits);
 
 /* NVFP4_ABI_VERSION of the loaded library. */
 NVFP4_API int nvfp4_abi_version(void);

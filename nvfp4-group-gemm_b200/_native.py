@@ -57,6 +57,7 @@ EXPORTED_SYMBOLS = (
     "nvfp4_sf_to_blocked",
     "nvfp4_workspace_check",
     "nvfp4_grouped_gemm_noalloc",
+    "nvfp4_noalloc_check",
     "nvfp4_grouped_gemm_segments",
     "nvfp4_plan_create",
     "nvfp4_plan_launch",
@@ -219,6 +220,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_workspace_check.restype = i32
         lib.nvfp4_grouped_gemm_noalloc.argtypes = [vp, i32, u32, vp]
         lib.nvfp4_grouped_gemm_noalloc.restype = i32
+        lib.nvfp4_noalloc_check.argtypes = [vp, ctypes.POINTER(ctypes.c_uint)]
+        lib.nvfp4_noalloc_check.restype = i32
         lib.nvfp4_grouped_gemm_segments.argtypes = [vp, i32, u32, vp, vp, i64,
                                                     ctypes.POINTER(SegmentOutput), vp, sz, vp]
         lib.nvfp4_grouped_gemm_segments.restype = i32

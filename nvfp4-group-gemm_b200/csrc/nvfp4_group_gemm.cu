@@ -505,9 +505,12 @@ struct SegmentArgs {
 // and upload descriptors into `ws`, launch. `rec` holds num_groups records of host
 // scratch; `use_cache` selects the cached tensor-map encoder. With `seg`, each group's
 // m is the slab's row count and the rows it multiplies are read on the device.
+// `clear_header` zeroes the workspace header (error word, tile counters) on `s` once the
+// table has passed every host-side check, before anything is uploaded or launched.
 int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int flags, uint8_t* ws,
                       size_t ws_bytes, cudaStream_t s, GroupDev* rec, bool use_cache,
-                      const SegmentArgs* seg = nullptr, LaunchSpec* prepared = nullptr) {
+                      const SegmentArgs* seg = nullptr, LaunchSpec* prepared = nullptr,
+                      bool clear_header = false) {
   const bool gated = (flags & NVFP4_FLAG_GATED) != 0;
   // Tile shape: CTA pairs (256-row tiles) when the groups are tall enough to fill
   // them, single CTAs (128-row tiles) otherwise; 256 MMA columns unless asked otherwise.
@@ -597,6 +600,11 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
 
   GroupDev* groups_dev = reinterpret_cast<GroupDev*>(ws + ws_groups_offset());
   TmaDesc* maps_dev = reinterpret_cast<TmaDesc*>(ws + ws_maps_offset(num_groups));
+
+  if (clear_header) {
+    e = cudaMemsetAsync(ws, 0, offsetof(WorkspaceHeader, reserved), s);
+    if (e != cudaSuccess) return cuda_fail(e, "clear workspace header");
+  }
 
   if ((flags & NVFP4_FLAG_REUSE_DESCRIPTORS) == 0) {
     static thread_local UploadParams up;  // ~26 KB: kept off the caller's stack
@@ -995,17 +1003,32 @@ constexpr size_t kNoAllocScratchBytes = ws_total_bytes(NVFP4_NOALLOC_MAX_GROUPS)
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 struct NoAllocState {
-  std::once_flag once;
-  cudaError_t status = cudaSuccess;
-  void* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+  std::mutex mu;
+  void* scratch = nullptr;  // device address of g_noalloc_scratch on this device, once found
 };
 NoAllocState g_noalloc[kMaxDevices];
 
-// Runs once per device, with that device current: the host-side symbol is only a
-// stand-in, so the kernel must be given the device address looked up here.
-void init_noalloc(NoAllocState& st) {
-  st.status = cudaGetSymbolAddress(&st.scratch, g_noalloc_scratch);
-  if (st.status != cudaSuccess) st.scratch = nullptr;
+// The device address of the scratch array on the current device. The host-side symbol is
+// only a stand-in, so kernels must be given the address looked up here, with the device
+// current. Only a successful lookup is kept: a failed one (for example a first call made
+// inside a stream capture) is retried by the next call.
+int noalloc_scratch(uint8_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_INVALID_ARGUMENT, "device %d", dev);
+  NoAllocState& na = g_noalloc[dev];
+  std::lock_guard<std::mutex> lock(na.mu);
+  if (na.scratch == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return cuda_fail(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
+                       "cudaGetSymbolAddress(scratch)");
+    na.scratch = p;
+  }
+  *out = static_cast<uint8_t*>(na.scratch);
+  return NVFP4_OK;
 }
 
 }  // namespace
@@ -1021,23 +1044,24 @@ extern "C" NVFP4_API int nvfp4_grouped_gemm_noalloc(const nvfp4_group* groups, i
                 "use nvfp4_grouped_gemm with a caller-provided workspace",
                 num_groups, NVFP4_NOALLOC_MAX_GROUPS);
   if (num_groups == 0) return NVFP4_OK;
-
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_INVALID_ARGUMENT, "device %d", dev);
-  NoAllocState& na = g_noalloc[dev];
-  std::call_once(na.once, init_noalloc, std::ref(na));
-  if (na.scratch == nullptr) return cuda_fail(na.status, "cudaGetSymbolAddress(scratch)");
-
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* ws = static_cast<uint8_t*>(na.scratch);
-  // The device error word keeps whatever the previous call left: start this call at zero,
-  // together with the tile-schedule counters (which every completed launch leaves at zero).
-  e = cudaMemsetAsync(ws, 0, offsetof(WorkspaceHeader, reserved), s);
-  if (e != cudaSuccess) return cuda_fail(e, "clear scratch error word");
-  // Fixed-size host staging and uncached encoding: no heap use on this path.
+  uint8_t* ws = nullptr;
+  st = noalloc_scratch(&ws);
+  if (st != NVFP4_OK) return st;
+  // Fixed-size host staging and uncached encoding: no heap use on this path. The header
+  // (device error word, tile counters) keeps what the previous call left; the shared
+  // implementation zeroes it on this call's stream once the table has passed its checks,
+  // so a rejected call queues no write to the shared array.
   static thread_local GroupDev rec[NVFP4_NOALLOC_MAX_GROUPS];
-  return grouped_gemm_impl(groups, num_groups, flags, ws, kNoAllocScratchBytes, s, rec,
-                           /*use_cache=*/false);
+  return grouped_gemm_impl(groups, num_groups, flags, ws, kNoAllocScratchBytes,
+                           static_cast<cudaStream_t>(stream), rec, /*use_cache=*/false,
+                           /*seg=*/nullptr, /*prepared=*/nullptr, /*clear_header=*/true);
+}
+
+extern "C" NVFP4_API int nvfp4_noalloc_check(void* stream, unsigned int* device_error_bits) {
+  g_last_error.clear();
+  if (device_error_bits) *device_error_bits = 0;
+  uint8_t* ws = nullptr;
+  int st = noalloc_scratch(&ws);
+  if (st != NVFP4_OK) return st;
+  return nvfp4_workspace_check(ws, stream, device_error_bits);
 }

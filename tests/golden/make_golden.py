@@ -2,7 +2,8 @@
 
 Two steps, two machines:
 
-``python tests/golden/make_golden.py inputs``  (build container, needs the reference tree)
+``python tests/golden/make_golden.py inputs PATH/TO/REFERENCE_IMPL.md``  (needs the reference tree)
+    The listing file is the argument, or the NVFP4_REFERENCE_IMPL environment variable.
     Executes the reference harness's own Python listings from
     ``REFERENCE_IMPL.md`` (``to_blocked``, ``create_reordered_scale_factor_tensor``,
     ``_create_fp4_tensors``, ``generate_input``) on the CPU -- the only change is
@@ -30,7 +31,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 INPUTS = os.path.join(HERE, "golden_inputs.npz")
 OUTPUTS = os.path.join(HERE, "golden_outputs.npz")
-REFERENCE_IMPL = os.environ.get("NVFP4_REFERENCE_IMPL", "/root/reference/REFERENCE_IMPL.md")
+REFERENCE_IMPL = os.environ.get("NVFP4_REFERENCE_IMPL")
 
 # (name, generator, m, n, k, seed, extra)
 CASES = [
@@ -48,6 +49,9 @@ CASES = [
 def _load_reference_namespace():
     import torch
 
+    if not REFERENCE_IMPL:
+        sys.exit("the reference's REFERENCE_IMPL.md is needed: pass its path after `inputs` "
+                 "or set NVFP4_REFERENCE_IMPL")
     src = open(REFERENCE_IMPL).read()
     blocks = re.findall(r"```python\n(.*?)```", src, re.S)
     wanted = ("sf_vec_size", "def to_blocked", "def create_reordered_scale_factor_tensor",
@@ -148,6 +152,8 @@ def make_outputs(path: str) -> None:
 if __name__ == "__main__":
     mode = sys.argv[1] if len(sys.argv) > 1 else ""
     if mode == "inputs":
+        if len(sys.argv) > 2:
+            REFERENCE_IMPL = sys.argv[2]
         make_inputs()
     elif mode == "outputs":
         make_outputs(sys.argv[2] if len(sys.argv) > 2 else OUTPUTS)
