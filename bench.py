@@ -11,15 +11,23 @@ Our arm (default):
     both sides, max over ranks). Inputs (232 MB for cfg2) exceed the 126 MB L2.
   * `e2e`: the same metric through the public API with host buffers: every step
     copies the operands from pinned host memory, calls custom_kernel and copies
-    the fp16 outputs back.
+    the fp16 outputs back (two buffer sets: a step's H2D overlaps the previous
+    step's call and D2H; `e2e.serial` keeps everything on one stream).
   * `roofline`: the grouped-GEMM kernel against the dense FP4 tensor peak derived
     from MEASURED_PEAKS.json (4 x the measured cuBLAS bf16 figure: the sustained one for
     `value`, which is timed after a 1 s load window with the clocks sampled around it;
     `burst` reports the same calls timed right after warm-up against the burst figure).
   * `cpu_baseline`: the CPU oracle (numpy restatement of the reference's
     ref_kernel) on the full configuration, rank 0 at N=1 only.
-With N GPUs each rank runs its own set of experts of the same shape (weak scaling;
-expert parallelism needs no collective on the data path).
+  * `nvfp4_peak`: cuBLASLt's dense NVFP4 rate measured on the same GPU (8192^3);
+    `roofline.frac_of_measured_nvfp4` divides by it.
+  * `sharded_cfg5` (every N): cfg5's 256 experts split over the N ranks (strong
+    scaling of one configuration), with and (N > 1) without the NCCL all-gather
+    of all fp16 outputs to every rank.
+  * `configs` + `geomean_us_per_call` (N = 1): BASELINE's headline form, us per
+    isolated call of configs 1-5, their geomean and each one's roofline fraction.
+With N GPUs each rank runs its own set of experts of the same shape for `value` (weak
+scaling; expert parallelism needs no collective on the data path).
 
 Reference arm (--impl reference): the reference's CPU path (the oracle port of
 ref_kernel) timed on the host cores; rank 0 only.
@@ -41,6 +49,7 @@ sys.path.insert(0, ROOT)
 PEAK_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_BYTES = 126 * 1000 * 1000
 FP4_PER_BF16 = 4.0  # dense FP4 : dense BF16 tensor throughput on B200 (9 : 2.25 PFLOP/s)
+NOMINAL_FP4_TFLOPS = 9000.0  # B200 dense FP4, nominal
 
 
 def parse_args():
@@ -49,7 +58,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg2")
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference_gpu"])
     ap.add_argument("--tile-n", type=int, default=None)
     ap.add_argument("--cta", default=None, choices=[None, "pair", "single", "weights"])
     ap.add_argument("--split-k", action="store_true",
@@ -57,6 +66,9 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the measured NVFP4 peak, the cfg5 expert split and the "
+                         "configs 1-5 record")
     ap.add_argument("--op", default="gemm", choices=["gemm", "quantize", "moe"],
                     help="gemm: the grouped GEMM (default); quantize: the NVFP4 activation "
                          "quantiser on the configuration's A rows (bf16 [sum M_g, K]); moe: the "
@@ -210,36 +222,86 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_all_configs(args):
+HEADLINE_CONFIGS = ("cfg1", "cfg2", "cfg3", "cfg4", "cfg5")
+
+
+def measure_nvfp4_peak(dev, seconds: float = 2.0) -> dict:
+    """Dense block-scaled NVFP4 rate of the library GEMM on this GPU: torch._scaled_mm
+    (cuBLASLt, E4M3 scales per 16 elements, fp16 out) at M = N = K = 8192, the shape of the
+    bf16 figures in MEASURED_PEAKS.json. `burst`: best of 10 calls right after warm-up;
+    `sustained`: calls back to back for `seconds`, the median rate of the second half's
+    chunks of 20 calls."""
+    import torch
+
+    M = N = K = 8192
+    g = torch.Generator(device=dev).manual_seed(5)
+    # The reference generator's value set (codes {0, +-0.5, +-1, +-1.5}, scales {1, 2}).
+    a = torch.randint(0, 256, (M, K // 2), dtype=torch.uint8, device=dev, generator=g) & 0xBB
+    b = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g) & 0xBB
+    sf = lambda rows: (0x38 + 8 * torch.randint(0, 2, (rows * K // 16,), device=dev,
+                                                generator=g, dtype=torch.int32)).to(torch.uint8)
+    f4, e4 = torch.float4_e2m1fn_x2, torch.float8_e4m3fn
+    a4, bt = a.view(f4), b.view(f4).t()
+    sa, sb = sf(M).view(e4), sf(N).view(e4)
+    flops = 2.0 * M * N * K
+
+    def call():
+        return torch._scaled_mm(a4, bt, sa, sb, out_dtype=torch.float16)
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize(dev)
+    best = float("inf")
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        call()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        best = min(best, e0.elapsed_time(e1))
+    rates = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(20):
+            call()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        rates.append(20 * flops / (e0.elapsed_time(e1) * 1e-3) / 1e12)
+    tail = rates[len(rates) // 2:] or rates
+    return {"burst_tflops": flops / (best * 1e-3) / 1e12,
+            "sustained_tflops": statistics.median(tail),
+            "what": f"torch._scaled_mm NVFP4 (cuBLASLt block-scaled, fp16 out) {M}x{N}x{K}: "
+                    f"best of 10 (burst); back to back for {seconds:.0f} s (sustained)"}
+
+
+def headline_configs(pkg, dev, steps: int, warmup: int, peaks: dict, nvfp4_peak: dict | None):
     """BASELINE's headline form: microseconds per call of configs 1-5 through the prepared
     launch (one GPU, device-resident inputs, a 256 MiB L2 flush before each call of a
-    configuration whose inputs fit in L2), their geometric mean, and each configuration's
-    fraction of its roofline. One JSON line."""
+    configuration whose inputs fit in L2; events around each call, median), their
+    geometric mean, and each configuration's fraction of its roofline (burst peaks: every
+    call is timed on its own)."""
     import math
 
     import torch
 
-    import submission
-
-    pkg = submission.load_package()
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    peaks, kind = load_peaks()
     tensor_peak = FP4_PER_BF16 * float(peaks["bf16_tflops"])
     hbm_peak = float(peaks["hbm_gbs"])
+    fp4_peak = nvfp4_peak["burst_tflops"] if nvfp4_peak else None
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     per = {}
-    for cfg in ("cfg1", "cfg2", "cfg3", "cfg4", "cfg5"):
+    for cfg in HEADLINE_CONFIGS:
         prob = pkg.workloads.make_config(cfg, seed=0, device=dev)
         plan = pkg.GroupedGemmPlan(prob.a, prob.b, prob.sfa, prob.sfb, prob.c,
                                    prob.problem_sizes(), alpha=prob.alpha, b2=prob.b2,
                                    sfb2=prob.sfb2, alpha2=prob.alpha2)
-        for _ in range(max(args.warmup, 3)):
+        for _ in range(max(warmup, 3)):
             plan.run()
         torch.cuda.synchronize(dev)
         small = prob.input_bytes() < L2_BYTES
         times = []
-        for _ in range(args.steps):
+        for _ in range(steps):
             if small:
                 flush.fill_(1)
             e0 = torch.cuda.Event(enable_timing=True)
@@ -251,23 +313,251 @@ def run_all_configs(args):
             times.append(e0.elapsed_time(e1) * 1e3)
         us = sorted(times)[len(times) // 2]
         flops, nbytes = prob.flops(), prob.algorithmic_bytes()
+        tflops = flops / (us * 1e-6) / 1e12
         bound = "tensor" if flops / nbytes >= tensor_peak * 1e12 / (hbm_peak * 1e9) else "hbm"
-        frac = (flops / (us * 1e-6) / 1e12 / tensor_peak if bound == "tensor"
-                else nbytes / (us * 1e-6) / 1e9 / hbm_peak)
-        per[cfg] = {"us_per_call": us, "tflops": flops / (us * 1e-6) / 1e12, "bound": bound,
-                    "frac_of_roofline": frac, "errors": plan.check_device_errors()}
+        frac = tflops / tensor_peak if bound == "tensor" else nbytes / (us * 1e-6) / 1e9 / hbm_peak
+        entry = {"us_per_call": us, "tflops": tflops, "gbs": nbytes / (us * 1e-6) / 1e9,
+                 "bound": bound, "frac_of_roofline": frac,
+                 "flops": flops, "algorithmic_bytes": nbytes,
+                 "device_error_bits": plan.check_device_errors()}
+        if bound == "tensor" and fp4_peak:
+            entry["frac_of_measured_nvfp4_burst"] = tflops / fp4_peak
+        per[cfg] = entry
         del plan, prob
         torch.cuda.empty_cache()
     geo = math.exp(sum(math.log(v["us_per_call"]) for v in per.values()) / len(per))
+    return {"geomean_us_per_call": geo, "per_config": per,
+            "timing": "one call per event pair, median of --steps calls; a 256 MiB L2 flush "
+                      "before each call of a configuration whose inputs fit in L2",
+            "peaks": "tensor-bound: 4 x burst bf16 (MEASURED_PEAKS.json) and the measured "
+                     "NVFP4 burst rate; hbm-bound: hbm_gbs"}
+
+
+def run_all_configs(args):
+    """`--config all`: the headline configurations alone, one JSON line."""
+    import torch
+
+    import submission
+
+    pkg = submission.load_package()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks, kind = load_peaks()
+    rec = headline_configs(pkg, dev, args.steps, args.warmup, peaks, None)
     print(json.dumps({
-        "metric": "us/call (geomean of configs 1-5)", "value": geo, "unit": "us",
-        "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "metric": "us/call (geomean of configs 1-5)", "value": rec["geomean_us_per_call"],
+        "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
         "dtype": "e2m1xe4m3->f32->f16", "data": "synthetic (seeded)",
-        "config": {"workload": "cfg1..cfg5", "timing": "median of per-call events; L2 flushed "
-                   "before each call when a configuration's inputs fit in L2"},
-        "per_config": per, "peak_source": f"{kind}: burst bf16 x 4 / HBM copy",
+        "config": {"workload": "cfg1..cfg5", "timing": rec["timing"]},
+        "per_config": rec["per_config"], "peak_source": f"{kind}: burst bf16 x 4 / HBM copy",
     }), flush=True)
+
+
+def sharded_cfg5(pkg, dev, world: int, rank: int, steps: int, warmup: int, barrier,
+                 max_over_ranks, sum_over_ranks, tensor_peak: float, gather_group_ok: bool):
+    """cfg5 (256 gated experts, 262144 routed rows) with its experts split over the ranks:
+    rank r computes expert_shard(256, P, r) (strong scaling of the one configuration;
+    P = 1 is the whole configuration on one GPU). Calls back to back, events around
+    `steps` calls, max over ranks. With P > 1 the same calls followed by the NCCL
+    all-gather of every expert's fp16 output to every rank (the GEMM writes into the
+    gather's send slab; ExpertOutputGather)."""
+    import torch
+
+    EP = pkg.expert_parallel
+    G = len(pkg.workloads.config_rows("cfg5")[0])
+    sh = EP.expert_shard(G, world, rank)
+    prob = pkg.workloads.make_config("cfg5", seed=0, device=dev, experts=slice(sh.start, sh.stop))
+    all_m = prob.meta["all_m"]
+    gat = None
+    if world > 1 and gather_group_ok:
+        gat = EP.ExpertOutputGather(all_m, prob.n, dev)
+        prob.c = list(gat.local_outputs)
+    plan = pkg.GroupedGemmPlan(prob.a, prob.b, prob.sfa, prob.sfb, prob.c, prob.problem_sizes(),
+                               alpha=prob.alpha, b2=prob.b2, sfb2=prob.sfb2, alpha2=prob.alpha2)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, n):
+        for _ in range(max(warmup, 3)):
+            fn()
+        torch.cuda.synchronize(dev)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / n)
+
+    n = max(3, min(steps, 20))
+    ms = timed(lambda: plan.run(stream), n)
+    flops_job = sum_over_ranks(prob.flops())
+    tf = flops_job / (ms * 1e-3) / 1e12
+    rec = {"us_per_call": ms * 1e3, "tflops": tf, "steps": n,
+           "frac_of_per_gpu_peak": tf / (world * tensor_peak),
+           "experts_per_rank": len(sh), "rows_this_rank": int(sum(prob.m)),
+           "flops_total": flops_job, "scaling": "strong",
+           "device_error_bits": plan.check_device_errors(stream),
+           "what": "GroupedGemmPlan.run of this rank's expert shard, back to back, max over "
+                   "ranks; frac against P x 4 x sustained bf16"}
+    if gat is not None:
+        def both():
+            plan.run(stream)
+            gat.run()
+
+        gms = timed(both, n)
+        rec["with_gather"] = {
+            "us_per_call": gms * 1e3, "tflops": flops_job / (gms * 1e-3) / 1e12,
+            "bytes_received_per_rank": gat.bytes_received,
+            "what": "the same calls, each followed by one NCCL all_gather_into_tensor of the "
+                    "fp16 output slabs (every expert's output on every rank)"}
+    del plan, gat, prob
+    torch.cuda.empty_cache()
+    return rec
+
+
+REFERENCE_MODULE = os.path.join(ROOT, "baseline", "_ref", "submission.py")
+
+
+def load_reference_module():
+    """The reference's own kernel module (its submission.py, installed unmodified into
+    baseline/_ref by baseline/install_reference.py), imported under another name so that
+    it does not shadow this repository's submission.py. None if it is not installed."""
+    import importlib.util
+
+    if not os.path.exists(REFERENCE_MODULE):
+        return None
+    ref_dir = os.path.dirname(REFERENCE_MODULE)
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)  # its `from task import input_t, output_t`
+    spec = importlib.util.spec_from_file_location("nvfp4_reference_submission", REFERENCE_MODULE)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def reference_kernel_leg(pkg, dev, cfg: str, steps: int, warmup: int, ref=None) -> dict:
+    """The reference's own sm_100 kernel (CuTe DSL, submission.py:80-589) through its own
+    custom_kernel (submission.py:788-858, the 4-tuple grouped path) against this
+    library's custom_kernel, on the same device-resident inputs of configuration `cfg`
+    (global scale 1: the reference has none). Its JIT compile (the first call) is timed
+    apart and excluded. Both are timed the same two ways: one call per event pair (median;
+    a 256 MiB L2 flush before each call when the inputs fit in L2) and `steps` calls back
+    to back between one event pair. Outputs: the reference's and ours compared bit for bit,
+    and both against the CPU oracle on up to two groups (rtol = atol = 1e-2)."""
+    import numpy as np
+    import torch
+
+    from oracle import nvfp4_oracle as O
+
+    if ref is None:
+        ref = load_reference_module()
+    if ref is None:
+        return {"unavailable": "baseline/_ref/submission.py not installed "
+                               "(python baseline/install_reference.py REFERENCE_DIR)"}
+    prob = pkg.workloads.make_config(cfg, seed=0, device=dev)
+    if prob.gated:
+        return {"unavailable": f"{cfg} is gated: the reference's grouped path has no gated form"}
+    prob.alpha = [1.0] * prob.num_groups
+    data = prob.reference_data()
+    data = (data[0], data[1], data[2], [tuple(ps) for ps in data[3]])
+    stream = torch.cuda.current_stream(dev)
+    t0 = time.perf_counter()
+    ref.custom_kernel(data)
+    torch.cuda.synchronize(dev)
+    compile_s = time.perf_counter() - t0
+    ref_out = [c.clone() for c in prob.c]
+    for c in prob.c:
+        c.fill_(float("nan"))
+    pkg.custom_kernel(data)
+    torch.cuda.synchronize(dev)
+    ours_out = [c.clone() for c in prob.c]
+    equal = sum(int(torch.equal(x.view(torch.int16), y.view(torch.int16)))
+                for x, y in zip(ref_out, ours_out))
+    oracle = {}
+    for g in [g for g in range(prob.num_groups) if prob.m[g] > 0][:2]:
+        a, b = prob.a[g].cpu().numpy(), prob.b[g].cpu().numpy()
+        ref32 = O.ref_gemm_fp32(a, b, prob.sfa_plain[g].cpu().numpy(), prob.sfb_plain[g].cpu().numpy())
+        with np.errstate(over="ignore"):
+            exp = ref32.astype(np.float16)
+        r_ref = O.compare_fp16(ref_out[g].cpu().numpy(), exp, ref32, rtol=1e-2, atol=1e-2)
+        r_ours = O.compare_fp16(ours_out[g].cpu().numpy(), exp, ref32, rtol=1e-2, atol=1e-2)
+        oracle[f"group{g}"] = {"reference_ok": bool(r_ref["ok"]), "ours_ok": bool(r_ours["ok"]),
+                               "reference_mismatches": int(r_ref.get("mismatches", 0)),
+                               "ours_mismatches": int(r_ours.get("mismatches", 0))}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    small = prob.input_bytes() < L2_BYTES
+
+    def isolated(fn):
+        for _ in range(max(warmup, 3)):
+            fn()
+        torch.cuda.synchronize(dev)
+        times = []
+        for _ in range(steps):
+            if small:
+                flush.fill_(1)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            times.append(e0.elapsed_time(e1) * 1e3)
+        return sorted(times)[len(times) // 2]
+
+    def back_to_back(fn):
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) * 1e3 / steps
+
+    run_ref = lambda: ref.custom_kernel(data)
+    run_ours = lambda: pkg.custom_kernel(data)
+    rec = {"config": cfg, "compile_s": compile_s,
+           "reference_us_isolated": isolated(run_ref), "ours_us_isolated": isolated(run_ours),
+           "reference_us_back_to_back": back_to_back(run_ref),
+           "ours_us_back_to_back": back_to_back(run_ours),
+           "groups_bit_identical": f"{equal}/{prob.num_groups}", "oracle": oracle,
+           "flops": prob.flops(), "algorithmic_bytes": prob.algorithmic_bytes(),
+           "what": "the reference's custom_kernel (its CuTe-DSL sm_100 kernel, unmodified) vs "
+                   "this library's custom_kernel on the same inputs; times are device time per "
+                   "call including each API's own per-call host work"}
+    rec["speedup_isolated"] = rec["reference_us_isolated"] / rec["ours_us_isolated"]
+    rec["speedup_back_to_back"] = rec["reference_us_back_to_back"] / rec["ours_us_back_to_back"]
+    del prob, data, flush
+    torch.cuda.empty_cache()
+    return rec
+
+
+def run_reference_gpu(args):
+    """`--impl reference_gpu`: the reference's own GPU kernel against ours, one JSON line
+    with one record per configuration of `--config` (comma separated; 1 GPU, rank 0)."""
+    import torch
+
+    import submission
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    pkg = submission.load_package()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    t0 = time.perf_counter()
+    ref = load_reference_module()
+    import_s = time.perf_counter() - t0
+    recs = [reference_kernel_leg(pkg, dev, c, args.steps, args.warmup, ref)
+            for c in args.config.split(",")]
+    print(json.dumps({"impl": "reference_gpu", "metric": "us/call, reference kernel vs ours",
+                      "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "higher_is_better": False, "import_s": import_s, "records": recs}),
+          flush=True)
 
 
 def run_quantize(args):
@@ -661,6 +951,8 @@ def main():
         return run_all_configs(args)
     if args.impl == "reference":
         return run_reference(args)
+    if args.impl == "reference_gpu":
+        return run_reference_gpu(args)
 
     import torch
     import torch.distributed as dist
@@ -677,6 +969,11 @@ def main():
         import datetime
 
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+        # One line per rank on stderr (stdout carries only the JSON line): the NCCL
+        # communicator's size as this rank sees it.
+        print(f"[bench] rank {rank} of {dist.get_world_size()} (local {local_rank}) on "
+              f"{torch.cuda.get_device_name(dev)}, NCCL {torch.cuda.nccl.version()}",
+              file=sys.stderr, flush=True)
 
     # Each rank owns its own experts (seed = rank): weak scaling, no data-path collective.
     # With --shard-experts the ranks split one configuration's experts (strong scaling).
@@ -713,6 +1010,13 @@ def main():
             return x
         t = torch.tensor([x], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
         return float(t.item())
 
     # ---------------------------------------------------------------- device-resident timing
@@ -914,37 +1218,114 @@ def main():
         except Exception as exc:  # the library path is a comparison, not part of the product
             lib_base = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
 
-    # ---------------------------------------------------------------- end to end (host buffers)
-    e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
-    host_in = [t.cpu().pin_memory() for t in
-               prob.a + prob.b + prob.sfa + prob.sfb + (prob.b2 or []) + (prob.sfb2 or [])]
-    dev_in = prob.a + prob.b + prob.sfa + prob.sfb + (prob.b2 or []) + (prob.sfb2 or [])
-    host_out = [torch.empty(c.shape, dtype=c.dtype).pin_memory() for c in prob.c]
-    data = prob.reference_data()
-    scales = prob.global_scales()
+    # ---------------------------------------------------------------- measured NVFP4 peak
+    # The library's dense block-scaled FP4 rate on this GPU (every rank its own GPU, rank 0
+    # reports), beside the 4 x bf16 figure derived from MEASURED_PEAKS.json.
+    nvfp4_peak = None
+    if not args.no_extras:
+        try:
+            nvfp4_peak = measure_nvfp4_peak(dev)
+        except Exception as exc:  # a comparison figure, not part of the product
+            nvfp4_peak = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+    fp4_ok = nvfp4_peak is not None and "burst_tflops" in nvfp4_peak
 
-    def e2e_step():
-        for h, d in zip(host_in, dev_in):
-            d.copy_(h, non_blocking=True)
-        pkg.custom_kernel(data, global_scales=scales, tile_n=args.tile_n, stream=stream,
+    # ---------------------------------------------------------------- cfg5 split over the ranks
+    peaks, peak_kind = load_peaks()
+    sustained_key = "bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks else "bf16_tflops"
+    sharded = None
+    if not args.no_extras:
+        sharded = sharded_cfg5(pkg, dev, world, rank, args.steps, args.warmup, barrier,
+                               max_over_ranks, sum_over_ranks,
+                               FP4_PER_BF16 * float(peaks[sustained_key]), True)
+        if fp4_ok:
+            sharded["frac_of_measured_nvfp4_sustained"] = (
+                sharded["tflops"] / (world * nvfp4_peak["sustained_tflops"]))
+
+    # ---------------------------------------------------------------- headline configs (N = 1)
+    configs = None
+    if rank == 0 and world == 1 and not args.no_extras:
+        configs = headline_configs(pkg, dev, args.steps, args.warmup, peaks,
+                                   nvfp4_peak if fp4_ok else None)
+
+    # ---------------------------------------------------------------- end to end (host buffers)
+    # Every step copies its inputs from pinned host memory, calls custom_kernel and copies
+    # its fp16 outputs back. Two buffer sets: step i's H2D (copy stream) overlaps step i-1's
+    # kernel and D2H (second copy stream), events order each set's reuse. `serial` is the
+    # same step with all copies and the call on one stream, one step after another.
+    e2e_steps = args.e2e_steps or max(4, min(args.steps, 10))
+    probs = [prob, pkg.workloads.make_config(args.config, seed=seed, device=dev, experts=shard)]
+
+    def inputs_of(p):
+        return p.a + p.b + p.sfa + p.sfb + (p.b2 or []) + (p.sfb2 or [])
+
+    host_in = [t.cpu().pin_memory() for t in inputs_of(prob)]
+    dev_in = [inputs_of(p) for p in probs]
+    host_out = [[torch.empty(c.shape, dtype=c.dtype).pin_memory() for c in p.c] for p in probs]
+    datas = [p.reference_data() for p in probs]
+    scales = [p.global_scales() for p in probs]
+    h2d_stream = torch.cuda.Stream(dev)
+    d2h_stream = torch.cuda.Stream(dev)
+
+    def call(i, st):
+        pkg.custom_kernel(datas[i], global_scales=scales[i], tile_n=args.tile_n, stream=st,
                           cta=args.cta, split_k=args.split_k)
-        for h, c in zip(host_out, prob.c):
+
+    def e2e_serial_step():
+        for h, d in zip(host_in, dev_in[0]):
+            d.copy_(h, non_blocking=True)
+        call(0, stream)
+        for h, c in zip(host_out[0], probs[0].c):
             h.copy_(c, non_blocking=True)
 
-    e2e_step()
-    torch.cuda.synchronize(dev)
-    barrier()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    ev1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / e2e_steps
+    k_done = [torch.cuda.Event(), torch.cuda.Event()]
+    in_done = [torch.cuda.Event(), torch.cuda.Event()]
+    out_done = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def e2e_pipelined(n):
+        h2d_stream.wait_stream(stream)
+        d2h_stream.wait_stream(stream)
+        for i in range(n):
+            b = i % 2
+            with torch.cuda.stream(h2d_stream):
+                h2d_stream.wait_event(k_done[b])  # the kernel two steps back read set b
+                for h, d in zip(host_in, dev_in[b]):
+                    d.copy_(h, non_blocking=True)
+                in_done[b].record(h2d_stream)
+            stream.wait_event(in_done[b])
+            stream.wait_event(out_done[b])  # set b's outputs of two steps back are on the host
+            call(b, stream)
+            k_done[b].record(stream)
+            with torch.cuda.stream(d2h_stream):
+                d2h_stream.wait_event(k_done[b])
+                for h, c in zip(host_out[b], probs[b].c):
+                    h.copy_(c, non_blocking=True)
+                out_done[b].record(d2h_stream)
+        stream.wait_stream(h2d_stream)
+        stream.wait_stream(d2h_stream)
+
+    def e2e_timed(fn, n):
+        torch.cuda.synchronize(dev)
+        barrier()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        fn(n)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        return max_over_ranks(ev0.elapsed_time(ev1)) / n
+
+    e2e_pipelined(2)
+    e2e_serial_step()
+    e2e_ms = e2e_timed(e2e_pipelined, e2e_steps)
+    e2e_serial_ms = e2e_timed(lambda n: [e2e_serial_step() for _ in range(n)], e2e_steps)
+    same_out = all(torch.equal(x.view(torch.int16), y.view(torch.int16))
+                   for x, y in zip(probs[0].c, probs[1].c))
     h2d = sum(t.numel() * t.element_size() for t in host_in)
-    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    d2h = sum(t.numel() * t.element_size() for t in host_out[0])
+    data = datas[0]
+    scales = scales[0]
+    del probs[1], dev_in, datas
 
     # The drop-in call itself on device-resident inputs: custom_kernel(data) back to back
     # (device time per call, and the host time to issue one call).
@@ -978,10 +1359,8 @@ def main():
     if rank != 0:
         return
 
-    peaks, peak_kind = load_peaks()
     # `value` is timed inside a sustained-load window (the clocks above describe it), so
     # its roofline uses the sustained bf16 figure; the burst timing uses the burst one.
-    sustained_key = "bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks else "bf16_tflops"
     tensor_peak = FP4_PER_BF16 * float(peaks[sustained_key])
     burst_peak = FP4_PER_BF16 * float(peaks["bf16_tflops"])
     achieved = flops_rank / (ms_per_step * 1e-3) / 1e12
@@ -1027,7 +1406,13 @@ def main():
         "device_error_bits": errors,
         "e2e": {"value": flops_job / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "custom_kernel(data) with pinned-host copies of inputs and outputs"},
+                "api": "custom_kernel(data); every step: H2D of all inputs from pinned host "
+                       "memory, the call, D2H of all outputs; two buffer sets so that step i's "
+                       "H2D overlaps step i-1's call and D2H (two copy streams)",
+                "serial": {"value": flops_job / (e2e_serial_ms * 1e-3) / 1e12,
+                           "ms_per_step": e2e_serial_ms,
+                           "what": "the same step with copies and call on one stream"},
+                "buffer_sets_equal_outputs": same_out},
         "cuda_graph": graph_info,
         "custom_kernel_device_resident": {
             "us_per_call": ck_ms * 1e3, "host_us_per_call": sorted(ck_host)[len(ck_host) // 2] * 1e6,
@@ -1049,9 +1434,23 @@ def main():
                       "peak_source": f"{peak_kind}: 4 x {sustained_key} "
                                      f"({peaks[sustained_key]}; timed under sustained load)",
                       "traffic": traffic, "algorithmic_bytes": alg_bytes,
-                      "hbm_frac": hbm_gbs / hbm_peak}),
+                      "hbm_frac": hbm_gbs / hbm_peak,
+                      "frac_of_measured_nvfp4": (achieved / nvfp4_peak["sustained_tflops"]
+                                                 if fp4_ok else None),
+                      "frac_of_nominal_9pf": achieved / NOMINAL_FP4_TFLOPS,
+                      "peak_note": "frac: 4 x measured bf16 (the denominator of record); "
+                                   "frac_of_measured_nvfp4: cuBLASLt's dense NVFP4 rate "
+                                   "measured in this run (sustained); frac_of_nominal_9pf: "
+                                   "B200's nominal dense FP4 figure"}),
         "clocks": clk,
     }
+    if nvfp4_peak is not None:
+        line["nvfp4_peak"] = nvfp4_peak
+    if sharded is not None:
+        line["sharded_cfg5"] = sharded
+    if configs is not None:
+        line["geomean_us_per_call"] = configs["geomean_us_per_call"]
+        line["configs"] = configs
     if gather is not None:
         line["with_gather"] = gather
     if lib_base is not None:

@@ -80,6 +80,54 @@ def all_gather_expert_outputs(local_outputs: Sequence[torch.Tensor],
     return outs
 
 
+class ExpertOutputGather:
+    """Preallocated all-gather of every rank's per-expert fp16 outputs.
+
+    The same exchange as :func:`all_gather_expert_outputs` without its packing copy and
+    per-call allocations: ``local_outputs`` are [M_g, n] views into this rank's part of
+    the send slab, so the grouped GEMM writes its outputs where NCCL reads them, and
+    :meth:`run` is one ``all_gather_into_tensor``. ``outputs`` are views of the receive
+    slab in global expert order (rank r's experts expert_shard(G, P, r)); their contents
+    are those of the last :meth:`run`.
+    """
+
+    def __init__(self, rows_per_expert: Sequence[int], n: int, device: torch.device,
+                 group: dist.ProcessGroup | None = None):
+        self.group = group
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        self.rows = [int(m) for m in rows_per_expert]
+        self.n = int(n)
+        layout = slab_layout(self.rows, self.n, world)
+        self.max_elems = max(e for _, _, e in layout)
+        self.send = torch.zeros(self.max_elems, dtype=torch.float16, device=device)
+        self.recv = torch.empty(world * self.max_elems, dtype=torch.float16, device=device)
+        first, count, _ = layout[rank]
+        self.local_outputs = self._views(self.send, 0, first, count)
+        self.outputs = []
+        for r, (f, cnt, _) in enumerate(layout):
+            self.outputs += self._views(self.recv, r * self.max_elems, f, cnt)
+        self.bytes_received = int((world - 1) * self.max_elems * 2)
+
+    def _views(self, buf: torch.Tensor, base: int, first: int, count: int) -> list:
+        out, off = [], base
+        for g in range(first, first + count):
+            m = self.rows[g]
+            out.append(buf[off:off + m * self.n].view(m, self.n))
+            off += m * self.n
+        return out
+
+    def run(self) -> list:
+        if dist.get_backend(self.group) == "nccl":
+            dist.all_gather_into_tensor(self.recv.view(torch.uint8), self.send.view(torch.uint8),
+                                        group=self.group)
+        else:
+            world = dist.get_world_size(self.group)
+            dist.all_gather(list(self.recv.view(torch.uint8).chunk(world)),
+                            self.send.view(torch.uint8), group=self.group)
+        return self.outputs
+
+
 class ExpertParallelGroupedGemm:
     """Run this rank's shard of a grouped problem and optionally gather all outputs.
 

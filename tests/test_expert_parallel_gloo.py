@@ -94,6 +94,64 @@ def test_gather_matches_single_process(pkg, world, rows):
     assert sorted(covered) == list(range(len(rows)))
 
 
+def _slab_worker(rank, world, port, rows, n, q):
+    try:
+        import sys
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, root)
+        import submission
+
+        pkg = submission.load_package()
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=__import__("datetime").timedelta(seconds=60))
+        EP = pkg.expert_parallel
+        gat = EP.ExpertOutputGather(rows, n, torch.device("cpu"))
+        sh = EP.expert_shard(len(rows), world, rank)
+        assert len(gat.local_outputs) == len(sh)
+        results = []
+        for call in range(2):  # the slabs are reused: the second call overwrites the first
+            for g, t in zip(sh, gat.local_outputs):
+                t.copy_(_slab_rows(rows[g], n, g, call))
+            results.append([o.clone().numpy() for o in gat.run()])
+        q.put((rank, results))
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as e:  # report instead of hanging the parent
+        q.put((rank, repr(e)))
+
+
+def _slab_rows(m, n, expert, call):
+    return (torch.arange(m * n, dtype=torch.float32).view(m, n) * 0.25
+            + 1000 * expert + 7 * call).to(torch.float16)
+
+
+@pytest.mark.parametrize("world,rows", [(2, [5, 0, 17, 3, 64]), (3, [1, 2, 3, 0, 0, 7, 9])])
+def test_preallocated_gather_slabs(world, rows):
+    """ExpertOutputGather: each rank writes its experts' rows into its send-slab views;
+    after run() every rank holds every expert's rows in global order, on two calls."""
+    n = 24
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_slab_worker, args=(r, world, port, rows, n, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=180) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank in range(world):
+        assert isinstance(res[rank], list), res[rank]
+        for call, outs in enumerate(res[rank]):
+            assert len(outs) == len(rows)
+            for g, o in enumerate(outs):
+                assert np.array_equal(o, _slab_rows(rows[g], n, g, call).numpy()), (rank, call, g)
+
+
 def test_shard_bookkeeping(pkg):
     EP = pkg.expert_parallel
     for G in (0, 1, 7, 256):

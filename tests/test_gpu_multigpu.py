@@ -3,6 +3,8 @@ kernel and the outputs are all-gathered over NCCL (skipped when fewer than 2 GPU
 
 Each rank checks its own experts against the oracle; the parent then checks that every
 rank's gathered list equals, byte for byte, the concatenation of all ranks' local outputs.
+Two exchanges are covered: all_gather_expert_outputs (packs the outputs per call) and
+ExpertOutputGather (the GEMM writes its outputs into the preallocated send slab).
 """
 from __future__ import annotations
 
@@ -27,7 +29,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, gated, q):
+def _worker(rank, world, port, gated, slab, q):
     try:
         import sys
 
@@ -51,7 +53,16 @@ def _worker(rank, world, port, gated, q):
         sh = ep.shard
         prob = pkg.workloads.make_problem(f"ep{rank}", ROWS[sh.start:sh.stop], N, K, gated=gated,
                                           seed=100 + rank, device=dev, alpha_range=(0.5, 2.0))
-        outs = ep.run(prob, ROWS, gather=True)
+        if slab:
+            gat = EP.ExpertOutputGather(ROWS, N, dev)
+            for c, v in zip(prob.c, gat.local_outputs):
+                v.copy_(c)  # the harness's randn prefill, now in the slab
+            prob.c = list(gat.local_outputs)
+            pkg.grouped_gemm(prob.a, prob.b, prob.sfa, prob.sfb, prob.c, prob.problem_sizes(),
+                             alpha=prob.alpha, b2=prob.b2, sfb2=prob.sfb2, alpha2=prob.alpha2)
+            outs = gat.run()
+        else:
+            outs = ep.run(prob, ROWS, gather=True)
         torch.cuda.synchronize()
         # This rank's experts against the oracle.
         for i in range(prob.num_groups):
@@ -79,13 +90,14 @@ def _worker(rank, world, port, gated, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("gated", [False, True])
-def test_two_gpu_shards_and_nccl_gather(gated):
+@pytest.mark.parametrize("gated,slab", [(False, False), (True, False), (False, True), (True, True)])
+def test_two_gpu_shards_and_nccl_gather(gated, slab):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, gated, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, gated, slab, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = {}
