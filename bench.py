@@ -26,6 +26,9 @@ Our arm (default):
     of all fp16 outputs to every rank.
   * `configs` + `geomean_us_per_call` (N = 1): BASELINE's headline form, us per
     isolated call of configs 1-5, their geomean and each one's roofline fraction.
+  * `reference_kernel` (N = 1): the reference's own sm_100 CuTe-DSL kernel through its
+    own custom_kernel (installed unmodified by baseline/install_reference.py) on the
+    same inputs, timed beside this library's custom_kernel, outputs compared.
 With N GPUs each rank runs its own set of experts of the same shape for `value` (weak
 scaling; expert parallelism needs no collective on the data path).
 
@@ -1247,6 +1250,16 @@ def main():
         configs = headline_configs(pkg, dev, args.steps, args.warmup, peaks,
                                    nvfp4_peak if fp4_ok else None)
 
+    # ---------------------------------------------------------------- the reference's kernel (N = 1)
+    # The reference's own sm_100 kernel (its CuTe-DSL submission, unmodified) through its own
+    # custom_kernel on this configuration, beside this library's custom_kernel.
+    ref_kernel = None
+    if rank == 0 and world == 1 and not args.no_extras and not prob.gated:
+        try:
+            ref_kernel = reference_kernel_leg(pkg, dev, args.config, args.steps, args.warmup)
+        except Exception as exc:  # a comparison, not part of the product
+            ref_kernel = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+
     # ---------------------------------------------------------------- end to end (host buffers)
     # Every step copies its inputs from pinned host memory, calls custom_kernel and copies
     # its fp16 outputs back. Two buffer sets: step i's H2D (copy stream) overlaps step i-1's
@@ -1451,6 +1464,8 @@ def main():
     if configs is not None:
         line["geomean_us_per_call"] = configs["geomean_us_per_call"]
         line["configs"] = configs
+    if ref_kernel is not None:
+        line["reference_kernel"] = ref_kernel
     if gather is not None:
         line["with_gather"] = gather
     if lib_base is not None:

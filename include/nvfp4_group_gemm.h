@@ -67,6 +67,14 @@ typedef enum nvfp4_status {
                                        K >= 4096; single CTAs otherwise */
 #define NVFP4_FLAG_SPLIT_K 0x100u /* allow split-K of a single-CTA launch's last partial wave
                                      (needs the split scratch, see NVFP4_SPLIT_SCRATCH_BYTES) */
+#define NVFP4_FLAG_STREAM_K 0x200u /* weight-streaming launches (non-empty groups averaging
+                                      at most 64 rows, one K) with at least one full wave of
+                                      tiles: share the last full wave and the partial one out
+                                      as equal k-iteration ranges, one per CTA (needs the
+                                      split scratch). Off by default: measured slower than
+                                      dynamic tile claims (64 experts, N 1536, K 4096: 64.2 vs
+                                      53.0 us per call), whose balance follows the real cost
+                                      of each tile */
 #define NVFP4_FLAG_WEIGHT_STATIONARY 0x80u /* force the weight-stationary kernel (non-gated
                                               only): tiles of 128 weight rows x 64 token
                                               rows, computed as C^T so that small groups

@@ -37,6 +37,7 @@ FLAG_SINGLE_CTA = 0x20
 FLAG_DIAG_SKIP_MMA = 0x40
 FLAG_WEIGHT_STATIONARY = 0x80
 FLAG_SPLIT_K = 0x100
+FLAG_STREAM_K = 0x200
 
 # Device error bits (WorkspaceHeader::error_bits).
 DEV_ERR_PRODUCER_TIMEOUT = 1 << 0

@@ -133,6 +133,29 @@ __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity,
   }
 }
 
+// Stream-K hand-off counter: arrivals of a cut tile's two pieces count in the low byte;
+// this bit says the first piece's partial rows are stored.
+constexpr int32_t kSkPublished = 0x100;
+
+// Bounded wait until bit `bit` of a word that another SM sets (stream-K partial rows
+// published); same timeout and abort scheme as wait_phase.
+__device__ __forceinline__ bool wait_global_bit(const int32_t* word, int bit,
+                                                volatile uint32_t* abort_flag,
+                                                uint32_t* error_bits, uint32_t reason) {
+  const volatile int32_t* w = word;
+  const uint64_t t0 = ptx::globaltimer_ns();
+  while ((*w & bit) == 0) {
+    if (*abort_flag) return false;
+    if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      *abort_flag = 1u;
+      atomicOr(error_bits, reason);
+      return false;
+    }
+    __nanosleep(128);
+  }
+  return true;
+}
+
 // Warp-wide bounded wait with one decision for all lanes (the epilogue's TMEM
 // loads are warp-collective, so lanes must never disagree about a timeout).
 // Lane 0 waits; once it has seen the phase complete, every lane re-probes the
@@ -349,11 +372,26 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       bool ok = true;
       auto acquire_maps = [&](int grp) {
         const TmaDesc* m = p.maps + static_cast<size_t>(grp) * kMapsPerGroup;
-        ptx::tensormap_fence_acquire(&m[kMapA]);
-        ptx::tensormap_fence_acquire(&m[kMapB]);
-        if (GATED) ptx::tensormap_fence_acquire(&m[kMapB2]);
+        ptx::tensormap_acquire_prefetch(&m[kMapA]);
+        ptx::tensormap_acquire_prefetch(&m[kMapB]);
+        if (GATED) ptx::tensormap_acquire_prefetch(&m[kMapB2]);
       };
-      int unit = blockIdx.x;  // >= total_units only in segment launches: no tile
+      // Stream-K: whole tiles blockIdx.x, + grid, ... below stream_k_first_tile, then this
+      // CTA's k-iterations [sk_pos, sk_end) of the stream-K tiles (tile sk_first + it / kt).
+      const bool sk = p.stream_k_iters > 0;
+      const int sk_first = sk ? p.stream_k_first_tile : 0;
+      const int sk_kt = sk ? p.stream_k_ktiles : 1;
+      int64_t sk_pos = sk ? static_cast<int64_t>(blockIdx.x) * p.stream_k_iters : 0;
+      const int64_t sk_end =
+          sk ? (sk_pos + p.stream_k_iters < p.stream_k_total_iters ? sk_pos + p.stream_k_iters
+                                                                   : p.stream_k_total_iters)
+             : 0;
+      bool sk_whole = sk && static_cast<int>(blockIdx.x) < sk_first;  // in the round-robin part
+      auto sk_unit = [&](int64_t it) -> int {
+        return it < sk_end ? sk_first + static_cast<int>(it / sk_kt) : total_units;
+      };
+      int unit = !sk ? static_cast<int>(blockIdx.x)  // >= total_units only in segment launches
+                     : (sk_whole ? static_cast<int>(blockIdx.x) : sk_unit(sk_pos));
       int tile, split;
       unit_tile(p, unit, tile, split);
       int g = advance_group(tile_ends, groups, p.num_groups, 0, tile);
@@ -368,7 +406,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                         p.error_bits, kDevErrProducerTimeout))
           break;
         int k0 = 0, k1 = 0;
-        if (unit < total_units) unit_krange(p, split, gd.k / kBlockK, k0, k1);
+        if (unit < total_units) {
+          if (sk && !sk_whole) {
+            k0 = static_cast<int>(sk_pos - static_cast<int64_t>(unit - sk_first) * sk_kt);
+            const int64_t left = sk_end - sk_pos;
+            k1 = left < sk_kt - k0 ? k0 + static_cast<int>(left) : sk_kt;
+          } else {
+            unit_krange(p, split, gd.k / kBlockK, k0, k1);
+          }
+        }
         sched_info[4 * slot + 0] = unit;
         sched_info[4 * slot + 1] = g;
         sched_info[4 * slot + 2] = k0;
@@ -439,6 +485,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         int next_rb = rb;
         bool resolved = false;
         auto claim_next = [&]() -> int {
+          if (sk) {
+            if (sk_whole) {
+              const int nu = unit + static_cast<int>(gridDim.x);
+              return nu < sk_first ? nu : sk_unit(sk_pos);
+            }
+            return sk_unit(sk_pos + (k1 - k0));
+          }
           if (p.dynamic_schedule)
             return static_cast<int>(gridDim.x + atomicAdd(p.tile_counter, 1u));
           return unit + static_cast<int>(gridDim.x);
@@ -503,6 +556,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         if (!ok) break;
         if (!resolved) resolve_next();
+        if (sk_whole) {
+          if (unit + static_cast<int>(gridDim.x) >= sk_first) sk_whole = false;
+        } else {
+          sk_pos += k1 - k0;
+        }
         unit = next_unit;
         tile = next_tile;
         split = next_split;
@@ -628,6 +686,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         break;
       const int unit = sched_info[4 * slot + 0];
       const int g = sched_info[4 * slot + 1];
+      const int piece_k0 = sched_info[4 * slot + 2];
+      const int piece_k1 = sched_info[4 * slot + 3];
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&sched_empty[slot]);
       if (unit >= total_units) break;
@@ -637,7 +697,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const int rb = seg_row(p, g);  // C rows of the group start here
       const TmaDesc* map_c = p.maps + static_cast<size_t>(g) * kMapsPerGroup + kMapC;
       if (!DIRECT && split < 0 && g != acquired_g) {
-        if (lane == 0) ptx::tensormap_fence_acquire(map_c);
+        if (lane == 0) ptx::tensormap_acquire_prefetch(map_c);
         acquired_g = g;
       }
       const int acc = static_cast<int>(local & 1u);
@@ -756,6 +816,39 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
       };
       bool released = false;
+      // Stream-K piece of a tile cut by the range boundary of CTA sk_b (its later k-tiles
+      // are this CTA's first piece, its first k-tiles the previous CTA's last piece). Per
+      // warp quarter, the piece that counts in first (arrivals in the counter's low byte)
+      // stores its fp32 rows to slot sk_b and then publishes them (kSkPublished, set with
+      // atomicOr so that no arrival can carry into it); the other waits for that bit, adds the
+      // stored rows to its own (a two-term fp32 sum: the same bits whichever piece comes
+      // second) and stores C.
+      int sk_role = 0;  // 0: whole tile; 1: store the partial rows; 2: add them and store C
+      int32_t* sk_ctr = nullptr;
+      const float* sk_src = nullptr;
+      float* sk_dst = nullptr;
+      if (!GATED && p.stream_k_iters > 0 && row0 < gd.m &&
+          (piece_k0 > 0 || piece_k1 < gd.k / kBlockK)) {
+        const int sk_b = piece_k0 > 0 ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) + 1;
+        sk_ctr = p.split_counters + 4 * sk_b + quarter;
+        int old = 0;
+        if (lane == 0) old = atomicAdd(sk_ctr, 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        sk_role = (old & 0xff) == 0 ? 1 : 2;
+        sk_dst = p.split_partials +
+                 (static_cast<size_t>(sk_b) * kBlockM + 32 * quarter + lane) * MMA_N;
+        sk_src = sk_dst;
+        if (sk_role == 2) {
+          int ready = 1;
+          if (lane == 0)
+            ready = wait_global_bit(sk_ctr, kSkPublished, abort_flag, p.error_bits,
+                                    kDevErrEpilogueTimeout)
+                        ? 1 : 0;
+          ready = __shfl_sync(0xffffffffu, ready, 0);
+          if (!ready) break;
+          __threadfence();
+        }
+      }
       if (row0 < gd.m) {
         const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(32 * quarter) << 16) +
                                acc * Cfg::kAccStride;
@@ -800,7 +893,47 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
             continue;
           }
+          if (sk_role == 1) {
+            // First piece of a cut tile: its fp32 rows go to the boundary's slot.
+            if (row < gd.m) {
+              float4* dv = reinterpret_cast<float4*>(sk_dst + box * 64);
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                dv[c] = make_float4(__uint_as_float(v0[4 * c]), __uint_as_float(v0[4 * c + 1]),
+                                    __uint_as_float(v0[4 * c + 2]), __uint_as_float(v0[4 * c + 3]));
+                dv[8 + c] = make_float4(__uint_as_float(v1[4 * c]), __uint_as_float(v1[4 * c + 1]),
+                                        __uint_as_float(v1[4 * c + 2]), __uint_as_float(v1[4 * c + 3]));
+              }
+            }
+            continue;
+          }
+          if (sk_role == 2 && row < gd.m) {
+            // Second piece: add the stored rows (written by another SM: read through L2).
+            const float4* sv = reinterpret_cast<const float4*>(sk_src + box * 64);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const float4 f = __ldcg(sv + c);
+              v0[4 * c] = __float_as_uint(__uint_as_float(v0[4 * c]) + f.x);
+              v0[4 * c + 1] = __float_as_uint(__uint_as_float(v0[4 * c + 1]) + f.y);
+              v0[4 * c + 2] = __float_as_uint(__uint_as_float(v0[4 * c + 2]) + f.z);
+              v0[4 * c + 3] = __float_as_uint(__uint_as_float(v0[4 * c + 3]) + f.w);
+              const float4 h = __ldcg(sv + 8 + c);
+              v1[4 * c] = __float_as_uint(__uint_as_float(v1[4 * c]) + h.x);
+              v1[4 * c + 1] = __float_as_uint(__uint_as_float(v1[4 * c + 1]) + h.y);
+              v1[4 * c + 2] = __float_as_uint(__uint_as_float(v1[4 * c + 2]) + h.z);
+              v1[4 * c + 3] = __float_as_uint(__uint_as_float(v1[4 * c + 3]) + h.w);
+            }
+          }
           emit_box(v0, v1, u0, u1, box, DIRECT);
+        }
+        if (sk_role == 1) {
+          // Publish the stored rows to the other piece's warp.
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) atomicOr(sk_ctr, kSkPublished);
+        } else if (sk_role == 2) {
+          __syncwarp();
+          if (lane == 0) atomicExch(sk_ctr, 0);  // 0 again for the next launch
         }
       }
       if (!released) {

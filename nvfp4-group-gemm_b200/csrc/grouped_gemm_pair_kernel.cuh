@@ -136,13 +136,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         // Tensor maps of a group are acquired before its first loads: here for the CTA's
         // first tile, and otherwise behind the previous tile's first loads (below).
         auto acquire_maps = [&](const TmaDesc* m) {
-          ptx::tensormap_fence_acquire(&m[kMapA]);
-          ptx::tensormap_fence_acquire(&m[kMapB]);
-          ptx::tensormap_fence_acquire(&m[kMapSfa]);
-          ptx::tensormap_fence_acquire(&m[kMapSfb]);
+          ptx::tensormap_acquire_prefetch(&m[kMapA]);
+          ptx::tensormap_acquire_prefetch(&m[kMapB]);
+          ptx::tensormap_acquire_prefetch(&m[kMapSfa]);
+          ptx::tensormap_acquire_prefetch(&m[kMapSfb]);
           if (GATED) {
-            ptx::tensormap_fence_acquire(&m[kMapB2]);
-            ptx::tensormap_fence_acquire(&m[kMapSfb2]);
+            ptx::tensormap_acquire_prefetch(&m[kMapB2]);
+            ptx::tensormap_acquire_prefetch(&m[kMapSfb2]);
           }
         };
         if (g != acquired_g) {
@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       next_gd = groups[g_next];
       const TmaDesc* map_c = p.maps + static_cast<size_t>(g) * kMapsPerGroup + kMapC;
       if (g != acquired_g) {
-        if (lane == 0) ptx::tensormap_fence_acquire(map_c);
+        if (lane == 0) ptx::tensormap_acquire_prefetch(map_c);
         acquired_g = g;
       }
       const int tl = tile - gd.tile_start;

@@ -146,6 +146,22 @@ struct GemmParams {
   const int64_t* row_dest;
   uint8_t* dest_base[8];
   int64_t dest_ld;
+  // Stream-K schedule of the weight-streaming kernel (stream_k_iters > 0; every group has
+  // stream_k_ktiles k-tiles). Tiles [0, stream_k_first_tile) are whole units taken round
+  // robin (CTA c: c, c + grid, ...), so that the tiles running at any moment are
+  // neighbours (the m-tiles that share a weight tile run together and share it in L2).
+  // The remaining tiles form a tile-major iteration space of stream_k_total_iters
+  // k-iterations (tile stream_k_first_tile + j owns [j * ktiles, (j + 1) * ktiles)); CTA c
+  // then runs iterations [c * stream_k_iters, (c + 1) * stream_k_iters) of it, so every CTA
+  // ends with the same amount of work. A tile cut by the range boundary of CTA b (b >= 1)
+  // is computed in two pieces, its first k-tiles by CTA b - 1 and the rest by CTA b; per
+  // epilogue warp, the piece that finishes first stores its fp32 rows to split_partials
+  // slot b and the other adds them to its own and stores C (split_counters[4 b + warp
+  // quarter] orders the two; 0 between launches).
+  int32_t stream_k_iters;
+  int32_t stream_k_ktiles;
+  int64_t stream_k_total_iters;
+  int32_t stream_k_first_tile;
 };
 
 // Destination of slab row r of a scattered output (nullptr: not stored).

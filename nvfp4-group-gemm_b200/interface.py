@@ -339,7 +339,8 @@ def grouped_gemm_table(table: np.ndarray, flags: int, device: torch.device,
     s = stream or torch.cuda.current_stream(device)
     G = int(table.shape[0])
     ws = _workspace_for(device, s, _native.workspace_size_with_split(G)
-                        if flags & _native.FLAG_SPLIT_K else _native.workspace_size(G))
+                        if flags & (_native.FLAG_SPLIT_K | _native.FLAG_STREAM_K)
+                        else _native.workspace_size(G))
     with torch.cuda.device(device):
         _native.grouped_gemm_raw(table, flags, ws.buf.data_ptr(), ws.nbytes, s.cuda_stream)
     ws.drop_plan()

@@ -81,7 +81,7 @@ def _table(N, **kw):
     (dict(a=0), 0, 4),              # NULL operand of a non-empty group
     (dict(c=0x50008), 0, 3),        # misaligned output
     (dict(b2=0), 1, 4),             # gated without up weights
-    (dict(), 0x200, 1),             # unknown flag bit
+    (dict(), 0x400, 1),             # unknown flag bit
     (dict(), 0x10 | 0x20, 1),       # exclusive CTA modes
     (dict(), 0x10 | 0x2, 1),        # pairs need 256-column tiles
     (dict(), 0x2 | 0x4, 1),         # exclusive tile flags
