@@ -32,14 +32,27 @@
 
 namespace nvfp4 {
 
+// K bytes of A/B rows per pipeline stage of the pair kernel: 128 (a whole 256-element
+// k-tile, 128-byte swizzle) or 64 (half a k-tile, 64-byte swizzle: twice the stages of half
+// the size, released after two MMAs instead of four). The host encodes the pair launches'
+// operand and scale maps to match.
+#ifndef NVFP4_PAIR_STAGE_KBYTES
+#define NVFP4_PAIR_STAGE_KBYTES 128
+#endif
+constexpr int kPairStageKBytes = NVFP4_PAIR_STAGE_KBYTES;
+static_assert(kPairStageKBytes == 128 || kPairStageKBytes == 64, "64 or 128 K bytes per stage");
+constexpr int kPairStagesPerKTile = kRowBytesPerStage / kPairStageKBytes;
+constexpr int kPairSfBlocksPerStage = kPairStageKBytes / 32;  // one 512-B block per 64 K
+constexpr int kPairSfRowsPerStage = 4 * kPairSfBlocksPerStage;  // 128-byte rows of a scale map
+
 template <bool GATED, int STAGES>
 struct PairConfig {
   static constexpr int kMmaN = 256;
   static constexpr int kOutN = GATED ? 128 : 256;  // output columns per tile
-  static constexpr int kABytes = 128 * kRowBytesPerStage;
-  static constexpr int kBBytes = 128 * kRowBytesPerStage;  // this CTA's half of B
-  static constexpr int kSfaBytes = 4 * kSfBlockBytes;       // this CTA's 128 A rows
-  static constexpr int kSfbBytes = 2 * 4 * kSfBlockBytes;   // all 256 B rows
+  static constexpr int kABytes = 128 * kPairStageKBytes;
+  static constexpr int kBBytes = 128 * kPairStageKBytes;  // this CTA's half of B
+  static constexpr int kSfaBytes = kPairSfBlocksPerStage * kSfBlockBytes;      // its 128 A rows
+  static constexpr int kSfbBytes = 2 * kPairSfBlocksPerStage * kSfBlockBytes;  // all 256 B rows
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
   static constexpr uint32_t kPairTxBytes = 2u * kStageBytes;  // both CTAs, every stage
   // Overlapped accumulator stages (stride 192 columns) and one scale-factor slot.
@@ -167,22 +180,25 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const int sfb1_y0 = (GATED ? nt : 2 * nt + 1) * rest_k * 4;
         const bool warm_a = kL2PrefetchModePair == 2 || (kL2PrefetchModePair == 1 && nt == 0);
         const bool warm_b = kL2PrefetchModePair == 2 || (kL2PrefetchModePair == 1 && mt == 0);
-        auto prefetch_ktile = [&](int kp) {
+        // Stages of this tile (kPairStagesPerKTile per 256-element k-tile).
+        const int kstages = ktiles * kPairStagesPerKTile;
+        const int prefetch_ahead = kL2PrefetchKTiles * kPairStagesPerKTile;
+        auto prefetch_stage = [&](int kp) {
           if (warm_a) {
-            ptx::tma_prefetch_l2_2d(&maps[kMapA], kp * kRowBytesPerStage, row_a);
-            ptx::tma_prefetch_l2_2d(&maps[kMapSfa], 0, sfa_y0 + kp * 16);
+            ptx::tma_prefetch_l2_2d(&maps[kMapA], kp * kPairStageKBytes, row_a);
+            ptx::tma_prefetch_l2_2d(&maps[kMapSfa], 0, sfa_y0 + kp * kPairSfRowsPerStage);
           }
           if (warm_b) {
-            ptx::tma_prefetch_l2_2d(map_b, kp * kRowBytesPerStage, row_b);
-            ptx::tma_prefetch_l2_2d(&maps[kMapSfb], 0, sfb0_y0 + kp * 16);
-            ptx::tma_prefetch_l2_2d(map_sfb1, 0, sfb1_y0 + kp * 16);
+            ptx::tma_prefetch_l2_2d(map_b, kp * kPairStageKBytes, row_b);
+            ptx::tma_prefetch_l2_2d(&maps[kMapSfb], 0, sfb0_y0 + kp * kPairSfRowsPerStage);
+            ptx::tma_prefetch_l2_2d(map_sfb1, 0, sfb1_y0 + kp * kPairSfRowsPerStage);
           }
         };
         if (warm_a || warm_b)
-          for (int kp = 0; kp < kL2PrefetchKTiles && kp < ktiles; ++kp) prefetch_ktile(kp);
-        for (int kt = 0; kt < ktiles; ++kt) {
-          if ((warm_a || warm_b) && kt + kL2PrefetchKTiles < ktiles)
-            prefetch_ktile(kt + kL2PrefetchKTiles);
+          for (int kp = 0; kp < prefetch_ahead && kp < kstages; ++kp) prefetch_stage(kp);
+        for (int kt = 0; kt < kstages; ++kt) {
+          if ((warm_a || warm_b) && kt + prefetch_ahead < kstages)
+            prefetch_stage(kt + prefetch_ahead);
           if (!wait_phase(&empty_bar[stage], phase ^ 1u, abort_flag, p.error_bits,
                                   kDevErrProducerTimeout)) {
             ok = false;
@@ -198,13 +214,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint8_t* sB = sA + Cfg::kABytes;
           uint8_t* sSFA = sB + Cfg::kBBytes;
           uint8_t* sSFB = sSFA + Cfg::kSfaBytes;
-          const int kx = kt * kRowBytesPerStage;
+          const int kx = kt * kPairStageKBytes;
+          const int sfy = kt * kPairSfRowsPerStage;
           ptx::tma_load_2d_pair(sA, &maps[kMapA], full_leader, kx, row_a);
           ptx::tma_load_2d_pair(sB, map_b, full_leader, kx, row_b);
-          ptx::tma_load_2d_pair(sSFA, &maps[kMapSfa], full_leader, 0, sfa_y0 + kt * 16);
-          ptx::tma_load_2d_pair(sSFB, &maps[kMapSfb], full_leader, 0, sfb0_y0 + kt * 16);
-          ptx::tma_load_2d_pair(sSFB + 4 * kSfBlockBytes, map_sfb1, full_leader, 0,
-                                sfb1_y0 + kt * 16);
+          ptx::tma_load_2d_pair(sSFA, &maps[kMapSfa], full_leader, 0, sfa_y0 + sfy);
+          ptx::tma_load_2d_pair(sSFB, &maps[kMapSfb], full_leader, 0, sfb0_y0 + sfy);
+          ptx::tma_load_2d_pair(sSFB + kPairSfBlocksPerStage * kSfBlockBytes, map_sfb1,
+                                full_leader, 0, sfb1_y0 + sfy);
           if (kt == 0 && g_next != acquired_g) {
             acquire_maps(p.maps + static_cast<size_t>(g_next) * kMapsPerGroup);
             acquired_g = g_next;
@@ -257,7 +274,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         acc_parity ^= 1u << acc;
         ptx::tcgen05_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
-        for (int kt = 0; kt < ktiles; ++kt) {
+        for (int kt = 0; kt < ktiles * kPairStagesPerKTile; ++kt) {
           if (!wait_phase(&full_bar[stage], phase, abort_flag, p.error_bits,
                                   kDevErrMmaTimeout)) {
             ok = false;
@@ -271,21 +288,24 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const uint32_t sfa_t = tmem_base + Cfg::kSfColBase;
           const uint32_t sfb_t = sfa_t + Cfg::kSfaCols;
 #pragma unroll
-          for (int kb = 0; kb < 4; ++kb)
+          for (int kb = 0; kb < kPairSfBlocksPerStage; ++kb)
             ptx::tmem_cp_32x128b_warpx4_pair(sfa_t + 4 * kb,
                                              ptx::make_sf_block_desc(sSFA + kb * kSfBlockBytes));
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
 #pragma unroll
-            for (int kb = 0; kb < 4; ++kb)
+            for (int kb = 0; kb < kPairSfBlocksPerStage; ++kb)
               ptx::tmem_cp_32x128b_warpx4_pair(
                   sfb_t + Cfg::kSfbColsPerMma * kb + 4 * j,
-                  ptx::make_sf_block_desc(sSFB + j * 4 * kSfBlockBytes + kb * kSfBlockBytes));
+                  ptx::make_sf_block_desc(sSFB + j * kPairSfBlocksPerStage * kSfBlockBytes +
+                                          kb * kSfBlockBytes));
           }
-          const uint64_t a_desc = ptx::make_sw128_kmajor_desc(sA);
-          const uint64_t b_desc = ptx::make_sw128_kmajor_desc(sB);
+          const uint64_t a_desc = kPairStageKBytes == 128 ? ptx::make_sw128_kmajor_desc(sA)
+                                                          : ptx::make_sw64_kmajor_desc(sA);
+          const uint64_t b_desc = kPairStageKBytes == 128 ? ptx::make_sw128_kmajor_desc(sB)
+                                                          : ptx::make_sw64_kmajor_desc(sB);
 #pragma unroll
-          for (int kb = 0; kb < 4; ++kb) {
+          for (int kb = 0; kb < kPairSfBlocksPerStage; ++kb) {
             ptx::mma_mxf4nvf4_pair(d_tmem, a_desc + 2 * kb, b_desc + 2 * kb, Cfg::kIdesc,
                                    sfa_t + 4 * kb, sfb_t + Cfg::kSfbColsPerMma * kb,
                                    (kt | kb) != 0 ? 1u : 0u);

@@ -186,7 +186,7 @@ using Kn128 = GemmConfig<128, false, 5>;
 using Kn256 = GemmConfig<256, false, 3>;
 using Kgated = GemmConfig<256, true, 3>;
 using Kstream = GemmConfig<256, false, 4, true>;  // weight-streaming shapes
-constexpr int kPairStages = 5;
+constexpr int kPairStages = 5 * kPairStagesPerKTile;  // 190 KiB of operands in flight
 using Kpair = PairConfig<false, kPairStages>;
 using KpairGated = PairConfig<true, kPairStages>;
 constexpr int kSwapStages = 7;
@@ -319,10 +319,15 @@ std::mutex g_map_cache_mu;
 std::unordered_map<MapKey, TmaDesc, MapKeyHash> g_map_cache;
 constexpr size_t kMapCacheMax = 1 << 14;
 
-enum : uint32_t { kKindOperand = 0, kKindOutput = 1, kKindScales = 2, kKindOperand64 = 3 };
+enum : uint32_t {
+  kKindOperand = 0, kKindOutput = 1, kKindScales = 2, kKindOperand64 = 3,
+  kKindOperandHalf = 4, kKindScalesHalf = 5
+};
 
 // kKindOperand: e2m1 operand [rows, row_elems bytes] (uint8 view), box 128 B x 128 rows,
-//   128B swizzle, zero fill outside the tensor; kKindOperand64: the same with 64-row boxes.
+//   128B swizzle, zero fill outside the tensor; kKindOperand64: the same with 64-row boxes;
+//   kKindOperandHalf: box 64 B x 128 rows with the 64B swizzle (pair kernels with half-k-tile
+//   stages).
 // kKindOutput:  fp16 output [rows, row_elems], box 64 x 32, 128B swizzle.
 // kKindScales:  blocked scale bytes as `rows` rows of 128 bytes, box 128 B x 16 rows =
 //   one 2-KiB k-tile chunk of a 128-row block, zero fill outside.
@@ -331,13 +336,15 @@ bool encode_map_uncached(uint32_t kind, const void* addr, uint32_t rows, uint32_
   CUtensorMap m;
   cuuint32_t estr[2] = {1, 1};
   CUresult r;
-  if (kind == kKindOperand || kind == kKindOperand64) {
+  if (kind == kKindOperand || kind == kKindOperand64 || kind == kKindOperandHalf) {
+    const bool half = kind == kKindOperandHalf;
     cuuint64_t dims[2] = {row_elems, rows};
     cuuint64_t strides[1] = {row_elems};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(kRowBytesPerStage),
-                         static_cast<cuuint32_t>(kind == kKindOperand ? kBlockM : 64)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(half ? 64 : kRowBytesPerStage),
+                         static_cast<cuuint32_t>(kind == kKindOperand64 ? 64 : kBlockM)};
     r = g_encoder.fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(addr), dims, strides,
-                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     half ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   } else if (kind == kKindOutput) {
     cuuint64_t dims[2] = {row_elems, rows};
@@ -349,7 +356,7 @@ bool encode_map_uncached(uint32_t kind, const void* addr, uint32_t rows, uint32_
   } else {
     cuuint64_t dims[2] = {128, rows};
     cuuint64_t strides[1] = {128};
-    cuuint32_t box[2] = {128, 16};
+    cuuint32_t box[2] = {128, kind == kKindScalesHalf ? 8u : 16u};
     r = g_encoder.fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(addr), dims, strides,
                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -637,14 +644,19 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
         // Blocked scale bytes of an R-row operand, in rows of 128 bytes.
         const uint32_t sfa_rows = static_cast<uint32_t>(((gr.m + 127) / 128) * (gr.k / 64) * 4);
         const uint32_t sfb_rows = static_cast<uint32_t>(((gr.n + 127) / 128) * (gr.k / 64) * 4);
-        bool ok = encode_map(kKindOperand, gr.a, gr.m, kb, &mp[kMapA], use_cache) &&
-                  encode_map(kKindOperand, gr.b, gr.n, kb, &mp[kMapB], use_cache) &&
+        // Pair kernels with half-k-tile stages load A/B through 64-byte boxes and scales in
+        // 1-KiB chunks; every other kernel uses whole-k-tile boxes.
+        const bool half = pair && kPairStagesPerKTile == 2;
+        const uint32_t opk = half ? kKindOperandHalf : kKindOperand;
+        const uint32_t sfk = half ? kKindScalesHalf : kKindScales;
+        bool ok = encode_map(opk, gr.a, gr.m, kb, &mp[kMapA], use_cache) &&
+                  encode_map(opk, gr.b, gr.n, kb, &mp[kMapB], use_cache) &&
                   encode_map(kKindOutput, gr.c, gr.m, gr.n, &mp[kMapC], use_cache) &&
-                  encode_map(kKindScales, gr.sfa, sfa_rows, 128, &mp[kMapSfa], use_cache) &&
-                  encode_map(kKindScales, gr.sfb, sfb_rows, 128, &mp[kMapSfb], use_cache) &&
+                  encode_map(sfk, gr.sfa, sfa_rows, 128, &mp[kMapSfa], use_cache) &&
+                  encode_map(sfk, gr.sfb, sfb_rows, 128, &mp[kMapSfb], use_cache) &&
                   (!gated ||
-                   (encode_map(kKindOperand, gr.b2, gr.n, kb, &mp[kMapB2], use_cache) &&
-                    encode_map(kKindScales, gr.sfb2, sfb_rows, 128, &mp[kMapSfb2], use_cache))) &&
+                   (encode_map(opk, gr.b2, gr.n, kb, &mp[kMapB2], use_cache) &&
+                    encode_map(sfk, gr.sfb2, sfb_rows, 128, &mp[kMapSfb2], use_cache))) &&
                   (!swap || encode_map(kKindOperand64, gr.a, gr.m, kb, &mp[kMapA64], use_cache));
         if (!ok) return fail(NVFP4_ERR_DRIVER, "group %d: cuTensorMapEncodeTiled rejected a tensor", i);
       }

@@ -244,6 +244,12 @@ __device__ __forceinline__ uint64_t make_sw128_kmajor_desc(uint32_t smem_addr) {
   return make_smem_desc(smem_addr, 16, 1024, 2);
 }
 
+// K-major operand tile with rows of exactly 64 bytes written by TMA with the 64-byte
+// swizzle: 8-row swizzle atoms of 512 bytes stacked along M/N.
+__device__ __forceinline__ uint64_t make_sw64_kmajor_desc(uint32_t smem_addr) {
+  return make_smem_desc(smem_addr, 16, 512, 4);
+}
+
 // 32 rows x 16 bytes, contiguous (one 128x4 scale-factor block): core matrices of
 // 8 rows x 16 bytes, 128 bytes apart, no swizzle.
 __device__ __forceinline__ uint64_t make_sf_block_desc(uint32_t smem_addr) {
