@@ -372,9 +372,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       bool ok = true;
       auto acquire_maps = [&](int grp) {
         const TmaDesc* m = p.maps + static_cast<size_t>(grp) * kMapsPerGroup;
-        ptx::tensormap_acquire_prefetch(&m[kMapA]);
-        ptx::tensormap_acquire_prefetch(&m[kMapB]);
-        if (GATED) ptx::tensormap_acquire_prefetch(&m[kMapB2]);
+        ptx::tensormap_fence_acquire(&m[kMapA]);
+        ptx::tensormap_fence_acquire(&m[kMapB]);
+        if (GATED) ptx::tensormap_fence_acquire(&m[kMapB2]);
       };
       // Stream-K: whole tiles blockIdx.x, + grid, ... below stream_k_first_tile, then this
       // CTA's k-iterations [sk_pos, sk_end) of the stream-K tiles (tile sk_first + it / kt).
@@ -697,7 +697,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const int rb = seg_row(p, g);  // C rows of the group start here
       const TmaDesc* map_c = p.maps + static_cast<size_t>(g) * kMapsPerGroup + kMapC;
       if (!DIRECT && split < 0 && g != acquired_g) {
-        if (lane == 0) ptx::tensormap_acquire_prefetch(map_c);
+        if (lane == 0) ptx::tensormap_fence_acquire(map_c);
         acquired_g = g;
       }
       const int acc = static_cast<int>(local & 1u);

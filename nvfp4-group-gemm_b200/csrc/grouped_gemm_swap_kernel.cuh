@@ -111,8 +111,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       bool ok = true;
       auto acquire_maps = [&](int grp) {
         const TmaDesc* m = p.maps + static_cast<size_t>(grp) * kMapsPerGroup;
-        ptx::tensormap_acquire_prefetch(&m[kMapA64]);
-        ptx::tensormap_acquire_prefetch(&m[kMapB]);
+        ptx::tensormap_fence_acquire(&m[kMapA64]);
+        ptx::tensormap_fence_acquire(&m[kMapB]);
       };
       int tile = blockIdx.x;  // grid <= total_tiles: every CTA has a first tile
       int g = advance_group(tile_ends, groups, p.num_groups, 0, tile);

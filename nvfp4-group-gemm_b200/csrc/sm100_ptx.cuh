@@ -87,13 +87,6 @@ __device__ __forceinline__ void tensormap_fence_acquire(const void* desc) {
                : "memory");
 }
 
-// Acquire a tensor map and start fetching it into the TMA unit's descriptor cache, so
-// that the first copy through it does not wait for the 128-byte map to arrive from memory.
-__device__ __forceinline__ void tensormap_acquire_prefetch(const void* desc) {
-  tensormap_fence_acquire(desc);
-  tma_prefetch_desc(desc);
-}
-
 // 2-D tiled load; x is the innermost coordinate in elements of the map's type.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* desc, uint64_t* bar,
                                             int32_t x, int32_t y) {
