@@ -279,7 +279,8 @@ def measure_nvfp4_peak(dev, seconds: float = 2.0) -> dict:
                     f"best of 10 (burst); back to back for {seconds:.0f} s (sustained)"}
 
 
-def headline_configs(pkg, dev, steps: int, warmup: int, peaks: dict, nvfp4_peak: dict | None):
+def headline_configs(pkg, dev, steps: int, warmup: int, peaks: dict, nvfp4_peak: dict | None,
+                     sample_clocks: bool = True):
     """BASELINE's headline form: microseconds per call of configs 1-5 through the prepared
     launch (one GPU, device-resident inputs, a 256 MiB L2 flush before each call of a
     configuration whose inputs fit in L2; events around each call, median), their
@@ -294,6 +295,7 @@ def headline_configs(pkg, dev, steps: int, warmup: int, peaks: dict, nvfp4_peak:
     fp4_peak = nvfp4_peak["burst_tflops"] if nvfp4_peak else None
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     per = {}
+    clocks = ClockSampler(dev.index if dev.index is not None else 0, enabled=sample_clocks)
     for cfg in HEADLINE_CONFIGS:
         prob = pkg.workloads.make_config(cfg, seed=0, device=dev)
         plan = pkg.GroupedGemmPlan(prob.a, prob.b, prob.sfa, prob.sfb, prob.c,
@@ -329,7 +331,7 @@ def headline_configs(pkg, dev, steps: int, warmup: int, peaks: dict, nvfp4_peak:
         del plan, prob
         torch.cuda.empty_cache()
     geo = math.exp(sum(math.log(v["us_per_call"]) for v in per.values()) / len(per))
-    return {"geomean_us_per_call": geo, "per_config": per,
+    return {"geomean_us_per_call": geo, "per_config": per, "clocks": clocks.stop(),
             "timing": "one call per event pair, median of --steps calls; a 256 MiB L2 flush "
                       "before each call of a configuration whose inputs fit in L2",
             "peaks": "tensor-bound: 4 x burst bf16 (MEASURED_PEAKS.json) and the measured "
@@ -346,7 +348,7 @@ def run_all_configs(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     peaks, kind = load_peaks()
-    rec = headline_configs(pkg, dev, args.steps, args.warmup, peaks, None)
+    rec = headline_configs(pkg, dev, args.steps, args.warmup, peaks, None, not args.no_clocks)
     print(json.dumps({
         "metric": "us/call (geomean of configs 1-5)", "value": rec["geomean_us_per_call"],
         "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
@@ -1022,6 +1024,16 @@ def main():
         dist.all_reduce(t)
         return float(t.item())
 
+    # ---------------------------------------------------------------- headline configs (N = 1)
+    # Isolated calls of configs 1-5, timed first, before the sustained-load measurements
+    # below, so that each configuration is timed like a run of that shape alone on a warm
+    # GPU (not on one held at its power limit by seconds of earlier work); the clocks
+    # sampled during this record are reported with it.
+    configs = None
+    if rank == 0 and world == 1 and not args.no_extras:
+        configs = headline_configs(pkg, dev, args.steps, args.warmup, load_peaks()[0], None,
+                                   not args.no_clocks)
+
     # ---------------------------------------------------------------- device-resident timing
     for _ in range(max(args.warmup, 3)):
         step()
@@ -1232,6 +1244,11 @@ def main():
             nvfp4_peak = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
     fp4_ok = nvfp4_peak is not None and "burst_tflops" in nvfp4_peak
 
+    if configs is not None and fp4_ok:
+        for v in configs["per_config"].values():
+            if v["bound"] == "tensor":
+                v["frac_of_measured_nvfp4_burst"] = v["tflops"] / nvfp4_peak["burst_tflops"]
+
     # ---------------------------------------------------------------- cfg5 split over the ranks
     peaks, peak_kind = load_peaks()
     sustained_key = "bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks else "bf16_tflops"
@@ -1243,12 +1260,6 @@ def main():
         if fp4_ok:
             sharded["frac_of_measured_nvfp4_sustained"] = (
                 sharded["tflops"] / (world * nvfp4_peak["sustained_tflops"]))
-
-    # ---------------------------------------------------------------- headline configs (N = 1)
-    configs = None
-    if rank == 0 and world == 1 and not args.no_extras:
-        configs = headline_configs(pkg, dev, args.steps, args.warmup, peaks,
-                                   nvfp4_peak if fp4_ok else None)
 
     # ---------------------------------------------------------------- the reference's kernel (N = 1)
     # The reference's own sm_100 kernel (its CuTe-DSL submission, unmodified) through its own

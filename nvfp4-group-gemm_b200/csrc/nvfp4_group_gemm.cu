@@ -273,6 +273,7 @@ int current_device_state(DeviceState** out) {
   DeviceState& ds = g_dev[dev];
   std::call_once(ds.once, init_device, dev, std::ref(ds));
   if (ds.status != NVFP4_OK) return fail(ds.status, "%s", ds.detail.c_str());
+
   *out = &ds;
   return NVFP4_OK;
 }
@@ -549,17 +550,24 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
     } else {
       // Pairs pay off when the groups fill most of a 256-row tile, or when K is long
       // enough that the halved B traffic outweighs the padding of 128-255-row groups
-      // (measured: G=8, M 64-248, K=7168 -> 39 vs 48 us; same M, K=2048 -> 32 vs 30 us).
-      pair = active > 0 && (rows >= 192 * active || (rows >= 96 * active && max_k >= 4096));
+      // (measured per call, pair vs single CTA: G=8, M 64-248, K=7168 -> 43.2 vs 51.2 us;
+      // G=8, M 40-196, N=7168, K=2048 -> 30.7 vs 32.8 us).
+      pair = active > 0 && (rows >= 192 * active || (rows >= 96 * active && max_k >= 2048));
       // Small groups: weight-stationary tiles carry no padding rows (non-gated launches
       // without a forced tile width).
       swap = !pair && !gated && seg == nullptr && (flags & NVFP4_FLAG_TILE_N256) == 0 &&
              active > 0 && rows <= static_cast<int64_t>(kSwapMaxAvgRows) * active;
     }
   }
-  const int mma_n = gated ? 256 : ((flags & NVFP4_FLAG_TILE_N128) ? 128 : 256);
-  const int out_n = swap ? 128 : (gated ? 128 : mma_n);
-  const int tile_m = swap ? Kswap::kTokens : (pair ? 256 : kBlockM);
+  int mma_n = gated ? 256 : ((flags & NVFP4_FLAG_TILE_N128) ? 128 : 256);
+  int out_n = swap ? 128 : (gated ? 128 : mma_n);
+  int tile_m = swap ? Kswap::kTokens : (pair ? 256 : kBlockM);
+  // Tile shape chosen by the library (no tile or kernel flag): it may still switch to
+  // 128 x 128 tiles below, once the device's size is known.
+  const bool auto_shape =
+      !gated && seg == nullptr &&
+      (flags & (NVFP4_FLAG_TILE_N128 | NVFP4_FLAG_TILE_N256 | NVFP4_FLAG_SINGLE_CTA |
+                NVFP4_FLAG_CTA_PAIR | NVFP4_FLAG_WEIGHT_STATIONARY | NVFP4_FLAG_SPLIT_K)) == 0;
 
   int64_t total_tiles = 0;
   for (int i = 0; i < num_groups; ++i) {
@@ -607,6 +615,35 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
   DeviceState& ds = g_dev[dev];
   std::call_once(ds.once, init_device, dev, std::ref(ds));
   if (ds.status != NVFP4_OK) return fail(ds.status, "%s", ds.detail.c_str());
+
+  // Launches too small to give every SM (or CTA pair) a tile are bound by the latency of
+  // one tile's k-loop: when 128 x 128 tiles fit in one wave they halve each SM's MMA work
+  // per tile and use more SMs (measured per call, auto shape vs 128 x 128: M=128, N=256,
+  // K=512 12.3 vs 10.3 us; G=2, M 192/320, N 3072, K 4096 18.4 vs 16.4 us; G=2, M 128/384,
+  // N 4096, K 1536 14.3 vs 13.4 us).
+  if (auto_shape && !swap && (pair ? total_tiles < ds.pair_clusters : total_tiles < ds.num_sms)) {
+    int64_t small_tiles = 0;
+    for (int i = 0; i < num_groups; ++i)
+      if (rec[i].tile_end > rec[i].tile_start)
+        small_tiles += static_cast<int64_t>((groups[i].m + kBlockM - 1) / kBlockM) *
+                       ((groups[i].n + 127) / 128);
+    if (small_tiles <= ds.num_sms) {
+      pair = false;
+      mma_n = out_n = 128;
+      tile_m = kBlockM;
+      total_tiles = 0;  // the same tile bookkeeping as above, for the new tile shape
+      for (int i = 0; i < num_groups; ++i) {
+        GroupDev& d = rec[i];
+        d.tiles_m = 1;
+        d.tile_start = static_cast<int32_t>(total_tiles);
+        if (groups[i].m > 0 && groups[i].n > 0) {
+          d.tiles_m = (groups[i].m + tile_m - 1) / tile_m;
+          total_tiles += static_cast<int64_t>(d.tiles_m) * ((groups[i].n + out_n - 1) / out_n);
+        }
+        d.tile_end = static_cast<int32_t>(total_tiles);
+      }
+    }
+  }
   std::call_once(g_encoder.once, init_encoder, std::ref(g_encoder));
   if (g_encoder.fn == nullptr)
     return fail(NVFP4_ERR_DRIVER, "cuTensorMapEncodeTiled entry point not available from the driver");
