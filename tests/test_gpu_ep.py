@@ -97,6 +97,9 @@ def _worker(rank, world, port, cta, q):
                 out_equal=bool(torch.equal(out.view(torch.int16), ref.view(torch.int16))),
                 rel=float((out.float() - ref.float()).norm() / ref.float().norm()),
                 finite=bool(torch.isfinite(out.float()).all())))
+            # The peer's next call starts by publishing its counts into this rank's matrix:
+            # read this call's exchange state before either rank moves on.
+            dist.barrier(device_ids=[rank])
         # CUDA graph of the whole exchange (NCCL barriers included), replayed on new inputs
         # written into the captured tensors: identical to an eager call.
         x, ids, wts = _inputs(77 + rank, dev)
