@@ -419,6 +419,32 @@ def sharded_cfg5(pkg, dev, world: int, rank: int, steps: int, warmup: int, barri
             "bytes_received_per_rank": gat.bytes_received,
             "what": "the same calls, each followed by one NCCL all_gather_into_tensor of the "
                     "fp16 output slabs (every expert's output on every rank)"}
+        # The same exchange fused into the GEMM: its epilogue stores every output tile into
+        # each peer's copy of the output slabs over NVLink (nvfp4_grouped_gemm_replicated);
+        # a one-element all-reduce per call orders the ranks.
+        del plan
+        fused = EP.FusedOutputGather(all_m, prob.n, dev)
+
+        def fused_call():
+            fused.gemm(prob.a, prob.b, prob.sfa, prob.sfb, prob.problem_sizes(),
+                       alpha=prob.alpha, b2=prob.b2, sfb2=prob.sfb2, alpha2=prob.alpha2,
+                       stream=stream)
+            fused.barrier()
+
+        fms = timed(fused_call, n)
+        rec["fused_gather"] = {
+            "us_per_call": fms * 1e3, "tflops": flops_job / (fms * 1e-3) / 1e12,
+            "bytes_sent_per_rank": fused.bytes_sent,
+            "device_error_bits": fused.check_device_errors(stream),
+            "equal_to_nccl_gather": all(
+                torch.equal(x.view(torch.int16), y.view(torch.int16))
+                for x, y in zip(fused.outputs, gat.outputs)),
+            "what": "one kernel per call: the grouped GEMM whose epilogue also stores every "
+                    "output tile into every other rank's copy of the output slabs over NVLink "
+                    "(every expert's output on every rank), then a one-element NCCL "
+                    "all-reduce as the cross-rank barrier"}
+        del fused
+        plan = gat = None
     del plan, gat, prob
     torch.cuda.empty_cache()
     return rec

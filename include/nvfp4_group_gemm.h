@@ -354,6 +354,27 @@ NVFP4_API const char* nvfp4_strerror(int status);
 NVFP4_API const char* nvfp4_last_error_detail(void);
 
 /*
+ * nvfp4_grouped_gemm whose fp16 output is also written, tile by tile from the kernel's
+ * epilogue, into num_replicas (1..7) copies of the output buffers on other GPUs: every row
+ * stored at c also goes to (uint8_t*)c + replica_offsets[i] for each i. The copies are other
+ * GPUs' memory mapped into this process at the same layout as the local outputs (for
+ * example one symmetric-memory allocation holding every rank's output slab, offsets = peer
+ * base - local base), so an expert-parallel GEMM followed by an all-gather of its outputs is
+ * one kernel whose NVLink stores overlap its math. The stores are plain 16-byte stores (no
+ * multicast); they are complete when the kernel is, and the caller orders them with the
+ * replicas' owners (e.g. a cross-rank barrier on the stream) before those read the rows or
+ * the next call writes them again. Offsets must be non-zero multiples of 16;
+ * NVFP4_FLAG_WEIGHT_STATIONARY is not accepted. No counterpart in the reference, which runs
+ * on one GPU; this is the fused form of the output all-gather of its expert-parallel
+ * deployment (north star (5)).
+ */
+NVFP4_API int nvfp4_grouped_gemm_replicated(const nvfp4_group* groups, int num_groups,
+                                            unsigned int flags, void* workspace,
+                                            size_t workspace_bytes,
+                                            const int64_t* replica_offsets, int num_replicas,
+                                            void* stream);
+
+/*
  * Allocation-free variant of nvfp4_grouped_gemm. No counterpart in the reference.
  *
  * For callers that cannot allocate device memory where they run the GEMM:

@@ -60,6 +60,7 @@ EXPORTED_SYMBOLS = (
     "nvfp4_grouped_gemm_noalloc",
     "nvfp4_noalloc_check",
     "nvfp4_grouped_gemm_segments",
+    "nvfp4_grouped_gemm_replicated",
     "nvfp4_plan_create",
     "nvfp4_plan_launch",
     "nvfp4_plan_destroy",
@@ -77,6 +78,7 @@ EXPORTED_SYMBOLS = (
 
 ABI_VERSION = 2   # NVFP4_ABI_VERSION
 EP_MAX_RANKS = 8  # NVFP4_EP_MAX_RANKS
+MAX_REPLICAS = 7  # replicas nvfp4_grouped_gemm_replicated accepts
 EP_ERR_CAPACITY = 1 << 0  # an expert segment did not fit the owner's receive slab
 
 
@@ -221,6 +223,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_workspace_check.restype = i32
         lib.nvfp4_grouped_gemm_noalloc.argtypes = [vp, i32, u32, vp]
         lib.nvfp4_grouped_gemm_noalloc.restype = i32
+        lib.nvfp4_grouped_gemm_replicated.argtypes = [vp, i32, u32, vp, sz, vp, i32, vp]
+        lib.nvfp4_grouped_gemm_replicated.restype = i32
         lib.nvfp4_noalloc_check.argtypes = [vp, ctypes.POINTER(ctypes.c_uint)]
         lib.nvfp4_noalloc_check.restype = i32
         lib.nvfp4_grouped_gemm_segments.argtypes = [vp, i32, u32, vp, vp, i64,

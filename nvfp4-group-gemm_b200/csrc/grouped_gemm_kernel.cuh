@@ -779,12 +779,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             // multiple of 8, so a chunk is either inside the row or past its end).
             const int col = nt * Cfg::kOutN + box * 64 + half * 32;
             if (out_row != nullptr) {
-              uint4* dst = reinterpret_cast<uint4*>(out_row + static_cast<size_t>(col) * sizeof(__half));
+              // The local row, then each replica of it (replicas only without scattering).
+              for (int r = -1; r < (scatter ? 0 : p.num_replicas); ++r) {
+                uint4* dst = reinterpret_cast<uint4*>(
+                    out_row + (r < 0 ? 0 : p.replica_offset[r]) +
+                    static_cast<size_t>(col) * sizeof(__half));
 #pragma unroll
-              for (int c = 0; c < 4; ++c)
-                if (col + 8 * c < gd.n)
-                  dst[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
-                                      packed[4 * c + 3]);
+                for (int c = 0; c < 4; ++c)
+                  if (col + 8 * c < gd.n)
+                    dst[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
+                                        packed[4 * c + 3]);
+              }
             }
           } else {
             // Row `lane` of the 32 x 128 B box, 16-byte chunks XOR-swizzled by (row & 7)
@@ -812,6 +817,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                               nt * Cfg::kOutN + box * 64, rb + row0);
             ptx::bulk_commit_group();
           }
+          // Replicas: the same staged box, four 128-byte row pieces per warp store (whole
+          // lines over NVLink), while the TMA store writes the local copy.
+          for (int r = 0; r < p.num_replicas; ++r)
+            store_box_rows(my_bufs + (stores & 1u) * Cfg::kEpiBufBytes,
+                           out_row != nullptr ? out_row + p.replica_offset[r] : nullptr,
+                           nt * Cfg::kOutN + box * 64, gd.n, lane);
           ++stores;
         }
       };

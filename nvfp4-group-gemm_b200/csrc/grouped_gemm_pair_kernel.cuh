@@ -376,6 +376,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         uint8_t* out_row = nullptr;
         if (scatter && row0 + lane < gd.m)
           out_row = scatter_row(p, static_cast<int64_t>(rb) + row0 + lane);
+        // This thread's C row (for replicated output; nullptr past the group's rows).
+        uint8_t* c_row = row0 + lane < gd.m
+                             ? gd.c + static_cast<size_t>(rb + row0 + lane) * gd.n * sizeof(__half)
+                             : nullptr;
 #pragma unroll 1
         for (int bi = 0; bi < kBoxes; ++bi) {
           const int box = (first_box + bi) % kBoxes;
@@ -455,6 +459,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                               nt * Cfg::kOutN + box * 64, rb + row0);
             ptx::bulk_commit_group();
           }
+          // Replicas: the same staged box into each peer copy of C, four 128-byte row
+          // pieces per warp store, while the TMA store writes the local copy.
+          for (int r = 0; r < p.num_replicas; ++r)
+            store_box_rows(my_bufs + (stores & 1u) * Cfg::kEpiBufBytes,
+                           c_row != nullptr ? c_row + p.replica_offset[r] : nullptr,
+                           nt * Cfg::kOutN + box * 64, gd.n, lane);
           ++stores;
         }
       }

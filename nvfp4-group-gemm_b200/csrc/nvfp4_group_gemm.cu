@@ -524,7 +524,8 @@ struct SegmentArgs {
 int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int flags, uint8_t* ws,
                       size_t ws_bytes, cudaStream_t s, GroupDev* rec, bool use_cache,
                       const SegmentArgs* seg = nullptr, LaunchSpec* prepared = nullptr,
-                      bool clear_header = false) {
+                      bool clear_header = false, const int64_t* replica_offsets = nullptr,
+                      int num_replicas = 0) {
   const bool gated = (flags & NVFP4_FLAG_GATED) != 0;
   // Tile shape: CTA pairs (256-row tiles) when the groups are tall enough to fill
   // them, single CTAs (128-row tiles) otherwise; 256 MMA columns unless asked otherwise.
@@ -559,6 +560,7 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
              active > 0 && rows <= static_cast<int64_t>(kSwapMaxAvgRows) * active;
     }
   }
+  if (num_replicas > 0) swap = false;  // the weight-stationary kernel has no replicated output
   int mma_n = gated ? 256 : ((flags & NVFP4_FLAG_TILE_N128) ? 128 : 256);
   int out_n = swap ? 128 : (gated ? 128 : mma_n);
   int tile_m = swap ? Kswap::kTokens : (pair ? 256 : kBlockM);
@@ -705,6 +707,9 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
   }
 
   GemmParams gp;
+  gp.num_replicas = num_replicas;
+  for (int i = 0; i < kMaxReplicas; ++i)
+    gp.replica_offset[i] = i < num_replicas ? replica_offsets[i] : 0;
   gp.seg_rows = nullptr;
   gp.seg_total_tiles = nullptr;
   const nvfp4_segment_output* out = seg != nullptr ? seg->output : nullptr;
@@ -963,6 +968,40 @@ NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, unsi
   return grouped_gemm_impl(groups, num_groups, flags, static_cast<uint8_t*>(workspace),
                            workspace_bytes, static_cast<cudaStream_t>(stream), rec.data(),
                            /*use_cache=*/true);
+}
+
+NVFP4_API int nvfp4_grouped_gemm_replicated(const nvfp4_group* groups, int num_groups,
+                                            unsigned int flags, void* workspace,
+                                            size_t workspace_bytes,
+                                            const int64_t* replica_offsets, int num_replicas,
+                                            void* stream) {
+  g_last_error.clear();
+  int st = check_common_args(groups, num_groups, flags);
+  if (st != NVFP4_OK) return st;
+  if (num_replicas < 1 || num_replicas > kMaxReplicas)
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "num_replicas=%d outside [1, %d]", num_replicas,
+                kMaxReplicas);
+  if (replica_offsets == nullptr) return fail(NVFP4_ERR_NULL_POINTER, "replica_offsets is NULL");
+  for (int i = 0; i < num_replicas; ++i)
+    if (replica_offsets[i] == 0 || (replica_offsets[i] & 15) != 0)
+      return fail(NVFP4_ERR_MISALIGNED,
+                  "replica %d: offset %lld must be a non-zero multiple of 16 bytes", i,
+                  static_cast<long long>(replica_offsets[i]));
+  if (flags & NVFP4_FLAG_WEIGHT_STATIONARY)
+    return fail(NVFP4_ERR_INVALID_ARGUMENT,
+                "replicated output is not available with NVFP4_FLAG_WEIGHT_STATIONARY");
+  if (num_groups == 0) return NVFP4_OK;
+  if (workspace == nullptr) return fail(NVFP4_ERR_WORKSPACE, "workspace is NULL");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(NVFP4_ERR_WORKSPACE, "workspace not 256-byte aligned");
+  if (workspace_bytes < ws_total_bytes(num_groups))
+    return fail(NVFP4_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes,
+                ws_total_bytes(num_groups));
+  std::vector<GroupDev> rec(static_cast<size_t>(num_groups));
+  return grouped_gemm_impl(groups, num_groups, flags, static_cast<uint8_t*>(workspace),
+                           workspace_bytes, static_cast<cudaStream_t>(stream), rec.data(),
+                           /*use_cache=*/true, /*seg=*/nullptr, /*prepared=*/nullptr,
+                           /*clear_header=*/false, replica_offsets, num_replicas);
 }
 
 }  // extern "C"

@@ -109,6 +109,9 @@ struct UploadParams {
 };
 static_assert(sizeof(UploadParams) <= 32000, "kernel parameter block too large");
 
+// Peer copies an epilogue can replicate its fp16 output into (one box of 8 GPUs).
+constexpr int kMaxReplicas = 7;
+
 struct GemmParams {
   const GroupDev* groups;
   const TmaDesc* maps;
@@ -162,6 +165,11 @@ struct GemmParams {
   int32_t stream_k_ktiles;
   int64_t stream_k_total_iters;
   int32_t stream_k_first_tile;
+  // Replicated fp16 output (num_replicas > 0): every C row a kernel stores also goes to
+  // c_row + replica_offset[i] (byte offsets into other GPUs' copies of the output buffers,
+  // mapped into this process), straight from the epilogue, tile by tile.
+  int32_t num_replicas;
+  int64_t replica_offset[kMaxReplicas];
 };
 
 // Destination of slab row r of a scattered output (nullptr: not stored).

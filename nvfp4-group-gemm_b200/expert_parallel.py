@@ -128,6 +128,123 @@ class ExpertOutputGather:
         return self.outputs
 
 
+class FusedOutputGather:
+    """The output all-gather of an expert-parallel grouped GEMM, fused into the GEMM.
+
+    One symmetric-memory allocation holds, on every rank, the fp16 output slab of every
+    rank (rank r's experts ``expert_shard(G, P, r)`` in slab r, the layout of
+    :class:`ExpertOutputGather`'s receive buffer). :meth:`gemm` runs this rank's experts with
+    ``nvfp4_grouped_gemm_replicated``: the kernel stores each output tile into this rank's
+    slab locally and, from its epilogue, into the same slab of every other rank's copy over
+    NVLink, so the exchange overlaps the math tile by tile. After :meth:`barrier` (a
+    one-element NCCL all-reduce on the stream) every rank holds every expert's output in
+    ``outputs`` (global expert order). The caller orders reuse: a rank's next :meth:`gemm`
+    writes into its peers' copies, so they must be done reading the previous results.
+    """
+
+    def __init__(self, rows_per_expert: Sequence[int], n: int, device: torch.device,
+                 group: dist.ProcessGroup | None = None):
+        from torch.distributed import _symmetric_memory as symm
+
+        from . import _native
+
+        self.group = group if group is not None else dist.group.WORLD
+        world = dist.get_world_size(self.group)
+        rank = dist.get_rank(self.group)
+        if world - 1 > _native.MAX_REPLICAS:
+            raise ValueError(f"at most {_native.MAX_REPLICAS + 1} ranks")
+        self.world, self.rank = world, rank
+        self.rows = [int(m) for m in rows_per_expert]
+        self.n = int(n)
+        layout = slab_layout(self.rows, self.n, world)
+        self.max_elems = max(e for _, _, e in layout)
+        nbytes = world * self.max_elems * 2
+        self._symm = symm.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        self._symm.zero_()
+        try:
+            handle = symm.rendezvous(self._symm, self.group)
+        except RuntimeError:  # older releases want the group registered first
+            symm.enable_symm_mem_for_group(self.group.group_name)
+            handle = symm.rendezvous(self._symm, self.group)
+        self._handle = handle
+        bases = [int(b) for b in handle.buffer_ptrs]
+        # Every rank's copy has the same layout: a peer's copy of a byte is at
+        # (its base - this base) from this rank's copy of it.
+        self.replica_offsets = [bases[p] - bases[rank] for p in range(world) if p != rank]
+        self.slabs = self._symm[:nbytes].view(torch.float16)
+        first, count, _ = layout[rank]
+        self.local_outputs = self._views(rank * self.max_elems, first, count)
+        self.outputs = []
+        for r, (f, cnt, _) in enumerate(layout):
+            self.outputs += self._views(r * self.max_elems, f, cnt)
+        self.bytes_sent = int((world - 1) * layout[rank][2] * 2)
+        self._bar = torch.zeros(1, dtype=torch.int32, device=device)
+        self._table = None
+        self._ws = None
+        self._sig = None
+
+    def _views(self, base: int, first: int, count: int) -> list:
+        out, off = [], base
+        for g in range(first, first + count):
+            m = self.rows[g]
+            out.append(self.slabs[off:off + m * self.n].view(m, self.n))
+            off += m * self.n
+        return out
+
+    def gemm(self, a, b, sfa, sfb, problem_sizes, *, alpha=None, b2=None, sfb2=None,
+             alpha2=None, cta: str | None = None,
+             stream: torch.cuda.Stream | None = None) -> list:
+        """This rank's experts (operands as for :func:`interface.grouped_gemm`, outputs into
+        ``local_outputs``) with every output row also stored into the peers' copies."""
+        import ctypes
+
+        import numpy as np
+
+        from . import _native
+        from .interface import _prepare
+
+        sig = (tuple(t.data_ptr() for t in list(a) + list(b) + list(sfa) + list(sfb)),
+               tuple(tuple(ps) for ps in problem_sizes), None if alpha is None else tuple(alpha),
+               None if b2 is None else tuple(t.data_ptr() for t in list(b2) + list(sfb2)),
+               None if alpha2 is None else tuple(alpha2), cta)
+        reuse = sig == self._sig and self._table is not None
+        if not reuse:
+            prepared = _prepare(a, b, sfa, sfb, self.local_outputs, problem_sizes, alpha, b2,
+                                sfb2, alpha2, None, cta)
+            if prepared is None:
+                return self.local_outputs
+            self._table, self._flags, dev = prepared
+            G = int(self._table.shape[0])
+            if self._ws is None or self._ws.numel() < _native.workspace_size(G):
+                self._ws = torch.zeros(_native.workspace_size(G), dtype=torch.uint8, device=dev)
+            self._sig = sig
+        s = (stream or torch.cuda.current_stream(self._symm.device)).cuda_stream
+        lib = _native.load_library()
+        flags = self._flags | (_native.FLAG_REUSE_DESCRIPTORS if reuse else 0)
+        t = self._table
+        if self.world == 1:
+            st = lib.nvfp4_grouped_gemm(t.ctypes.data, int(t.shape[0]), flags,
+                                        self._ws.data_ptr(), self._ws.numel(), s)
+        else:
+            offs = np.asarray(self.replica_offsets, dtype=np.int64)
+            st = lib.nvfp4_grouped_gemm_replicated(
+                t.ctypes.data, int(t.shape[0]), flags, self._ws.data_ptr(), self._ws.numel(),
+                offs.ctypes.data_as(ctypes.c_void_p), len(self.replica_offsets), s)
+        _native.check(st, lib)
+        return self.local_outputs
+
+    def barrier(self) -> None:
+        """Cross-rank barrier on the current stream: after it every rank's kernel (and so
+        every replica store) has completed."""
+        dist.all_reduce(self._bar, group=self.group)
+
+    def check_device_errors(self, stream: torch.cuda.Stream | None = None) -> int:
+        from . import _native
+
+        s = (stream or torch.cuda.current_stream(self._symm.device)).cuda_stream
+        return 0 if self._ws is None else _native.workspace_check(self._ws.data_ptr(), s)
+
+
 class ExpertParallelGroupedGemm:
     """Run this rank's shard of a grouped problem and optionally gather all outputs.
 

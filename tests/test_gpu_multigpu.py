@@ -3,8 +3,11 @@ kernel and the outputs are all-gathered over NCCL (skipped when fewer than 2 GPU
 
 Each rank checks its own experts against the oracle; the parent then checks that every
 rank's gathered list equals, byte for byte, the concatenation of all ranks' local outputs.
-Two exchanges are covered: all_gather_expert_outputs (packs the outputs per call) and
-ExpertOutputGather (the GEMM writes its outputs into the preallocated send slab).
+Three exchanges are covered: all_gather_expert_outputs (packs the outputs per call),
+ExpertOutputGather (the GEMM writes its outputs into the preallocated send slab of one NCCL
+all-gather) and FusedOutputGather (the GEMM's epilogue stores every output tile into each
+peer's copy of the slab over NVLink; two calls, the second after A changed in place, so the
+descriptor-reuse path is covered too).
 """
 from __future__ import annotations
 
@@ -29,7 +32,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, gated, slab, q):
+def _worker(rank, world, port, gated, mode, q):
     try:
         import sys
 
@@ -53,7 +56,8 @@ def _worker(rank, world, port, gated, slab, q):
         sh = ep.shard
         prob = pkg.workloads.make_problem(f"ep{rank}", ROWS[sh.start:sh.stop], N, K, gated=gated,
                                           seed=100 + rank, device=dev, alpha_range=(0.5, 2.0))
-        if slab:
+        calls = 1
+        if mode == "slab":
             gat = EP.ExpertOutputGather(ROWS, N, dev)
             for c, v in zip(prob.c, gat.local_outputs):
                 v.copy_(c)  # the harness's randn prefill, now in the slab
@@ -61,25 +65,26 @@ def _worker(rank, world, port, gated, slab, q):
             pkg.grouped_gemm(prob.a, prob.b, prob.sfa, prob.sfb, prob.c, prob.problem_sizes(),
                              alpha=prob.alpha, b2=prob.b2, sfb2=prob.sfb2, alpha2=prob.alpha2)
             outs = gat.run()
+        elif mode == "fused":
+            gat = EP.FusedOutputGather(ROWS, N, dev)
+            prob.c = list(gat.local_outputs)
+            calls = 2
         else:
             outs = ep.run(prob, ROWS, gather=True)
-        torch.cuda.synchronize()
-        # This rank's experts against the oracle.
-        for i in range(prob.num_groups):
-            if prob.m[i] == 0:
-                continue
-            a, b = prob.a[i].cpu().numpy(), prob.b[i].cpu().numpy()
-            sfa, sfb = prob.sfa_plain[i].cpu().numpy(), prob.sfb_plain[i].cpu().numpy()
-            got = prob.c[i].cpu().numpy()
-            if gated:
-                exp = O.ref_gated(a, b, prob.b2[i].cpu().numpy(), sfa, sfb,
-                                  prob.sfb2_plain[i].cpu().numpy(), prob.alpha[i], prob.alpha2[i])
-                ref32 = None
-            else:
-                ref32 = O.ref_gemm_fp32(a, b, sfa, sfb) * np.float32(prob.alpha[i])
-                exp = ref32.astype(np.float16)
-            res = O.compare_fp16(got, exp, ref32, rtol=1e-2, atol=1e-2)
-            assert res["ok"], (rank, i, res)
+        for call in range(calls):
+            if mode == "fused":
+                if call:
+                    for t in prob.a:
+                        t ^= 0x11  # new operand values behind the same pointers
+                    dist.barrier(device_ids=[rank])  # peers are done reading the last call
+                gat.gemm(prob.a, prob.b, prob.sfa, prob.sfb, prob.problem_sizes(),
+                         alpha=prob.alpha, b2=prob.b2, sfb2=prob.sfb2, alpha2=prob.alpha2)
+                gat.barrier()
+                outs = gat.outputs
+            torch.cuda.synchronize()
+            _check_local(prob, gated, rank, O)
+        if mode == "fused":
+            assert gat.check_device_errors() == 0
         local = [c.cpu().numpy() for c in prob.c]
         gathered = [o.cpu().numpy() for o in outs]
         q.put((rank, local, gathered, (sh.start, sh.stop)))
@@ -89,14 +94,37 @@ def _worker(rank, world, port, gated, slab, q):
         q.put((rank, repr(e), None, None))
 
 
+def _check_local(prob, gated, rank, O):
+    """This rank's experts against the oracle."""
+    for i in range(prob.num_groups):
+        if prob.m[i] == 0:
+            continue
+        a, b = prob.a[i].cpu().numpy(), prob.b[i].cpu().numpy()
+        sfa, sfb = prob.sfa_plain[i].cpu().numpy(), prob.sfb_plain[i].cpu().numpy()
+        got = prob.c[i].cpu().numpy()
+        if gated:
+            exp = O.ref_gated(a, b, prob.b2[i].cpu().numpy(), sfa, sfb,
+                              prob.sfb2_plain[i].cpu().numpy(), prob.alpha[i], prob.alpha2[i])
+            ref32 = None
+        else:
+            ref32 = O.ref_gemm_fp32(a, b, sfa, sfb) * np.float32(prob.alpha[i])
+            exp = ref32.astype(np.float16)
+        res = O.compare_fp16(got, exp, ref32, rtol=1e-2, atol=1e-2)
+        assert res["ok"], (rank, i, res)
+
+
+MODES = [(g, m) for m in ("list", "slab", "fused") for g in (False, True)]
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("gated,slab", [(False, False), (True, False), (False, True), (True, True)])
-def test_two_gpu_shards_and_nccl_gather(gated, slab):
+@pytest.mark.parametrize("gated,mode", MODES, ids=[f"{m}-{'gated' if g else 'plain'}"
+                                                   for g, m in MODES])
+def test_two_gpu_shards_and_nccl_gather(gated, mode):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, gated, slab, q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, gated, mode, q))
              for r in range(world)]
     for p in procs:
         p.start()
