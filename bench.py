@@ -368,6 +368,7 @@ def sharded_cfg5(pkg, dev, world: int, rank: int, steps: int, warmup: int, barri
     all-gather of every expert's fp16 output to every rank (the GEMM writes into the
     gather's send slab; ExpertOutputGather)."""
     import torch
+    import torch.distributed as dist
 
     EP = pkg.expert_parallel
     G = len(pkg.workloads.config_rows("cfg5")[0])
@@ -423,7 +424,22 @@ def sharded_cfg5(pkg, dev, world: int, rank: int, steps: int, warmup: int, barri
         # each peer's copy of the output slabs over NVLink (nvfp4_grouped_gemm_replicated);
         # a one-element all-reduce per call orders the ranks.
         del plan
-        fused = EP.FusedOutputGather(all_m, prob.n, dev)
+        # Every rank must agree before the collective timing below: a rank that could not
+        # set up the symmetric-memory gather makes all of them skip it.
+        try:
+            fused = EP.FusedOutputGather(all_m, prob.n, dev)
+            fused_err = None
+        except Exception as exc:  # reported in the line, not fatal to the bench
+            fused, fused_err = None, f"{type(exc).__name__}: {exc}"[:200]
+        agree = torch.tensor([0 if fused is None else 1], dtype=torch.int32, device=dev)
+        dist.all_reduce(agree, op=dist.ReduceOp.MIN)
+        if int(agree.item()) == 0:
+            rec["fused_gather"] = {"unavailable": fused_err or "set-up failed on another rank"}
+            del fused
+            plan = gat = None
+            del plan, gat, prob
+            torch.cuda.empty_cache()
+            return rec
 
         def fused_call():
             fused.gemm(prob.a, prob.b, prob.sfa, prob.sfb, prob.problem_sizes(),
