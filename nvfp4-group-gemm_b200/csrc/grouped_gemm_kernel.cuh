@@ -296,7 +296,10 @@ __device__ __forceinline__ void release_tile_counter(uint32_t* counter) {
   }
 }
 
-template <int MMA_N, bool GATED, int STAGES, bool DIRECT = false>
+// STREAMK: the instantiation that runs the stream-K schedule (p.stream_k_iters > 0); the
+// others compile without its code (its epilogue hand-off cost the weight-streaming kernel
+// 77 registers and ~4 % per call when it was always built in).
+template <int MMA_N, bool GATED, int STAGES, bool DIRECT = false, bool STREAMK = false>
 __global__ void __launch_bounds__(kNumThreads, 1)
     nvfp4_grouped_gemm_kernel(const __grid_constant__ GemmParams p) {
   using Cfg = GemmConfig<MMA_N, GATED, STAGES, DIRECT>;
@@ -378,7 +381,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       };
       // Stream-K: whole tiles blockIdx.x, + grid, ... below stream_k_first_tile, then this
       // CTA's k-iterations [sk_pos, sk_end) of the stream-K tiles (tile sk_first + it / kt).
-      const bool sk = p.stream_k_iters > 0;
+      const bool sk = STREAMK && p.stream_k_iters > 0;
       const int sk_first = sk ? p.stream_k_first_tile : 0;
       const int sk_kt = sk ? p.stream_k_ktiles : 1;
       int64_t sk_pos = sk ? static_cast<int64_t>(blockIdx.x) * p.stream_k_iters : 0;
@@ -838,7 +841,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int32_t* sk_ctr = nullptr;
       const float* sk_src = nullptr;
       float* sk_dst = nullptr;
-      if (!GATED && p.stream_k_iters > 0 && row0 < gd.m &&
+      if (STREAMK && !GATED && p.stream_k_iters > 0 && row0 < gd.m &&
           (piece_k0 > 0 || piece_k1 < gd.k / kBlockK)) {
         const int sk_b = piece_k0 > 0 ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) + 1;
         sk_ctr = p.split_counters + 4 * sk_b + quarter;

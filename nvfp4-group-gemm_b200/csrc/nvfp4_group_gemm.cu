@@ -240,6 +240,8 @@ void init_device(int dev, DeviceState& st) {
       {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_kernel<256, true, 3>), Kgated::kSmemBytes},
       {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_kernel<256, false, 4, true>),
        Kstream::kSmemBytes},
+      {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_kernel<256, false, 4, true, true>),
+       Kstream::kSmemBytes},
       {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_pair_kernel<false, kPairStages>),
        Kpair::kSmemBytes},
       {reinterpret_cast<const void*>(&nvfp4_grouped_gemm_pair_kernel<true, kPairStages>),
@@ -465,10 +467,10 @@ cudaError_t launch_gemm(Kernel kernel, const GemmParams& gp, int grid, int smem,
   return cudaLaunchKernelEx(&cfg, kernel, gp);
 }
 
-template <int MMA_N, bool GATED, int STAGES, bool DIRECT = false>
+template <int MMA_N, bool GATED, int STAGES, bool DIRECT = false, bool STREAMK = false>
 cudaError_t launch_single(const GemmParams& gp, int grid, cudaStream_t stream) {
   using Cfg = GemmConfig<MMA_N, GATED, STAGES, DIRECT>;
-  return launch_gemm(nvfp4_grouped_gemm_kernel<MMA_N, GATED, STAGES, DIRECT>, gp, grid,
+  return launch_gemm(nvfp4_grouped_gemm_kernel<MMA_N, GATED, STAGES, DIRECT, STREAMK>, gp, grid,
                      Cfg::kSmemBytes, 1, stream);
 }
 
@@ -483,7 +485,7 @@ cudaError_t launch_pair(const GemmParams& gp, int clusters, cudaStream_t stream)
 // grid and its parameters. grouped_gemm_impl builds one per call; a prepared plan
 // (nvfp4_plan_create) keeps it and replays only the launch.
 enum class KernelKind : int {
-  kSwap, kPair, kPairGated, kSingleGated, kSingle128, kStream, kSingle256
+  kSwap, kPair, kPairGated, kSingleGated, kSingle128, kStream, kSingle256, kStreamK
 };
 struct LaunchSpec {
   GemmParams gp;
@@ -501,6 +503,7 @@ cudaError_t run_spec(const LaunchSpec& sp, cudaStream_t s) {
     case KernelKind::kSingleGated: return launch_single<256, true, 3>(sp.gp, sp.grid, s);
     case KernelKind::kSingle128: return launch_single<128, false, 5>(sp.gp, sp.grid, s);
     case KernelKind::kStream: return launch_single<256, false, 4, true>(sp.gp, sp.grid, s);
+    case KernelKind::kStreamK: return launch_single<256, false, 4, true, true>(sp.gp, sp.grid, s);
     case KernelKind::kSingle256: return launch_single<256, false, 3>(sp.gp, sp.grid, s);
   }
   return cudaErrorInvalidValue;
@@ -824,6 +827,7 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
       sp.gp.stream_k_first_tile = static_cast<int32_t>(first);
       sp.gp.dynamic_schedule = 0;
       sp.grid = static_cast<int>(sms);
+      sp.kind = KernelKind::kStreamK;
     }
   }
   if (prepared != nullptr) {  // a plan: descriptors uploaded, the launch is replayed later
