@@ -378,6 +378,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         ptx::tensormap_fence_acquire(&m[kMapA]);
         ptx::tensormap_fence_acquire(&m[kMapB]);
         if (GATED) ptx::tensormap_fence_acquire(&m[kMapB2]);
+        if (DIRECT) ptx::tensormap_fence_acquire(&m[kMapA64]);
       };
       // Stream-K: whole tiles blockIdx.x, + grid, ... below stream_k_first_tile, then this
       // CTA's k-iterations [sk_pos, sk_end) of the stream-K tiles (tile sk_first + it / kt).
@@ -447,8 +448,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const int row_a = rb + mt * kBlockM;
         const uint8_t* sfa_blk =
             gd.sfa + static_cast<size_t>(rb / kBlockM + mt) * rest_k * kSfBlockBytes;
-        const uint32_t tx = Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes +
-                            (sfb_blk1 != nullptr ? 2 : 1) * 4 * kSfBlockBytes;
+        // Weight-streaming tiles of at most 64 rows load A through the 64-row box: rows
+        // 64-127 of the stage's A tile then keep stale bytes, which only feed accumulator
+        // rows that are never stored, and the TMA unit fills 8 KiB less per stage.
+        const bool a_half = DIRECT && gd.m - mt * kBlockM <= 64;
+        const uint32_t tx = (a_half ? Cfg::kABytes / 2 : Cfg::kABytes) + Cfg::kBBytes +
+                            Cfg::kSfaBytes + (sfb_blk1 != nullptr ? 2 : 1) * 4 * kSfBlockBytes;
         // L2 warm-up of k-tile `kp` of this tile (A, B halves, scale blocks). In mode 1 only
         // operands that other CTAs also read are warmed (A when the group has several
         // n-tiles, B when it has several m-tiles): every prefetch box is TMA work, and on
@@ -523,7 +528,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint8_t* sSFB = sSFA + Cfg::kSfaBytes;
           ptx::mbar_arrive_expect_tx(&full_bar[stage], tx);
           const int kx = kt * kRowBytesPerStage;
-          ptx::tma_load_2d(sA, &maps[kMapA], &full_bar[stage], kx, row_a);
+          ptx::tma_load_2d(sA, &maps[a_half ? kMapA64 : kMapA], &full_bar[stage], kx, row_a);
           if (GATED) {
             ptx::tma_load_2d(sB, &maps[kMapB], &full_bar[stage], kx, nt * 128);
             ptx::tma_load_2d(sB + 128 * kRowBytesPerStage, &maps[kMapB2], &full_bar[stage], kx,

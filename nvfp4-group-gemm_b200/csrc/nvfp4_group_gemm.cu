@@ -699,7 +699,10 @@ int grouped_gemm_impl(const nvfp4_group* groups, int num_groups, unsigned int fl
                   (!gated ||
                    (encode_map(opk, gr.b2, gr.n, kb, &mp[kMapB2], use_cache) &&
                     encode_map(sfk, gr.sfb2, sfb_rows, 128, &mp[kMapSfb2], use_cache))) &&
-                  (!swap || encode_map(kKindOperand64, gr.a, gr.m, kb, &mp[kMapA64], use_cache));
+                  // 64-row A boxes: the weight-stationary kernel's token tiles, and the
+                  // weight-streaming kernel's tiles of at most 64 rows.
+                  (!(swap || (!pair && !gated)) ||
+                   encode_map(kKindOperand64, gr.a, gr.m, kb, &mp[kMapA64], use_cache));
         if (!ok) return fail(NVFP4_ERR_DRIVER, "group %d: cuTensorMapEncodeTiled rejected a tensor", i);
       }
       nvfp4_upload_descriptors_kernel<<<count, 32, 0, s>>>(up);
