@@ -86,6 +86,9 @@ def parse_args():
     ap.add_argument("--tokens", type=int, default=32768,
                     help="--op moe: tokens per step (32768 = cfg5's 262144 routed rows; 64 = a "
                          "decode step)")
+    ap.add_argument("--ep-return", default="both", choices=["sums", "rows", "both"],
+                    help="--op moe over N > 1 GPUs: how expert outputs return to their tokens' "
+                         "ranks (owner-side sums, per-pair rows, or both timed in turn)")
     return ap.parse_args()
 
 
@@ -757,51 +760,77 @@ def run_moe_ep(args, world):
     wts = torch.softmax(top.values, dim=1)
     s_x = pkg.global_scale_for(x)
     s_h = 0.01  # fixed SiLU-output scale (values do not change the timing)
-    blk = pkg.expert_parallel.EPMoEBlock(weights, E, T, topk, s_x, s_h)
-    for _ in range(max(args.warmup, 3)):
-        blk.run(x, ids, wts)
-    torch.cuda.synchronize(dev)
-    dist.barrier(device_ids=[local_rank])
     steps = max(1, min(args.steps, 10))
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        blk.run(x, ids, wts)
-    e1.record()
-    torch.cuda.synchronize(dev)
-    ms_rank = e0.elapsed_time(e1) / steps
-    t = torch.tensor([ms_rank], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    # One instrumented call: device time between the stages (this rank).
-    evs = []
-    blk.run(x, ids, wts, stage_events=evs)
-    torch.cuda.synchronize(dev)
-    stage_us = {n: a.elapsed_time(b) * 1e3 for (_, a), (n, b) in zip(evs[:-1], evs[1:])}
-    # The same call captured in a CUDA graph (NCCL barriers included) and replayed.
-    graph = blk.capture(x, ids, wts)
-    graph.replay()
-    torch.cuda.synchronize(dev)
-    dist.barrier(device_ids=[local_rank])
-    e0.record()
-    for _ in range(steps):
-        graph.replay()
-    e1.record()
-    torch.cuda.synchronize(dev)
-    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    graph_ms = float(t.item())
-    del graph
-    err = blk.check_errors()
     pairs = torch.tensor([int((ids >= 0).sum().item())], dtype=torch.float64, device=dev)
     dist.all_reduce(pairs)
     flops = 6.0 * float(pairs.item()) * H * I
+
+    def measure(mode):
+        """Eager, per-stage and CUDA-graph timings of one EPMoEBlock in `mode` (max over
+        ranks), its output on this rank, and its exchange error bits."""
+        blk = pkg.expert_parallel.EPMoEBlock(weights, E, T, topk, s_x, s_h, return_mode=mode)
+        for _ in range(max(args.warmup, 3)):
+            blk.run(x, ids, wts)
+        torch.cuda.synchronize(dev)
+        dist.barrier(device_ids=[local_rank])
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            blk.run(x, ids, wts)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        # One instrumented call: device time between the stages (this rank).
+        evs = []
+        blk.run(x, ids, wts, stage_events=evs)
+        torch.cuda.synchronize(dev)
+        stage_us = {n: a.elapsed_time(b) * 1e3 for (_, a), (n, b) in zip(evs[:-1], evs[1:])}
+        out = blk.out.clone()
+        # The same call captured in a CUDA graph (NCCL barriers included) and replayed.
+        graph = blk.capture(x, ids, wts)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        dist.barrier(device_ids=[local_rank])
+        e0.record()
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        graph_ms = float(t.item())
+        del graph
+        err = blk.check_errors()
+        dist.barrier(device_ids=[local_rank])
+        del blk
+        torch.cuda.empty_cache()
+        return {"return_mode": mode, "ms_per_step": ms, "us_per_call": ms * 1e3,
+                "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "stage_us_rank0": stage_us, "exchange_error_bits": err,
+                "cuda_graph": {"ms_per_step": graph_ms,
+                               "value": flops / (graph_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                               "what": "EPMoEBlock.capture, one call per replay, max over ranks"}}, out
+
+    modes = ["sums", "rows"] if args.ep_return == "both" else [args.ep_return]
+    runs, outs = [], []
+    for mode in modes:
+        r, o = measure(mode)
+        runs.append(r)
+        outs.append(o)
+    if len(outs) == 2:  # the two return forms differ only by the fp16 rounding of the sums
+        d = (outs[0].float() - outs[1].float()).norm() / outs[1].float().norm()
+        runs[1]["rel_diff_vs_sums"] = float(d.item())
+    main_run = runs[0]
+    ms, graph_ms, err = main_run["ms_per_step"], main_run["cuda_graph"]["ms_per_step"], \
+        main_run["exchange_error_bits"]
+    stage_us = main_run["stage_us_rank0"]
     tf = flops / (ms * 1e-3) / 1e12
     peaks, kind = load_peaks()
     peak = world * FP4_PER_BF16 * float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
     dist.barrier(device_ids=[local_rank])
-    del blk
     dist.destroy_process_group()
     if rank != 0:
         return
@@ -815,14 +844,21 @@ def run_moe_ep(args, world):
         "data": "synthetic (seeded; bf16 N(0,1) tokens, uniform top-8 routing, reference-set weights)",
         "config": {"workload": "moe-ep:cfg5", "experts": E, "tokens": args.tokens,
                    "tokens_per_rank": T, "experts_per_rank": epr, "topk": topk, "hidden": H,
-                   "intermediate": I, "parallelism": f"ep{world} (NVFP4 rows over NVLink peer "
-                   "stores; expert output rows stored back to their tokens' ranks by the down "
-                   "GEMM's epilogue; 3 NCCL one-element barriers per call)"},
+                   "intermediate": I, "return_mode": main_run["return_mode"],
+                   "parallelism": f"ep{world} (NVFP4 rows over NVLink peer stores; "
+                   + ("each token's rows summed on each owner, one fp16 row per (token, owner) "
+                      "stored back to the token's rank" if main_run["return_mode"] == "sums" else
+                      "expert output rows stored back to their tokens' ranks by the down "
+                      "GEMM's epilogue") + "; 3 NCCL one-element barriers per call)"},
         "api": "expert_parallel.EPMoEBlock.run",
         "gpu_launches_per_call": "route 3, quantise 1, publish 1, layout 1, dispatch 1, "
-                                 "scale layout 1, segment set-up + GEMM x2, combine 1 (+3 NCCL)",
+                                 + ("publish pairs 1, " if main_run["return_mode"] == "sums" else "")
+                                 + "scale layout 1, segment set-up + GEMM x2, "
+                                 + ("return sums 1, " if main_run["return_mode"] == "sums" else "")
+                                 + "combine 1 (+3 NCCL)",
         "exchange_error_bits": err,
         "stage_us_rank0": stage_us,
+        "other_return_modes": runs[1:],
         "cuda_graph": {"ms_per_step": graph_ms, "value": flops / (graph_ms * 1e-3) / 1e12,
                        "unit": "TFLOP/s", "what": "EPMoEBlock.capture, one call per replay, max "
                                                   "over ranks"},

@@ -318,6 +318,19 @@ NVFP4_API int nvfp4_moe_combine(const void* y, int64_t ldy, const int32_t* dest,
  *   nvfp4_ep_combine: out[t] = bf16(sum_j w[t, j] * ret[t * topk + j]) over kept pairs
  *     (fp32, slot order: bit-identical to nvfp4_moe_combine over the same rows)
  *
+ * Owner-side sums (a token's slots that meet on one owner return as one row):
+ *
+ *   after nvfp4_ep_dispatch, nvfp4_ep_publish_pairs: into every owner's pair tables
+ *     ([world, tokens * topk] int32 rows and fp32 weights, row q = source rank q; every rank
+ *     has the same tokens * topk) each pair's slab row there (-1 where it did not go) and,
+ *     on its owner, its routing weight                                                       |
+ *   owner: the down GEMM writes its output rows locally ([capacity, cols] fp16, slab order);
+ *     nvfp4_ep_return_sums: for every source rank q and token t with pairs here,
+ *     fp16(sum_j w[t, j] * y[row_j]) (fp32, slot order) -> row t * world + rank of rank q's
+ *     [tokens, world, cols] fp16 return buffer                                             |
+ *   nvfp4_ep_combine_sums: out[t] = bf16(sum_p ret[t, p]) over the owners p (ascending) that
+ *     hold a kept pair of t (fp32)
+ *
  * A segment that does not fit the owner's receive slab is dropped on every rank (its pairs
  * get remote_rows -1) and bit 0x1 is set in the layout's error word. No counterpart in the
  * reference (single GPU).
@@ -340,6 +353,17 @@ NVFP4_API int nvfp4_ep_dispatch(const int32_t* topk_ids, int tokens, int topk, i
 NVFP4_API int nvfp4_ep_combine(const int32_t* remote_rows, const float* weights, int tokens,
                                int topk, const void* ret, int cols, void* out, int64_t ldo,
                                void* stream);
+NVFP4_API int nvfp4_ep_publish_pairs(const int32_t* topk_ids, const int32_t* remote_rows,
+                                     const float* weights, int tokens, int topk, int num_experts,
+                                     int rank, int world, nvfp4_ep_peers pair_rows,
+                                     nvfp4_ep_peers pair_weights, void* stream);
+NVFP4_API int nvfp4_ep_return_sums(const int32_t* pair_rows, const float* pair_weights,
+                                   int tokens, int topk, int rank, int world, const void* y,
+                                   int64_t ldy, int cols, nvfp4_ep_peers ret, void* stream);
+NVFP4_API int nvfp4_ep_combine_sums(const int32_t* topk_ids, const int32_t* remote_rows,
+                                    int tokens, int topk, int num_experts, int world,
+                                    const void* ret, int cols, void* out, int64_t ldo,
+                                    void* stream);
 
 /*
  * Synchronise `stream`, then read and clear the device error word of `workspace`.

@@ -74,6 +74,9 @@ EXPORTED_SYMBOLS = (
     "nvfp4_ep_layout",
     "nvfp4_ep_dispatch",
     "nvfp4_ep_combine",
+    "nvfp4_ep_publish_pairs",
+    "nvfp4_ep_return_sums",
+    "nvfp4_ep_combine_sums",
 )
 
 ABI_VERSION = 2   # NVFP4_ABI_VERSION
@@ -258,6 +261,13 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_ep_dispatch.restype = i32
         lib.nvfp4_ep_combine.argtypes = [vp, vp, i32, i32, vp, i32, vp, i64, vp]
         lib.nvfp4_ep_combine.restype = i32
+        lib.nvfp4_ep_publish_pairs.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, EpPeers,
+                                               EpPeers, vp]
+        lib.nvfp4_ep_publish_pairs.restype = i32
+        lib.nvfp4_ep_return_sums.argtypes = [vp, vp, i32, i32, i32, i32, vp, i64, i32, EpPeers, vp]
+        lib.nvfp4_ep_return_sums.restype = i32
+        lib.nvfp4_ep_combine_sums.argtypes = [vp, vp, i32, i32, i32, i32, vp, i32, vp, i64, vp]
+        lib.nvfp4_ep_combine_sums.restype = i32
         if path is None:
             _lib = lib
         return lib

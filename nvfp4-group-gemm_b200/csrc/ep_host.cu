@@ -138,4 +138,85 @@ NVFP4_API int nvfp4_ep_combine(const int32_t* remote_rows, const float* weights,
   return NVFP4_OK;
 }
 
+NVFP4_API int nvfp4_ep_publish_pairs(const int32_t* topk_ids, const int32_t* remote_rows,
+                                     const float* weights, int tokens, int topk, int num_experts,
+                                     int rank, int world, nvfp4_ep_peers pair_rows,
+                                     nvfp4_ep_peers pair_weights, void* stream) {
+  g_last_error.clear();
+  int st = check_ep_world(num_experts, rank, world);
+  if (st != NVFP4_OK) return st;
+  if (tokens < 0 || topk <= 0)
+    return fail(NVFP4_ERR_BAD_SHAPE, "tokens=%d topk=%d", tokens, topk);
+  if (tokens == 0) return NVFP4_OK;
+  if (topk_ids == nullptr || remote_rows == nullptr || weights == nullptr)
+    return fail(NVFP4_ERR_NULL_POINTER, "a pair table input is NULL");
+  if ((st = check_peers(pair_rows, world, "pair_rows", false)) != NVFP4_OK) return st;
+  if ((st = check_peers(pair_weights, world, "pair_weights", false)) != NVFP4_OK) return st;
+  const int64_t pairs = static_cast<int64_t>(tokens) * topk;
+  const int64_t blocks = std::min<int64_t>((pairs + 255) / 256, 148 * 8);
+  nvfp4_ep_publish_pairs_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                                  static_cast<cudaStream_t>(stream)>>>(
+      topk_ids, remote_rows, weights, pairs, num_experts, rank, world, to_peers(pair_rows),
+      to_peers(pair_weights));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "publish pairs launch");
+  return NVFP4_OK;
+}
+
+NVFP4_API int nvfp4_ep_return_sums(const int32_t* pair_rows, const float* pair_weights,
+                                   int tokens, int topk, int rank, int world, const void* y,
+                                   int64_t ldy, int cols, nvfp4_ep_peers ret, void* stream) {
+  g_last_error.clear();
+  if (world < 1 || world > kEpMaxRanks || rank < 0 || rank >= world)
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "rank %d of world %d (1..%d ranks)", rank, world,
+                kEpMaxRanks);
+  if (tokens < 0 || topk <= 0 || cols <= 0 || cols % 8 != 0)
+    return fail(NVFP4_ERR_BAD_SHAPE, "tokens=%d topk=%d cols=%d (cols a multiple of 8)", tokens,
+                topk, cols);
+  if (tokens == 0) return NVFP4_OK;
+  if (pair_rows == nullptr || pair_weights == nullptr || y == nullptr)
+    return fail(NVFP4_ERR_NULL_POINTER, "a return-sum buffer is NULL");
+  if (!aligned16(y) || ldy % 8 != 0 || ldy < cols)
+    return fail(NVFP4_ERR_MISALIGNED, "y 16-byte aligned, ldy a multiple of 8 >= cols");
+  int st = check_peers(ret, world, "ret", true);
+  if (st != NVFP4_OK) return st;
+  const int groups = (cols + 256 * kEpSumParts - 1) / (256 * kEpSumParts);
+  const int64_t warps = static_cast<int64_t>(world) * tokens * groups;
+  const int64_t blocks = std::min<int64_t>((warps + 7) / 8, 148 * 16);
+  nvfp4_ep_return_sums_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                                static_cast<cudaStream_t>(stream)>>>(
+      pair_rows, pair_weights, tokens, topk, rank, world, static_cast<const __half*>(y), ldy,
+      cols, to_peers(ret));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "return sums launch");
+  return NVFP4_OK;
+}
+
+NVFP4_API int nvfp4_ep_combine_sums(const int32_t* topk_ids, const int32_t* remote_rows,
+                                    int tokens, int topk, int num_experts, int world,
+                                    const void* ret, int cols, void* out, int64_t ldo,
+                                    void* stream) {
+  g_last_error.clear();
+  int st = check_ep_world(num_experts, 0, world);
+  if (st != NVFP4_OK) return st;
+  if (tokens < 0 || topk <= 0 || cols <= 0 || cols % 8 != 0)
+    return fail(NVFP4_ERR_BAD_SHAPE, "tokens=%d topk=%d cols=%d (cols a multiple of 8)", tokens,
+                topk, cols);
+  if (tokens == 0) return NVFP4_OK;
+  if (topk_ids == nullptr || remote_rows == nullptr || ret == nullptr || out == nullptr)
+    return fail(NVFP4_ERR_NULL_POINTER, "a combine buffer is NULL");
+  if (!aligned16(out) || !aligned16(ret) || ldo % 8 != 0 || ldo < cols)
+    return fail(NVFP4_ERR_MISALIGNED, "ret and out 16-byte aligned, ldo a multiple of 8 >= cols");
+  const int groups = (cols + 256 * kEpSumParts - 1) / (256 * kEpSumParts);
+  const int64_t warps = static_cast<int64_t>(tokens) * groups;
+  const int64_t blocks = std::min<int64_t>((warps + 7) / 8, 148 * 16);
+  nvfp4_ep_combine_sums_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                                 static_cast<cudaStream_t>(stream)>>>(
+      topk_ids, remote_rows, tokens, topk, num_experts, world, static_cast<const __half*>(ret),
+      cols, static_cast<__nv_bfloat16*>(out), ldo);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "combine sums launch");
+  return NVFP4_OK;
+}
+
 }  // extern "C"

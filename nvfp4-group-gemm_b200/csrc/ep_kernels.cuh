@@ -17,6 +17,14 @@
 //    epilogue stores every output row into its token's rank's return buffer)        |
 //   combine:         rank q sums its pairs' returned rows (local reads)
 //
+// Or, with owner-side sums (return_sums): after dispatch rank q also publishes, into every
+// owner's [P, tokens * topk] pair tables, each pair's slab row there (-1 when the pair went
+// elsewhere) and its routing weight; the owner's down GEMM writes its rows locally, and
+// return_sums adds each source token's rows of this owner (slot order, fp32) and stores one
+// fp16 row per (token, owner) into the token's rank                                 |
+//   combine_sums:    rank q adds its tokens' per-owner rows in owner order (local reads)
+// A token whose slots meet on one owner then sends one row back instead of one per slot.
+//
 // The kernels only load and store: no kernel waits on another rank, so the barriers (a
 // one-element NCCL all-reduce on the same stream) carry all cross-rank ordering.
 #pragma once
@@ -172,6 +180,175 @@ __global__ void __launch_bounds__(256) nvfp4_ep_combine_kernel(
     combine_slots(t, topk, col, active, ret, cols, weights,
                   [&](int64_t i) -> int64_t { return __ldg(remote_rows + i) < 0 ? -1 : i; }, acc);
     if (active) store_bf16x8(out + t * ldo + col, acc);
+  }
+}
+
+// ---- owner-side sums -----------------------------------------------------------------------
+// Pair tables (one [world, pairs] int32 and one [world, pairs] fp32 array on every rank, pairs
+// = tokens * topk, the same on every rank): row q holds source rank q's pairs.
+
+// One thread per pair of this rank: in every owner's table, the pair's slab row there (-1 on
+// the owners it did not go to, and everywhere for dropped pairs), and on its owner its
+// routing weight. The tables are rewritten in full on every call, so no entry is stale.
+__global__ void __launch_bounds__(256) nvfp4_ep_publish_pairs_kernel(
+    const int32_t* __restrict__ ids, const int32_t* __restrict__ remote_rows,
+    const float* __restrict__ weights, int64_t pairs, int num_experts, int rank, int world,
+    EpPeers pair_rows, EpPeers pair_weights) {
+  const int epr = num_experts / world;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < pairs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = ids[i];
+    const int32_t row = remote_rows[i];
+    const int owner = (row >= 0 && e >= 0 && e < num_experts) ? e / epr : -1;
+    const int64_t at = static_cast<int64_t>(rank) * pairs + i;
+    for (int p = 0; p < world; ++p)
+      static_cast<int32_t*>(pair_rows.ptr[p])[at] = p == owner ? row : -1;
+    if (owner >= 0) static_cast<float*>(pair_weights.ptr[owner])[at] = weights[i];
+  }
+  __threadfence_system();
+}
+
+// Adds one fp16x8 word group, scaled by w (w = 1: unscaled), to acc (fp32 products and sums).
+__device__ __forceinline__ void add_half8(float* acc, const uint4& raw, float w, bool scale) {
+  const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&words[k]));
+    acc[2 * k] = __fadd_rn(acc[2 * k], scale ? __fmul_rn(w, f.x) : f.x);
+    acc[2 * k + 1] = __fadd_rn(acc[2 * k + 1], scale ? __fmul_rn(w, f.y) : f.y);
+  }
+}
+
+// Columns per warp task of the two kernels below: two 256-column parts (8 columns per lane
+// each), so a lane keeps up to 16 x 16 bytes of rows in flight.
+constexpr int kEpSumParts = 2;
+
+// One warp per (token t, source rank q, 512-column group), on the owner, tasks ordered token
+// first so that stores to every rank run side by side: the fp32 sum, in slot order, of
+// w_j * y[row_j] over t's pairs that came here (each product and each sum rounded to fp32,
+// as in the slot-order combine), rounded to fp16 and stored as row (t * world + rank) of rank
+// q's [tokens, world, cols] return buffer. Tokens with no pair here store nothing (their rank
+// knows and skips the row). Per window of 8 slots, the rows' indices and weights, then every
+// row load of both parts are issued before the first add.
+__global__ void __launch_bounds__(256) nvfp4_ep_return_sums_kernel(
+    const int32_t* __restrict__ pair_rows, const float* __restrict__ pair_weights, int tokens,
+    int topk, int rank, int world, const __half* __restrict__ y, int64_t ldy, int cols,
+    EpPeers ret) {
+  const int lane = threadIdx.x & 31;
+  const int groups = (cols + 256 * kEpSumParts - 1) / (256 * kEpSumParts);
+  const int64_t pairs = static_cast<int64_t>(tokens) * topk;
+  const int64_t tasks = static_cast<int64_t>(tokens) * world * groups;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t task = warp0; task < tasks; task += nwarps) {
+    const int64_t tq = task / groups;  // t * world + q
+    const int64_t t = tq / world;
+    const int q = static_cast<int>(tq % world);
+    const int col0 = static_cast<int>(task % groups) * 256 * kEpSumParts + lane * 8;
+    const int32_t* rows = pair_rows + static_cast<int64_t>(q) * pairs + t * topk;
+    const float* wts = pair_weights + static_cast<int64_t>(q) * pairs + t * topk;
+    float acc[kEpSumParts][8];
+#pragma unroll
+    for (int u = 0; u < kEpSumParts; ++u)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[u][i] = 0.0f;
+    bool any = false;
+    for (int j0 = 0; j0 < topk; j0 += 8) {
+      const int jn = topk - j0 < 8 ? topk - j0 : 8;
+      int32_t r[8];
+      float w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) r[j] = j < jn ? __ldg(rows + j0 + j) : -1;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = r[j] >= 0 ? __ldg(wts + j0 + j) : 0.0f;
+      uint4 raw[8][kEpSumParts];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int u = 0; u < kEpSumParts; ++u) {
+          const int col = col0 + 256 * u;
+          raw[j][u] = (r[j] >= 0 && col < cols)
+                          ? __ldg(reinterpret_cast<const uint4*>(y + r[j] * ldy + col))
+                          : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (r[j] < 0) continue;
+        any = true;
+#pragma unroll
+        for (int u = 0; u < kEpSumParts; ++u) add_half8(acc[u], raw[j][u], w[j], true);
+      }
+    }
+    if (!any) continue;
+    __half* dst_row = static_cast<__half*>(ret.ptr[q]) + (t * world + rank) * cols;
+#pragma unroll
+    for (int u = 0; u < kEpSumParts; ++u) {
+      const int col = col0 + 256 * u;
+      if (col >= cols) continue;
+      uint32_t packed[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const __half2 h = __floats2half2_rn(acc[u][2 * k], acc[u][2 * k + 1]);
+        packed[k] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(dst_row + col) =
+          make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    }
+  }
+  __threadfence_system();
+}
+
+// out[t, :] = bf16( sum over owners p (ascending) that hold at least one kept pair of t of
+// fp32(ret[t, p, :]) ), fp32 sums. One warp per (token, 512-column group); the rows of two
+// owners (both parts) are loaded before they are added.
+__global__ void __launch_bounds__(256) nvfp4_ep_combine_sums_kernel(
+    const int32_t* __restrict__ ids, const int32_t* __restrict__ remote_rows, int tokens,
+    int topk, int num_experts, int world, const __half* __restrict__ ret, int cols,
+    __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int lane = threadIdx.x & 31;
+  const int groups = (cols + 256 * kEpSumParts - 1) / (256 * kEpSumParts);
+  const int epr = num_experts / world;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t task = warp0; task < static_cast<int64_t>(tokens) * groups; task += nwarps) {
+    const int64_t t = task / groups;
+    const int col0 = static_cast<int>(task % groups) * 256 * kEpSumParts + lane * 8;
+    uint32_t owners = 0;  // bit p: owner p holds a kept pair of t
+    for (int j = 0; j < topk; ++j) {
+      const int e = __ldg(ids + t * topk + j);
+      if (__ldg(remote_rows + t * topk + j) >= 0 && e >= 0 && e < num_experts)
+        owners |= 1u << (e / epr);
+    }
+    float acc[kEpSumParts][8];
+#pragma unroll
+    for (int u = 0; u < kEpSumParts; ++u)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[u][i] = 0.0f;
+    for (int p0 = 0; p0 < world; p0 += 2) {
+      uint4 raw[2][kEpSumParts];
+#pragma unroll
+      for (int v = 0; v < 2; ++v)
+#pragma unroll
+        for (int u = 0; u < kEpSumParts; ++u) {
+          const int p = p0 + v;
+          const int col = col0 + 256 * u;
+          raw[v][u] = (p < world && ((owners >> p) & 1u) && col < cols)
+                          ? __ldg(reinterpret_cast<const uint4*>(ret + (t * world + p) * cols + col))
+                          : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        const int p = p0 + v;
+        if (p >= world || !((owners >> p) & 1u)) continue;
+#pragma unroll
+        for (int u = 0; u < kEpSumParts; ++u) add_half8(acc[u], raw[v][u], 1.0f, false);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kEpSumParts; ++u) {
+      const int col = col0 + 256 * u;
+      if (col < cols) store_bf16x8(out + t * ldo + col, acc[u]);
+    }
   }
 }
 

@@ -287,18 +287,29 @@ class EPMoEBlock:
     route + quantise the local tokens; publish per-expert counts into every rank's count
     matrix | layout (all ranks derive the same placement); dispatch codes + scale rows (and
     each row's return address) into the owners' receive slabs | owner: scales to the blocked
-    layout, gated GEMM over its expert segments with NVFP4 output, down GEMM whose epilogue
-    stores every output row into its token's rank (NVLink stores overlapping the GEMM) |
-    combine: weighted fp32 sum of each token's returned rows in slot order, bf16.
+    layout, gated GEMM over its expert segments with NVFP4 output, then the down GEMM and
+    the return, in one of two forms (``return_mode``):
+
+    * ``"sums"`` (default): dispatch also publishes each pair's slab row and routing weight
+      into its owner's pair tables; the down GEMM writes its rows locally, and
+      nvfp4_ep_return_sums adds each source token's rows of this owner (weighted, slot
+      order, fp32) and stores one fp16 row per (token, owner) into the token's rank |
+      combine: fp32 sum of each token's per-owner rows in owner order, bf16. A token's slots
+      that meet on one owner cross NVLink as one row.
+    * ``"rows"``: the down GEMM's epilogue stores every output row into its token's rank
+      (NVLink stores overlapping the GEMM) | combine: weighted fp32 sum of each token's
+      returned rows in slot order, bf16 -- bit-identical to the single-GPU MoEBlock.
 
     The receive slabs hold ``world * tokens * topk + 127 * E/P`` rows (every pair of every
     rank routed here, plus segment padding), so the exchange never drops a pair. Count
-    matrix, receive slabs, return addresses and the return buffer ([tokens * topk, H] fp16)
-    live in one torch symmetric-memory allocation.
+    matrix, receive slabs, return addresses, pair tables and the return buffer ([tokens,
+    world, H] fp16 for sums, [tokens * topk, H] for rows) live in one torch symmetric-memory
+    allocation.
     """
 
     def __init__(self, local_weights, num_experts: int, tokens: int, topk: int,
-                 act_scale: float, hidden_scale: float, group=None, cta: str | None = None):
+                 act_scale: float, hidden_scale: float, group=None, cta: str | None = None,
+                 return_mode: str = "sums"):
         import numpy as np
         from torch.distributed import _symmetric_memory as symm
 
@@ -307,6 +318,9 @@ class EPMoEBlock:
 
         if cta not in (None, "pair", "single"):
             raise ValueError(f"cta must be None, 'pair' or 'single', got {cta!r}")
+        if return_mode not in ("sums", "rows"):
+            raise ValueError(f"return_mode must be 'sums' or 'rows', got {return_mode!r}")
+        self.return_mode = return_mode
         self.group = group if group is not None else dist.group.WORLD
         world = dist.get_world_size(self.group)
         rank = dist.get_rank(self.group)
@@ -336,15 +350,20 @@ class EPMoEBlock:
         self.capacity = cap
 
         # One symmetric allocation: count matrix | received codes | received plain scales |
-        # return address of each received row | returned expert rows of this rank's pairs.
+        # return address of each received row | returned rows (sums: one per token and owner;
+        # rows: one per pair) | pair tables of the sums (slab row and weight of each source
+        # rank's pairs here).
+        sums = return_mode == "sums"
+
         def up(n):
             return (n + 255) // 256 * 256
         sizes = [world * num_experts * 4, cap * hdim // 2, cap * hdim // 16, cap * 8,
-                 pairs * hdim * 2]
+                 (tokens * world if sums else pairs) * hdim * 2,
+                 world * pairs * 4 if sums else 0, world * pairs * 4 if sums else 0]
         offs = [0]
         for n in sizes[:-1]:
             offs.append(offs[-1] + up(n))
-        total = offs[-1] + up(sizes[-1])
+        total = offs[-1] + max(up(sizes[-1]), 256)
         self._symm = symm.empty(total, dtype=torch.uint8, device=dev)
         self._symm.zero_()
         try:
@@ -361,11 +380,19 @@ class EPMoEBlock:
         self._recv_codes = sl[1].view(cap, hdim // 2)
         self._recv_sf = sl[2].view(cap, hdim // 16)
         self._recv_meta = sl[3].view(torch.int64)
-        self._ret = sl[4].view(torch.float16).view(pairs, hdim)
-        # The down GEMM's output rows go to the token's rank: row r of this rank's slab to
-        # return buffer (recv_meta[r] >> 40) at pair (recv_meta[r] & (2^40 - 1)).
-        self._scatter = _native.SegmentOutput.scattered(
-            self._recv_meta.data_ptr(), [b + delta + offs[4] for b in bases], hdim * 2)
+        if sums:
+            self._ret = sl[4].view(torch.float16).view(tokens, world, hdim)
+            self._pair_rows = sl[5].view(torch.int32).view(world, pairs)
+            self._pair_w = sl[6].view(torch.float32).view(world, pairs)
+            # The down GEMM's rows stay here (slab order); return_sums reads them.
+            self._y = torch.empty((cap, hdim), dtype=torch.float16, device=dev)
+            self._scatter = None
+        else:
+            self._ret = sl[4].view(torch.float16).view(pairs, hdim)
+            # The down GEMM's output rows go to the token's rank: row r of this rank's slab to
+            # return buffer (recv_meta[r] >> 40) at pair (recv_meta[r] & (2^40 - 1)).
+            self._scatter = _native.SegmentOutput.scattered(
+                self._recv_meta.data_ptr(), [b + delta + offs[4] for b in bases], hdim * 2)
 
         i32 = dict(dtype=torch.int32, device=dev)
         u8 = dict(dtype=torch.uint8, device=dev)
@@ -408,9 +435,11 @@ class EPMoEBlock:
         self._t1 = slab_table(self._recv_codes, self._recv_sfa, self._a2, P["w_gate"], P["sf_gate"],
                               idim, hdim, s_x * np.asarray(W.s_gate, dtype=np.float32),
                               P["w_up"], P["sf_up"], s_x * np.asarray(W.s_up, dtype=np.float32))
-        # c of the down GEMM is never written (scattered output); any valid aligned address.
-        self._t2 = slab_table(self._a2, self._sfa2, self._ret, P["w_down"], P["sf_down"], hdim,
-                              idim, s_h * np.asarray(W.s_down, dtype=np.float32))
+        # c of the down GEMM: the local slab (sums), or never written (rows: scattered output;
+        # any valid aligned address).
+        self._t2 = slab_table(self._a2, self._sfa2, self._y if sums else self._ret, P["w_down"],
+                              P["sf_down"], hdim, idim,
+                              s_h * np.asarray(W.s_down, dtype=np.float32))
         self._nvfp4_out = _native.SegmentOutput.nvfp4(self._sfa2.data_ptr(), self.hidden_scale)
         ws_bytes = _native.workspace_size(epr)
         self._ws1 = torch.zeros(ws_bytes, **u8)
@@ -469,6 +498,14 @@ class EPMoEBlock:
                                   self._qx.data_ptr(), self._qx.stride(0), self._sfx.data_ptr(), H,
                                   self._peers[1], self._peers[2], self._peers[3], cap,
                                   self.remote_rows.data_ptr(), s), lib)
+        w = topk_weights
+        if w.dtype != torch.float32 or not w.is_contiguous():
+            self._w.copy_(w)
+            w = self._w
+        if self._scatter is None:
+            chk(lib.nvfp4_ep_publish_pairs(topk_ids.data_ptr(), self.remote_rows.data_ptr(),
+                                           w.data_ptr(), T, K, E, rank, world, self._peers[5],
+                                           self._peers[6], s), lib)
         mark("layout + dispatch")
         self._barrier()
         mark("barrier")
@@ -484,16 +521,24 @@ class EPMoEBlock:
                                           self.seg_counts.data_ptr(), T * K,
                                           self._ws2.data_ptr(), self._ws_bytes, s, self._scatter)
         self._uploaded = True
-        mark("down GEMM + return rows")
+        if self._scatter is None:
+            mark("down GEMM")
+            chk(lib.nvfp4_ep_return_sums(self._pair_rows.data_ptr(), self._pair_w.data_ptr(), T,
+                                         K, rank, world, self._y.data_ptr(), self._y.stride(0), H,
+                                         self._peers[4], s), lib)
+            mark("return sums")
+        else:
+            mark("down GEMM + return rows")
         self._barrier()
         mark("barrier 2")
-        w = topk_weights
-        if w.dtype != torch.float32 or not w.is_contiguous():
-            self._w.copy_(w)
-            w = self._w
-        chk(lib.nvfp4_ep_combine(self.remote_rows.data_ptr(), w.data_ptr(), T, K,
-                                 self._ret.data_ptr(), H, self.out.data_ptr(), self.out.stride(0),
-                                 s), lib)
+        if self._scatter is None:
+            chk(lib.nvfp4_ep_combine_sums(topk_ids.data_ptr(), self.remote_rows.data_ptr(), T, K,
+                                          E, world, self._ret.data_ptr(), H,
+                                          self.out.data_ptr(), self.out.stride(0), s), lib)
+        else:
+            chk(lib.nvfp4_ep_combine(self.remote_rows.data_ptr(), w.data_ptr(), T, K,
+                                     self._ret.data_ptr(), H, self.out.data_ptr(),
+                                     self.out.stride(0), s), lib)
         mark("combine")
         return self.out
 

@@ -78,3 +78,37 @@ def place_pairs(ids_per_rank, num_experts: int, world: int, capacity: int):
             next_row[e] += 1
         remote.append(rows.astype(np.int32))
     return counts.astype(np.int32), remote, received
+
+
+def presum_combine(y_pairs: np.ndarray, kept: np.ndarray, owner: np.ndarray,
+                   weights: np.ndarray, world: int):
+    """Owner-side sums followed by the per-owner combine (nvfp4_ep_return_sums +
+    nvfp4_ep_combine_sums). y_pairs fp16 [tokens, topk, cols]: each pair's down-GEMM row;
+    kept [tokens, topk]: pairs that reached their owner; owner [tokens, topk]: the rank owning
+    the pair's expert; weights fp32 [tokens, topk].
+
+    partial[t, p] = fp16(sum_j w[t, j] * y[t, j]) over t's kept pairs owned by p, slots in
+    order, each product and each sum rounded to fp32 (the slot-order combine's arithmetic);
+    out[t] = bf16(sum_p fp32(partial[t, p])) over the owners p (ascending) holding at least
+    one kept pair of t. Returns (partial fp16 [tokens, world, cols], has [tokens, world],
+    out bf16 bit patterns [tokens, cols])."""
+    y32 = np.asarray(y_pairs, dtype=np.float16).astype(np.float32)
+    tokens, topk, cols = y32.shape
+    w = np.asarray(weights, dtype=np.float32)
+    kept = np.asarray(kept, dtype=bool)
+    owner = np.asarray(owner)
+    partial = np.zeros((tokens, world, cols), dtype=np.float16)
+    has = np.zeros((tokens, world), dtype=bool)
+    for p in range(world):
+        acc = np.zeros((tokens, cols), dtype=np.float32)
+        for j in range(topk):
+            ok = kept[:, j] & (owner[:, j] == p)
+            prod = (w[:, j:j + 1] * y32[:, j]).astype(np.float32)
+            acc = np.where(ok[:, None], (acc + prod).astype(np.float32), acc)
+            has[:, p] |= ok
+        partial[:, p] = acc.astype(np.float16)
+    out = np.zeros((tokens, cols), dtype=np.float32)
+    for p in range(world):
+        out = np.where(has[:, p:p + 1], (out + partial[:, p].astype(np.float32)).astype(np.float32),
+                       out)
+    return partial, has, M.fp32_to_bf16_bits(out)

@@ -5,11 +5,16 @@ than 2 GPUs.
 
 Each rank checks, for its own tokens: the placement (count matrix, segments, every pair's
 row in its owner's slab) against the CPU oracle of the exchange, and the block's output
-bit for bit against the single-GPU MoEBlock run over the same tokens with all experts (the
-same rows meet the same weights in both; tiles forced to single CTAs so both pick the same
-kernels). Two calls with different tokens and routings check the buffers' reuse; a CUDA
-graph of a whole call (NCCL barriers included), replayed on new inputs, must equal an
-eager call.
+against the single-GPU MoEBlock run over the same tokens with all experts, whose down-GEMM
+rows are the same rows (tiles forced to single CTAs so both pick the same kernels):
+
+* return_mode "rows": bit for bit equal to MoEBlock's output (same rows, same weights, same
+  slot-order arithmetic);
+* return_mode "sums": the per-(token, owner) rows in the return buffer and the output bit
+  for bit equal to the oracle's owner-side sums (``presum_combine``) over MoEBlock's rows.
+
+Two calls with different tokens and routings check the buffers' reuse; a CUDA graph of a
+whole call (NCCL barriers included), replayed on new inputs, must equal an eager call.
 """
 from __future__ import annotations
 
@@ -44,7 +49,7 @@ def _inputs(seed, dev):
     return x.to(dev), ids.to(dev), wts.to(dev)
 
 
-def _worker(rank, world, port, cta, q):
+def _worker(rank, world, port, cta, mode, q):
     try:
         import sys
 
@@ -73,7 +78,7 @@ def _worker(rank, world, port, cta, q):
         local = pkg.moe.ExpertWeights(**{f: getattr(W, f)[sl] for f in (
             "w_gate", "sf_gate", "w_up", "sf_up", "w_down", "sf_down", "s_gate", "s_up", "s_down")})
         s_x, s_h = 0.004, 0.002
-        ep = pkg.expert_parallel.EPMoEBlock(local, E, T, TOPK, s_x, s_h, cta=cta)
+        ep = pkg.expert_parallel.EPMoEBlock(local, E, T, TOPK, s_x, s_h, cta=cta, return_mode=mode)
         ref_blk = pkg.moe.MoEBlock(W, T, TOPK, s_x, s_h, cta=cta)
         checks = []
         for call in range(2):
@@ -87,7 +92,22 @@ def _worker(rank, world, port, cta, q):
             all_ids = [_inputs(1000 * call + r, "cpu")[1].numpy() for r in range(world)]
             counts, remote, _ = EPO.place_pairs(all_ids, E, world, ep.capacity)
             seg_off, seg_cnt, send_base, dropped = EPO.ep_layout(counts, world, rank, ep.capacity)
-            checks.append(dict(
+            sums = {}
+            if mode == "sums":
+                # MoEBlock's down-GEMM row of every pair, then the owner-side sums over them.
+                dest = ref_blk.dest.cpu().numpy().reshape(T, TOPK)
+                y = ref_blk._y.cpu().numpy()[np.maximum(dest, 0)]
+                kept = ep.remote_rows.cpu().numpy().reshape(T, TOPK) >= 0
+                owner = ids.cpu().numpy() // epr
+                part, has, bits = EPO.presum_combine(y, kept, owner, wts.cpu().numpy(), world)
+                ret = ep._ret.cpu().numpy()
+                sums = dict(
+                    kept_is_dest=bool(np.array_equal(kept, dest >= 0)),
+                    partials=bool(np.array_equal(ret[has].view(np.uint16),
+                                                 part[has].view(np.uint16))),
+                    out_oracle=bool(np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16),
+                                                   bits)))
+            checks.append(dict(sums,
                 err=err, dropped=dropped,
                 mat=np.array_equal(ep._mat.cpu().numpy(), counts),
                 seg=np.array_equal(ep.seg_offsets.cpu().numpy(), seg_off) and
@@ -128,13 +148,14 @@ def _worker(rank, world, port, cta, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("cta", ["single", None])
-def test_ep_moe_block_two_gpus(cta):
+@pytest.mark.parametrize("cta,mode", [("single", "sums"), ("single", "rows"), (None, "sums")])
+def test_ep_moe_block_two_gpus(cta, mode):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, cta, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cta, mode, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = {}
@@ -152,8 +173,10 @@ def test_ep_moe_block_two_gpus(cta):
             assert c["err"] == 0 and not c["dropped"], (rank, call, c)
             assert c["mat"] and c["seg"] and c["send"] and c["rows"], (rank, call, c)
             assert c["finite"], (rank, call, c)
-            if cta == "single":
+            if cta == "single" and mode == "rows":
                 assert c["out_equal"], (rank, call, c)
+            elif cta == "single":
+                assert c["kept_is_dest"] and c["partials"] and c["out_oracle"], (rank, call, c)
             else:
                 assert c["rel"] < 1e-2, (rank, call, c)
     for p in procs:
