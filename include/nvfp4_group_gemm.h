@@ -318,12 +318,16 @@ NVFP4_API int nvfp4_moe_combine(const void* y, int64_t ldy, const int32_t* dest,
  *   nvfp4_ep_combine: out[t] = bf16(sum_j w[t, j] * ret[t * topk + j]) over kept pairs
  *     (fp32, slot order: bit-identical to nvfp4_moe_combine over the same rows)
  *
- * Owner-side sums (a token's slots that meet on one owner return as one row):
+ * Owner-side sums (a token's slots that meet on one owner travel as one row each way):
  *
- *   after nvfp4_ep_dispatch, nvfp4_ep_publish_pairs: into every owner's pair tables
- *     ([world, tokens * topk] int32 rows and fp32 weights, row q = source rank q; every rank
- *     has the same tokens * topk) each pair's slab row there (-1 where it did not go) and,
- *     on its owner, its routing weight                                                       |
+ *   nvfp4_ep_dispatch_tokens instead of nvfp4_ep_dispatch: remote_rows as nvfp4_ep_dispatch
+ *     gives them, and each token's codes and plain scale row once into every owner holding
+ *     a kept pair of it ([world * tokens] token-slab rows there, row rank * tokens + t);
+ *   nvfp4_ep_publish_pairs: into every owner's pair tables ([world, tokens * topk] int32 rows
+ *     and fp32 weights, row q = source rank q; every rank has the same tokens * topk) each
+ *     pair's slab row there (-1 where it did not go) and, on its owner, its routing weight |
+ *   owner: nvfp4_ep_expand copies each received pair's token row from the token slabs into
+ *     its receive-slab row (what nvfp4_ep_dispatch would have stored there);
  *   owner: the down GEMM writes its output rows locally ([capacity, cols] fp16, slab order);
  *     nvfp4_ep_return_sums: for every source rank q and token t with pairs here,
  *     fp16(sum_j w[t, j] * y[row_j]) (fp32, slot order) -> row t * world + rank of rank q's
@@ -353,6 +357,16 @@ NVFP4_API int nvfp4_ep_dispatch(const int32_t* topk_ids, int tokens, int topk, i
 NVFP4_API int nvfp4_ep_combine(const int32_t* remote_rows, const float* weights, int tokens,
                                int topk, const void* ret, int cols, void* out, int64_t ldo,
                                void* stream);
+NVFP4_API int nvfp4_ep_dispatch_tokens(const int32_t* topk_ids, int tokens, int topk,
+                                       int num_experts, int rank, int world, const int32_t* dest,
+                                       const int32_t* offsets, const int32_t* send_base,
+                                       const void* codes, int64_t ld_codes, const void* sf_blocked,
+                                       int cols, nvfp4_ep_peers tok_codes, nvfp4_ep_peers tok_sf,
+                                       int64_t recv_capacity, int32_t* remote_rows, void* stream);
+NVFP4_API int nvfp4_ep_expand(const int32_t* pair_rows, int tokens, int topk, int world,
+                              const void* tok_codes, const void* tok_sf, int cols,
+                              void* recv_codes, void* recv_sf, int64_t recv_capacity,
+                              void* stream);
 NVFP4_API int nvfp4_ep_publish_pairs(const int32_t* topk_ids, const int32_t* remote_rows,
                                      const float* weights, int tokens, int topk, int num_experts,
                                      int rank, int world, nvfp4_ep_peers pair_rows,

@@ -74,6 +74,8 @@ EXPORTED_SYMBOLS = (
     "nvfp4_ep_layout",
     "nvfp4_ep_dispatch",
     "nvfp4_ep_combine",
+    "nvfp4_ep_dispatch_tokens",
+    "nvfp4_ep_expand",
     "nvfp4_ep_publish_pairs",
     "nvfp4_ep_return_sums",
     "nvfp4_ep_combine_sums",
@@ -261,6 +263,11 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.nvfp4_ep_dispatch.restype = i32
         lib.nvfp4_ep_combine.argtypes = [vp, vp, i32, i32, vp, i32, vp, i64, vp]
         lib.nvfp4_ep_combine.restype = i32
+        lib.nvfp4_ep_dispatch_tokens.argtypes = [vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, i64,
+                                                 vp, i32, EpPeers, EpPeers, i64, vp, vp]
+        lib.nvfp4_ep_dispatch_tokens.restype = i32
+        lib.nvfp4_ep_expand.argtypes = [vp, i32, i32, i32, vp, vp, i32, vp, vp, i64, vp]
+        lib.nvfp4_ep_expand.restype = i32
         lib.nvfp4_ep_publish_pairs.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, EpPeers,
                                                EpPeers, vp]
         lib.nvfp4_ep_publish_pairs.restype = i32

@@ -138,6 +138,68 @@ NVFP4_API int nvfp4_ep_combine(const int32_t* remote_rows, const float* weights,
   return NVFP4_OK;
 }
 
+NVFP4_API int nvfp4_ep_dispatch_tokens(const int32_t* topk_ids, int tokens, int topk,
+                                       int num_experts, int rank, int world, const int32_t* dest,
+                                       const int32_t* offsets, const int32_t* send_base,
+                                       const void* codes, int64_t ld_codes, const void* sf_blocked,
+                                       int cols, nvfp4_ep_peers tok_codes, nvfp4_ep_peers tok_sf,
+                                       int64_t recv_capacity, int32_t* remote_rows, void* stream) {
+  g_last_error.clear();
+  int st = check_ep_world(num_experts, rank, world);
+  if (st != NVFP4_OK) return st;
+  if (tokens < 0 || topk <= 0 || cols <= 0 || cols % 256 != 0)
+    return fail(NVFP4_ERR_BAD_SHAPE, "tokens=%d topk=%d cols=%d (cols a multiple of 256)",
+                tokens, topk, cols);
+  if (tokens == 0) return NVFP4_OK;
+  if (topk_ids == nullptr || dest == nullptr || offsets == nullptr || send_base == nullptr ||
+      codes == nullptr || sf_blocked == nullptr || remote_rows == nullptr)
+    return fail(NVFP4_ERR_NULL_POINTER, "a dispatch buffer is NULL");
+  if (!aligned16(codes) || ld_codes % 16 != 0 || ld_codes < cols / 2 ||
+      (reinterpret_cast<uintptr_t>(sf_blocked) & 3u) != 0)
+    return fail(NVFP4_ERR_MISALIGNED, "codes 16-byte aligned with ld a multiple of 16 >= cols/2, "
+                "scales 4-byte aligned");
+  if ((st = check_peers(tok_codes, world, "tok_codes", true)) != NVFP4_OK) return st;
+  if ((st = check_peers(tok_sf, world, "tok_sf", true)) != NVFP4_OK) return st;
+  const int64_t blocks = std::min<int64_t>((static_cast<int64_t>(tokens) + 7) / 8, 148 * 16);
+  nvfp4_ep_dispatch_tokens_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                                    static_cast<cudaStream_t>(stream)>>>(
+      topk_ids, tokens, topk, num_experts, rank, world, dest, offsets, send_base,
+      static_cast<const uint8_t*>(codes), ld_codes, static_cast<const uint8_t*>(sf_blocked), cols,
+      to_peers(tok_codes), to_peers(tok_sf), recv_capacity, remote_rows);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "dispatch tokens launch");
+  return NVFP4_OK;
+}
+
+NVFP4_API int nvfp4_ep_expand(const int32_t* pair_rows, int tokens, int topk, int world,
+                              const void* tok_codes, const void* tok_sf, int cols,
+                              void* recv_codes, void* recv_sf, int64_t recv_capacity,
+                              void* stream) {
+  g_last_error.clear();
+  if (world < 1 || world > kEpMaxRanks)
+    return fail(NVFP4_ERR_INVALID_ARGUMENT, "world %d (1..%d ranks)", world, kEpMaxRanks);
+  if (tokens < 0 || topk <= 0 || cols <= 0 || cols % 256 != 0 || recv_capacity < 0)
+    return fail(NVFP4_ERR_BAD_SHAPE, "tokens=%d topk=%d cols=%d (cols a multiple of 256)",
+                tokens, topk, cols);
+  if (tokens == 0) return NVFP4_OK;
+  if (pair_rows == nullptr || tok_codes == nullptr || tok_sf == nullptr ||
+      recv_codes == nullptr || recv_sf == nullptr)
+    return fail(NVFP4_ERR_NULL_POINTER, "an expand buffer is NULL");
+  if (!aligned16(tok_codes) || !aligned16(tok_sf) || !aligned16(recv_codes) ||
+      !aligned16(recv_sf))
+    return fail(NVFP4_ERR_MISALIGNED, "token and receive slabs must be 16-byte aligned");
+  const int64_t warps = static_cast<int64_t>(world) * tokens * topk;
+  const int64_t blocks = std::min<int64_t>((warps + 7) / 8, 148 * 16);
+  nvfp4_ep_expand_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                           static_cast<cudaStream_t>(stream)>>>(
+      pair_rows, tokens, topk, world, static_cast<const uint8_t*>(tok_codes),
+      static_cast<const uint8_t*>(tok_sf), cols, static_cast<uint8_t*>(recv_codes),
+      static_cast<uint8_t*>(recv_sf), recv_capacity);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "expand launch");
+  return NVFP4_OK;
+}
+
 NVFP4_API int nvfp4_ep_publish_pairs(const int32_t* topk_ids, const int32_t* remote_rows,
                                      const float* weights, int tokens, int topk, int num_experts,
                                      int rank, int world, nvfp4_ep_peers pair_rows,

@@ -185,7 +185,93 @@ __global__ void __launch_bounds__(256) nvfp4_ep_combine_kernel(
 
 // ---- owner-side sums -----------------------------------------------------------------------
 // Pair tables (one [world, pairs] int32 and one [world, pairs] fp32 array on every rank, pairs
-// = tokens * topk, the same on every rank): row q holds source rank q's pairs.
+// = tokens * topk, the same on every rank): row q holds source rank q's pairs. Token slabs
+// ([world, tokens] rows of codes and of plain scales on every rank): row q * tokens + t holds
+// source rank q's token t.
+
+// One warp per token t of this rank: each slot's row in its owner's slab (remote_rows[i], the
+// row nvfp4_ep_dispatch gives pair i; -1 when dropped), then the token's codes (cols/2 bytes)
+// and its scales as a plain row (cols/16 bytes) once into each owner that holds a kept pair of
+// t, at token-slab row rank * tokens + t: a token whose slots meet on one owner crosses
+// NVLink once. The owner places the rows with nvfp4_ep_expand.
+__global__ void __launch_bounds__(256) nvfp4_ep_dispatch_tokens_kernel(
+    const int32_t* __restrict__ ids, int tokens, int topk, int num_experts, int rank, int world,
+    const int32_t* __restrict__ dest, const int32_t* __restrict__ offsets,
+    const int32_t* __restrict__ send_base, const uint8_t* __restrict__ codes, int64_t ld_codes,
+    const uint8_t* __restrict__ sf_blocked, int cols, EpPeers tok_codes, EpPeers tok_sf,
+    int64_t capacity, int32_t* __restrict__ remote_rows) {
+  const int lane = threadIdx.x & 31;
+  const int epr = num_experts / world;
+  const int code_chunks = cols / 32;
+  const int sf_chunks = cols / 256;
+  const int rest_k = cols / 64;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t t = warp0; t < tokens; t += nwarps) {
+    uint32_t owners = 0;
+    for (int j0 = 0; j0 < topk; j0 += 32) {
+      const int j = j0 + lane;
+      int owner = -1;
+      if (j < topk) {
+        const int64_t i = t * topk + j;
+        const int e = ids[i];
+        const int32_t d = dest[i];
+        int64_t row = -1;
+        if (e >= 0 && e < num_experts && d >= 0 && send_base[e] >= 0) {
+          row = static_cast<int64_t>(send_base[e]) + (d - offsets[e]);
+          if (row >= capacity) row = -1;
+        }
+        remote_rows[i] = static_cast<int32_t>(row);
+        if (row >= 0) owner = e / epr;
+      }
+      for (int p = 0; p < world; ++p)
+        if (__ballot_sync(0xffffffffu, owner == p)) owners |= 1u << p;
+    }
+    const int64_t slab_row = static_cast<int64_t>(rank) * tokens + t;
+    const uint4* src = reinterpret_cast<const uint4*>(codes + t * ld_codes);
+    for (int p = 0; p < world; ++p) {
+      if (!((owners >> p) & 1u)) continue;
+      uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(tok_codes.ptr[p]) +
+                                            slab_row * (cols / 2));
+      copy_row_chunks(src, dst, code_chunks, lane);
+      uint4* sdst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(tok_sf.ptr[p]) +
+                                             slab_row * (cols / 16));
+      for (int c = lane; c < sf_chunks; c += 32) {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          w[k] = __ldg(reinterpret_cast<const uint32_t*>(
+              sf_blocked + blocked_sf_offset(t, 16 * c + 4 * k, rest_k)));
+        sdst[c] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+  __threadfence_system();
+}
+
+// One warp per pair (source rank q, pair i) of the pair table, on the owner: a pair placed
+// here (pair_rows[q, i] = r, 0 <= r < capacity) gets its token's codes and plain scale row
+// from token-slab row q * tokens + i / topk copied into receive-slab row r (local copies).
+__global__ void __launch_bounds__(256) nvfp4_ep_expand_kernel(
+    const int32_t* __restrict__ pair_rows, int tokens, int topk, int world,
+    const uint8_t* __restrict__ tok_codes, const uint8_t* __restrict__ tok_sf, int cols,
+    uint8_t* __restrict__ recv_codes, uint8_t* __restrict__ recv_sf, int64_t capacity) {
+  const int lane = threadIdx.x & 31;
+  const int64_t pairs = static_cast<int64_t>(tokens) * topk;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t qi = warp0; qi < static_cast<int64_t>(world) * pairs; qi += nwarps) {
+    const int64_t r = __ldg(pair_rows + qi);
+    if (r < 0 || r >= capacity) continue;
+    const int64_t q = qi / pairs;
+    const int64_t src_row = q * tokens + (qi % pairs) / topk;
+    copy_row_chunks(reinterpret_cast<const uint4*>(tok_codes + src_row * (cols / 2)),
+                    reinterpret_cast<uint4*>(recv_codes + r * (cols / 2)), cols / 32, lane);
+    const uint4* ssrc = reinterpret_cast<const uint4*>(tok_sf + src_row * (cols / 16));
+    uint4* sdst = reinterpret_cast<uint4*>(recv_sf + r * (cols / 16));
+    for (int c = lane; c < cols / 256; c += 32) sdst[c] = __ldg(ssrc + c);
+  }
+}
 
 // One thread per pair of this rank: in every owner's table, the pair's slab row there (-1 on
 // the owners it did not go to, and everywhere for dropped pairs), and on its owner its

@@ -290,12 +290,14 @@ class EPMoEBlock:
     layout, gated GEMM over its expert segments with NVFP4 output, then the down GEMM and
     the return, in one of two forms (``return_mode``):
 
-    * ``"sums"`` (default): dispatch also publishes each pair's slab row and routing weight
-      into its owner's pair tables; the down GEMM writes its rows locally, and
-      nvfp4_ep_return_sums adds each source token's rows of this owner (weighted, slot
-      order, fp32) and stores one fp16 row per (token, owner) into the token's rank |
-      combine: fp32 sum of each token's per-owner rows in owner order, bf16. A token's slots
-      that meet on one owner cross NVLink as one row.
+    * ``"sums"`` (default): dispatch sends each token once to every owner of its pairs (not
+      once per pair) and publishes each pair's slab row and routing weight into its owner's
+      pair tables | the owner copies the token rows into its receive slab
+      (nvfp4_ep_expand); the down GEMM writes its rows locally, and nvfp4_ep_return_sums
+      adds each source token's rows of this owner (weighted, slot order, fp32) and stores
+      one fp16 row per (token, owner) into the token's rank | combine: fp32 sum of each
+      token's per-owner rows in owner order, bf16. A token's slots that meet on one owner
+      cross NVLink as one row each way.
     * ``"rows"``: the down GEMM's epilogue stores every output row into its token's rank
       (NVLink stores overlapping the GEMM) | combine: weighted fp32 sum of each token's
       returned rows in slot order, bf16 -- bit-identical to the single-GPU MoEBlock.
@@ -352,14 +354,17 @@ class EPMoEBlock:
         # One symmetric allocation: count matrix | received codes | received plain scales |
         # return address of each received row | returned rows (sums: one per token and owner;
         # rows: one per pair) | pair tables of the sums (slab row and weight of each source
-        # rank's pairs here).
+        # rank's pairs here) | token slabs of the sums (codes, plain scales of each source
+        # rank's tokens with pairs here).
         sums = return_mode == "sums"
 
         def up(n):
             return (n + 255) // 256 * 256
         sizes = [world * num_experts * 4, cap * hdim // 2, cap * hdim // 16, cap * 8,
                  (tokens * world if sums else pairs) * hdim * 2,
-                 world * pairs * 4 if sums else 0, world * pairs * 4 if sums else 0]
+                 world * pairs * 4 if sums else 0, world * pairs * 4 if sums else 0,
+                 world * tokens * hdim // 2 if sums else 0,
+                 world * tokens * hdim // 16 if sums else 0]
         offs = [0]
         for n in sizes[:-1]:
             offs.append(offs[-1] + up(n))
@@ -384,6 +389,8 @@ class EPMoEBlock:
             self._ret = sl[4].view(torch.float16).view(tokens, world, hdim)
             self._pair_rows = sl[5].view(torch.int32).view(world, pairs)
             self._pair_w = sl[6].view(torch.float32).view(world, pairs)
+            self._tok_codes = sl[7].view(world * tokens, hdim // 2)
+            self._tok_sf = sl[8].view(world * tokens, hdim // 16)
             # The down GEMM's rows stay here (slab order); return_sums reads them.
             self._y = torch.empty((cap, hdim), dtype=torch.float16, device=dev)
             self._scatter = None
@@ -493,11 +500,20 @@ class EPMoEBlock:
         chk(lib.nvfp4_ep_layout(self._mat.data_ptr(), E, rank, world, cap,
                                 self.seg_offsets.data_ptr(), self.seg_counts.data_ptr(),
                                 self.send_base.data_ptr(), self._err.data_ptr(), s), lib)
-        chk(lib.nvfp4_ep_dispatch(topk_ids.data_ptr(), T, K, E, rank, world, self._dest.data_ptr(),
-                                  self._offsets.data_ptr(), self.send_base.data_ptr(),
-                                  self._qx.data_ptr(), self._qx.stride(0), self._sfx.data_ptr(), H,
-                                  self._peers[1], self._peers[2], self._peers[3], cap,
-                                  self.remote_rows.data_ptr(), s), lib)
+        if self._scatter is None:
+            chk(lib.nvfp4_ep_dispatch_tokens(topk_ids.data_ptr(), T, K, E, rank, world,
+                                             self._dest.data_ptr(), self._offsets.data_ptr(),
+                                             self.send_base.data_ptr(), self._qx.data_ptr(),
+                                             self._qx.stride(0), self._sfx.data_ptr(), H,
+                                             self._peers[7], self._peers[8], cap,
+                                             self.remote_rows.data_ptr(), s), lib)
+        else:
+            chk(lib.nvfp4_ep_dispatch(topk_ids.data_ptr(), T, K, E, rank, world,
+                                      self._dest.data_ptr(), self._offsets.data_ptr(),
+                                      self.send_base.data_ptr(), self._qx.data_ptr(),
+                                      self._qx.stride(0), self._sfx.data_ptr(), H, self._peers[1],
+                                      self._peers[2], self._peers[3], cap,
+                                      self.remote_rows.data_ptr(), s), lib)
         w = topk_weights
         if w.dtype != torch.float32 or not w.is_contiguous():
             self._w.copy_(w)
@@ -509,6 +525,12 @@ class EPMoEBlock:
         mark("layout + dispatch")
         self._barrier()
         mark("barrier")
+        if self._scatter is None:
+            chk(lib.nvfp4_ep_expand(self._pair_rows.data_ptr(), T, K, world,
+                                    self._tok_codes.data_ptr(), self._tok_sf.data_ptr(), H,
+                                    self._recv_codes.data_ptr(), self._recv_sf.data_ptr(), cap, s),
+                lib)
+            mark("expand")
         _native.sf_to_blocked_raw(self._recv_sf.data_ptr(), self._recv_sfa.data_ptr(), cap,
                                   H // 16, H // 16, s)
         flags = (_native.FLAG_REUSE_DESCRIPTORS if self._uploaded else 0) | self._cta_flags
