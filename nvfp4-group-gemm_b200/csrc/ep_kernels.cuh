@@ -305,17 +305,27 @@ __device__ __forceinline__ void add_half8(float* acc, const uint4& raw, float w,
   }
 }
 
-// Columns per warp task of the two kernels below: two 256-column parts (8 columns per lane
-// each), so a lane keeps up to 16 x 16 bytes of rows in flight.
-constexpr int kEpSumParts = 2;
+// Columns per warp task of the two kernels below: 256-column parts (8 columns per lane
+// each), and the window of a token's slots whose rows return_sums loads before adding them,
+// so a lane keeps up to parts x window x 16 bytes in flight. Build constants; at cfg5's
+// shape on 2 GPUs (return_sums / combine_sums, µs): 4 x 4 453 / 160, 2 x 8 502 / 164,
+// 2 x 4 483 / 167, 4 x 2 520 / 160, 1 x 8 640 / 264, 7 x 2 680 / 190, 7 x 4 637 / 193.
+#ifndef NVFP4_EP_SUM_PARTS
+#define NVFP4_EP_SUM_PARTS 4
+#endif
+constexpr int kEpSumParts = NVFP4_EP_SUM_PARTS;
+#ifndef NVFP4_EP_SUM_WINDOW
+#define NVFP4_EP_SUM_WINDOW 4
+#endif
+constexpr int kEpSumWindow = NVFP4_EP_SUM_WINDOW;
 
-// One warp per (token t, source rank q, 512-column group), on the owner, tasks ordered token
+// One warp per (token t, source rank q, group of kEpSumParts 256-column parts), on the owner, tasks ordered token
 // first so that stores to every rank run side by side: the fp32 sum, in slot order, of
 // w_j * y[row_j] over t's pairs that came here (each product and each sum rounded to fp32,
 // as in the slot-order combine), rounded to fp16 and stored as row (t * world + rank) of rank
 // q's [tokens, world, cols] return buffer. Tokens with no pair here store nothing (their rank
-// knows and skips the row). Per window of 8 slots, the rows' indices and weights, then every
-// row load of both parts are issued before the first add.
+// knows and skips the row). Per window of kEpSumWindow slots, the rows' indices and
+// weights, then every row load of every part are issued before the first add.
 __global__ void __launch_bounds__(256) nvfp4_ep_return_sums_kernel(
     const int32_t* __restrict__ pair_rows, const float* __restrict__ pair_weights, int tokens,
     int topk, int rank, int world, const __half* __restrict__ y, int64_t ldy, int cols,
@@ -339,17 +349,17 @@ __global__ void __launch_bounds__(256) nvfp4_ep_return_sums_kernel(
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[u][i] = 0.0f;
     bool any = false;
-    for (int j0 = 0; j0 < topk; j0 += 8) {
-      const int jn = topk - j0 < 8 ? topk - j0 : 8;
-      int32_t r[8];
-      float w[8];
+    for (int j0 = 0; j0 < topk; j0 += kEpSumWindow) {
+      const int jn = topk - j0 < kEpSumWindow ? topk - j0 : kEpSumWindow;
+      int32_t r[kEpSumWindow];
+      float w[kEpSumWindow];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) r[j] = j < jn ? __ldg(rows + j0 + j) : -1;
+      for (int j = 0; j < kEpSumWindow; ++j) r[j] = j < jn ? __ldg(rows + j0 + j) : -1;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) w[j] = r[j] >= 0 ? __ldg(wts + j0 + j) : 0.0f;
-      uint4 raw[8][kEpSumParts];
+      for (int j = 0; j < kEpSumWindow; ++j) w[j] = r[j] >= 0 ? __ldg(wts + j0 + j) : 0.0f;
+      uint4 raw[kEpSumWindow][kEpSumParts];
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < kEpSumWindow; ++j)
 #pragma unroll
         for (int u = 0; u < kEpSumParts; ++u) {
           const int col = col0 + 256 * u;
@@ -358,7 +368,7 @@ __global__ void __launch_bounds__(256) nvfp4_ep_return_sums_kernel(
                           : make_uint4(0u, 0u, 0u, 0u);
         }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < kEpSumWindow; ++j) {
         if (r[j] < 0) continue;
         any = true;
 #pragma unroll
@@ -385,8 +395,8 @@ __global__ void __launch_bounds__(256) nvfp4_ep_return_sums_kernel(
 }
 
 // out[t, :] = bf16( sum over owners p (ascending) that hold at least one kept pair of t of
-// fp32(ret[t, p, :]) ), fp32 sums. One warp per (token, 512-column group); the rows of two
-// owners (both parts) are loaded before they are added.
+// fp32(ret[t, p, :]) ), fp32 sums. One warp per (token, group of kEpSumParts 256-column
+// parts); the rows of two owners (every part) are loaded before they are added.
 __global__ void __launch_bounds__(256) nvfp4_ep_combine_sums_kernel(
     const int32_t* __restrict__ ids, const int32_t* __restrict__ remote_rows, int tokens,
     int topk, int num_experts, int world, const __half* __restrict__ ret, int cols,
