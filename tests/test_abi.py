@@ -233,3 +233,55 @@ def test_plan_create_validation(pkg, case, flags, status):
     assert out.value is None
     assert lib.nvfp4_plan_launch(None, None) == 1
     lib.nvfp4_plan_destroy(None)  # destroying nothing is allowed
+
+
+def test_expert_parallel_validation_before_launch(pkg):
+    """Every nvfp4_ep_* entry point rejects bad ranks, shapes, NULL and misaligned buffers
+    with its status code before anything is launched."""
+    from importlib import import_module
+
+    N = import_module(pkg.__name__ + "._native")
+    lib = pkg.load_library()
+    peers2 = N.EpPeers.of([0x10000, 0x20000])
+    nullpeer = N.EpPeers.of([0x10000, 0])
+    A, B, C, D = 0x1000, 0x2000, 0x3000, 0x4000
+    # publish counts / layout: world and expert checks
+    assert lib.nvfp4_ep_publish_counts(A, 16, 0, 9, peers2, None) == 1
+    assert lib.nvfp4_ep_publish_counts(A, 15, 0, 2, peers2, None) == 1
+    assert lib.nvfp4_ep_publish_counts(None, 16, 0, 2, peers2, None) == 4
+    assert lib.nvfp4_ep_layout(A, 16, 2, 2, 1024, B, C, D, A, None) == 1
+    # token-once dispatch
+    def dt(**kw):
+        a = dict(ids=A, tokens=4, topk=2, E=16, rank=0, world=2, codes=0x5000, ld=256,
+                 sf=0x6000, cols=512, tok=peers2, tsf=peers2)
+        a.update(kw)
+        return lib.nvfp4_ep_dispatch_tokens(a["ids"], a["tokens"], a["topk"], a["E"], a["rank"],
+                                            a["world"], B, C, D, a["codes"], a["ld"], a["sf"],
+                                            a["cols"], a["tok"], a["tsf"], 1 << 20, 0x7000, None)
+    assert dt(world=9) == 1
+    assert dt(cols=320) == 2
+    assert dt(tokens=0) == 0
+    assert dt(ids=0) == 4
+    assert dt(codes=0x5008) == 3
+    assert dt(ld=200) == 3
+    assert dt(tok=nullpeer) == 4
+    # expand
+    assert lib.nvfp4_ep_expand(A, 4, 2, 0, B, C, 512, D, 0x5000, 1024, None) == 1
+    assert lib.nvfp4_ep_expand(A, 4, 2, 2, B, C, 100, D, 0x5000, 1024, None) == 2
+    assert lib.nvfp4_ep_expand(0, 4, 2, 2, B, C, 512, D, 0x5000, 1024, None) == 4
+    assert lib.nvfp4_ep_expand(A, 4, 2, 2, B + 8, C, 512, D, 0x5000, 1024, None) == 3
+    # pair tables
+    assert lib.nvfp4_ep_publish_pairs(A, B, 0, 4, 2, 16, 0, 2, peers2, peers2, None) == 4
+    assert lib.nvfp4_ep_publish_pairs(A, B, C, 4, 2, 16, 0, 2, peers2, nullpeer, None) == 4
+    assert lib.nvfp4_ep_publish_pairs(A, B, C, 4, 0, 16, 0, 2, peers2, peers2, None) == 2
+    # return sums
+    assert lib.nvfp4_ep_return_sums(A, B, 4, 2, 2, 2, C, 512, 512, peers2, None) == 1
+    assert lib.nvfp4_ep_return_sums(A, B, 4, 2, 0, 2, C, 512, 12, peers2, None) == 2
+    assert lib.nvfp4_ep_return_sums(A, B, 4, 2, 0, 2, C + 8, 512, 512, peers2, None) == 3
+    assert lib.nvfp4_ep_return_sums(A, B, 4, 2, 0, 2, C, 256, 512, peers2, None) == 3
+    assert lib.nvfp4_ep_return_sums(A, B, 4, 2, 0, 2, C, 512, 512, nullpeer, None) == 4
+    # combine of the sums
+    assert lib.nvfp4_ep_combine_sums(A, B, 4, 2, 15, 2, C, 512, D, 512, None) == 1
+    assert lib.nvfp4_ep_combine_sums(A, B, 4, 2, 16, 2, C, 512, D + 8, 512, None) == 3
+    assert lib.nvfp4_ep_combine_sums(A, 0, 4, 2, 16, 2, C, 512, D, 512, None) == 4
+    assert lib.nvfp4_last_error_detail()
