@@ -275,3 +275,84 @@ def test_ep_placement_over_gloo_ranks():
         _, seg_off, seg_cnt = everything[owner]
         want = sorted(r for o, c in zip(seg_off, seg_cnt) for r in range(o, o + c))
         assert sorted(written) == want
+
+
+def _pair_rows(rank, tokens, topk, cols):
+    """The down GEMM's fp16 row of every pair of source `rank` (a stand-in any rank can
+    rebuild: seeded by the source rank)."""
+    rng = np.random.default_rng(1000 + rank)
+    return (rng.standard_normal((tokens, topk, cols)) * 3).astype(np.float16)
+
+
+def _presum_gloo_worker(rank, world, port, experts, tokens, topk, cols, q):
+    try:
+        import sys
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, root)
+        from oracle import nvfp4_ep_oracle as EPO
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=__import__("datetime").timedelta(seconds=60))
+        epr = experts // world
+        routing = []  # every source's (ids, weights, kept), rebuilt from seeds on every rank
+        for src in range(world):
+            ids = _ids(tokens, topk, experts, seed=src + 7)
+            w = np.random.default_rng(50 + src).random((tokens, topk)).astype(np.float32)
+            routing.append((ids, w, ids >= 0))
+        # As owner: one partial row per (source, token) with pairs here (return_sums), sent to
+        # the source rank (the device path stores them into its return buffer over NVLink).
+        outgoing = []
+        for src in range(world):
+            ids, w, kept = routing[src]
+            y = _pair_rows(src, tokens, topk, cols)
+            mine = kept & (ids // epr == rank)
+            part, has, _ = EPO.presum_combine(y, mine, np.where(mine, rank, -1), w, world)
+            outgoing.append((part[:, rank], has[:, rank]))
+        received = [None] * world
+        for src in range(world):  # rank src collects every owner's rows for its tokens
+            gathered = [None] * world
+            dist.all_gather_object(gathered, outgoing[src])
+            if src == rank:
+                received = gathered
+        # combine_sums: owner order, fp32, over the owners that hold a kept pair.
+        ids, w, kept = routing[rank]
+        owner = np.where(kept, ids // epr, -1)
+        acc = np.zeros((tokens, cols), dtype=np.float32)
+        for p in range(world):
+            part_p, has_p = received[p]
+            has_expect = (kept & (owner == p)).any(axis=1)
+            assert np.array_equal(has_p, has_expect)
+            acc = np.where(has_p[:, None], (acc + part_p.astype(np.float32)).astype(np.float32),
+                           acc)
+        from oracle import nvfp4_moe_oracle as M
+        got = M.fp32_to_bf16_bits(acc)
+        _, _, want = EPO.presum_combine(_pair_rows(rank, tokens, topk, cols), kept, owner, w,
+                                        world)
+        q.put((rank, bool(np.array_equal(got, want))))
+        dist.destroy_process_group()
+    except BaseException as e:
+        q.put((rank, repr(e)))
+
+
+def test_ep_owner_sums_over_gloo_ranks():
+    """Two CPU ranks play owners and sources of the owner-side sums: each owner sums the
+    rows of every source token it holds pairs of and sends one row per (token, owner) back
+    over gloo; each source's owner-order combine of what it received equals the one-process
+    oracle over its own tokens bit for bit."""
+    world, experts, tokens, topk, cols = 2, 16, 120, 4, 32
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_presum_gloo_worker,
+                         args=(r, world, port, experts, tokens, topk, cols, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res == {0: True, 1: True}, res
