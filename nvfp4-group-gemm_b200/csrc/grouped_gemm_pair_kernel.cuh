@@ -380,27 +380,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         uint8_t* c_row = row0 + lane < gd.m
                              ? gd.c + static_cast<size_t>(rb + row0 + lane) * gd.n * sizeof(__half)
                              : nullptr;
-#pragma unroll 1
-        for (int bi = 0; bi < kBoxes; ++bi) {
-          const int box = (first_box + bi) % kBoxes;
+        // Drains one box (32 rows x 64 columns of this warp's quarter) whose accumulator
+        // values (and, gated, the up projection's) are in registers.
+        auto drain_box = [&](int box, const uint32_t (&v0)[32], const uint32_t (&v1)[32],
+                             const uint32_t (&u0)[32], const uint32_t (&u1)[32]) {
           const uint32_t buf = my_bufs_s + (stores & 1u) * Cfg::kEpiBufBytes;
-          uint32_t v0[32], v1[32];
-          ptx::tmem_ld_32x32b_x32(t_acc + box * 64, v0);
-          ptx::tmem_ld_32x32b_x32(t_acc + box * 64 + 32, v1);
-          uint32_t u0[32], u1[32];
-          if (GATED) {
-            ptx::tmem_ld_32x32b_x32(t_acc + 128 + box * 64, u0);
-            ptx::tmem_ld_32x32b_x32(t_acc + 128 + box * 64 + 32, u1);
-          }
-          ptx::tmem_ld_wait();
-          if (bi == 0) {
-            // The box shared by both accumulator stages is drained: the next tile's
-            // MMAs may start.
-            ptx::tcgen05_fence_before_sync();
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive_cluster(release_bar);
-            released = true;
-          }
           if (GATED && p.out_sf != nullptr) {
             // NVFP4 output (codes and blocked scales; no fp16 staging).
             const int row = row0 + lane;
@@ -411,7 +395,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                                     p.out_d6, gd.c + r * (gd.n / 2) + col0 / 2,
                                     p.out_sf + blocked_sf_offset(r, col0 / 16, (gd.n + 63) / 64));
             }
-            continue;
+            return;
           }
           if (lane == 0) ptx::bulk_wait_group_read<1>();
           __syncwarp();
@@ -450,7 +434,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                            nt * Cfg::kOutN + box * 64, gd.n, lane);
             __syncwarp();  // the box is read before it is written again
             ++stores;
-            continue;
+            return;
           }
           ptx::fence_proxy_async_smem();
           __syncwarp();
@@ -466,6 +450,61 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                            c_row != nullptr ? c_row + p.replica_offset[r] : nullptr,
                            nt * Cfg::kOutN + box * 64, gd.n, lane);
           ++stores;
+        };
+        auto release_shared_box = [&]() {
+          // The box shared by both accumulator stages is drained: the next tile's MMAs may
+          // start.
+          ptx::tcgen05_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive_cluster(release_bar);
+          released = true;
+        };
+        if constexpr (GATED) {
+#pragma unroll 1
+          for (int bi = 0; bi < kBoxes; ++bi) {
+            const int box = (first_box + bi) % kBoxes;
+            uint32_t v0[32], v1[32], u0[32], u1[32];
+            ptx::tmem_ld_32x32b_x32(t_acc + box * 64, v0);
+            ptx::tmem_ld_32x32b_x32(t_acc + box * 64 + 32, v1);
+            ptx::tmem_ld_32x32b_x32(t_acc + 128 + box * 64, u0);
+            ptx::tmem_ld_32x32b_x32(t_acc + 128 + box * 64 + 32, u1);
+            ptx::tmem_ld_wait();
+            if (bi == 0) release_shared_box();
+            drain_box(box, v0, v1, u0, u1);
+          }
+        } else {
+          // Box bi + 1's TMEM loads are issued before box bi is converted and stored, so
+          // they run under its shared-memory writes and TMA store.
+          uint32_t a0[32], a1[32], b0[32], b1[32];
+          ptx::tmem_ld_32x32b_x32(t_acc + first_box * 64, a0);
+          ptx::tmem_ld_32x32b_x32(t_acc + first_box * 64 + 32, a1);
+#pragma unroll
+          for (int bi = 0; bi < kBoxes; ++bi) {
+            const int box = (first_box + bi) % kBoxes;
+            ptx::tmem_ld_wait();
+            if (bi & 1) {
+              ptx::reg_fence(b0);
+              ptx::reg_fence(b1);
+            } else {
+              ptx::reg_fence(a0);
+              ptx::reg_fence(a1);
+            }
+            if (bi == 0) release_shared_box();
+            if (bi + 1 < kBoxes) {
+              const int next = (first_box + bi + 1) % kBoxes;
+              if (bi & 1) {
+                ptx::tmem_ld_32x32b_x32(t_acc + next * 64, a0);
+                ptx::tmem_ld_32x32b_x32(t_acc + next * 64 + 32, a1);
+              } else {
+                ptx::tmem_ld_32x32b_x32(t_acc + next * 64, b0);
+                ptx::tmem_ld_32x32b_x32(t_acc + next * 64 + 32, b1);
+              }
+            }
+            if (bi & 1)
+              drain_box(box, b0, b1, b0, b1);
+            else
+              drain_box(box, a0, a1, a0, a1);
+          }
         }
       }
       if (!released) {
