@@ -128,11 +128,136 @@ class ExpertOutputGather:
         return self.outputs
 
 
+class ProcessGroupFabric:
+    """How the ranks of an expert-parallel group reach each other: one process per GPU in a
+    torch.distributed group (NCCL). Buffers come from torch symmetric memory, so every rank
+    maps every peer's copy over NVLink; the barrier is a one-element NCCL all-reduce on the
+    caller's stream (capturable in a CUDA graph); :meth:`meet` is a host-side barrier.
+
+    A fabric exposes ``world``, ``rank``, ``allocate(nbytes, device) -> (tensor, bases)``
+    (a zeroed uint8 tensor and, per rank, the device address of that rank's copy of its
+    first byte), ``barrier(device)`` and ``meet()``; :class:`FusedOutputGather` and
+    :class:`EPMoEBlock` take one as ``fabric=``."""
+
+    def __init__(self, group: dist.ProcessGroup | None = None):
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self._handles = []  # rendezvous handles keep the peers' mappings alive
+        self._bar = None
+
+    def allocate(self, nbytes: int, device: torch.device):
+        from torch.distributed import _symmetric_memory as symm
+
+        buf = symm.empty(nbytes, dtype=torch.uint8, device=device)
+        buf.zero_()
+        try:
+            handle = symm.rendezvous(buf, self.group)
+        except RuntimeError:  # older releases want the group registered first
+            symm.enable_symm_mem_for_group(self.group.group_name)
+            handle = symm.rendezvous(buf, self.group)
+        self._handles.append(handle)
+        if self._bar is None:  # made here, not in the first barrier (which may be captured)
+            self._bar = torch.zeros(1, dtype=torch.int32, device=device)
+        bases = [int(b) for b in handle.buffer_ptrs]
+        # The tensor sits at the same offset inside every rank's copy of the allocation.
+        delta = buf.data_ptr() - bases[self.rank]
+        return buf, [b + delta for b in bases]
+
+    def barrier(self, device: torch.device) -> None:
+        if self._bar is None or self._bar.device != device:
+            self._bar = torch.zeros(1, dtype=torch.int32, device=device)
+        dist.all_reduce(self._bar, group=self.group)
+
+    def meet(self) -> None:
+        dist.barrier(group=self.group)
+
+
+class SingleDeviceFabric:
+    """Every rank of an expert-parallel group emulated on one GPU.
+
+    Rank r's buffers are plain allocations on ``device``, so a "peer" address is an address
+    of the same GPU and the exchange kernels, the replicated GEMM epilogue and the return
+    paths run exactly as across GPUs, minus NVLink. The ranks' calls run one after another
+    on one stream (:func:`run_lockstep`), and stream order stands in for the barriers: no
+    kernel of this library waits on another rank, so the emulation cannot deadlock, and
+    it replays one of the interleavings the real ranks may take. Used to test world sizes
+    up to 8 on a one-GPU machine and to check a deployment's layouts before it gets GPUs.
+
+    ``fabric.rank_view(r)`` is the object to pass as ``fabric=`` to rank r's block; every
+    rank must allocate the same sizes in the same order (as every rank's constructor does).
+    """
+
+    def __init__(self, world: int, device: torch.device):
+        if world < 1:
+            raise ValueError("world must be >= 1")
+        self.world = int(world)
+        self.device = torch.device(device)
+        self._allocs = []             # per allocation: one tensor per rank
+        self._next = [0] * self.world  # allocations made so far, per rank
+
+    def rank_view(self, rank: int) -> "_EmulatedRank":
+        if not 0 <= rank < self.world:
+            raise ValueError(f"rank {rank} outside world of size {self.world}")
+        return _EmulatedRank(self, rank)
+
+
+class _EmulatedRank:
+    """One rank of a :class:`SingleDeviceFabric` (the ``fabric=`` argument of its blocks)."""
+
+    def __init__(self, fabric: SingleDeviceFabric, rank: int):
+        self.fabric, self.world, self.rank = fabric, fabric.world, rank
+
+    def allocate(self, nbytes: int, device: torch.device):
+        f = self.fabric
+        if torch.device(device) != f.device:
+            raise ValueError(f"emulated ranks live on {f.device}, not {device}")
+        i = f._next[self.rank]
+        f._next[self.rank] += 1
+        if i == len(f._allocs):
+            f._allocs.append([torch.zeros(nbytes, dtype=torch.uint8, device=f.device)
+                              for _ in range(f.world)])
+        bufs = f._allocs[i]
+        if bufs[self.rank].numel() != nbytes:
+            raise ValueError(f"rank {self.rank} asks for {nbytes} bytes in allocation {i}, "
+                             f"another rank for {bufs[self.rank].numel()}")
+        return bufs[self.rank], [b.data_ptr() for b in bufs]
+
+    def barrier(self, device: torch.device) -> None:
+        pass  # one stream: stream order is the barrier
+
+    def meet(self) -> None:
+        pass
+
+
+def run_lockstep(blocks: Sequence, inputs: Sequence) -> list:
+    """One call of every emulated rank's :class:`EPMoEBlock` (blocks built on the rank views
+    of one :class:`SingleDeviceFabric`, ``inputs[r] = (x, topk_ids, topk_weights)``): the
+    ranks' phases run in rank order on the current stream, each barrier point reached by
+    every rank before any rank passes it. Returns every rank's ``out``."""
+    if len(blocks) != len(inputs):
+        raise ValueError("one input triple per block")
+    pending = [blk.phases(*inp) for blk, inp in zip(blocks, inputs)]
+    while pending:
+        alive = []
+        for g in pending:
+            try:
+                next(g)
+                alive.append(g)
+            except StopIteration:
+                pass
+        if alive and len(alive) != len(pending):
+            raise RuntimeError("the ranks' calls reached different numbers of barriers")
+        pending = alive
+    return [blk.out for blk in blocks]
+
+
 class FusedOutputGather:
     """The output all-gather of an expert-parallel grouped GEMM, fused into the GEMM.
 
-    One symmetric-memory allocation holds, on every rank, the fp16 output slab of every
-    rank (rank r's experts ``expert_shard(G, P, r)`` in slab r, the layout of
+    One allocation of the fabric (``fabric=``; by default torch symmetric memory over the
+    process group, :class:`ProcessGroupFabric`) holds, on every rank, the fp16 output slab
+    of every rank (rank r's experts ``expert_shard(G, P, r)`` in slab r, the layout of
     :class:`ExpertOutputGather`'s receive buffer). :meth:`gemm` runs this rank's experts with
     ``nvfp4_grouped_gemm_replicated``: the kernel stores each output tile into this rank's
     slab locally and, from its epilogue, into the same slab of every other rank's copy over
@@ -143,14 +268,11 @@ class FusedOutputGather:
     """
 
     def __init__(self, rows_per_expert: Sequence[int], n: int, device: torch.device,
-                 group: dist.ProcessGroup | None = None):
-        from torch.distributed import _symmetric_memory as symm
-
+                 group: dist.ProcessGroup | None = None, fabric=None):
         from . import _native
 
-        self.group = group if group is not None else dist.group.WORLD
-        world = dist.get_world_size(self.group)
-        rank = dist.get_rank(self.group)
+        self.fabric = fabric if fabric is not None else ProcessGroupFabric(group)
+        world, rank = self.fabric.world, self.fabric.rank
         if world - 1 > _native.MAX_REPLICAS:
             raise ValueError(f"at most {_native.MAX_REPLICAS + 1} ranks")
         self.world, self.rank = world, rank
@@ -159,15 +281,7 @@ class FusedOutputGather:
         layout = slab_layout(self.rows, self.n, world)
         self.max_elems = max(e for _, _, e in layout)
         nbytes = world * self.max_elems * 2
-        self._symm = symm.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
-        self._symm.zero_()
-        try:
-            handle = symm.rendezvous(self._symm, self.group)
-        except RuntimeError:  # older releases want the group registered first
-            symm.enable_symm_mem_for_group(self.group.group_name)
-            handle = symm.rendezvous(self._symm, self.group)
-        self._handle = handle
-        bases = [int(b) for b in handle.buffer_ptrs]
+        self._symm, bases = self.fabric.allocate(max(nbytes, 256), torch.device(device))
         # Every rank's copy has the same layout: a peer's copy of a byte is at
         # (its base - this base) from this rank's copy of it.
         self.replica_offsets = [bases[p] - bases[rank] for p in range(world) if p != rank]
@@ -178,7 +292,6 @@ class FusedOutputGather:
         for r, (f, cnt, _) in enumerate(layout):
             self.outputs += self._views(r * self.max_elems, f, cnt)
         self.bytes_sent = int((world - 1) * layout[rank][2] * 2)
-        self._bar = torch.zeros(1, dtype=torch.int32, device=device)
         self._table = None
         self._ws = None
         self._sig = None
@@ -236,7 +349,7 @@ class FusedOutputGather:
     def barrier(self) -> None:
         """Cross-rank barrier on the current stream: after it every rank's kernel (and so
         every replica store) has completed."""
-        dist.all_reduce(self._bar, group=self.group)
+        self.fabric.barrier(self._symm.device)
 
     def check_device_errors(self, stream: torch.cuda.Stream | None = None) -> int:
         from . import _native
@@ -305,15 +418,16 @@ class EPMoEBlock:
     The receive slabs hold ``world * tokens * topk + 127 * E/P`` rows (every pair of every
     rank routed here, plus segment padding), so the exchange never drops a pair. Count
     matrix, receive slabs, return addresses, pair tables and the return buffer ([tokens,
-    world, H] fp16 for sums, [tokens * topk, H] for rows) live in one torch symmetric-memory
-    allocation.
+    world, H] fp16 for sums, [tokens * topk, H] for rows) live in one allocation of the
+    fabric (``fabric=``): torch symmetric memory over the process group by default
+    (:class:`ProcessGroupFabric`), or one GPU holding every rank (:class:`SingleDeviceFabric`,
+    calls driven by :func:`run_lockstep`).
     """
 
     def __init__(self, local_weights, num_experts: int, tokens: int, topk: int,
                  act_scale: float, hidden_scale: float, group=None, cta: str | None = None,
-                 return_mode: str = "sums"):
+                 return_mode: str = "sums", fabric=None):
         import numpy as np
-        from torch.distributed import _symmetric_memory as symm
 
         from . import _native
         from .layout import blocked_sf_bytes
@@ -323,9 +437,8 @@ class EPMoEBlock:
         if return_mode not in ("sums", "rows"):
             raise ValueError(f"return_mode must be 'sums' or 'rows', got {return_mode!r}")
         self.return_mode = return_mode
-        self.group = group if group is not None else dist.group.WORLD
-        world = dist.get_world_size(self.group)
-        rank = dist.get_rank(self.group)
+        self.fabric = fabric if fabric is not None else ProcessGroupFabric(group)
+        world, rank = self.fabric.world, self.fabric.rank
         if world > _native.EP_MAX_RANKS:
             raise ValueError(f"at most {_native.EP_MAX_RANKS} ranks")
         if num_experts % world:
@@ -369,17 +482,8 @@ class EPMoEBlock:
         for n in sizes[:-1]:
             offs.append(offs[-1] + up(n))
         total = offs[-1] + max(up(sizes[-1]), 256)
-        self._symm = symm.empty(total, dtype=torch.uint8, device=dev)
-        self._symm.zero_()
-        try:
-            self._handle = symm.rendezvous(self._symm, self.group)
-        except RuntimeError:  # older releases want the group registered first
-            symm.enable_symm_mem_for_group(self.group.group_name)
-            self._handle = symm.rendezvous(self._symm, self.group)
-        bases = [int(b) for b in self._handle.buffer_ptrs]
-        # The tensor sits at the same offset inside every rank's copy of the allocation.
-        delta = self._symm.data_ptr() - bases[rank]
-        self._peers = [_native.EpPeers.of([b + delta + o for b in bases]) for o in offs]
+        self._symm, bases = self.fabric.allocate(total, dev)
+        self._peers = [_native.EpPeers.of([b + o for b in bases]) for o in offs]
         sl = [self._symm[o:o + n] for o, n in zip(offs, sizes)]
         self._mat = sl[0].view(torch.int32).view(world, num_experts)
         self._recv_codes = sl[1].view(cap, hdim // 2)
@@ -399,7 +503,7 @@ class EPMoEBlock:
             # The down GEMM's output rows go to the token's rank: row r of this rank's slab to
             # return buffer (recv_meta[r] >> 40) at pair (recv_meta[r] & (2^40 - 1)).
             self._scatter = _native.SegmentOutput.scattered(
-                self._recv_meta.data_ptr(), [b + delta + offs[4] for b in bases], hdim * 2)
+                self._recv_meta.data_ptr(), [b + offs[4] for b in bases], hdim * 2)
 
         i32 = dict(dtype=torch.int32, device=dev)
         u8 = dict(dtype=torch.uint8, device=dev)
@@ -421,7 +525,6 @@ class EPMoEBlock:
         self._sfa2 = torch.zeros(blocked_sf_bytes(cap, idim // 16), **u8)
         self._w = torch.empty((tokens, topk), dtype=torch.float32, device=dev)
         self.out = torch.empty((tokens, hdim), dtype=torch.bfloat16, device=dev)
-        self._bar = torch.zeros(1, dtype=torch.int32, device=dev)
 
         W = local_weights
         P = W.pointers()
@@ -453,10 +556,7 @@ class EPMoEBlock:
         self._ws2 = torch.zeros(ws_bytes, **u8)
         self._ws_bytes = ws_bytes
         self._uploaded = False
-        dist.barrier(group=self.group)
-
-    def _barrier(self):
-        dist.all_reduce(self._bar, group=self.group)
+        self.fabric.meet()
 
     def run(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
             stage_events: list | None = None) -> torch.Tensor:
@@ -464,6 +564,15 @@ class EPMoEBlock:
         [tokens, H]) for this rank's tokens. Every rank of the group must call it. With
         ``stage_events`` (a list), (stage name, CUDA event recorded after it) pairs are
         appended for timing."""
+        for _ in self.phases(x, topk_ids, topk_weights, stage_events):
+            self.fabric.barrier(self.device)
+        return self.out
+
+    def phases(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+               stage_events: list | None = None):
+        """The call of :meth:`run` as a generator that yields at each of its three
+        cross-rank barriers (which the caller takes: :meth:`run` through the fabric,
+        :func:`run_lockstep` by running every emulated rank up to the same point)."""
         from . import _native
         from .quantize import _DTYPES
 
@@ -495,7 +604,7 @@ class EPMoEBlock:
         mark("route + quantise")
         chk(lib.nvfp4_ep_publish_counts(self._counts.data_ptr(), E, rank, world, self._peers[0], s),
             lib)
-        self._barrier()
+        yield
         mark("publish counts + barrier")
         chk(lib.nvfp4_ep_layout(self._mat.data_ptr(), E, rank, world, cap,
                                 self.seg_offsets.data_ptr(), self.seg_counts.data_ptr(),
@@ -523,7 +632,7 @@ class EPMoEBlock:
                                            w.data_ptr(), T, K, E, rank, world, self._peers[5],
                                            self._peers[6], s), lib)
         mark("layout + dispatch")
-        self._barrier()
+        yield
         mark("barrier")
         if self._scatter is None:
             chk(lib.nvfp4_ep_expand(self._pair_rows.data_ptr(), T, K, world,
@@ -551,7 +660,7 @@ class EPMoEBlock:
             mark("return sums")
         else:
             mark("down GEMM + return rows")
-        self._barrier()
+        yield
         mark("barrier 2")
         if self._scatter is None:
             chk(lib.nvfp4_ep_combine_sums(topk_ids.data_ptr(), self.remote_rows.data_ptr(), T, K,
@@ -562,7 +671,6 @@ class EPMoEBlock:
                                      self._ret.data_ptr(), H, self.out.data_ptr(),
                                      self.out.stride(0), s), lib)
         mark("combine")
-        return self.out
 
     def capture(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
                 warmup: int = 1) -> torch.cuda.CUDAGraph:

@@ -113,3 +113,49 @@ def test_reference_data_layout(pkg):
     assert tuple(c.shape) == (80, 256, 1) and c.dtype == torch.float16
     assert tuple(sfr[0][0].shape) == (32, 4, 1, 4, 8, 1)
     assert sizes == [(80, 256, 512, 1)]
+
+
+def test_single_device_fabric_allocations(pkg):
+    """Emulated ranks: one zeroed buffer per rank and allocation, every rank seeing every
+    rank's address; ranks that disagree on a size are rejected."""
+    EP = pkg.expert_parallel
+    fab = EP.SingleDeviceFabric(3, "cpu")
+    views = [fab.rank_view(r) for r in range(3)]
+    got = [v.allocate(4096, torch.device("cpu")) for v in views]
+    bases = got[0][1]
+    assert len(set(bases)) == 3
+    for r, (buf, b) in enumerate(got):
+        assert b == bases and buf.data_ptr() == bases[r] and buf.numel() == 4096
+        assert int(buf.sum()) == 0
+    second = [v.allocate(512, torch.device("cpu")) for v in views[:2]]
+    assert second[0][1] == second[1][1] and second[0][1][0] != bases[0]
+    with pytest.raises(ValueError):
+        views[2].allocate(1024, torch.device("cpu"))
+    with pytest.raises(ValueError):
+        fab.rank_view(3)
+    with pytest.raises(ValueError):
+        EP.SingleDeviceFabric(0, "cpu")
+
+
+def test_run_lockstep_order(pkg):
+    """Every emulated rank reaches a barrier point before any rank passes it."""
+    EP = pkg.expert_parallel
+    log = []
+
+    class Fake:
+        def __init__(self, rank, barriers):
+            self.rank, self.barriers, self.out = rank, barriers, rank
+
+        def phases(self, *args):
+            for k in range(self.barriers):
+                log.append((k, self.rank))
+                yield
+            log.append((self.barriers, self.rank))
+
+    outs = EP.run_lockstep([Fake(r, 3) for r in range(4)], [()] * 4)
+    assert outs == [0, 1, 2, 3]
+    assert log == [(k, r) for k in range(4) for r in range(4)]
+    with pytest.raises(RuntimeError):
+        EP.run_lockstep([Fake(0, 2), Fake(1, 3)], [(), ()])
+    with pytest.raises(ValueError):
+        EP.run_lockstep([Fake(0, 2)], [(), ()])
