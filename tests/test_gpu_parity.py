@@ -9,6 +9,8 @@ harness's distribution are also checked with the harness tolerance 1e-3
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -353,14 +355,19 @@ def test_cfg3_gated_full_size(pkg, cta):
 
 
 def test_cfg5_gated_checksum_subset(pkg):
-    """Full cfg5 launch (256 experts); oracle on a spread of experts (size-independent check)."""
-    prob = pkg.workloads.make_config("cfg5", seed=5, device="cuda")
+    """Full cfg5 launch (256 experts); oracle on a spread of experts (size-independent check).
+
+    The experts checked besides the first and the last are drawn from the seed
+    (``NVFP4_TEST_SEED``, default 5), so runs with other seeds check other experts."""
+    seed = int(os.environ.get("NVFP4_TEST_SEED", "5"))
+    picks = np.random.default_rng(seed).choice(np.arange(1, 255), size=6, replace=False)
+    prob = pkg.workloads.make_config("cfg5", seed=seed, device="cuda")
     run_custom_kernel(pkg, prob)
-    check_problem(prob, groups=[0, 1, 63, 128, 200, 255])
+    check_problem(prob, groups=[0, *sorted(int(g) for g in picks[:4]), 255])
     # every output element was written (the buffers were prefilled with randn; finite check
     # plus a recomputation of two experts in a second launch must agree bit for bit)
-    sub = pkg.workloads.make_config("cfg5", seed=5, device="cuda")
-    keep = [3, 250]
+    sub = pkg.workloads.make_config("cfg5", seed=seed, device="cuda")
+    keep = sorted(int(g) for g in picks[4:])
     pkg.grouped_gemm([sub.a[g] for g in keep], [sub.b[g] for g in keep],
                      [sub.sfa[g] for g in keep], [sub.sfb[g] for g in keep],
                      [sub.c[g] for g in keep], [sub.problem_sizes()[g] for g in keep],
