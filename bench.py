@@ -170,11 +170,9 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
-def cpu_baseline(cfg: str):
-    """Time the CPU oracle (numpy restatement of ref_kernel) on the configuration."""
-    import numpy as np
-
-    from oracle import nvfp4_oracle as O
+def _cpu_problem(cfg: str):
+    """The configuration's inputs on the host (seed 0, as rank 0 of the GPU arm) as numpy
+    arrays for the CPU oracle."""
     import submission
 
     pkg = submission.load_package()
@@ -184,7 +182,14 @@ def cpu_baseline(cfg: str):
                prob.sfb_plain[g].numpy(), prob.b2[g].numpy() if prob.gated else None,
                prob.sfb2_plain[g].numpy() if prob.gated else None, prob.alpha[g],
                prob.alpha2[g] if prob.gated else 1.0) for g in groups]
-    budget_s = 20.0
+    return prob, groups, arrays
+
+
+def _cpu_step(cfg: str, prob, groups, arrays, budget_s: float) -> dict:
+    """One bounded sample of the configuration through the CPU oracle (numpy restatement of
+    ref_kernel): groups in order until all are done or `budget_s` has passed."""
+    from oracle import nvfp4_oracle as O
+
     done_flops = 0.0
     t0 = time.perf_counter()
     calls = 0
@@ -205,24 +210,56 @@ def cpu_baseline(cfg: str):
             "us_per_call_extrapolated": dt / max(done_flops, 1.0) * prob.flops() * 1e6}
 
 
+def cpu_baseline(cfg: str, budget_s: float = 20.0) -> dict:
+    """Time the CPU oracle (numpy restatement of ref_kernel) on the configuration."""
+    prob, groups, arrays = _cpu_problem(cfg)
+    return _cpu_step(cfg, prob, groups, arrays, budget_s)
+
+
+def workload_config(args, prob, world: int, strong: bool) -> dict:
+    """The `config` record of a line: the workload both arms run."""
+    flush_l2 = prob.input_bytes() < L2_BYTES
+    return {"workload": args.config + (f"[experts {args.experts}]" if args.experts else ""),
+            "groups_per_gpu": prob.num_groups,
+            "m_per_group": prob.m if len(prob.m) <= 16 else f"{sum(prob.m)} rows",
+            "n": prob.n, "k": prob.k, "gated": prob.gated,
+            "input_bytes_per_gpu": prob.input_bytes(),
+            "l2": ("inputs smaller than L2 (126 MB): 256 MiB flush before every timed "
+                   "call, outside its events" if flush_l2 else
+                   "inputs larger than L2 (126 MB); no flush"),
+            "parallelism": f"ep{world} (" + ("experts of one configuration split over "
+                                              "the ranks" if strong else "every rank its own "
+                                              "experts") + ", no data-path collective)",
+            **({"split_k": True} if args.split_k else {})}
+
+
 def run_reference(args):
+    """The reference arm: the reference's arithmetic (ref_kernel, restated by the CPU oracle;
+    the reference's own ref_kernel needs torch._scaled_mm on a GPU) on the host cores, on the
+    GPU arm's workload, metric and step counts. Rank 0 alone runs it."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    res = []
-    for _ in range(args.warmup):
-        pass  # the CPU path has no warm-up state worth excluding beyond the first step below
-    steps = max(1, min(args.steps, 3))
-    for _ in range(steps):
-        res.append(cpu_baseline(args.config))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    prob, groups, arrays = _cpu_problem(args.config)
+    # Each step is a bounded sample, so that the whole run stays within about two minutes.
+    warmup = max(args.warmup, 3)
+    budget = max(0.5, 100.0 / max(1, args.steps + warmup))
+    for _ in range(warmup):
+        _cpu_step(args.config, prob, groups, arrays, budget)
+    res = [_cpu_step(args.config, prob, groups, arrays, budget) for _ in range(args.steps)]
     v = statistics.median(r["value"] for r in res)
+    strong = args.shard_experts and world > 1 and not args.experts
     line = {
         "impl": "reference", "metric": f"NVFP4 grouped GEMM TFLOP/s ({args.config})",
-        "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": steps,
-        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.config},
-        "cpu_baseline": {**res[0], "value": v},
+        "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": warmup, "higher_is_better": True,
+        "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; e2m1 codes uniform over 16, E4M3 scales 2^U{-4..3})",
+        "config": workload_config(args, prob, world, strong),
+        "cpu_baseline": {**res[len(res) // 2], "value": v,
+                         "sample": res[len(res) // 2]["sample"] +
+                         f" per step; median of {args.steps} steps after {warmup} warm-up"},
         "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -1491,18 +1528,7 @@ def main():
         "vs_baseline": None,
         "dtype": "e2m1xe4m3->f32->f16",
         "data": "synthetic (seeded; e2m1 codes uniform over 16, E4M3 scales 2^U{-4..3})",
-        "config": {"workload": args.config + (f"[experts {args.experts}]" if args.experts else ""),
-                   "groups_per_gpu": prob.num_groups,
-                   "m_per_group": prob.m if len(prob.m) <= 16 else f"{sum(prob.m)} rows",
-                   "n": prob.n, "k": prob.k, "gated": prob.gated,
-                   "input_bytes_per_gpu": prob.input_bytes(),
-                   "l2": ("inputs smaller than L2 (126 MB): 256 MiB flush before every timed "
-                          "call, outside its events" if flush_l2 else
-                          "inputs larger than L2 (126 MB); no flush"),
-                   "parallelism": f"ep{world} (" + ("experts of one configuration split over "
-                                                     "the ranks" if strong else "every rank its own "
-                                                     "experts") + ", no data-path collective)",
-                   **({"split_k": True} if args.split_k else {})},
+        "config": workload_config(args, prob, world, strong),
         "gpu_launches": args.steps,  # one persistent GEMM kernel per timed call (descriptors reused)
         "api": "GroupedGemmPlan.run (value, burst); custom_kernel(data) (e2e)",
         "device_error_bits": errors,
