@@ -752,25 +752,64 @@ def run_quantize(args):
     print(json.dumps(line), flush=True)
 
 
-def run_moe_ep(args, world):
-    """The expert-parallel MoE block (EPMoEBlock) at cfg5's shape over `world` GPUs: the
-    32768 tokens split evenly over the ranks, the 256 experts too (strong scaling of one
-    batch); routed rows cross NVLink in NVFP4 and results come back to their tokens' rank."""
-    import datetime
-
+def pcie_bandwidth(dev, s_h2d, s_d2h, nbytes: int = 256 << 20) -> dict:
+    """Host<->device copy rates of pinned memory on this GPU (GB/s, best of 5): each
+    direction alone, then both at once on the two streams."""
     import torch
-    import torch.distributed as dist
 
-    import submission
+    host_a = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    host_b = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dev_a = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    dev_b = torch.empty(nbytes, dtype=torch.uint8, device=dev)
 
-    pkg = submission.load_package()
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    def rate(fn, stream):
+        best = 0.0
+        for _ in range(5):
+            torch.cuda.synchronize(dev)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            best = max(best, nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+        return best
+
+    def h2d():
+        with torch.cuda.stream(s_h2d):
+            dev_a.copy_(host_a, non_blocking=True)
+
+    def d2h():
+        with torch.cuda.stream(s_d2h):
+            host_b.copy_(dev_b, non_blocking=True)
+
+    out = {"h2d_gbs": rate(h2d, s_h2d), "d2h_gbs": rate(d2h, s_d2h)}
+    both_h2d, both_d2h = 0.0, 0.0
+    for _ in range(5):
+        torch.cuda.synchronize(dev)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record(s_h2d)
+        ev[2].record(s_d2h)
+        h2d()
+        d2h()
+        ev[1].record(s_h2d)
+        ev[3].record(s_d2h)
+        torch.cuda.synchronize(dev)
+        both_h2d = max(both_h2d, nbytes / (ev[0].elapsed_time(ev[1]) * 1e-3) / 1e9)
+        both_d2h = max(both_d2h, nbytes / (ev[2].elapsed_time(ev[3]) * 1e-3) / 1e9)
+    out["h2d_concurrent_gbs"] = both_h2d
+    out["d2h_concurrent_gbs"] = both_d2h
+    return out
+
+
+def ep_block_inputs(pkg, dev, world: int, rank: int, tokens: int):
+    """Seeded inputs of the expert-parallel MoE block at cfg5's shape (256 experts, top-8,
+    H 7168, I 2048) for `rank` of `world`: this rank's NVFP4 expert weights (random codes,
+    scales 2^-1 / 2^0), tokens // world bf16 tokens and their uniform top-8 routing."""
+    import torch
+
     E, topk, H, I = 256, 8, 7168, 2048
-    T = args.tokens // world
+    T = tokens // world
     epr = E // world
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
 
@@ -797,6 +836,96 @@ def run_moe_ep(args, world):
     wts = torch.softmax(top.values, dim=1)
     s_x = pkg.global_scale_for(x)
     s_h = 0.01  # fixed SiLU-output scale (values do not change the timing)
+    return dict(E=E, topk=topk, H=H, I=I, T=T, epr=epr, weights=weights, x=x, ids=ids, wts=wts,
+                s_x=s_x, s_h=s_h)
+
+
+def ep_block_leg(pkg, dev, world: int, rank: int, steps: int, warmup: int, barrier,
+                 max_over_ranks, sum_over_ranks, tokens: int = 32768) -> dict:
+    """The expert-parallel MoE block (EPMoEBlock, owner-side sums) at cfg5's shape with the
+    tokens and the experts split over the ranks: strong scaling of one batch. At P = 1 the
+    same block runs as one rank (SingleDeviceFabric), so every N times the same code path.
+    Calls back to back, events around `steps` calls, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    EP = pkg.expert_parallel
+    # Every rank must set up before the timed collectives: a rank that could not makes all
+    # of them skip the leg.
+    try:
+        inp = ep_block_inputs(pkg, dev, world, rank, tokens)
+        fabric = EP.SingleDeviceFabric(1, dev).rank_view(0) if world == 1 else None
+        blk = EP.EPMoEBlock(inp["weights"], inp["E"], inp["T"], inp["topk"], inp["s_x"],
+                            inp["s_h"], fabric=fabric)
+        err = None
+    except Exception as exc:  # reported in the line, not fatal to the bench
+        blk, err = None, f"{type(exc).__name__}: {exc}"[:200]
+    if world > 1:
+        agree = torch.tensor([0 if blk is None else 1], dtype=torch.int32, device=dev)
+        dist.all_reduce(agree, op=dist.ReduceOp.MIN)
+        ok = int(agree.item()) == 1
+    else:
+        ok = blk is not None
+    if not ok:
+        return {"unavailable": err or "set-up failed on another rank"}
+    x, ids, wts = inp["x"], inp["ids"], inp["wts"]
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(warmup, 3)):
+        blk.run(x, ids, wts)
+    torch.cuda.synchronize(dev)
+    barrier()
+    n = max(3, min(steps, 10))
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        blk.run(x, ids, wts)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n)
+    evs = []
+    blk.run(x, ids, wts, stage_events=evs)
+    torch.cuda.synchronize(dev)
+    stage_us = {nm: a.elapsed_time(b) * 1e3 for (_, a), (nm, b) in zip(evs[:-1], evs[1:])}
+    pairs = sum_over_ranks(float((ids >= 0).sum().item()))
+    flops = 6.0 * pairs * inp["H"] * inp["I"]
+    rec = {"us_per_call": ms * 1e3, "tflops": flops / (ms * 1e-3) / 1e12, "steps": n,
+           "tokens_per_rank": inp["T"], "experts_per_rank": inp["epr"], "flops_total": flops,
+           "scaling": "strong", "return_mode": blk.return_mode,
+           "stage_us_rank0": stage_us, "exchange_error_bits": blk.check_errors(),
+           "what": "expert_parallel.EPMoEBlock.run (route, quantise, NVFP4 token rows to their "
+                   "experts' owners over NVLink peer stores, gated GEMM with NVFP4 output, down "
+                   "GEMM, weighted owner-side sums returned to the tokens' ranks, combine; 3 "
+                   "one-element NCCL barriers per call) of 32768 tokens x top-8 over 256 experts "
+                   "split over the ranks, back to back, max over ranks; one GPU: the same block "
+                   "as a single rank"}
+    barrier()
+    del blk, inp
+    torch.cuda.empty_cache()
+    return rec
+
+
+def run_moe_ep(args, world):
+    """The expert-parallel MoE block (EPMoEBlock) at cfg5's shape over `world` GPUs: the
+    32768 tokens split evenly over the ranks, the 256 experts too (strong scaling of one
+    batch); routed rows cross NVLink in NVFP4 and results come back to their tokens' rank."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import submission
+
+    pkg = submission.load_package()
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    inp = ep_block_inputs(pkg, dev, world, rank, args.tokens)
+    E, topk, H, I, T, epr = (inp[k] for k in ("E", "topk", "H", "I", "T", "epr"))
+    weights, x, ids, wts, s_x, s_h = (inp[k] for k in ("weights", "x", "ids", "wts", "s_x", "s_h"))
     steps = max(1, min(args.steps, 10))
     pairs = torch.tensor([int((ids >= 0).sum().item())], dtype=torch.float64, device=dev)
     dist.all_reduce(pairs)
@@ -1376,6 +1505,15 @@ def main():
             sharded["frac_of_measured_nvfp4_sustained"] = (
                 sharded["tflops"] / (world * nvfp4_peak["sustained_tflops"]))
 
+    # ---------------------------------------------------------------- EP MoE block, split over the ranks
+    ep_block = None
+    if not args.no_extras:
+        ep_block = ep_block_leg(pkg, dev, world, rank, args.steps, args.warmup, barrier,
+                                max_over_ranks, sum_over_ranks)
+        if "tflops" in ep_block:
+            ep_block["frac_of_per_gpu_peak"] = ep_block["tflops"] / (
+                world * FP4_PER_BF16 * float(peaks[sustained_key]))
+
     # ---------------------------------------------------------------- the reference's kernel (N = 1)
     # The reference's own sm_100 kernel (its CuTe-DSL submission, unmodified) through its own
     # custom_kernel on this configuration, beside this library's custom_kernel.
@@ -1465,6 +1603,8 @@ def main():
     data = datas[0]
     scales = scales[0]
     del probs[1], dev_in, datas
+    pcie = pcie_bandwidth(dev, h2d_stream, d2h_stream)
+    pcie_ms = max(h2d / (pcie["h2d_concurrent_gbs"] * 1e6), d2h / (pcie["d2h_concurrent_gbs"] * 1e6))
 
     # The drop-in call itself on device-resident inputs: custom_kernel(data) back to back
     # (device time per call, and the host time to issue one call).
@@ -1540,7 +1680,12 @@ def main():
                 "serial": {"value": flops_job / (e2e_serial_ms * 1e-3) / 1e12,
                            "ms_per_step": e2e_serial_ms,
                            "what": "the same step with copies and call on one stream"},
-                "buffer_sets_equal_outputs": same_out},
+                "buffer_sets_equal_outputs": same_out,
+                "pcie": dict(pcie, bound_ms_per_step=pcie_ms, frac=pcie_ms / e2e_ms,
+                             what="pinned-host copies of 256 MiB alone and with the other "
+                                  "direction running (two copy streams); bound_ms_per_step: "
+                                  "the step's H2D and D2H bytes at the concurrent rates; frac: "
+                                  "that bound over the measured e2e step")},
         "cuda_graph": graph_info,
         "custom_kernel_device_resident": {
             "us_per_call": ck_ms * 1e3, "host_us_per_call": sorted(ck_host)[len(ck_host) // 2] * 1e6,
@@ -1576,6 +1721,8 @@ def main():
         line["nvfp4_peak"] = nvfp4_peak
     if sharded is not None:
         line["sharded_cfg5"] = sharded
+    if ep_block is not None:
+        line["ep_block"] = ep_block
     if configs is not None:
         line["geomean_us_per_call"] = configs["geomean_us_per_call"]
         line["configs"] = configs
