@@ -1529,7 +1529,8 @@ def main():
     # its fp16 outputs back. Two buffer sets: step i's H2D (copy stream) overlaps step i-1's
     # kernel and D2H (second copy stream), events order each set's reuse. `serial` is the
     # same step with all copies and the call on one stream, one step after another.
-    e2e_steps = args.e2e_steps or max(4, min(args.steps, 10))
+    # The same K steps as `value` (at least 4, at most 50 to bound the run's length).
+    e2e_steps = args.e2e_steps or max(4, min(args.steps, 50))
     probs = [prob, pkg.workloads.make_config(args.config, seed=seed, device=dev, experts=shard)]
 
     def inputs_of(p):
@@ -1673,7 +1674,8 @@ def main():
         "api": "GroupedGemmPlan.run (value, burst); custom_kernel(data) (e2e)",
         "device_error_bits": errors,
         "e2e": {"value": flops_job / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms, "steps": e2e_steps,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "custom_kernel(data); every step: H2D of all inputs from pinned host "
                        "memory, the call, D2H of all outputs; two buffer sets so that step i's "
                        "H2D overlaps step i-1's call and D2H (two copy streams)",
