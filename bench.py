@@ -86,6 +86,9 @@ def parse_args():
     ap.add_argument("--tokens", type=int, default=32768,
                     help="--op moe: tokens per step (32768 = cfg5's 262144 routed rows; 64 = a "
                          "decode step)")
+    ap.add_argument("--ep", action="store_true",
+                    help="--op moe on one GPU: the expert-parallel block as a single rank "
+                         "(its exchange kernels included) instead of MoEBlock")
     ap.add_argument("--ep-return", default="both", choices=["sums", "rows", "both"],
                     help="--op moe over N > 1 GPUs: how expert outputs return to their tokens' "
                          "ranks (owner-side sums, per-pair rows, or both timed in turn)")
@@ -922,23 +925,37 @@ def run_moe_ep(args, world):
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    multi = world > 1
+    if multi:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+
+    def barrier():
+        if multi:
+            barrier()
+
+    def all_reduce(t, op=None):
+        if multi:
+            dist.all_reduce(t, op=op if op is not None else dist.ReduceOp.SUM)
+
     inp = ep_block_inputs(pkg, dev, world, rank, args.tokens)
     E, topk, H, I, T, epr = (inp[k] for k in ("E", "topk", "H", "I", "T", "epr"))
     weights, x, ids, wts, s_x, s_h = (inp[k] for k in ("weights", "x", "ids", "wts", "s_x", "s_h"))
     steps = max(1, min(args.steps, 10))
     pairs = torch.tensor([int((ids >= 0).sum().item())], dtype=torch.float64, device=dev)
-    dist.all_reduce(pairs)
+    all_reduce(pairs)
     flops = 6.0 * float(pairs.item()) * H * I
 
     def measure(mode):
         """Eager, per-stage and CUDA-graph timings of one EPMoEBlock in `mode` (max over
         ranks), its output on this rank, and its exchange error bits."""
-        blk = pkg.expert_parallel.EPMoEBlock(weights, E, T, topk, s_x, s_h, return_mode=mode)
+        # One GPU: the same block as a single rank (SingleDeviceFabric, no process group).
+        fabric = None if multi else pkg.expert_parallel.SingleDeviceFabric(1, dev).rank_view(0)
+        blk = pkg.expert_parallel.EPMoEBlock(weights, E, T, topk, s_x, s_h, return_mode=mode,
+                                             fabric=fabric)
         for _ in range(max(args.warmup, 3)):
             blk.run(x, ids, wts)
         torch.cuda.synchronize(dev)
-        dist.barrier(device_ids=[local_rank])
+        barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -947,7 +964,7 @@ def run_moe_ep(args, world):
         e1.record()
         torch.cuda.synchronize(dev)
         t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         # One instrumented call: device time between the stages (this rank).
         evs = []
@@ -959,18 +976,18 @@ def run_moe_ep(args, world):
         graph = blk.capture(x, ids, wts)
         graph.replay()
         torch.cuda.synchronize(dev)
-        dist.barrier(device_ids=[local_rank])
+        barrier()
         e0.record()
         for _ in range(steps):
             graph.replay()
         e1.record()
         torch.cuda.synchronize(dev)
         t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        all_reduce(t, op=dist.ReduceOp.MAX)
         graph_ms = float(t.item())
         del graph
         err = blk.check_errors()
-        dist.barrier(device_ids=[local_rank])
+        barrier()
         del blk
         torch.cuda.empty_cache()
         return {"return_mode": mode, "ms_per_step": ms, "us_per_call": ms * 1e3,
@@ -996,8 +1013,9 @@ def run_moe_ep(args, world):
     tf = flops / (ms * 1e-3) / 1e12
     peaks, kind = load_peaks()
     peak = world * FP4_PER_BF16 * float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
-    dist.barrier(device_ids=[local_rank])
-    dist.destroy_process_group()
+    barrier()
+    if multi:
+        dist.destroy_process_group()
     if rank != 0:
         return
     print(json.dumps({
@@ -1044,7 +1062,7 @@ def run_moe(args):
     import submission
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if world > 1:
+    if world > 1 or args.ep:
         return run_moe_ep(args, world)
 
     pkg = submission.load_package()
