@@ -302,11 +302,18 @@ def test_descriptor_reuse_and_rebuild(pkg):
 # ----------------------------------------------------------------------------
 # Scale-factor converter: bit-exact
 # ----------------------------------------------------------------------------
-@pytest.mark.parametrize("rows,cols", [(1, 1), (80, 32), (128, 4), (129, 5), (257, 448), (4096, 448)])
-def test_sf_to_blocked_bit_exact(pkg, rows, cols):
+# Byte-wise kernel: sf_cols or the row stride not a multiple of 16 (1, 4, 5 columns). Tiled
+# kernel (whole 16-byte chunks): the rest, including strided rows (ld > cols), a partial
+# last tile of blocks (448 columns = 3.5 tiles of 32 blocks) and ragged row counts.
+@pytest.mark.parametrize("rows,cols,ld", [(1, 1, 1), (80, 32, 32), (128, 4, 4), (129, 5, 5),
+                                          (257, 448, 448), (4096, 448, 448), (129, 16, 32),
+                                          (300, 144, 160), (77, 272, 288), (1000, 1024, 1024)])
+def test_sf_to_blocked_bit_exact(pkg, rows, cols, ld):
     rng = np.random.default_rng(rows * 1000 + cols)
     plain = rng.integers(0, 256, (rows, cols), dtype=np.uint8)
-    out = pkg.sf_to_blocked(torch.from_numpy(plain).cuda())
+    buf = torch.zeros((rows, ld), dtype=torch.uint8)
+    buf[:, :cols] = torch.from_numpy(plain)
+    out = pkg.sf_to_blocked(buf.cuda()[:, :cols])
     torch.cuda.synchronize()
     assert np.array_equal(_np(out), O.to_blocked(plain))
 
