@@ -270,12 +270,17 @@ NVFP4_API int nvfp4_ep_combine_sums(const int32_t* topk_ids, const int32_t* remo
   if (!aligned16(out) || !aligned16(ret) || ldo % 8 != 0 || ldo < cols)
     return fail(NVFP4_ERR_MISALIGNED, "ret and out 16-byte aligned, ldo a multiple of 8 >= cols");
   const int groups = (cols + 256 * kEpSumParts - 1) / (256 * kEpSumParts);
-  const int64_t warps = static_cast<int64_t>(tokens) * groups;
+  // A warp task covers a run of a token's column groups, so the token's owner mask (one
+  // round trip to the routing ids) is read once per run; launches with few tokens keep one
+  // group per task, so that every SM still gets warps.
+  const int per_task = static_cast<int64_t>(tokens) * groups > 148 * 64 ? groups : 1;
+  const int64_t warps =
+      static_cast<int64_t>(tokens) * ((groups + per_task - 1) / per_task);
   const int64_t blocks = std::min<int64_t>((warps + 7) / 8, 148 * 16);
   nvfp4_ep_combine_sums_kernel<<<static_cast<unsigned>(blocks), 256, 0,
                                  static_cast<cudaStream_t>(stream)>>>(
       topk_ids, remote_rows, tokens, topk, num_experts, world, static_cast<const __half*>(ret),
-      cols, static_cast<__nv_bfloat16*>(out), ldo);
+      cols, static_cast<__nv_bfloat16*>(out), ldo, per_task);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "combine sums launch");
   return NVFP4_OK;

@@ -400,50 +400,59 @@ __global__ void __launch_bounds__(256) nvfp4_ep_return_sums_kernel(
 __global__ void __launch_bounds__(256) nvfp4_ep_combine_sums_kernel(
     const int32_t* __restrict__ ids, const int32_t* __restrict__ remote_rows, int tokens,
     int topk, int num_experts, int world, const __half* __restrict__ ret, int cols,
-    __nv_bfloat16* __restrict__ out, int64_t ldo) {
+    __nv_bfloat16* __restrict__ out, int64_t ldo, int groups_per_task) {
   const int lane = threadIdx.x & 31;
   const int groups = (cols + 256 * kEpSumParts - 1) / (256 * kEpSumParts);
+  const int chunks = (groups + groups_per_task - 1) / groups_per_task;  // tasks per token
   const int epr = num_experts / world;
   const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  for (int64_t task = warp0; task < static_cast<int64_t>(tokens) * groups; task += nwarps) {
-    const int64_t t = task / groups;
-    const int col0 = static_cast<int>(task % groups) * 256 * kEpSumParts + lane * 8;
-    uint32_t owners = 0;  // bit p: owner p holds a kept pair of t
-    for (int j = 0; j < topk; ++j) {
+  for (int64_t task = warp0; task < static_cast<int64_t>(tokens) * chunks; task += nwarps) {
+    const int64_t t = task / chunks;
+    const int g0 = static_cast<int>(task % chunks) * groups_per_task;
+    const int g1 = min(groups, g0 + groups_per_task);
+    // Bit p: owner p holds a kept pair of t. The lanes read the token's slots side by side,
+    // once per task (a task covers groups_per_task column groups of the token).
+    uint32_t bit = 0;
+    for (int j = lane; j < topk; j += 32) {
       const int e = __ldg(ids + t * topk + j);
       if (__ldg(remote_rows + t * topk + j) >= 0 && e >= 0 && e < num_experts)
-        owners |= 1u << (e / epr);
+        bit |= 1u << (e / epr);
     }
-    float acc[kEpSumParts][8];
+    const uint32_t owners = __reduce_or_sync(0xffffffffu, bit);
+#pragma unroll 2
+    for (int g = g0; g < g1; ++g) {
+      const int col0 = g * 256 * kEpSumParts + lane * 8;
+      float acc[kEpSumParts][8];
 #pragma unroll
-    for (int u = 0; u < kEpSumParts; ++u)
+      for (int u = 0; u < kEpSumParts; ++u)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[u][i] = 0.0f;
-    for (int p0 = 0; p0 < world; p0 += 2) {
-      uint4 raw[2][kEpSumParts];
+        for (int i = 0; i < 8; ++i) acc[u][i] = 0.0f;
+      for (int p0 = 0; p0 < world; p0 += 2) {
+        uint4 raw[2][kEpSumParts];
 #pragma unroll
-      for (int v = 0; v < 2; ++v)
+        for (int v = 0; v < 2; ++v)
 #pragma unroll
-        for (int u = 0; u < kEpSumParts; ++u) {
+          for (int u = 0; u < kEpSumParts; ++u) {
+            const int p = p0 + v;
+            const int col = col0 + 256 * u;
+            raw[v][u] = (p < world && ((owners >> p) & 1u) && col < cols)
+                            ? __ldg(reinterpret_cast<const uint4*>(ret + (t * world + p) * cols + col))
+                            : make_uint4(0u, 0u, 0u, 0u);
+          }
+#pragma unroll
+        for (int v = 0; v < 2; ++v) {
           const int p = p0 + v;
-          const int col = col0 + 256 * u;
-          raw[v][u] = (p < world && ((owners >> p) & 1u) && col < cols)
-                          ? __ldg(reinterpret_cast<const uint4*>(ret + (t * world + p) * cols + col))
-                          : make_uint4(0u, 0u, 0u, 0u);
+          if (p >= world || !((owners >> p) & 1u)) continue;
+#pragma unroll
+          for (int u = 0; u < kEpSumParts; ++u) add_half8(acc[u], raw[v][u], 1.0f, false);
         }
-#pragma unroll
-      for (int v = 0; v < 2; ++v) {
-        const int p = p0 + v;
-        if (p >= world || !((owners >> p) & 1u)) continue;
-#pragma unroll
-        for (int u = 0; u < kEpSumParts; ++u) add_half8(acc[u], raw[v][u], 1.0f, false);
       }
-    }
 #pragma unroll
-    for (int u = 0; u < kEpSumParts; ++u) {
-      const int col = col0 + 256 * u;
-      if (col < cols) store_bf16x8(out + t * ldo + col, acc[u]);
+      for (int u = 0; u < kEpSumParts; ++u) {
+        const int col = col0 + 256 * u;
+        if (col < cols) store_bf16x8(out + t * ldo + col, acc[u]);
+      }
     }
   }
 }
