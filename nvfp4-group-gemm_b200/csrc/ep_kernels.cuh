@@ -395,8 +395,10 @@ __global__ void __launch_bounds__(256) nvfp4_ep_return_sums_kernel(
 }
 
 // out[t, :] = bf16( sum over owners p (ascending) that hold at least one kept pair of t of
-// fp32(ret[t, p, :]) ), fp32 sums. One warp per (token, group of kEpSumParts 256-column
-// parts); the rows of two owners (every part) are loaded before they are added.
+// fp32(ret[t, p, :]) ), fp32 sums. One warp per task: groups_per_task consecutive groups of
+// kEpSumParts 256-column parts of one token (all of them when the launch has enough tokens
+// to fill the GPU), so the token's owner mask is read once per task; within a group the rows
+// of two owners (every part) are loaded before they are added.
 __global__ void __launch_bounds__(256) nvfp4_ep_combine_sums_kernel(
     const int32_t* __restrict__ ids, const int32_t* __restrict__ remote_rows, int tokens,
     int topk, int num_experts, int world, const __half* __restrict__ ret, int cols,
